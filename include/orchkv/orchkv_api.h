@@ -1,0 +1,162 @@
+/*
+ * orchkv_api.h — data-plane C ABI (orchkv_*) of the B200 implementation.
+ *
+ * The reference entry points (src/api/orchkv_api.h:28-121) keep their names,
+ * arguments and return codes.  Slab layout is the reference's
+ * (src/api/orchkv_api.cu:8-18): one slab per (request, layer, KV head, token
+ * block), K rows in the first half, V rows in the second, token t at
+ * t*d_head*dtype_size within each half.
+ *
+ * What differs inside: the GPU slab pool, the pinned host-DRAM slab pool, the
+ * free stacks and every block's location live in GPU-visible memory and are
+ * changed only by CUDA kernels, so per-block calls and batched calls share one
+ * state.  Per-block calls are one small kernel plus a stream synchronisation
+ * (the reference issues one cudaMemcpyAsync + cudaStreamSynchronize per slab
+ * half).  Host pointers passed to prefill/append may be pageable, pinned, or
+ * device pointers (detected with cudaPointerGetAttributes).
+ *
+ * Entry points marked "B200" are new batched forms of the per-block calls.
+ */
+#ifndef ORCHKV_API_H
+#define ORCHKV_API_H
+
+#include <pthread.h>
+#include "kv_types.h"
+#include "tiered_manager.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct kv_request_ctx kv_request_ctx_t;   /* opaque request handle */
+
+/* Pool snapshots returned by the accessors (fields as in
+ * src/tiered_store/gpu_tier.h:10-20 and dram_tier.h:10-20; free_stack points
+ * to a host copy refreshed at each accessor call). */
+typedef struct gpu_tier {
+    int             device_id;
+    void           *pool_base;
+    size_t          pool_size;
+    size_t          slab_size;
+    uint32_t        total_slabs;
+    uint32_t        used_slabs;
+    uint32_t       *free_stack;
+    uint32_t        free_top;
+    pthread_mutex_t lock;
+} gpu_tier_t;
+
+typedef struct dram_tier {
+    void           *pool_base;
+    size_t          pool_size;
+    size_t          slab_size;
+    uint32_t        total_slabs;
+    uint32_t        used_slabs;
+    uint32_t       *free_stack;
+    uint32_t        free_top;
+    bool            is_pinned;
+    pthread_mutex_t lock;
+} dram_tier_t;
+
+/* ---- reference entry points --------------------------------------------- */
+int  orchkv_init(const orchkv_config_t *config);
+int  orchkv_shutdown(void);
+bool orchkv_is_initialized(void);
+
+kv_request_ctx_t *orchkv_request_create(uint64_t request_id, uint32_t n_layers,
+                                        uint32_t n_kv_heads);
+int  orchkv_request_destroy(kv_request_ctx_t *ctx);
+
+/* k_data / v_data: [n_kv_heads][seq_len][d_head] of dtype. */
+int  orchkv_prefill(kv_request_ctx_t *ctx, uint32_t layer_id, const void *k_data,
+                    const void *v_data, uint32_t seq_len);
+/* k_token / v_token: [n_kv_heads][d_head] of dtype. */
+int  orchkv_append_token(kv_request_ctx_t *ctx, uint32_t layer_id,
+                         const void *k_token, const void *v_token);
+/* Promotes DRAM/storage blocks to GPU first; returns device pointers to the K
+ * and V halves of the slab. */
+int  orchkv_get_kv_block(kv_request_ctx_t *ctx, uint32_t layer_id, uint32_t head_id,
+                         uint32_t block_idx, void **k_out, void **v_out);
+int  orchkv_evict_to_dram(kv_request_ctx_t *ctx, uint32_t layer_id,
+                          uint32_t head_id, uint32_t block_idx);
+int  orchkv_promote_to_gpu(kv_request_ctx_t *ctx, uint32_t layer_id,
+                           uint32_t head_id, uint32_t block_idx);
+int  orchkv_evict_to_storage(kv_request_ctx_t *ctx, uint32_t layer_id,
+                             uint32_t head_id, uint32_t block_idx);
+int  orchkv_promote_from_storage(kv_request_ctx_t *ctx, uint32_t layer_id,
+                                 uint32_t head_id, uint32_t block_idx);
+int  orchkv_evict_cold(kv_request_ctx_t *ctx, uint32_t layer_id,
+                       uint32_t head_id, uint32_t block_idx);
+void orchkv_storage_flush(void);
+int  orchkv_get_stats(orchkv_stats_t *stats);
+gpu_tier_t  *orchkv_gpu_tier(void);
+dram_tier_t *orchkv_dram_tier(void);
+
+/* ---- B200 ------------------------------------------------------------------ */
+
+/* Extra sizing not present in orchkv_config_t (kept out of that struct so its
+ * layout stays the reference's).  Zero fields take defaults. */
+typedef struct orchkv_config_ext {
+    uint32_t max_blocks;      /* block-id space; default gpu_slabs + dram_slabs
+                                 rounded up to a power of two                  */
+    uint32_t max_requests;    /* concurrent requests; default 4096             */
+    uint64_t table_entries;   /* block-table entries for all requests; default
+                                 max_blocks * 2                                 */
+    uint32_t reserved[12];
+} orchkv_config_ext_t;
+
+int  orchkv_init_ext(const orchkv_config_t *config, const orchkv_config_ext_t *ext);
+
+/* All data-plane GPU work runs on this stream (cudaStream_t; NULL restores
+ * the library's own stream). */
+int  orchkv_set_stream(void *stream);
+int  orchkv_sync(void);
+
+/* Block ids of the data plane become slots of `tm` (tm capacity must cover
+ * max_blocks): new blocks register themselves, migrations keep the
+ * scheduler's tier view current, destroyed requests unregister. */
+int  orchkv_attach_scheduler(tiered_manager_t *tm);
+
+/* orchkv_append_token for every (request, layer) pair, in request-major then
+ * layer order, as one launch sequence.  All requests must share n_layers and
+ * n_kv_heads.  k/v: [n][n_layers][n_kv_heads][d_head] of dtype, device or
+ * host memory.  All-or-nothing: ERR_TIER_FULL if the pools cannot hold the
+ * new blocks, ERR_STATE if some last block is not on the GPU. */
+int  orchkv_append_token_batch(kv_request_ctx_t *const *ctxs, uint32_t n,
+                               const void *k, const void *v);
+
+/* Batched orchkv_evict_to_dram / orchkv_promote_to_gpu over a device list of
+ * block ids, with exactly the per-block semantics applied in list order:
+ * blocks in the wrong tier (or pinned, for evict) are skipped; once the
+ * destination pool is empty the rest fail with TIER_FULL.  `count` (device
+ * uint32*) may be NULL to use max_n.  `result` (device uint32[2], may be NULL)
+ * receives {migrated, skipped}.  Asynchronous. */
+int  orchkv_evict_batch_to_dram(const uint32_t *block_ids, const uint32_t *count,
+                                uint32_t max_n, uint32_t *result);
+int  orchkv_promote_batch_to_gpu(const uint32_t *block_ids, const uint32_t *count,
+                                 uint32_t max_n, uint32_t *result);
+
+/* Device table [n*n_layers][n_kv_heads][ceil(row_len/tpb)] of block ids of
+ * the given requests (0xFFFFFFFF where a block does not exist), the layout
+ * tm_report_attn_probs takes.  Asynchronous. */
+int  orchkv_block_id_table(kv_request_ctx_t *const *ctxs, uint32_t n,
+                           uint32_t row_len, uint32_t *out);
+
+/* Introspection for tests and tools (synchronous). */
+int  orchkv_block_info(kv_request_ctx_t *ctx, uint32_t layer_id, uint32_t head_id,
+                       uint32_t block_idx, uint64_t *block_id, int *tier,
+                       uint32_t *slab, int *state, uint32_t *token_count);
+int  orchkv_set_block_flags(kv_request_ctx_t *ctx, uint32_t layer_id,
+                            uint32_t head_id, uint32_t block_idx, uint8_t flags);
+/* which: 0 = GPU pool, 1 = DRAM pool.  Copies the free stack (total entries)
+ * and its top. */
+int  orchkv_read_pool(int which, uint32_t *stack_out, uint32_t *top_out);
+/* Location words ((tier << 29) | slab) and states of all max_blocks ids. */
+int  orchkv_read_block_locs(uint32_t *loc_out, uint8_t *state_out);
+uint32_t orchkv_max_blocks(void);
+void *orchkv_gpu_pool_base(void);
+void *orchkv_dram_pool_base(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ORCHKV_API_H */

@@ -1,0 +1,696 @@
+// api.cu — host side of the orchkv data plane (orchkv_* C ABI).
+//
+// The reference keeps one global system (src/api/orchkv_api.cu:20-30) with a
+// cudaMalloc'd GPU slab pool, a pinned DRAM slab pool, host LIFO free stacks
+// and per-request host block vectors, and moves each slab with its own
+// cudaMemcpyAsync + stream sync.  Here the same global system keeps pools,
+// free stacks, block locations and request block tables in GPU-visible memory;
+// every state change is made by a kernel on one stream, so per-block calls
+// and batched calls observe one consistent state.  The DRAM pool is pinned
+// and mapped, so migration kernels read and write it directly over the host
+// link (fused gather+D2H and H2D+scatter).
+#include <errno.h>
+#include <fcntl.h>
+#include <stdlib.h>
+#include <string.h>
+#include <unistd.h>
+
+#include <map>
+#include <mutex>
+#include <vector>
+
+#include "kernels.h"
+#include "orchkv/orchkv_api.h"
+#include "pool.h"
+#include "tm_internal.h"
+
+using namespace okv;
+
+struct kv_request_ctx {
+    uint64_t request_id;
+    uint32_t L, H, mbph;
+    size_t region_off;     // words into the block-table array
+    size_t region_words;
+};
+
+namespace {
+
+struct Sys {
+    std::recursive_mutex mu;
+    bool inited = false;
+    orchkv_config_t cfg;
+    int device = 0;
+    cudaStream_t own = nullptr, stream = nullptr;
+    PoolDev p;
+    char *dev_meta = nullptr;         // stacks, loc/state/flags, counters
+    uint32_t *bt = nullptr;           // block-table array
+    size_t bt_words = 0;
+    std::map<size_t, size_t> free_regions;   // offset -> words
+    uint32_t *scratch = nullptr;
+    size_t scratch_words = 0;
+    CompatResult *res = nullptr;      // pinned
+    PoolCounters *h_ctr = nullptr;    // pinned
+    char *stage = nullptr;            // device staging for pageable inputs
+    size_t stage_cap = 0;
+    uint32_t **regions_dev = nullptr; // device array of region pointers
+    uint32_t **regions_host = nullptr;// pinned
+    uint32_t regions_cap = 0;
+    std::vector<uint32_t *> regions_last;
+    tiered_manager_t *attached = nullptr;
+    uint32_t active_requests = 0;
+    gpu_tier_t gsnap;
+    dram_tier_t dsnap;
+    std::vector<uint32_t> gsnap_stack, dsnap_stack;
+};
+
+Sys g;
+
+uint32_t pow2_at_least(uint64_t v)
+{
+    uint64_t c = 1;
+    while (c < v) c <<= 1;
+    return (uint32_t)c;
+}
+
+ReqDev req_dev(const kv_request_ctx *c)
+{
+    ReqDev r;
+    r.region = g.bt + c->region_off;
+    r.L = c->L;
+    r.H = c->H;
+    r.mbph = c->mbph;
+    return r;
+}
+
+int sync_result(int *rc_out)
+{
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    if (rc_out) *rc_out = g.res->rc;
+    return ORCHKV_OK;
+}
+
+// Resolve a caller pointer to something kernels can read: device and mapped
+// pinned memory are used in place, pageable memory is staged with one copy.
+int resolve_input(const void *ptr, size_t bytes, size_t stage_off, const char **out)
+{
+    *out = nullptr;
+    if (!ptr) return ORCHKV_OK;
+    cudaPointerAttributes a;
+    cudaError_t e = cudaPointerGetAttributes(&a, ptr);
+    if (e == cudaSuccess && (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged)) {
+        *out = (const char *)ptr;
+        return ORCHKV_OK;
+    }
+    if (e == cudaSuccess && a.type == cudaMemoryTypeHost && a.devicePointer) {
+        *out = (const char *)a.devicePointer;
+        return ORCHKV_OK;
+    }
+    cudaGetLastError();   // clear a failed attribute query
+    const size_t need = stage_off + bytes;
+    if (need > g.stage_cap) {
+        size_t cap = g.stage_cap ? g.stage_cap : (1 << 20);
+        while (cap < need) cap *= 2;
+        OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+        cudaFree(g.stage);
+        g.stage = nullptr;
+        g.stage_cap = 0;
+        OKV_CUDA_TRY(cudaMalloc((void **)&g.stage, cap));
+        g.stage_cap = cap;
+    }
+    OKV_CUDA_TRY(cudaMemcpyAsync(g.stage + stage_off, ptr, bytes, cudaMemcpyHostToDevice, g.stream));
+    *out = g.stage + stage_off;
+    return ORCHKV_OK;
+}
+
+int upload_regions(kv_request_ctx_t *const *ctxs, uint32_t n, uint32_t *L, uint32_t *H,
+                   uint32_t *mbph)
+{
+    if (!ctxs || n == 0) return ORCHKV_ERR_INVALID;
+    for (uint32_t i = 0; i < n; i++) {
+        if (!ctxs[i]) return ORCHKV_ERR_INVALID;
+        if (ctxs[i]->L != ctxs[0]->L || ctxs[i]->H != ctxs[0]->H) return ORCHKV_ERR_INVALID;
+    }
+    *L = ctxs[0]->L;
+    *H = ctxs[0]->H;
+    *mbph = ctxs[0]->mbph;
+    std::vector<uint32_t *> want(n);
+    for (uint32_t i = 0; i < n; i++) want[i] = g.bt + ctxs[i]->region_off;
+    if (want == g.regions_last) return ORCHKV_OK;
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    if (n > g.regions_cap) {
+        cudaFree(g.regions_dev);
+        cudaFreeHost(g.regions_host);
+        g.regions_dev = nullptr;
+        g.regions_host = nullptr;
+        OKV_CUDA_TRY(cudaMalloc((void **)&g.regions_dev, (size_t)n * sizeof(uint32_t *)));
+        OKV_CUDA_TRY(cudaMallocHost((void **)&g.regions_host, (size_t)n * sizeof(uint32_t *)));
+        g.regions_cap = n;
+    }
+    memcpy(g.regions_host, want.data(), (size_t)n * sizeof(uint32_t *));
+    OKV_CUDA_TRY(cudaMemcpyAsync(g.regions_dev, g.regions_host, (size_t)n * sizeof(uint32_t *),
+                                 cudaMemcpyHostToDevice, g.stream));
+    g.regions_last = want;
+    return ORCHKV_OK;
+}
+
+size_t region_alloc(size_t words)
+{
+    for (auto it = g.free_regions.begin(); it != g.free_regions.end(); ++it) {
+        if (it->second >= words) {
+            const size_t off = it->first, len = it->second;
+            g.free_regions.erase(it);
+            if (len > words) g.free_regions[off + words] = len - words;
+            return off;
+        }
+    }
+    return (size_t)-1;
+}
+
+void region_free(size_t off, size_t words)
+{
+    auto it = g.free_regions.emplace(off, words).first;
+    auto nx = std::next(it);
+    if (nx != g.free_regions.end() && it->first + it->second == nx->first) {
+        it->second += nx->second;
+        g.free_regions.erase(nx);
+    }
+    if (it != g.free_regions.begin()) {
+        auto pv = std::prev(it);
+        if (pv->first + pv->second == it->first) {
+            pv->second += it->second;
+            g.free_regions.erase(it);
+        }
+    }
+}
+
+void release_all()
+{
+    if (g.stream) cudaStreamSynchronize(g.stream);
+    cudaFree(g.p.gpu_base);
+    if (g.p.dram_base) cudaFreeHost(g.p.dram_base);
+    cudaFree(g.dev_meta);
+    cudaFree(g.bt);
+    cudaFree(g.scratch);
+    cudaFree(g.stage);
+    cudaFree(g.regions_dev);
+    cudaFreeHost(g.regions_host);
+    cudaFreeHost(g.res);
+    cudaFreeHost(g.h_ctr);
+    if (g.own) cudaStreamDestroy(g.own);
+    g.p = PoolDev();
+    g.dev_meta = nullptr;
+    g.bt = nullptr;
+    g.scratch = nullptr;
+    g.stage = nullptr;
+    g.stage_cap = 0;
+    g.regions_dev = nullptr;
+    g.regions_host = nullptr;
+    g.regions_cap = 0;
+    g.regions_last.clear();
+    g.res = nullptr;
+    g.h_ctr = nullptr;
+    g.own = g.stream = nullptr;
+    g.free_regions.clear();
+    g.attached = nullptr;
+    g.active_requests = 0;
+}
+
+int compat(kv_request_ctx_t *ctx, int op, uint32_t l, uint32_t h, uint32_t bi, uint32_t arg)
+{
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (!ctx) return ORCHKV_ERR_NOT_FOUND;
+    int rc = launch_compat_op(g.p, req_dev(ctx), op, l, h, bi, arg, g.res, g.stream);
+    if (rc) return rc;
+    int krc = 0;
+    rc = sync_result(&krc);
+    return rc ? rc : krc;
+}
+
+}  // namespace
+
+// Access for the no-device-copy paths of other translation units.
+cudaStream_t orchkv_stream_internal() { return g.stream; }
+
+extern "C" {
+
+int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (g.inited) return ORCHKV_ERR_ALREADY;
+    if (!cfg) return ORCHKV_ERR_INVALID;
+    const size_t e = dtype_size(cfg->dtype);
+    const size_t slab = kv_block_data_bytes(cfg->tokens_per_block, cfg->d_head, cfg->dtype);
+    if (e == 0 || slab == 0 || cfg->gpu_pool_bytes < slab || cfg->dram_pool_bytes < slab ||
+        cfg->max_blocks_per_head == 0)
+        return ORCHKV_ERR_INVALID;
+    g.cfg = *cfg;
+    g.device = cfg->gpu_device_id;
+    OKV_CUDA_TRY(cudaSetDevice(g.device));
+    OKV_CUDA_TRY(cudaStreamCreateWithFlags(&g.own, cudaStreamNonBlocking));
+    g.stream = g.own;
+
+    PoolDev &p = g.p;
+    p = PoolDev();
+    p.slab = slab;
+    p.half = slab / 2;
+    p.row = (uint32_t)(cfg->d_head * e);
+    p.tpb = cfg->tokens_per_block;
+    const uint64_t g_total = cfg->gpu_pool_bytes / slab, d_total = cfg->dram_pool_bytes / slab;
+    if (g_total > kLocSlabMask || d_total > kLocSlabMask) return ORCHKV_ERR_INVALID;
+    p.g_total = (uint32_t)g_total;
+    p.d_total = (uint32_t)d_total;
+    uint64_t mb = ext && ext->max_blocks ? ext->max_blocks : pow2_at_least(g_total + d_total);
+    if (mb > 0x7FFFFFFFull) mb = 0x7FFFFFFFull;
+    p.max_blocks = (uint32_t)mb;
+
+    if (cudaMalloc((void **)&p.gpu_base, (size_t)p.g_total * slab) != cudaSuccess) {
+        fprintf(stderr, "[orchkv] GPU pool allocation of %zu MB failed\n",
+                ((size_t)p.g_total * slab) >> 20);
+        release_all();
+        return ORCHKV_ERR_CUDA;
+    }
+    // The DRAM tier must be pinned and mapped: migration kernels address it.
+    if (cudaHostAlloc((void **)&p.dram_base, (size_t)p.d_total * slab,
+                      cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+        fprintf(stderr, "[orchkv] pinned DRAM pool allocation of %zu MB failed\n",
+                ((size_t)p.d_total * slab) >> 20);
+        p.dram_base = nullptr;
+        release_all();
+        return ORCHKV_ERR_CUDA;
+    }
+    char *dram_dev = nullptr;
+    if (cudaHostGetDevicePointer((void **)&dram_dev, p.dram_base, 0) != cudaSuccess ||
+        dram_dev != p.dram_base) {
+        fprintf(stderr, "[orchkv] DRAM pool is not addressable at its host address\n");
+        release_all();
+        return ORCHKV_ERR_CUDA;
+    }
+
+    const size_t meta = ((size_t)p.g_total + p.d_total + p.max_blocks) * 4 +
+                        (size_t)p.max_blocks * 6 + sizeof(PoolCounters) + 8 * 256;
+    if (cudaMalloc((void **)&g.dev_meta, meta) != cudaSuccess) { release_all(); return ORCHKV_ERR_CUDA; }
+    char *q = g.dev_meta;
+    auto take = [&](size_t sz) { char *r = q; q += (sz + 255) & ~size_t(255); return r; };
+    p.g_stack = (uint32_t *)take((size_t)p.g_total * 4);
+    p.d_stack = (uint32_t *)take((size_t)p.d_total * 4);
+    p.id_stack = (uint32_t *)take((size_t)p.max_blocks * 4);
+    p.loc = (uint32_t *)take((size_t)p.max_blocks * 4);
+    p.state = (uint8_t *)take(p.max_blocks);
+    p.flags = (uint8_t *)take(p.max_blocks);
+    p.ctr = (PoolCounters *)take(sizeof(PoolCounters));
+
+    // stacks hold N-1 ... 0 so the first pops return 0, 1, 2, ...
+    // (src/tiered_store/gpu_tier.cu:41-42)
+    {
+        uint64_t mx = p.g_total > p.d_total ? p.g_total : p.d_total;
+        if (p.max_blocks > mx) mx = p.max_blocks;
+        std::vector<uint32_t> fill(mx);
+        auto up = [&](uint32_t *dst, uint32_t n) -> int {
+            for (uint32_t i = 0; i < n; i++) fill[i] = n - 1 - i;
+            OKV_CUDA_TRY(cudaMemcpy(dst, fill.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+            return ORCHKV_OK;
+        };
+        int rc = up(p.g_stack, p.g_total);
+        if (!rc) rc = up(p.d_stack, p.d_total);
+        if (!rc) rc = up(p.id_stack, p.max_blocks);
+        if (rc) { release_all(); return rc; }
+    }
+    OKV_CUDA_TRY(cudaMemset(p.loc, 0xFF, (size_t)p.max_blocks * 4));  // tier 7: no block
+    OKV_CUDA_TRY(cudaMemset(p.state, KV_STATE_EVICTED, p.max_blocks));
+    OKV_CUDA_TRY(cudaMemset(p.flags, 0, p.max_blocks));
+    PoolCounters c0;
+    memset(&c0, 0, sizeof(c0));
+    c0.g_top = p.g_total;
+    c0.d_top = p.d_total;
+    c0.id_top = p.max_blocks;
+    OKV_CUDA_TRY(cudaMemcpy(p.ctr, &c0, sizeof(c0), cudaMemcpyHostToDevice));
+
+    g.bt_words = ext && ext->table_entries ? ext->table_entries : (size_t)p.max_blocks * 2 + 65536;
+    if (cudaMalloc((void **)&g.bt, g.bt_words * 4) != cudaSuccess) { release_all(); return ORCHKV_ERR_CUDA; }
+    g.free_regions.clear();
+    g.free_regions[0] = g.bt_words;
+    g.scratch_words = (size_t)p.max_blocks * 2 + p.max_blocks / 1024 + 4096 +
+                      (size_t)2 * (ext && ext->max_requests ? ext->max_requests : 4096) * 256;
+    if (cudaMalloc((void **)&g.scratch, g.scratch_words * 4) != cudaSuccess) {
+        release_all();
+        return ORCHKV_ERR_CUDA;
+    }
+    OKV_CUDA_TRY(cudaMallocHost((void **)&g.res, sizeof(CompatResult)));
+    OKV_CUDA_TRY(cudaMallocHost((void **)&g.h_ctr, sizeof(PoolCounters)));
+    memset(g.res, 0, sizeof(CompatResult));
+    g.active_requests = 0;
+    g.inited = true;
+    return ORCHKV_OK;
+}
+
+int orchkv_init(const orchkv_config_t *config) { return orchkv_init_ext(config, nullptr); }
+
+int orchkv_shutdown(void)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    release_all();
+    g.inited = false;
+    return ORCHKV_OK;
+}
+
+bool orchkv_is_initialized(void) { return g.inited; }
+
+kv_request_ctx_t *orchkv_request_create(uint64_t request_id, uint32_t n_layers,
+                                        uint32_t n_kv_heads)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited || n_layers == 0 || n_kv_heads == 0) return nullptr;
+    const uint32_t mbph = g.cfg.max_blocks_per_head;
+    const size_t words = req_region_words(n_layers, n_kv_heads, mbph);
+    const size_t off = region_alloc(words);
+    if (off == (size_t)-1) return nullptr;
+    kv_request_ctx_t *c = new (std::nothrow) kv_request_ctx_t();
+    if (!c) { region_free(off, words); return nullptr; }
+    c->request_id = request_id;
+    c->L = n_layers;
+    c->H = n_kv_heads;
+    c->mbph = mbph;
+    c->region_off = off;
+    c->region_words = words;
+    uint32_t *r = g.bt + off;
+    if (cudaMemsetAsync(r, 0, (1 + n_layers) * 4, g.stream) != cudaSuccess ||
+        cudaMemsetAsync(r + 1 + n_layers, 0xFF, (words - 1 - n_layers) * 4, g.stream) != cudaSuccess) {
+        region_free(off, words);
+        delete c;
+        return nullptr;
+    }
+    g.active_requests++;
+    return c;
+}
+
+int orchkv_request_destroy(kv_request_ctx_t *ctx)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!ctx) return ORCHKV_ERR_INVALID;
+    if (!g.inited) { delete ctx; return ORCHKV_ERR_INIT; }
+    int rc = launch_request_free(g.p, req_dev(ctx), g.stream);
+    if (rc) return rc;
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    region_free(ctx->region_off, ctx->region_words);
+    g.regions_last.clear();
+    if (g.active_requests) g.active_requests--;
+    delete ctx;
+    return ORCHKV_OK;
+}
+
+int orchkv_prefill(kv_request_ctx_t *ctx, uint32_t layer, const void *k, const void *v,
+                   uint32_t seq_len)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (!ctx || layer >= ctx->L) return ORCHKV_ERR_INVALID;
+    const size_t bytes = (size_t)ctx->H * seq_len * g.p.row;
+    const char *kd, *vd;
+    int rc = resolve_input(k, bytes, 0, &kd);
+    if (!rc) rc = resolve_input(v, bytes, bytes, &vd);
+    if (rc) return rc;
+    rc = launch_prefill(g.p, req_dev(ctx), layer, kd, vd, seq_len, g.scratch, g.res, g.stream);
+    if (rc) return rc;
+    int krc = 0;
+    rc = sync_result(&krc);
+    return rc ? rc : krc;
+}
+
+int orchkv_append_token(kv_request_ctx_t *ctx, uint32_t layer, const void *k, const void *v)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (!ctx || layer >= ctx->L) return ORCHKV_ERR_INVALID;
+    const size_t bytes = (size_t)ctx->H * g.p.row;
+    const char *kd, *vd;
+    int rc = resolve_input(k, bytes, 0, &kd);
+    if (!rc) rc = resolve_input(v, bytes, bytes, &vd);
+    if (rc) return rc;
+    rc = launch_append_one(g.p, req_dev(ctx), layer, kd, vd, g.res, g.stream);
+    if (rc) return rc;
+    int krc = 0;
+    rc = sync_result(&krc);
+    return rc ? rc : krc;
+}
+
+int orchkv_get_kv_block(kv_request_ctx_t *ctx, uint32_t l, uint32_t h, uint32_t bi,
+                        void **k_out, void **v_out)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    const int rc = compat(ctx, OP_GET, l, h, bi, 0);
+    if (rc) return rc;
+    if (k_out) *k_out = (void *)g.res->k_ptr;
+    if (v_out) *v_out = (void *)g.res->v_ptr;
+    return ORCHKV_OK;
+}
+
+int orchkv_evict_to_dram(kv_request_ctx_t *ctx, uint32_t l, uint32_t h, uint32_t bi)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    return compat(ctx, OP_EVICT, l, h, bi, 0);
+}
+
+int orchkv_promote_to_gpu(kv_request_ctx_t *ctx, uint32_t l, uint32_t h, uint32_t bi)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    return compat(ctx, OP_PROMOTE, l, h, bi, 0);
+}
+
+// The file tier (src/tiered_store/orchfs_tier.c) is not part of this build yet.
+int orchkv_evict_to_storage(kv_request_ctx_t *, uint32_t, uint32_t, uint32_t)
+{
+    return g.inited ? ORCHKV_ERR_INIT : ORCHKV_ERR_INIT;
+}
+
+int orchkv_promote_from_storage(kv_request_ctx_t *, uint32_t, uint32_t, uint32_t)
+{
+    return ORCHKV_ERR_INIT;
+}
+
+int orchkv_evict_cold(kv_request_ctx_t *ctx, uint32_t l, uint32_t h, uint32_t bi)
+{
+    int rc = orchkv_evict_to_dram(ctx, l, h, bi);
+    if (rc != ORCHKV_OK) return rc;
+    return orchkv_evict_to_storage(ctx, l, h, bi);
+}
+
+void orchkv_storage_flush(void) {}
+
+int orchkv_get_stats(orchkv_stats_t *s)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (!s) return ORCHKV_ERR_INVALID;
+    OKV_CUDA_TRY(cudaMemcpyAsync(g.h_ctr, g.p.ctr, sizeof(PoolCounters), cudaMemcpyDeviceToHost, g.stream));
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    const PoolCounters &c = *g.h_ctr;
+    memset(s, 0, sizeof(*s));
+    s->gpu_pool_total = (size_t)g.p.g_total * g.p.slab;
+    s->gpu_slabs_total = g.p.g_total;
+    s->gpu_slabs_used = g.p.g_total - c.g_top;
+    s->gpu_pool_used = (size_t)s->gpu_slabs_used * g.p.slab;
+    s->dram_pool_total = (size_t)g.p.d_total * g.p.slab;
+    s->dram_slabs_total = g.p.d_total;
+    s->dram_slabs_used = g.p.d_total - c.d_top;
+    s->dram_pool_used = (size_t)s->dram_slabs_used * g.p.slab;
+    s->total_blocks = c.live_blocks;
+    s->transfers_d2h = c.transfers_d2h;
+    s->transfers_h2d = c.transfers_h2d;
+    s->bytes_d2h = c.bytes_d2h;
+    s->bytes_h2d = c.bytes_h2d;
+    return ORCHKV_OK;
+}
+
+gpu_tier_t *orchkv_gpu_tier(void)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return nullptr;
+    uint32_t top = 0;
+    g.gsnap_stack.resize(g.p.g_total);
+    if (orchkv_read_pool(0, g.gsnap_stack.data(), &top) != ORCHKV_OK) return nullptr;
+    gpu_tier_t &t = g.gsnap;
+    t.device_id = g.device;
+    t.pool_base = g.p.gpu_base;
+    t.pool_size = (size_t)g.p.g_total * g.p.slab;
+    t.slab_size = g.p.slab;
+    t.total_slabs = g.p.g_total;
+    t.used_slabs = g.p.g_total - top;
+    t.free_stack = g.gsnap_stack.data();
+    t.free_top = top;
+    return &t;
+}
+
+dram_tier_t *orchkv_dram_tier(void)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return nullptr;
+    uint32_t top = 0;
+    g.dsnap_stack.resize(g.p.d_total);
+    if (orchkv_read_pool(1, g.dsnap_stack.data(), &top) != ORCHKV_OK) return nullptr;
+    dram_tier_t &t = g.dsnap;
+    t.pool_base = g.p.dram_base;
+    t.pool_size = (size_t)g.p.d_total * g.p.slab;
+    t.slab_size = g.p.slab;
+    t.total_slabs = g.p.d_total;
+    t.used_slabs = g.p.d_total - top;
+    t.free_stack = g.dsnap_stack.data();
+    t.free_top = top;
+    t.is_pinned = true;
+    return &t;
+}
+
+// ---- B200 ------------------------------------------------------------------
+
+int orchkv_set_stream(void *stream)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    g.stream = stream ? (cudaStream_t)stream : g.own;
+    if (g.attached) tm_set_stream(g.attached, g.stream);
+    return ORCHKV_OK;
+}
+
+int orchkv_sync(void)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    return ORCHKV_OK;
+}
+
+int orchkv_attach_scheduler(tiered_manager_t *tm)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (!tm) {
+        g.p.attached = 0;
+        g.attached = nullptr;
+        return ORCHKV_OK;
+    }
+    TmImpl *t = tm_impl(tm);
+    if (!t) return ORCHKV_ERR_INVALID;
+    if (t->cap < g.p.max_blocks) return ORCHKV_ERR_INVALID;
+    int rc = tm_set_stream(tm, g.stream);
+    if (rc) return rc;
+    g.p.sd = t->d;
+    g.p.attached = 1;
+    g.attached = tm;
+    return ORCHKV_OK;
+}
+
+int orchkv_append_token_batch(kv_request_ctx_t *const *ctxs, uint32_t n, const void *k,
+                              const void *v)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    uint32_t L, H, mbph;
+    int rc = upload_regions(ctxs, n, &L, &H, &mbph);
+    if (rc) return rc;
+    const size_t P = (size_t)n * L;
+    if (2 * P + 16 > g.scratch_words) return ORCHKV_ERR_INVALID;
+    const size_t bytes = P * H * g.p.row;
+    const char *kd, *vd;
+    rc = resolve_input(k, bytes, 0, &kd);
+    if (!rc) rc = resolve_input(v, bytes, bytes, &vd);
+    if (rc) return rc;
+    rc = launch_append_batch(g.p, g.regions_dev, n, L, H, mbph, kd, vd, g.scratch, g.stream);
+    if (rc) return rc;
+    // the all-or-nothing verdict is needed by the caller: read it back
+    uint32_t err = 0;
+    OKV_CUDA_TRY(cudaMemcpyAsync(&g.h_ctr->err, g.scratch + 2 * P, 4, cudaMemcpyDeviceToHost, g.stream));
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    err = g.h_ctr->err;
+    return (int)err;
+}
+
+int orchkv_evict_batch_to_dram(const uint32_t *ids, const uint32_t *count, uint32_t max_n,
+                               uint32_t *result)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (max_n && !ids) return ORCHKV_ERR_INVALID;
+    if ((size_t)2 * max_n + max_n / 1024 + 32 > g.scratch_words) return ORCHKV_ERR_INVALID;
+    return launch_migrate_batch(g.p, 0, ids, count, max_n, result, g.scratch, g.stream);
+}
+
+int orchkv_promote_batch_to_gpu(const uint32_t *ids, const uint32_t *count, uint32_t max_n,
+                                uint32_t *result)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (max_n && !ids) return ORCHKV_ERR_INVALID;
+    if ((size_t)2 * max_n + max_n / 1024 + 32 > g.scratch_words) return ORCHKV_ERR_INVALID;
+    return launch_migrate_batch(g.p, 1, ids, count, max_n, result, g.scratch, g.stream);
+}
+
+int orchkv_block_id_table(kv_request_ctx_t *const *ctxs, uint32_t n, uint32_t row_len,
+                          uint32_t *out)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (!out || row_len == 0) return ORCHKV_ERR_INVALID;
+    uint32_t L, H, mbph;
+    int rc = upload_regions(ctxs, n, &L, &H, &mbph);
+    if (rc) return rc;
+    return launch_id_table(g.p, g.regions_dev, n, L, H, mbph, row_len, out, g.stream);
+}
+
+int orchkv_block_info(kv_request_ctx_t *ctx, uint32_t l, uint32_t h, uint32_t bi,
+                      uint64_t *block_id, int *tier, uint32_t *slab, int *state,
+                      uint32_t *token_count)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    const int rc = compat(ctx, OP_INFO, l, h, bi, 0);
+    if (rc) return rc;
+    const CompatResult &r = *g.res;
+    if (block_id) *block_id = r.id;
+    if (tier) *tier = (int)loc_tier(r.loc);
+    if (slab) *slab = loc_slab(r.loc);
+    if (state) *state = (int)r.state;
+    if (token_count) *token_count = r.tok;
+    return ORCHKV_OK;
+}
+
+int orchkv_set_block_flags(kv_request_ctx_t *ctx, uint32_t l, uint32_t h, uint32_t bi,
+                           uint8_t flags)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    return compat(ctx, OP_SET_FLAGS, l, h, bi, flags);
+}
+
+int orchkv_read_pool(int which, uint32_t *stack_out, uint32_t *top_out)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (which != 0 && which != 1) return ORCHKV_ERR_INVALID;
+    OKV_CUDA_TRY(cudaMemcpyAsync(g.h_ctr, g.p.ctr, sizeof(PoolCounters), cudaMemcpyDeviceToHost, g.stream));
+    const uint32_t total = which == 0 ? g.p.g_total : g.p.d_total;
+    if (stack_out)
+        OKV_CUDA_TRY(cudaMemcpyAsync(stack_out, which == 0 ? g.p.g_stack : g.p.d_stack,
+                                     (size_t)total * 4, cudaMemcpyDeviceToHost, g.stream));
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    if (top_out) *top_out = which == 0 ? g.h_ctr->g_top : g.h_ctr->d_top;
+    return ORCHKV_OK;
+}
+
+int orchkv_read_block_locs(uint32_t *loc_out, uint8_t *state_out)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (loc_out)
+        OKV_CUDA_TRY(cudaMemcpyAsync(loc_out, g.p.loc, (size_t)g.p.max_blocks * 4,
+                                     cudaMemcpyDeviceToHost, g.stream));
+    if (state_out)
+        OKV_CUDA_TRY(cudaMemcpyAsync(state_out, g.p.state, g.p.max_blocks,
+                                     cudaMemcpyDeviceToHost, g.stream));
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    return ORCHKV_OK;
+}
+
+uint32_t orchkv_max_blocks(void) { return g.inited ? g.p.max_blocks : 0; }
+void *orchkv_gpu_pool_base(void) { return g.inited ? g.p.gpu_base : nullptr; }
+void *orchkv_dram_pool_base(void) { return g.inited ? g.p.dram_base : nullptr; }
+
+}  // extern "C"

@@ -1,0 +1,70 @@
+// kernels.h — host-side launchers of the orchkv B200 CUDA kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace okv {
+
+// ---- scoring (sched_kernels.cu) ---------------------------------------------
+int launch_score(const float *probs, uint32_t R, uint32_t Hq, uint32_t Hkv,
+                 uint32_t T, uint32_t tpb, const uint32_t *lens,
+                 const uint32_t *ids, const SchedDev &d, unsigned long long step,
+                 cudaStream_t s);
+int launch_report_apply(const uint32_t *slots, const float *psum, const float *pmax,
+                        uint32_t n, const SchedDev &d, unsigned long long step,
+                        cudaStream_t s);
+int launch_report_batch(const uint32_t *ids, const float *w, uint32_t n,
+                        const SchedDev &d, unsigned long long step, cudaStream_t s);
+int launch_sweep(const SchedDev &d, const SchedParams &p, bool step_done,
+                 bool classify, ClassCounts *counts, cudaStream_t s);
+int launch_registry_count(const uint32_t *reg_slot, const uint8_t *reg_tier,
+                          uint32_t n, const SchedDev &d, float th_gpu,
+                          float th_dram, uint32_t *count, cudaStream_t s);
+// Slot writes applied in list order: op 0 = register (tracker + classifier
+// reset, flags, tier, state), 1 = unregister, 2 = update tier/flags/state.
+// `b` packs per entry {op, flags, tier, state}.
+int launch_slot_ops(const uint32_t *slots, const uint8_t *b, uint32_t n,
+                    const SchedDev &d, cudaStream_t s);
+
+// ---- selection (select_kernels.cu) -------------------------------------------
+enum SelectMode { kSelectColdest = 0, kSelectPrefetch = 1 };
+
+struct SelectScratch {
+    uint32_t *hist_local;    // [4096 + 16]
+    uint32_t *hist_global;   // [4096 + 16]
+    uint32_t *state;         // SelState words
+    uint32_t *tile_counts;   // [2 * max_tiles]
+    uint32_t *tile_offsets;  // [2 * max_tiles]
+    uint32_t max_tiles;
+};
+
+// Host hook run between passes (multi-GPU): reduce `hist_local` into
+// `hist_global` over `nwords` words.  NULL = single device (device copy).
+typedef int (*hist_reduce_fn)(const uint32_t *local, uint32_t *global, uint32_t nwords,
+                              cudaStream_t s, void *ctx);
+typedef int (*tie_gather_fn)(const uint32_t *local_one, uint32_t *all_out,
+                             cudaStream_t s, void *ctx);
+
+struct SelectArgs {
+    SelectMode mode;
+    uint32_t k;          // explicit k (used when frac < 0)
+    float frac;          // >= 0: k = floor(frac * eligible)
+    float th_gpu, th_dram;
+    uint32_t max_out;
+    uint32_t *out_ids;
+    uint32_t *out_count;
+    hist_reduce_fn reduce;
+    tie_gather_fn gather;
+    void *comm_ctx;
+    int rank, world;
+    uint32_t *gather_buf;  // device [world]
+};
+
+int launch_select(const SchedDev &d, const SelectScratch &sc, const SelectArgs &a,
+                  cudaStream_t s);
+size_t select_scratch_words(uint32_t cap, uint32_t *max_tiles);
+
+}  // namespace okv

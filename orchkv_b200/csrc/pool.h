@@ -1,0 +1,87 @@
+// pool.h — device view of the data plane (slab pools, block records,
+// request block tables) shared by pool_kernels.cu and api.cu.
+#pragma once
+
+#include "common.cuh"
+
+namespace okv {
+
+struct PoolCounters {
+    uint32_t g_top, d_top, id_top, err;
+    unsigned long long transfers_d2h, transfers_h2d, bytes_d2h, bytes_h2d;
+    uint32_t last_done, last_skipped, live_blocks, pad;
+    unsigned long long scratch[4];
+};
+
+struct PoolDev {
+    char *gpu_base;
+    char *dram_base;                 // pinned + mapped host memory (UVA pointer)
+    unsigned long long slab, half;   // bytes
+    uint32_t row;                    // d_head * dtype bytes
+    uint32_t tpb;
+    uint32_t g_total, d_total, max_blocks;
+    uint32_t *g_stack, *d_stack, *id_stack;
+    uint32_t *loc;                   // (tier << 29) | slab, per block id
+    uint8_t *state, *flags;          // per block id
+    PoolCounters *ctr;
+    SchedDev sd;                     // attached scheduler (valid if attached)
+    int attached;
+};
+
+// A request's region in the block-table array:
+//   [0]              seq_len
+//   [1 .. L]         tokens held per layer (identical for all heads)
+//   [1+L ..]         block ids, [layer][head][max_blocks_per_head]
+struct ReqDev {
+    uint32_t *region;
+    uint32_t L, H, mbph;
+};
+
+__host__ __device__ inline uint32_t *req_tok(const ReqDev &r) { return r.region + 1; }
+__host__ __device__ inline uint32_t *req_table(const ReqDev &r) { return r.region + 1 + r.L; }
+__host__ __device__ inline size_t req_region_words(uint32_t L, uint32_t H, uint32_t mbph)
+{
+    return 1 + (size_t)L + (size_t)L * H * mbph;
+}
+
+// Result of a per-block (compat) operation, written by the kernel into
+// pinned host memory and read after the stream synchronises.
+struct CompatResult {
+    int rc;
+    uint32_t id;
+    unsigned long long k_ptr, v_ptr;
+    uint32_t loc, state, tok, pad;
+};
+
+enum CompatOp : int {
+    OP_EVICT = 0,
+    OP_PROMOTE = 1,
+    OP_GET = 2,          // promote if on DRAM, return pointers
+    OP_INFO = 3,
+    OP_SET_FLAGS = 4,
+};
+
+// ---- launchers (pool_kernels.cu) -------------------------------------------
+int launch_compat_op(const PoolDev &p, const ReqDev &r, int op, uint32_t l, uint32_t h,
+                     uint32_t bi, uint32_t arg, CompatResult *res, cudaStream_t s);
+int launch_append_one(const PoolDev &p, const ReqDev &r, uint32_t l, const char *k,
+                      const char *v, CompatResult *res, cudaStream_t s);
+int launch_prefill(const PoolDev &p, const ReqDev &r, uint32_t l, const char *k,
+                   const char *v, uint32_t seq_len, uint32_t *scratch,
+                   CompatResult *res, cudaStream_t s);
+// Batched append over n requests x L layers.  regions: device array of n
+// region pointers.  scratch: >= 2*n*L + 16 words.
+int launch_append_batch(const PoolDev &p, uint32_t *const *regions, uint32_t n, uint32_t L,
+                        uint32_t H, uint32_t mbph, const char *k, const char *v,
+                        uint32_t *scratch, cudaStream_t s);
+// Batched migration.  dir 0 = evict (GPU -> DRAM), 1 = promote (DRAM -> GPU).
+// scratch: >= 2*max_n + 2*tiles + 16 words where tiles = ceil(max_n/1024).
+int launch_migrate_batch(const PoolDev &p, int dir, const uint32_t *ids,
+                         const uint32_t *count, uint32_t max_n, uint32_t *result,
+                         uint32_t *scratch, cudaStream_t s);
+int launch_id_table(const PoolDev &p, uint32_t *const *regions, uint32_t n, uint32_t L,
+                    uint32_t H, uint32_t mbph, uint32_t row_len, uint32_t *out,
+                    cudaStream_t s);
+int launch_request_free(const PoolDev &p, const ReqDev &r, cudaStream_t s);
+
+}  // namespace okv

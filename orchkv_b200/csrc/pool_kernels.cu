@@ -1,0 +1,746 @@
+// pool_kernels.cu — data-plane kernels: per-block (compat) operations,
+// paged append (K6), prefill, batched migration gather/scatter (K4/K5), block
+// id tables and request teardown.
+//
+// Every kernel that pops or pushes a free stack reproduces the order in which
+// the reference's per-block host loops pop and push
+// (src/tiered_store/gpu_tier.cu:65-93, src/tiered_store/dram_tier.cu:70-98),
+// so a batched call leaves pools, free stacks and block locations exactly as
+// the equivalent sequence of per-block calls would.
+#include "pool.h"
+
+namespace okv {
+
+namespace {
+
+constexpr int kTileN = 1024;       // list entries per tile in batched migration
+
+// ---- attached-scheduler hooks ----------------------------------------------
+
+__device__ __forceinline__ void sched_register(const PoolDev &p, uint32_t id, uint8_t flags)
+{
+    if (!p.attached) return;
+    const SchedDev &d = p.sd;
+    const uint32_t s = id & d.mask;
+    d.sum[s] = 0.f; d.mx[s] = 0.f; d.ema[s] = 0.f; d.hits[s] = 0;
+    d.last[s] = kStepNever; d.tact[s] = 1;
+    d.hot[s] = 0.f;
+    d.heat[s] = (flags & KV_FLAG_ATTN_SINK) ? 0 : 2;
+    d.cflags[s] = flags; d.cact[s] = 1;
+    d.bflags[s] = flags; d.tier[s] = TIER_GPU_HBM; d.bstate[s] = KV_STATE_HOT;
+}
+
+__device__ __forceinline__ void sched_move(const PoolDev &p, uint32_t id, uint8_t tier,
+                                           uint8_t state)
+{
+    if (!p.attached) return;
+    const uint32_t s = id & p.sd.mask;
+    p.sd.tier[s] = tier;
+    p.sd.bstate[s] = state;
+}
+
+__device__ __forceinline__ void sched_unregister(const PoolDev &p, uint32_t id)
+{
+    if (!p.attached) return;
+    const SchedDev &d = p.sd;
+    const uint32_t s = id & d.mask;
+    d.sum[s] = 0.f; d.mx[s] = 0.f; d.ema[s] = 0.f; d.hits[s] = 0;
+    d.last[s] = 0; d.tact[s] = 0;
+    d.hot[s] = 0.f; d.heat[s] = 0; d.cflags[s] = 0; d.cact[s] = 0;
+    d.bflags[s] = 0; d.tier[s] = TIER_NONE; d.bstate[s] = 0;
+}
+
+// ---- cooperative copies ----------------------------------------------------
+
+// Copy `bytes` with `nt` cooperating threads (index `t`).  16-byte vectors when
+// both ends and the length allow it, 4-byte words or bytes otherwise.
+__device__ __forceinline__ void coop_copy(char *dst, const char *src, unsigned long long bytes,
+                                          unsigned t, unsigned nt)
+{
+    const uintptr_t a = (uintptr_t)dst | (uintptr_t)src | (uintptr_t)bytes;
+    if ((a & 15) == 0) {
+        const uint4 *s = reinterpret_cast<const uint4 *>(src);
+        uint4 *d = reinterpret_cast<uint4 *>(dst);
+        const unsigned long long n = bytes >> 4;
+        unsigned long long i = t;
+        for (; i + 3 * (unsigned long long)nt < n; i += 4 * (unsigned long long)nt) {
+            uint4 v0 = s[i], v1 = s[i + nt], v2 = s[i + 2 * nt], v3 = s[i + 3 * nt];
+            d[i] = v0; d[i + nt] = v1; d[i + 2 * nt] = v2; d[i + 3 * nt] = v3;
+        }
+        for (; i < n; i += nt) d[i] = s[i];
+    } else if ((a & 3) == 0) {
+        const uint32_t *s = reinterpret_cast<const uint32_t *>(src);
+        uint32_t *d = reinterpret_cast<uint32_t *>(dst);
+        for (unsigned long long i = t; i < (bytes >> 2); i += nt) d[i] = s[i];
+    } else {
+        for (unsigned long long i = t; i < bytes; i += nt) dst[i] = src[i];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Per-block operations (one CTA): the reference's orchkv_evict_to_dram /
+// orchkv_promote_to_gpu / orchkv_get_kv_block (src/api/orchkv_api.cu:321-428)
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256)
+compat_op_kernel(PoolDev p, ReqDev r, int op, uint32_t l, uint32_t h, uint32_t bi,
+                 uint32_t arg, CompatResult *res)
+{
+    __shared__ int rc, dir;
+    __shared__ uint32_t id, src, dst;
+    if (threadIdx.x == 0) {
+        rc = ORCHKV_OK;
+        dir = -1;
+        id = kNoBlock;
+        if (l >= r.L || h >= r.H) {
+            rc = ORCHKV_ERR_NOT_FOUND;
+        } else {
+            const uint32_t tok = req_tok(r)[l];
+            const uint32_t nb = (tok + p.tpb - 1) / p.tpb;
+            if (bi >= nb || bi >= r.mbph) rc = ORCHKV_ERR_NOT_FOUND;
+            else id = req_table(r)[((size_t)l * r.H + h) * r.mbph + bi];
+            if (rc == ORCHKV_OK && id >= p.max_blocks) rc = ORCHKV_ERR_NOT_FOUND;
+        }
+        if (rc == ORCHKV_OK) {
+            const uint32_t w = p.loc[id];
+            const uint32_t tier = loc_tier(w);
+            PoolCounters *c = p.ctr;
+            if (op == OP_EVICT) {
+                if (tier != TIER_GPU_HBM) rc = ORCHKV_ERR_STATE;
+                else if (p.flags[id] & KV_FLAG_PIN) rc = ORCHKV_ERR_LOCKED;
+                else if (c->d_top == 0) rc = ORCHKV_ERR_TIER_FULL;
+                else { src = loc_slab(w); dst = p.d_stack[--c->d_top]; dir = 0; }
+            } else if (op == OP_PROMOTE || op == OP_GET) {
+                if (tier == TIER_HOST_DRAM) {
+                    if (c->g_top == 0) rc = ORCHKV_ERR_TIER_FULL;
+                    else { src = loc_slab(w); dst = p.g_stack[--c->g_top]; dir = 1; }
+                } else if (op == OP_PROMOTE || tier != TIER_GPU_HBM) {
+                    rc = ORCHKV_ERR_STATE;
+                }
+            } else if (op == OP_SET_FLAGS) {
+                p.flags[id] = (uint8_t)arg;
+                if (p.attached) p.sd.bflags[id & p.sd.mask] = (uint8_t)arg;
+            }
+        }
+    }
+    __syncthreads();
+    if (dir == 0)
+        coop_copy(p.dram_base + dst * p.slab, p.gpu_base + src * p.slab, p.slab, threadIdx.x, blockDim.x);
+    else if (dir == 1)
+        coop_copy(p.gpu_base + dst * p.slab, p.dram_base + src * p.slab, p.slab, threadIdx.x, blockDim.x);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        PoolCounters *c = p.ctr;
+        if (dir == 0) {
+            p.loc[id] = make_loc(TIER_HOST_DRAM, dst);
+            p.state[id] = KV_STATE_WARM;
+            p.g_stack[c->g_top++] = src;
+            c->transfers_d2h++;
+            c->bytes_d2h += p.slab;
+            sched_move(p, id, TIER_HOST_DRAM, KV_STATE_WARM);
+        } else if (dir == 1) {
+            p.loc[id] = make_loc(TIER_GPU_HBM, dst);
+            p.state[id] = KV_STATE_HOT;
+            p.d_stack[c->d_top++] = src;
+            c->transfers_h2d++;
+            c->bytes_h2d += p.slab;
+            sched_move(p, id, TIER_GPU_HBM, KV_STATE_HOT);
+        }
+        res->rc = rc;
+        res->id = id;
+        if (id != kNoBlock && id < p.max_blocks) {
+            const uint32_t w = p.loc[id];
+            res->loc = w;
+            res->state = p.state[id];
+            if (loc_tier(w) == TIER_GPU_HBM) {
+                res->k_ptr = (unsigned long long)(p.gpu_base + (unsigned long long)loc_slab(w) * p.slab);
+                res->v_ptr = res->k_ptr + p.half;
+            } else {
+                res->k_ptr = res->v_ptr = 0;
+            }
+            const uint32_t tok = req_tok(r)[l];
+            const uint32_t last = (tok + p.tpb - 1) / p.tpb - 1;
+            res->tok = bi < last ? p.tpb : tok - last * p.tpb;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// orchkv_append_token (src/api/orchkv_api.cu:263-317 with
+// kv_request_alloc_blocks_for_layer, src/core/kv_request.c:128-211), one CTA.
+// ---------------------------------------------------------------------------
+
+constexpr int kMaxHeads = 256;
+
+__global__ void __launch_bounds__(256)
+append_one_kernel(PoolDev p, ReqDev r, uint32_t l, const char *k, const char *v,
+                  CompatResult *res)
+{
+    __shared__ int rc;
+    __shared__ uint32_t n_ok, slot;
+    __shared__ uint32_t slab_of[kMaxHeads];
+    if (threadIdx.x == 0) {
+        rc = ORCHKV_OK;
+        n_ok = 0;
+        PoolCounters *c = p.ctr;
+        uint32_t *tokp = req_tok(r) + l;
+        const uint32_t tok = *tokp;
+        const bool need_new = (tok % p.tpb) == 0;
+        const uint32_t b = tok / p.tpb;
+        if (need_new && (c->id_top < r.H || c->g_top < r.H || b >= r.mbph)) {
+            rc = ORCHKV_ERR_TIER_FULL;
+        } else {
+            *tokp = tok + 1;
+            slot = tok % p.tpb;
+            uint32_t *tab = req_table(r) + (size_t)l * r.H * r.mbph;
+            if (need_new) {
+                // block ids in head order, then one slab per head in head order
+                for (uint32_t hh = 0; hh < r.H; hh++) {
+                    const uint32_t id = p.id_stack[--c->id_top];
+                    tab[(size_t)hh * r.mbph + b] = id;
+                    p.loc[id] = make_loc(TIER_NONE, 0);
+                    p.state[id] = KV_STATE_FREE;
+                    p.flags[id] = 0;
+                }
+                for (uint32_t hh = 0; hh < r.H; hh++) {
+                    const uint32_t id = tab[(size_t)hh * r.mbph + b];
+                    const uint32_t g = p.g_stack[--c->g_top];
+                    p.loc[id] = make_loc(TIER_GPU_HBM, g);
+                    p.state[id] = KV_STATE_HOT;
+                    c->live_blocks++;
+                    sched_register(p, id, 0);
+                }
+            }
+            for (uint32_t hh = 0; hh < r.H; hh++) {
+                const uint32_t id = tab[(size_t)hh * r.mbph + b];
+                const uint32_t w = p.loc[id];
+                if (loc_tier(w) != TIER_GPU_HBM) { rc = ORCHKV_ERR_STATE; break; }
+                slab_of[hh] = loc_slab(w);
+                n_ok = hh + 1;
+            }
+            if (k) { c->transfers_h2d += n_ok; c->bytes_h2d += (unsigned long long)n_ok * p.row; }
+            if (v) { c->transfers_h2d += n_ok; c->bytes_h2d += (unsigned long long)n_ok * p.row; }
+            if (rc == ORCHKV_OK && l == 0) r.region[0] += 1;
+        }
+    }
+    __syncthreads();
+    const unsigned warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (uint32_t hh = warp; hh < n_ok; hh += nw) {
+        char *dst = p.gpu_base + (unsigned long long)slab_of[hh] * p.slab + (unsigned long long)slot * p.row;
+        if (k) coop_copy(dst, k + (size_t)hh * p.row, p.row, lane, 32);
+        if (v) coop_copy(dst + p.half, v + (size_t)hh * p.row, p.row, lane, 32);
+    }
+    if (threadIdx.x == 0) res->rc = rc;
+}
+
+// ---------------------------------------------------------------------------
+// orchkv_prefill (src/api/orchkv_api.cu:204-255)
+// ---------------------------------------------------------------------------
+
+__global__ void prefill_plan_kernel(PoolDev p, ReqDev r, uint32_t l, uint32_t seq,
+                                    int has_k, int has_v, uint32_t *scratch,
+                                    CompatResult *res)
+{
+    PoolCounters *c = p.ctr;
+    uint32_t *tokp = req_tok(r) + l;
+    const uint32_t tok = *tokp;
+    const uint32_t total = tok + seq;
+    const uint32_t needed = (total + p.tpb - 1) / p.tpb;
+    const uint32_t have = (tok + p.tpb - 1) / p.tpb;
+    scratch[0] = 0;        // new blocks per head
+    scratch[1] = have;
+    scratch[2] = total;
+    int rc = ORCHKV_OK;
+    if (needed > have) {
+        const uint32_t nn = needed - have;
+        if (needed > r.mbph || c->id_top < nn * r.H || c->g_top < nn * r.H) {
+            rc = ORCHKV_ERR_TIER_FULL;
+        } else {
+            uint32_t *tab = req_table(r) + (size_t)l * r.H * r.mbph;
+            // ids: block-major then head (kv_request.c:177-204)
+            for (uint32_t j = 0; j < nn; j++)
+                for (uint32_t hh = 0; hh < r.H; hh++) {
+                    const uint32_t id = p.id_stack[--c->id_top];
+                    tab[(size_t)hh * r.mbph + have + j] = id;
+                    p.flags[id] = 0;
+                }
+            // slabs: head-major then block (orchkv_api.cu:219-226)
+            for (uint32_t hh = 0; hh < r.H; hh++)
+                for (uint32_t j = 0; j < nn; j++) {
+                    const uint32_t id = tab[(size_t)hh * r.mbph + have + j];
+                    const uint32_t g = p.g_stack[--c->g_top];
+                    p.loc[id] = make_loc(TIER_GPU_HBM, g);
+                    p.state[id] = KV_STATE_HOT;
+                    c->live_blocks++;
+                    sched_register(p, id, 0);
+                    const uint32_t ts = (have + j) * p.tpb;
+                    if (ts < seq) {
+                        uint32_t cnt = total - ts < p.tpb ? total - ts : p.tpb;
+                        const unsigned long long bytes = (unsigned long long)cnt * p.row;
+                        if (has_k) { c->transfers_h2d++; c->bytes_h2d += bytes; }
+                        if (has_v) { c->transfers_h2d++; c->bytes_h2d += bytes; }
+                    }
+                }
+            scratch[0] = nn;
+        }
+    }
+    if (rc == ORCHKV_OK) {
+        *tokp = total;
+        if (l == 0) r.region[0] += seq;
+    }
+    res->rc = rc;
+}
+
+__global__ void __launch_bounds__(256)
+prefill_copy_kernel(PoolDev p, ReqDev r, uint32_t l, const char *k, const char *v,
+                    uint32_t seq, const uint32_t *scratch)
+{
+    const uint32_t nn = scratch[0], have = scratch[1], total = scratch[2];
+    const uint32_t n_items = nn * r.H;
+    const unsigned warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const unsigned lane = threadIdx.x & 31;
+    const unsigned nwarps = (gridDim.x * blockDim.x) >> 5;
+    const uint32_t *tab = req_table(r) + (size_t)l * r.H * r.mbph;
+    for (uint32_t it = warp; it < n_items; it += nwarps) {
+        const uint32_t hh = it / nn, j = it % nn;
+        const uint32_t ts = (have + j) * p.tpb;
+        if (ts >= seq) continue;             // source offset beyond the buffer
+        uint32_t cnt = total - ts < p.tpb ? total - ts : p.tpb;
+        if (cnt > seq - ts) cnt = seq - ts;  // stay inside this head's rows
+        const uint32_t id = tab[(size_t)hh * r.mbph + have + j];
+        char *dst = p.gpu_base + (unsigned long long)loc_slab(p.loc[id]) * p.slab;
+        const size_t off = ((size_t)hh * seq + ts) * p.row;
+        const unsigned long long bytes = (unsigned long long)cnt * p.row;
+        if (k) coop_copy(dst, k + off, bytes, lane, 32);
+        if (v) coop_copy(dst + p.half, v + off, bytes, lane, 32);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Batched append over (request, layer) pairs: plan (one CTA) + write kernel.
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(1024)
+append_plan_kernel(PoolDev p, uint32_t *const *regions, uint32_t n, uint32_t L, uint32_t H,
+                   uint32_t mbph, int has_k, int has_v, uint32_t *scratch)
+{
+    __shared__ uint32_t tmp[33];
+    __shared__ uint32_t carry, bad_state, bad_width;
+    const uint32_t P = n * L;
+    if (threadIdx.x == 0) { carry = 0; bad_state = 0; bad_width = 0; }
+    __syncthreads();
+    for (uint32_t base = 0; base < P; base += blockDim.x) {
+        const uint32_t pr = base + threadIdx.x;
+        uint32_t need = 0;
+        if (pr < P) {
+            const uint32_t i = pr / L, l = pr % L;
+            const uint32_t *reg = regions[i];
+            const uint32_t tok = reg[1 + l];
+            need = (tok % p.tpb) == 0;
+            if (tok / p.tpb >= mbph) atomicOr(&bad_width, 1u);
+            if (!need) {
+                const uint32_t *tab = reg + 1 + L + (size_t)l * H * mbph;
+                const uint32_t b = (tok - 1) / p.tpb;
+                for (uint32_t hh = 0; hh < H; hh++)
+                    if (loc_tier(p.loc[tab[(size_t)hh * mbph + b]]) != TIER_GPU_HBM)
+                        atomicOr(&bad_state, 1u);
+            }
+            scratch[2 * pr] = tok;
+        }
+        uint32_t total;
+        const uint32_t ex = block_excl_scan(need, tmp, &total);
+        if (pr < P) scratch[2 * pr + 1] = need ? carry + ex : kNoBlock;
+        __syncthreads();
+        if (threadIdx.x == 0) carry += total;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        PoolCounters *c = p.ctr;
+        const uint32_t need_slabs = carry * H;
+        uint32_t err = ORCHKV_OK;
+        if (bad_state) err = (uint32_t)ORCHKV_ERR_STATE;
+        else if (bad_width || c->g_top < need_slabs || c->id_top < need_slabs)
+            err = (uint32_t)ORCHKV_ERR_TIER_FULL;
+        scratch[2 * P] = err;
+        scratch[2 * P + 1] = c->g_top;
+        scratch[2 * P + 2] = c->id_top;
+        if (err == ORCHKV_OK) {
+            c->g_top -= need_slabs;
+            c->id_top -= need_slabs;
+            c->live_blocks += need_slabs;
+            const unsigned long long rows = (unsigned long long)P * H;
+            if (has_k) { c->transfers_h2d += rows; c->bytes_h2d += rows * p.row; }
+            if (has_v) { c->transfers_h2d += rows; c->bytes_h2d += rows * p.row; }
+        } else {
+            c->err = err;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256)
+append_write_kernel(PoolDev p, uint32_t *const *regions, uint32_t n, uint32_t L, uint32_t H,
+                    uint32_t mbph, const char *k, const char *v, const uint32_t *scratch)
+{
+    const uint32_t P = n * L;
+    if (scratch[2 * P] != ORCHKV_OK) return;
+    const unsigned long long warp =
+        ((unsigned long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const unsigned lane = threadIdx.x & 31;
+    if (warp >= (unsigned long long)P * H) return;
+    const uint32_t pr = (uint32_t)(warp / H), hh = (uint32_t)(warp % H);
+    const uint32_t i = pr / L, l = pr % L;
+    uint32_t *reg = regions[i];
+    const uint32_t tok = scratch[2 * pr], ord = scratch[2 * pr + 1];
+    const uint32_t b = tok / p.tpb, slot = tok % p.tpb;
+    uint32_t *tab = reg + 1 + L + (size_t)l * H * mbph;
+    uint32_t g;
+    if (ord != kNoBlock) {
+        const uint32_t j = ord * H + hh;
+        const uint32_t id = p.id_stack[scratch[2 * P + 2] - 1 - j];
+        g = p.g_stack[scratch[2 * P + 1] - 1 - j];
+        if (lane == 0) {
+            tab[(size_t)hh * mbph + b] = id;
+            p.loc[id] = make_loc(TIER_GPU_HBM, g);
+            p.state[id] = KV_STATE_HOT;
+            p.flags[id] = 0;
+            sched_register(p, id, 0);
+        }
+    } else {
+        g = loc_slab(p.loc[tab[(size_t)hh * mbph + b]]);
+    }
+    char *dst = p.gpu_base + (unsigned long long)g * p.slab + (unsigned long long)slot * p.row;
+    const size_t src = ((size_t)pr * H + hh) * p.row;
+    if (k) coop_copy(dst, k + src, p.row, lane, 32);
+    if (v) coop_copy(dst + p.half, v + src, p.row, lane, 32);
+    if (hh == 0 && lane == 0) {
+        reg[1 + l] = tok + 1;
+        if (l == 0) reg[0] += 1;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Batched migration: validity count per tile, tile scan + pool bookkeeping,
+// per-entry plan (metadata + free-stack pushes), then the slab copy.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ bool mig_valid(const PoolDev &p, int dir, uint32_t id)
+{
+    if (id >= p.max_blocks) return false;
+    const uint32_t w = p.loc[id];
+    if (dir == 0) return loc_tier(w) == TIER_GPU_HBM && !(p.flags[id] & KV_FLAG_PIN);
+    return loc_tier(w) == TIER_HOST_DRAM;
+}
+
+__device__ __forceinline__ uint32_t list_len(const uint32_t *count, uint32_t max_n)
+{
+    if (!count) return max_n;
+    const uint32_t c = *count;
+    return c < max_n ? c : max_n;
+}
+
+__global__ void __launch_bounds__(256)
+mig_count_kernel(PoolDev p, int dir, const uint32_t *ids, const uint32_t *count,
+                 uint32_t max_n, uint32_t *tile_cnt)
+{
+    __shared__ uint32_t tmp[33];
+    const uint32_t n = list_len(count, max_n);
+    const uint32_t base = blockIdx.x * kTileN;
+    uint32_t c = 0;
+    for (uint32_t j = threadIdx.x; j < kTileN; j += blockDim.x) {
+        const uint32_t e = base + j;
+        if (e < n && mig_valid(p, dir, ids[e])) c++;
+    }
+    uint32_t tot;
+    block_excl_scan(c, tmp, &tot);
+    if (threadIdx.x == 0) tile_cnt[blockIdx.x] = tot;
+}
+
+__global__ void __launch_bounds__(1024)
+mig_scan_kernel(PoolDev p, int dir, const uint32_t *count, uint32_t max_n, uint32_t tiles,
+                uint32_t *tile_cnt, uint32_t *meta, uint32_t *result)
+{
+    __shared__ uint32_t tmp[33];
+    __shared__ uint32_t carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (uint32_t b0 = 0; b0 < tiles; b0 += blockDim.x) {
+        const uint32_t t = b0 + threadIdx.x;
+        const uint32_t c = t < tiles ? tile_cnt[t] : 0;
+        uint32_t tot;
+        const uint32_t ex = block_excl_scan(c, tmp, &tot);
+        if (t < tiles) tile_cnt[t] = carry + ex;   // becomes the tile base
+        __syncthreads();
+        if (threadIdx.x == 0) carry += tot;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        PoolCounters *c = p.ctr;
+        const uint32_t n = list_len(count, max_n);
+        const uint32_t valid = carry;
+        uint32_t *dst_top = dir == 0 ? &c->d_top : &c->g_top;
+        uint32_t *src_top = dir == 0 ? &c->g_top : &c->d_top;
+        const uint32_t avail = *dst_top;
+        const uint32_t done = valid < avail ? valid : avail;
+        meta[0] = done;
+        meta[1] = *dst_top;
+        meta[2] = *src_top;
+        *dst_top -= done;
+        *src_top += done;
+        if (dir == 0) { c->transfers_d2h += done; c->bytes_d2h += (unsigned long long)done * p.slab; }
+        else          { c->transfers_h2d += done; c->bytes_h2d += (unsigned long long)done * p.slab; }
+        c->last_done = done;
+        c->last_skipped = n - done;
+        if (result) { result[0] = done; result[1] = n - done; }
+    }
+}
+
+__global__ void __launch_bounds__(256)
+mig_plan_kernel(PoolDev p, int dir, const uint32_t *ids, const uint32_t *count,
+                uint32_t max_n, const uint32_t *tile_base, const uint32_t *meta,
+                uint32_t *plan_src, uint32_t *plan_dst)
+{
+    __shared__ uint32_t tmp[33];
+    const uint32_t n = list_len(count, max_n);
+    const uint32_t done = meta[0], dst_top = meta[1], src_top = meta[2];
+    const uint32_t base = blockIdx.x * kTileN;
+    // 4 consecutive entries per thread keeps the list order inside the tile
+    const uint32_t e0 = base + threadIdx.x * 4;
+    bool val[4];
+    uint32_t idv[4], c = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint32_t e = e0 + j;
+        idv[j] = e < n ? ids[e] : kNoBlock;
+        val[j] = e < n && mig_valid(p, dir, idv[j]);
+        c += val[j];
+    }
+    uint32_t o = tile_base[blockIdx.x] + block_excl_scan(c, tmp, nullptr);
+    uint32_t *dstk = dir == 0 ? p.d_stack : p.g_stack;
+    uint32_t *srck = dir == 0 ? p.g_stack : p.d_stack;
+    const uint32_t dst_tier = dir == 0 ? TIER_HOST_DRAM : TIER_GPU_HBM;
+    const uint8_t new_state = dir == 0 ? KV_STATE_WARM : KV_STATE_HOT;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        if (!val[j]) continue;
+        if (o < done) {
+            const uint32_t id = idv[j];
+            const uint32_t s = loc_slab(p.loc[id]);
+            const uint32_t d = dstk[dst_top - 1 - o];
+            srck[src_top + o] = s;
+            p.loc[id] = make_loc(dst_tier, d);
+            p.state[id] = new_state;
+            sched_move(p, id, (uint8_t)dst_tier, new_state);
+            plan_src[o] = s;
+            plan_dst[o] = d;
+        }
+        o++;
+    }
+}
+
+// One warp per slab; 16-byte lanes, eight vectors in flight per lane.
+__global__ void __launch_bounds__(256)
+mig_copy_kernel(const char *src_base, char *dst_base, unsigned long long slab,
+                const uint32_t *plan_src, const uint32_t *plan_dst, const uint32_t *meta)
+{
+    const uint32_t done = meta[0];
+    const unsigned lane = threadIdx.x & 31;
+    const unsigned long long nvec = slab >> 4;
+    const unsigned long long warp0 = ((unsigned long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const unsigned long long nwarps = ((unsigned long long)gridDim.x * blockDim.x) >> 5;
+    for (unsigned long long w = warp0; w < done; w += nwarps) {
+        const uint4 *s = reinterpret_cast<const uint4 *>(src_base + plan_src[w] * slab);
+        uint4 *d = reinterpret_cast<uint4 *>(dst_base + plan_dst[w] * slab);
+        unsigned long long i = lane;
+        for (; i + 7 * 32 < nvec; i += 8 * 32) {
+            uint4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = s[i + u * 32];
+#pragma unroll
+            for (int u = 0; u < 8; u++) d[i + u * 32] = v[u];
+        }
+        for (; i < nvec; i += 32) d[i] = s[i];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Block-id table for the scoring kernel
+// ---------------------------------------------------------------------------
+
+__global__ void id_table_kernel(PoolDev p, uint32_t *const *regions, uint32_t n, uint32_t L,
+                                uint32_t H, uint32_t mbph, uint32_t nb, uint32_t *out)
+{
+    const unsigned long long total = (unsigned long long)n * L * H * nb;
+    for (unsigned long long e = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x;
+         e < total; e += (unsigned long long)gridDim.x * blockDim.x) {
+        const uint32_t b = (uint32_t)(e % nb);
+        const unsigned long long rh = e / nb;
+        const uint32_t hh = (uint32_t)(rh % H);
+        const unsigned long long pr = rh / H;
+        const uint32_t i = (uint32_t)(pr / L), l = (uint32_t)(pr % L);
+        const uint32_t *reg = regions[i];
+        const uint32_t tok = reg[1 + l];
+        const uint32_t nbl = (tok + p.tpb - 1) / p.tpb;
+        out[e] = (b < nbl && b < mbph) ? reg[1 + L + ((size_t)l * H + hh) * mbph + b] : kNoBlock;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Request teardown (src/api/orchkv_api.cu:149-183): free slabs and ids in
+// (layer, head, block) order.  One CTA, contiguous chunks per thread.
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(1024)
+request_free_kernel(PoolDev p, ReqDev r)
+{
+    __shared__ uint32_t tmp[33];
+    const size_t E = (size_t)r.L * r.H * r.mbph;
+    const size_t per = (E + blockDim.x - 1) / blockDim.x;
+    const size_t e0 = threadIdx.x * per;
+    const uint32_t *tok = req_tok(r);
+    const uint32_t *tab = req_table(r);
+    uint32_t ng = 0, nd = 0, ni = 0;
+    for (size_t e = e0; e < e0 + per && e < E; e++) {
+        const uint32_t bi = (uint32_t)(e % r.mbph);
+        const uint32_t l = (uint32_t)(e / ((size_t)r.H * r.mbph));
+        if (bi >= (tok[l] + p.tpb - 1) / p.tpb) continue;
+        const uint32_t id = tab[e];
+        if (id >= p.max_blocks) continue;
+        ni++;
+        const uint32_t t = loc_tier(p.loc[id]);
+        ng += t == TIER_GPU_HBM;
+        nd += t == TIER_HOST_DRAM;
+    }
+    uint32_t tg, td, ti;
+    uint32_t og = block_excl_scan(ng, tmp, &tg);
+    uint32_t od = block_excl_scan(nd, tmp, &td);
+    uint32_t oi = block_excl_scan(ni, tmp, &ti);
+    PoolCounters *c = p.ctr;
+    const uint32_t gtop = c->g_top, dtop = c->d_top, itop = c->id_top;
+    __syncthreads();
+    for (size_t e = e0; e < e0 + per && e < E; e++) {
+        const uint32_t bi = (uint32_t)(e % r.mbph);
+        const uint32_t l = (uint32_t)(e / ((size_t)r.H * r.mbph));
+        if (bi >= (tok[l] + p.tpb - 1) / p.tpb) continue;
+        const uint32_t id = tab[e];
+        if (id >= p.max_blocks) continue;
+        const uint32_t w = p.loc[id];
+        if (loc_tier(w) == TIER_GPU_HBM) p.g_stack[gtop + og++] = loc_slab(w);
+        else if (loc_tier(w) == TIER_HOST_DRAM) p.d_stack[dtop + od++] = loc_slab(w);
+        p.id_stack[itop + oi++] = id;
+        p.loc[id] = make_loc(TIER_NONE, 0);
+        p.state[id] = KV_STATE_EVICTED;
+        p.flags[id] = 0;
+        sched_unregister(p, id);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        c->g_top = gtop + tg;
+        c->d_top = dtop + td;
+        c->id_top = itop + ti;
+        c->live_blocks -= ti;
+    }
+}
+
+unsigned copy_grid(uint32_t items, int per_cta)
+{
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    unsigned g = (items + per_cta - 1) / per_cta;
+    const unsigned cap = (unsigned)sms * 16;
+    if (g > cap) g = cap;
+    return g ? g : 1;
+}
+
+}  // namespace
+
+int launch_compat_op(const PoolDev &p, const ReqDev &r, int op, uint32_t l, uint32_t h,
+                     uint32_t bi, uint32_t arg, CompatResult *res, cudaStream_t s)
+{
+    compat_op_kernel<<<1, 256, 0, s>>>(p, r, op, l, h, bi, arg, res);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_append_one(const PoolDev &p, const ReqDev &r, uint32_t l, const char *k,
+                      const char *v, CompatResult *res, cudaStream_t s)
+{
+    if (r.H > (uint32_t)kMaxHeads) return ORCHKV_ERR_INVALID;
+    append_one_kernel<<<1, 256, 0, s>>>(p, r, l, k, v, res);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_prefill(const PoolDev &p, const ReqDev &r, uint32_t l, const char *k,
+                   const char *v, uint32_t seq_len, uint32_t *scratch, CompatResult *res,
+                   cudaStream_t s)
+{
+    prefill_plan_kernel<<<1, 1, 0, s>>>(p, r, l, seq_len, k != nullptr, v != nullptr,
+                                        scratch, res);
+    const uint32_t items = ((seq_len + p.tpb - 1) / p.tpb + 1) * r.H;
+    prefill_copy_kernel<<<copy_grid(items, 8), 256, 0, s>>>(p, r, l, k, v, seq_len, scratch);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_append_batch(const PoolDev &p, uint32_t *const *regions, uint32_t n, uint32_t L,
+                        uint32_t H, uint32_t mbph, const char *k, const char *v,
+                        uint32_t *scratch, cudaStream_t s)
+{
+    append_plan_kernel<<<1, 1024, 0, s>>>(p, regions, n, L, H, mbph, k != nullptr,
+                                          v != nullptr, scratch);
+    const unsigned long long warps = (unsigned long long)n * L * H;
+    append_write_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(p, regions, n, L, H, mbph,
+                                                                     k, v, scratch);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_migrate_batch(const PoolDev &p, int dir, const uint32_t *ids,
+                         const uint32_t *count, uint32_t max_n, uint32_t *result,
+                         uint32_t *scratch, cudaStream_t s)
+{
+    if (max_n == 0) return ORCHKV_OK;
+    const uint32_t tiles = (max_n + kTileN - 1) / kTileN;
+    uint32_t *meta = scratch;                  // [16]
+    uint32_t *tile_cnt = scratch + 16;         // [tiles]
+    uint32_t *plan_src = tile_cnt + tiles;     // [max_n]
+    uint32_t *plan_dst = plan_src + max_n;     // [max_n]
+    mig_count_kernel<<<tiles, 256, 0, s>>>(p, dir, ids, count, max_n, tile_cnt);
+    mig_scan_kernel<<<1, 1024, 0, s>>>(p, dir, count, max_n, tiles, tile_cnt, meta, result);
+    mig_plan_kernel<<<tiles, 256, 0, s>>>(p, dir, ids, count, max_n, tile_cnt, meta, plan_src,
+                                          plan_dst);
+    const char *src_base = dir == 0 ? p.gpu_base : p.dram_base;
+    char *dst_base = dir == 0 ? p.dram_base : p.gpu_base;
+    mig_copy_kernel<<<copy_grid(max_n, 8), 256, 0, s>>>(src_base, dst_base, p.slab, plan_src,
+                                                        plan_dst, meta);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_id_table(const PoolDev &p, uint32_t *const *regions, uint32_t n, uint32_t L,
+                    uint32_t H, uint32_t mbph, uint32_t row_len, uint32_t *out,
+                    cudaStream_t s)
+{
+    const uint32_t nb = (row_len + p.tpb - 1) / p.tpb;
+    const unsigned long long total = (unsigned long long)n * L * H * nb;
+    unsigned g = (unsigned)((total + 255) / 256);
+    if (g > 148 * 16) g = 148 * 16;
+    if (g == 0) g = 1;
+    id_table_kernel<<<g, 256, 0, s>>>(p, regions, n, L, H, mbph, nb, out);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_request_free(const PoolDev &p, const ReqDev &r, cudaStream_t s)
+{
+    request_free_kernel<<<1, 1024, 0, s>>>(p, r);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+}  // namespace okv

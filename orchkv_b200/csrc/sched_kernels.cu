@@ -1,0 +1,422 @@
+// sched_kernels.cu — attention scoring (K1) and the tracker/classifier sweep
+// (K2) of the orchkv B200 scheduler.
+//
+// K1 replaces the managers' per-block torch reduction + pybind report loop
+// (python/orchkv/fast_kvcache_manager.py:221-235) and attn_tracker_update
+// (src/scheduler/attention_tracker.c:27-33,75-118).  K2 replaces the
+// O(capacity) host sweeps attn_tracker_step_done
+// (src/scheduler/attention_tracker.c:120-150) and hcc_update_all
+// (src/scheduler/hotcold_classifier.c:69-83,161-185).
+//
+// Float semantics: every product and sum in K2 uses __fmul_rn / __fadd_rn /
+// __fdiv_rn so no FMA is formed and each operation rounds exactly as the
+// reference's single-precision host code; the recency table is built on the
+// host with libm expf (as the reference does) and only read here.
+#include "kernels.h"
+
+namespace okv {
+
+// ---------------------------------------------------------------------------
+// K1: per-block attention mass
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float4 ld_stream(const float4 *p)
+{
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void record_mass(const SchedDev &d, uint32_t id, float w,
+                                            unsigned long long step)
+{
+    if (id == kNoBlock) return;
+    const uint32_t s = id & d.mask;
+    if (!d.tact[s]) return;                     // inactive slots ignore reports
+    d.sum[s] = __fadd_rn(d.sum[s], w);
+    if (w > d.mx[s]) d.mx[s] = w;
+    d.last[s] = step;
+}
+
+constexpr int kScoreWarps = 8;     // warps per CTA
+constexpr int kScoreU = 4;         // float4 columns per lane per row: 512-token tiles
+
+// One warp per tile (row r, KV head h, 512-token chunk).  Lane l of step u
+// loads float4 column (chunk*128 + u*32 + l) of each of the G query-head rows
+// of KV group h: every load instruction is one fully coalesced 512-byte line.
+// Token blocks of tpb tokens cover tpb/4 consecutive lanes and are summed with
+// xor-shuffles; one lane per block records the mass.
+template <int LOG_LPB>
+__global__ void __launch_bounds__(kScoreWarps * 32)
+score_vec_kernel(const float *__restrict__ probs, uint32_t Hq, uint32_t Hkv,
+                 uint32_t T, uint32_t tpb, const uint32_t *__restrict__ lens,
+                 const uint32_t *__restrict__ ids, uint32_t nb, uint32_t n_chunks,
+                 unsigned long long n_tiles, SchedDev d, unsigned long long step)
+{
+    constexpr int LPB = 1 << LOG_LPB;
+    const int lane = threadIdx.x & 31;
+    const unsigned long long tile =
+        (unsigned long long)blockIdx.x * kScoreWarps + (threadIdx.x >> 5);
+    if (tile >= n_tiles) return;
+    const uint32_t c = (uint32_t)(tile % n_chunks);
+    const unsigned long long rh = tile / n_chunks;
+    const uint32_t h = (uint32_t)(rh % Hkv);
+    const unsigned long long r = rh / Hkv;
+    const uint32_t G = Hq / Hkv;
+    uint32_t len = lens ? lens[r] : T;
+    if (len > T) len = T;
+    const uint32_t T4 = T >> 2;
+    const float4 *base = reinterpret_cast<const float4 *>(probs + (r * Hq + (unsigned long long)h * G) * T);
+
+    float4 acc[kScoreU];
+#pragma unroll
+    for (int u = 0; u < kScoreU; u++) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+    const uint32_t col0 = c * (32 * kScoreU) + lane;
+    for (uint32_t g = 0; g < G; g++) {
+        const float4 *row = base + (unsigned long long)g * T4;
+        float4 v[kScoreU];
+#pragma unroll
+        for (int u = 0; u < kScoreU; u++) {
+            const uint32_t col = col0 + u * 32;
+            v[u] = col < T4 ? ld_stream(row + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kScoreU; u++) {
+            acc[u].x += v[u].x; acc[u].y += v[u].y;
+            acc[u].z += v[u].z; acc[u].w += v[u].w;
+        }
+    }
+
+    const uint32_t *idrow = ids + rh * nb;
+#pragma unroll
+    for (int u = 0; u < kScoreU; u++) {
+        const uint32_t col = col0 + u * 32;
+        const uint32_t t0 = col * 4;
+        // tokens at or beyond the row's valid length contribute nothing
+        float4 a = acc[u];
+        if (t0 + 0 >= len) a.x = 0.f;
+        if (t0 + 1 >= len) a.y = 0.f;
+        if (t0 + 2 >= len) a.z = 0.f;
+        if (t0 + 3 >= len) a.w = 0.f;
+        float s = (a.x + a.y) + (a.z + a.w);
+#pragma unroll
+        for (int o = 1; o < LPB; o <<= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+        if ((lane & (LPB - 1)) == 0 && col < T4 && t0 < len) {
+            const uint32_t b = t0 / tpb;
+            record_mass(d, idrow[b], s, step);
+        }
+    }
+}
+
+// Fallback for any geometry the vector kernel does not take (tpb not a power
+// of two in [4,128], T not a multiple of 4, unaligned rows): one thread per
+// (row, KV head, block), summing in the oracle's loop order.
+__global__ void score_scalar_kernel(const float *__restrict__ probs, uint32_t Hq,
+                                    uint32_t Hkv, uint32_t T, uint32_t tpb,
+                                    const uint32_t *__restrict__ lens,
+                                    const uint32_t *__restrict__ ids, uint32_t nb,
+                                    unsigned long long n_items, SchedDev d,
+                                    unsigned long long step)
+{
+    const unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_items) return;
+    const uint32_t b = (uint32_t)(i % nb);
+    const unsigned long long rh = i / nb;
+    const uint32_t h = (uint32_t)(rh % Hkv);
+    const unsigned long long r = rh / Hkv;
+    const uint32_t G = Hq / Hkv;
+    uint32_t len = lens ? lens[r] : T;
+    if (len > T) len = T;
+    const uint32_t t0 = b * tpb;
+    if (t0 >= len) return;
+    uint32_t t1 = t0 + tpb;
+    if (t1 > len) t1 = len;
+    float acc = 0.0f;
+    for (uint32_t g = 0; g < G; g++) {
+        const float *row = probs + ((r * Hq) + (unsigned long long)h * G + g) * T;
+        for (uint32_t t = t0; t < t1; t++) acc = __fadd_rn(acc, row[t]);
+    }
+    record_mass(d, ids[rh * nb + b], acc, step);
+}
+
+int launch_score(const float *probs, uint32_t R, uint32_t Hq, uint32_t Hkv,
+                 uint32_t T, uint32_t tpb, const uint32_t *lens,
+                 const uint32_t *ids, const SchedDev &d, unsigned long long step,
+                 cudaStream_t s)
+{
+    if (!probs || !ids || R == 0 || Hq == 0 || Hkv == 0 || T == 0 || tpb == 0 ||
+        Hq % Hkv != 0)
+        return ORCHKV_ERR_INVALID;
+    const uint32_t nb = (T + tpb - 1) / tpb;
+    const bool pow2 = (tpb & (tpb - 1)) == 0;
+    const bool vec_ok = pow2 && tpb >= 4 && tpb <= 128 && (T % 4) == 0 &&
+                        ((uintptr_t)probs % 16) == 0;
+    if (vec_ok) {
+        const uint32_t n_chunks = (T + 128 * kScoreU - 1) / (128 * kScoreU);
+        const unsigned long long n_tiles = (unsigned long long)R * Hkv * n_chunks;
+        const unsigned long long grid = (n_tiles + kScoreWarps - 1) / kScoreWarps;
+        const int log_lpb = __builtin_ctz(tpb / 4);
+#define OKV_SCORE_CASE(L)                                                              \
+    case L:                                                                            \
+        score_vec_kernel<L><<<(unsigned)grid, kScoreWarps * 32, 0, s>>>(               \
+            probs, Hq, Hkv, T, tpb, lens, ids, nb, n_chunks, n_tiles, d, step);        \
+        break;
+        switch (log_lpb) {
+            OKV_SCORE_CASE(0) OKV_SCORE_CASE(1) OKV_SCORE_CASE(2)
+            OKV_SCORE_CASE(3) OKV_SCORE_CASE(4) OKV_SCORE_CASE(5)
+            default: return ORCHKV_ERR_INVALID;
+        }
+#undef OKV_SCORE_CASE
+    } else {
+        const unsigned long long n_items = (unsigned long long)R * Hkv * nb;
+        const unsigned grid = (unsigned)((n_items + 255) / 256);
+        score_scalar_kernel<<<grid, 256, 0, s>>>(probs, Hq, Hkv, T, tpb, lens, ids, nb,
+                                                 n_items, d, step);
+    }
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Report application (per-block reports buffered on the host, or device lists)
+// ---------------------------------------------------------------------------
+
+__global__ void report_apply_kernel(const uint32_t *__restrict__ slots,
+                                    const float *__restrict__ psum,
+                                    const float *__restrict__ pmax, uint32_t n,
+                                    SchedDev d, unsigned long long step)
+{
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint32_t s = slots[i] & d.mask;
+    if (!d.tact[s]) return;
+    d.sum[s] = __fadd_rn(d.sum[s], psum[i]);
+    if (pmax[i] > d.mx[s]) d.mx[s] = pmax[i];
+    d.last[s] = step;
+}
+
+int launch_report_apply(const uint32_t *slots, const float *psum, const float *pmax,
+                        uint32_t n, const SchedDev &d, unsigned long long step,
+                        cudaStream_t s)
+{
+    if (n == 0) return ORCHKV_OK;
+    report_apply_kernel<<<(n + 255) / 256, 256, 0, s>>>(slots, psum, pmax, n, d, step);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+__global__ void report_batch_kernel(const uint32_t *__restrict__ ids,
+                                    const float *__restrict__ w, uint32_t n, SchedDev d,
+                                    unsigned long long step)
+{
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    record_mass(d, ids[i], w[i], step);
+}
+
+int launch_report_batch(const uint32_t *ids, const float *w, uint32_t n,
+                        const SchedDev &d, unsigned long long step, cudaStream_t s)
+{
+    if (n == 0) return ORCHKV_OK;
+    report_batch_kernel<<<(n + 255) / 256, 256, 0, s>>>(ids, w, n, d, step);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+// ---------------------------------------------------------------------------
+// K2: step_done (EMA) and classification sweep
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float hotness_of(const SchedDev &d, uint32_t i,
+                                            const SchedParams &p,
+                                            unsigned long long step)
+{
+    const unsigned long long last = d.last[i];
+    const unsigned long long gap =
+        (last == kStepNever) ? step : (step > last ? step - last : 0ull);
+    const float rec = gap >= (unsigned long long)kDecayTable ? 0.0f : d.table[gap];
+    float freq = 0.0f;
+    if (step != 0) {
+        freq = __fdiv_rn(__uint2float_rn(d.hits[i]), __ull2float_rn(step));
+        if (freq > 1.0f) freq = 1.0f;
+    }
+    const float t0 = __fmul_rn(p.alpha, d.ema[i]);
+    const float t1 = __fmul_rn(p.beta, rec);
+    const float t2 = __fmul_rn(p.gamma, freq);
+    return __fadd_rn(__fadd_rn(t0, t1), t2);
+}
+
+template <bool STEP, bool CLASSIFY>
+__global__ void __launch_bounds__(256)
+sweep_kernel(SchedDev d, SchedParams p, ClassCounts *counts)
+{
+    uint32_t n_hot = 0, n_warm = 0, n_cold = 0, n_sink = 0;
+    const unsigned long long cstep = STEP ? p.step + 1 : p.step;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < d.cap;
+         i += gridDim.x * blockDim.x) {
+        const bool ta = d.tact[i] != 0;
+        if (STEP && ta) {
+            const float e = d.ema[i];
+            if (d.last[i] == p.step) {
+                d.ema[i] = __fadd_rn(__fmul_rn(p.lambda, e), __fmul_rn(p.one_minus, d.sum[i]));
+                d.hits[i] = d.hits[i] + 1;
+            } else {
+                d.ema[i] = __fmul_rn(e, p.lambda);
+            }
+            d.sum[i] = 0.0f;
+            d.mx[i] = 0.0f;
+        }
+        if (CLASSIFY) {
+            const bool ca = d.cact[i] != 0;
+            if (ca && ta) {
+                const float h = hotness_of(d, i, p, cstep);
+                const uint8_t f = d.cflags[i];
+                uint8_t lvl;
+                if (f & KV_FLAG_ATTN_SINK) lvl = 0;
+                else if (h >= p.th_hot) lvl = 0;
+                else if (h >= p.th_warm) lvl = 1;
+                else lvl = 2;
+                d.hot[i] = h;
+                d.heat[i] = lvl;
+            }
+            if (ca && counts) {
+                const uint8_t lvl = d.heat[i];
+                n_hot += lvl == 0;
+                n_warm += lvl == 1;
+                n_cold += lvl == 2;
+                n_sink += (d.cflags[i] & KV_FLAG_ATTN_SINK) != 0;
+            }
+        }
+    }
+    if (CLASSIFY && counts) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            n_hot += __shfl_xor_sync(0xFFFFFFFFu, n_hot, o);
+            n_warm += __shfl_xor_sync(0xFFFFFFFFu, n_warm, o);
+            n_cold += __shfl_xor_sync(0xFFFFFFFFu, n_cold, o);
+            n_sink += __shfl_xor_sync(0xFFFFFFFFu, n_sink, o);
+        }
+        if ((threadIdx.x & 31) == 0 && (n_hot | n_warm | n_cold | n_sink)) {
+            atomicAdd(&counts->n_hot, n_hot);
+            atomicAdd(&counts->n_warm, n_warm);
+            atomicAdd(&counts->n_cold, n_cold);
+            atomicAdd(&counts->n_sink, n_sink);
+        }
+    }
+}
+
+static unsigned sweep_grid(uint32_t cap)
+{
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    unsigned want = (cap + 255) / 256;
+    unsigned cap_grid = (unsigned)sms * 8;
+    return want < cap_grid ? (want ? want : 1) : cap_grid;
+}
+
+int launch_sweep(const SchedDev &d, const SchedParams &p, bool step_done, bool classify,
+                 ClassCounts *counts, cudaStream_t s)
+{
+    if (counts) OKV_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(ClassCounts), s));
+    const unsigned g = sweep_grid(d.cap);
+    if (step_done && classify) sweep_kernel<true, true><<<g, 256, 0, s>>>(d, p, counts);
+    else if (step_done) sweep_kernel<true, false><<<g, 256, 0, s>>>(d, p, counts);
+    else if (classify) sweep_kernel<false, true><<<g, 256, 0, s>>>(d, p, counts);
+    else return ORCHKV_OK;
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Prefetch scan count over the manager's registry
+// (src/scheduler/tiered_manager.c:284-312 + prefetch_scheduler.c:131-172)
+// ---------------------------------------------------------------------------
+
+__global__ void registry_count_kernel(const uint32_t *__restrict__ reg_slot,
+                                      const uint8_t *__restrict__ reg_tier, uint32_t n,
+                                      SchedDev d, float th_gpu, float th_dram,
+                                      uint32_t *count)
+{
+    uint32_t c = 0;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += gridDim.x * blockDim.x) {
+        const uint8_t t = reg_tier[i];
+        if (t == TIER_GPU_HBM || t == TIER_NONE) continue;
+        const uint32_t s = reg_slot[i] & d.mask;
+        if (!d.tact[s]) continue;
+        const float e = d.ema[s];
+        if (e >= th_gpu || (e >= th_dram && t != TIER_HOST_DRAM)) c++;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
+    if ((threadIdx.x & 31) == 0 && c) atomicAdd(count, c);
+}
+
+int launch_registry_count(const uint32_t *reg_slot, const uint8_t *reg_tier, uint32_t n,
+                          const SchedDev &d, float th_gpu, float th_dram,
+                          uint32_t *count, cudaStream_t s)
+{
+    OKV_CUDA_TRY(cudaMemsetAsync(count, 0, sizeof(uint32_t), s));
+    if (n == 0) return ORCHKV_OK;
+    unsigned g = (n + 255) / 256;
+    if (g > 1184) g = 1184;
+    registry_count_kernel<<<g, 256, 0, s>>>(reg_slot, reg_tier, n, d, th_gpu, th_dram, count);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Slot (un)registration: tracker register (attention_tracker.c:179-191),
+// classifier register (hotcold_classifier.c:104-116), and resets (:193-202,
+// :118-126), applied in list order by one thread (lists are small and may
+// repeat a slot).
+// ---------------------------------------------------------------------------
+
+__global__ void slot_ops_kernel(const uint32_t *slots, const uint8_t *b, uint32_t n,
+                                SchedDev d)
+{
+    if (blockIdx.x != 0 || threadIdx.x != 0) return;
+    for (uint32_t j = 0; j < n; j++) {
+        const uint32_t s = slots[j] & d.mask;
+        const uint8_t op = b[4 * j], fl = b[4 * j + 1], ti = b[4 * j + 2], st = b[4 * j + 3];
+        if (op == 0) {
+            d.sum[s] = 0.f; d.mx[s] = 0.f; d.ema[s] = 0.f; d.hits[s] = 0;
+            d.last[s] = kStepNever; d.tact[s] = 1;
+            d.hot[s] = 0.f;
+            d.heat[s] = (fl & KV_FLAG_ATTN_SINK) ? 0 : 2;
+            d.cflags[s] = fl;
+            d.cact[s] = 1;
+            d.bflags[s] = fl;
+            d.tier[s] = ti;
+            d.bstate[s] = st;
+        } else if (op == 1) {
+            d.sum[s] = 0.f; d.mx[s] = 0.f; d.ema[s] = 0.f; d.hits[s] = 0;
+            d.last[s] = 0; d.tact[s] = 0;
+            d.hot[s] = 0.f; d.heat[s] = 0; d.cflags[s] = 0; d.cact[s] = 0;
+            d.bflags[s] = 0; d.tier[s] = TIER_NONE; d.bstate[s] = 0;
+        } else {
+            d.tier[s] = ti;
+            d.bflags[s] = fl;
+            d.bstate[s] = st;
+        }
+    }
+}
+
+int launch_slot_ops(const uint32_t *slots, const uint8_t *b, uint32_t n,
+                    const SchedDev &d, cudaStream_t s)
+{
+    if (n == 0) return ORCHKV_OK;
+    slot_ops_kernel<<<1, 32, 0, s>>>(slots, b, n, d);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+}  // namespace okv

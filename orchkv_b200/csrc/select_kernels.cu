@@ -1,0 +1,367 @@
+// select_kernels.cu — exact k-smallest selection over the scheduler's slots
+// (K3), replacing the reference's victim ordering
+// (python/orchkv/fast_kvcache_manager.py:300-341: sort all candidate blocks by
+// tm_get_block_score, take the first k) and the prefetch heap
+// (src/scheduler/prefetch_scheduler.c:131-228).
+//
+// Keys are 32-bit orderable transforms of the selection value; ties are
+// broken by ascending slot, which is what a stable sort over ascending block
+// ids gives.  Three histogram passes (bits 31..20, 19..8, 7..0) find the k-th
+// key exactly; an ordered compaction then writes the winners in ascending
+// slot order.  Everything stays on the device: the host only enqueues.
+// Between passes an optional hook reduces the histograms across ranks (NCCL
+// all-reduce), so every rank agrees on the global k-th key, and a gather of
+// per-rank tie counts splits the boundary ties in global (rank, slot) order.
+#include "kernels.h"
+
+namespace okv {
+
+namespace {
+
+constexpr int kBins = 4096;
+constexpr int kTile = 4096;          // keys per compaction tile
+constexpr int kTileThreads = 256;    // 16 keys per thread
+constexpr int kHistThreads = 512;
+
+// selection state words
+enum : int {
+    S_K = 0,        // k actually selected (global)
+    S_KREM = 1,     // remaining count inside the current prefix bin
+    S_PREFIX = 2,   // key bits fixed so far
+    S_NELIG = 3,    // eligible count (global)
+    S_KTH = 4,      // k-th key
+    S_TAKE = 5,     // boundary ties this rank takes
+    S_DONE = 6,     // 1 = nothing to select
+    S_OUT = 7,      // output count (this rank)
+    S_WORDS = 16,
+};
+
+__device__ __forceinline__ uint32_t key_coldest(const SchedDev &d, uint32_t i)
+{
+    if (!d.tact[i] || !d.cact[i]) return kKeyInvalid;
+    if (d.tier[i] != TIER_GPU_HBM) return kKeyInvalid;
+    if (d.bflags[i] & (KV_FLAG_PIN | KV_FLAG_ATTN_SINK)) return kKeyInvalid;
+    if (d.bstate[i] == KV_STATE_MIGRATING) return kKeyInvalid;
+    return orderable(d.hot[i]);
+}
+
+__device__ __forceinline__ uint32_t key_prefetch(const SchedDev &d, uint32_t i,
+                                                 float th_gpu, float th_dram)
+{
+    if (!d.tact[i]) return kKeyInvalid;
+    const uint8_t t = d.tier[i];
+    if (t == TIER_GPU_HBM || t == TIER_NONE) return kKeyInvalid;
+    const float e = d.ema[i];
+    float prio;
+    if (e >= th_gpu) prio = e;
+    else if (e >= th_dram && t != TIER_HOST_DRAM) prio = __fmul_rn(e, 0.5f);
+    else return kKeyInvalid;
+    uint32_t k = ~orderable(prio);           // descending priority
+    return k == kKeyInvalid ? kKeyInvalid - 1 : k;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kHistThreads)
+sel_pass0_kernel(SchedDev d, float th_gpu, float th_dram, uint32_t *hist)
+{
+    __shared__ uint32_t sh[kBins];
+    for (int b = threadIdx.x; b < kBins; b += blockDim.x) sh[b] = 0;
+    __syncthreads();
+    uint32_t n_el = 0;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < d.cap;
+         i += gridDim.x * blockDim.x) {
+        const uint32_t k = MODE == kSelectColdest ? key_coldest(d, i)
+                                                  : key_prefetch(d, i, th_gpu, th_dram);
+        d.key[i] = k;
+        if (k != kKeyInvalid) {
+            atomicAdd(&sh[k >> 20], 1u);
+            n_el++;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) n_el += __shfl_xor_sync(0xFFFFFFFFu, n_el, o);
+    if ((threadIdx.x & 31) == 0 && n_el) atomicAdd(&hist[kBins], n_el);
+    __syncthreads();
+    for (int b = threadIdx.x; b < kBins; b += blockDim.x)
+        if (sh[b]) atomicAdd(&hist[b], sh[b]);
+}
+
+// PASS 1: bins on bits 19..8 of keys whose bits 31..20 equal the prefix.
+// PASS 2: bins on bits 7..0 of keys whose bits 31..8 equal the prefix.
+template <int PASS>
+__global__ void __launch_bounds__(kHistThreads)
+sel_pass_kernel(const uint32_t *__restrict__ key, uint32_t n, const uint32_t *state,
+                uint32_t *hist)
+{
+    __shared__ uint32_t sh[kBins];
+    if (state[S_DONE]) return;
+    const uint32_t prefix = state[S_PREFIX];
+    constexpr int nb = PASS == 1 ? 4096 : 256;
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) sh[b] = 0;
+    __syncthreads();
+    const uint32_t want = PASS == 1 ? (prefix >> 20) : (prefix >> 8);
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += gridDim.x * blockDim.x) {
+        const uint32_t k = key[i];
+        if (k == kKeyInvalid) continue;
+        if (PASS == 1) {
+            if ((k >> 20) == want) atomicAdd(&sh[(k >> 8) & 0xFFF], 1u);
+        } else {
+            if ((k >> 8) == want) atomicAdd(&sh[k & 0xFF], 1u);
+        }
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < nb; b += blockDim.x)
+        if (sh[b]) atomicAdd(&hist[b], sh[b]);
+}
+
+// One CTA of 1024 threads: find the bin holding the k_rem-th key.
+__global__ void __launch_bounds__(1024)
+sel_scan_kernel(const uint32_t *hist, uint32_t *state, int pass, uint32_t k_req,
+                float frac, int single_rank)
+{
+    __shared__ uint32_t tmp[33];
+    __shared__ uint32_t found_b, found_before;
+    if (pass == 0 && threadIdx.x == 0) {
+        const uint32_t n_el = hist[kBins];
+        uint32_t kt;
+        if (frac >= 0.0f) kt = (uint32_t)floor((double)frac * (double)n_el);
+        else kt = k_req < n_el ? k_req : n_el;
+        state[S_NELIG] = n_el;
+        state[S_K] = kt;
+        state[S_KREM] = kt;
+        state[S_PREFIX] = 0;
+        state[S_DONE] = kt == 0;
+        state[S_OUT] = 0;
+        state[S_TAKE] = 0;
+        state[S_KTH] = 0;
+    }
+    __syncthreads();
+    if (state[S_DONE]) return;
+    const uint32_t k_rem = state[S_KREM];
+    const int nb = pass == 2 ? 256 : kBins;
+    const int per = (nb + blockDim.x - 1) / blockDim.x;
+    const int b0 = threadIdx.x * per;
+    uint32_t local = 0;
+    for (int j = 0; j < per; j++)
+        if (b0 + j < nb) local += hist[b0 + j];
+    uint32_t base = block_excl_scan(local, tmp, nullptr);
+    for (int j = 0; j < per; j++) {
+        const int b = b0 + j;
+        if (b >= nb) break;
+        const uint32_t c = hist[b];
+        if (base < k_rem && k_rem <= base + c) {
+            found_b = (uint32_t)b;
+            found_before = base;
+        }
+        base += c;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t b = found_b;
+        const uint32_t rem = k_rem - found_before;
+        uint32_t prefix = state[S_PREFIX];
+        if (pass == 0) prefix = b << 20;
+        else if (pass == 1) prefix |= b << 8;
+        else prefix |= b;
+        state[S_PREFIX] = prefix;
+        state[S_KREM] = rem;
+        if (pass == 2) {
+            state[S_KTH] = prefix;
+            if (single_rank) state[S_TAKE] = rem;
+        }
+    }
+}
+
+// Multi-rank tie split: this rank's ties are hist_local[kth & 0xFF] of pass 2.
+__global__ void sel_tie_local_kernel(const uint32_t *hist_local, const uint32_t *state,
+                                     uint32_t *one)
+{
+    one[0] = state[S_DONE] ? 0u : hist_local[state[S_KTH] & 0xFF];
+}
+
+__global__ void sel_tie_split_kernel(const uint32_t *all, int rank, uint32_t *state)
+{
+    if (state[S_DONE]) return;
+    uint32_t before = 0;
+    for (int r = 0; r < rank; r++) before += all[r];
+    const uint32_t need = state[S_KREM];
+    const uint32_t mine = all[rank];
+    uint32_t take = need > before ? need - before : 0;
+    state[S_TAKE] = take < mine ? take : mine;
+}
+
+__global__ void __launch_bounds__(kTileThreads)
+sel_count_kernel(const uint32_t *__restrict__ key, uint32_t n, const uint32_t *state,
+                 uint32_t *tile_counts)
+{
+    __shared__ uint32_t tmp[33];
+    const uint32_t done = state[S_DONE];
+    const uint32_t kth = state[S_KTH];
+    const uint32_t base = blockIdx.x * kTile + threadIdx.x * 16;
+    uint32_t lt = 0, eq = 0;
+    if (!done) {
+        for (int j = 0; j < 16; j++) {
+            const uint32_t i = base + j;
+            if (i >= n) break;
+            const uint32_t k = key[i];
+            lt += k < kth;
+            eq += k == kth;
+        }
+    }
+    uint32_t tl, te;
+    block_excl_scan(lt, tmp, &tl);
+    block_excl_scan(eq, tmp, &te);
+    if (threadIdx.x == 0) {
+        tile_counts[2 * blockIdx.x] = tl;
+        tile_counts[2 * blockIdx.x + 1] = te;
+    }
+}
+
+__global__ void __launch_bounds__(1024)
+sel_offsets_kernel(const uint32_t *tile_counts, uint32_t n_tiles, uint32_t *tile_offsets,
+                   uint32_t *state, uint32_t *out_count)
+{
+    __shared__ uint32_t tmp[33];
+    __shared__ uint32_t carry_lt, carry_eq;
+    if (threadIdx.x == 0) { carry_lt = 0; carry_eq = 0; }
+    __syncthreads();
+    const uint32_t take = state[S_TAKE];
+    for (uint32_t t0 = 0; t0 < n_tiles; t0 += blockDim.x) {
+        const uint32_t t = t0 + threadIdx.x;
+        const uint32_t lt = t < n_tiles ? tile_counts[2 * t] : 0;
+        const uint32_t eq = t < n_tiles ? tile_counts[2 * t + 1] : 0;
+        uint32_t sum_lt, sum_eq;
+        const uint32_t bl = block_excl_scan(lt, tmp, &sum_lt) + carry_lt;
+        const uint32_t be = block_excl_scan(eq, tmp, &sum_eq) + carry_eq;
+        if (t < n_tiles) {
+            tile_offsets[2 * t] = bl + (be < take ? be : take);
+            tile_offsets[2 * t + 1] = be;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) { carry_lt += sum_lt; carry_eq += sum_eq; }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        const uint32_t out = state[S_DONE] ? 0 : carry_lt + (carry_eq < take ? carry_eq : take);
+        state[S_OUT] = out;
+        if (out_count) *out_count = out;
+    }
+}
+
+__global__ void __launch_bounds__(kTileThreads)
+sel_write_kernel(const uint32_t *__restrict__ key, uint32_t n, const uint32_t *state,
+                 const uint32_t *tile_offsets, uint32_t *out, uint32_t max_out)
+{
+    __shared__ uint32_t tmp[33];
+    if (state[S_DONE]) return;
+    const uint32_t kth = state[S_KTH];
+    const uint32_t take = state[S_TAKE];
+    const uint32_t base = blockIdx.x * kTile + threadIdx.x * 16;
+    uint32_t ks[16];
+    uint32_t eq = 0;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const uint32_t i = base + j;
+        ks[j] = i < n ? key[i] : kKeyInvalid;
+        eq += ks[j] == kth && i < n;
+    }
+    const uint32_t tie_base = block_excl_scan(eq, tmp, nullptr) + tile_offsets[2 * blockIdx.x + 1];
+    uint32_t sel = 0;
+    uint32_t tie_rank = tie_base;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const bool in = base + j < n;
+        if (!in) continue;
+        if (ks[j] < kth) sel++;
+        else if (ks[j] == kth) { if (tie_rank < take) sel++; tie_rank++; }
+    }
+    uint32_t pos = block_excl_scan(sel, tmp, nullptr) + tile_offsets[2 * blockIdx.x];
+    tie_rank = tie_base;
+#pragma unroll
+    for (int j = 0; j < 16; j++) {
+        const uint32_t i = base + j;
+        if (i >= n) continue;
+        bool s = false;
+        if (ks[j] < kth) s = true;
+        else if (ks[j] == kth) { s = tie_rank < take; tie_rank++; }
+        if (s) {
+            if (pos < max_out) out[pos] = i;
+            pos++;
+        }
+    }
+}
+
+unsigned hist_grid(uint32_t n)
+{
+    unsigned g = (n + kHistThreads * 4 - 1) / (kHistThreads * 4);
+    if (g < 1) g = 1;
+    if (g > 296) g = 296;   // two CTAs per SM of 148: bounded global atomics
+    return g;
+}
+
+}  // namespace
+
+size_t select_scratch_words(uint32_t cap, uint32_t *max_tiles)
+{
+    const uint32_t tiles = (cap + kTile - 1) / kTile;
+    if (max_tiles) *max_tiles = tiles;
+    return (size_t)2 * (kBins + 16) + S_WORDS + (size_t)4 * tiles;
+}
+
+int launch_select(const SchedDev &d, const SelectScratch &sc, const SelectArgs &a,
+                  cudaStream_t s)
+{
+    const uint32_t n = d.cap;
+    const bool multi = a.reduce != nullptr && a.world > 1;
+    uint32_t *hg = multi ? sc.hist_global : sc.hist_local;
+    const unsigned g = hist_grid(n);
+
+    // pass 0: keys + top-12-bit histogram + eligible count
+    OKV_CUDA_TRY(cudaMemsetAsync(sc.hist_local, 0, (kBins + 16) * 4, s));
+    if (a.mode == kSelectColdest)
+        sel_pass0_kernel<kSelectColdest><<<g, kHistThreads, 0, s>>>(d, a.th_gpu, a.th_dram, sc.hist_local);
+    else
+        sel_pass0_kernel<kSelectPrefetch><<<g, kHistThreads, 0, s>>>(d, a.th_gpu, a.th_dram, sc.hist_local);
+    OKV_CUDA_TRY(cudaGetLastError());
+    if (multi && a.reduce(sc.hist_local, hg, kBins + 1, s, a.comm_ctx) != ORCHKV_OK)
+        return ORCHKV_ERR_CUDA;
+    sel_scan_kernel<<<1, 1024, 0, s>>>(hg, sc.state, 0, a.k, a.frac, !multi);
+
+    // pass 1
+    OKV_CUDA_TRY(cudaMemsetAsync(sc.hist_local, 0, kBins * 4, s));
+    sel_pass_kernel<1><<<g, kHistThreads, 0, s>>>(d.key, n, sc.state, sc.hist_local);
+    OKV_CUDA_TRY(cudaGetLastError());
+    if (multi && a.reduce(sc.hist_local, hg, kBins, s, a.comm_ctx) != ORCHKV_OK)
+        return ORCHKV_ERR_CUDA;
+    sel_scan_kernel<<<1, 1024, 0, s>>>(hg, sc.state, 1, a.k, a.frac, !multi);
+
+    // pass 2
+    OKV_CUDA_TRY(cudaMemsetAsync(sc.hist_local, 0, 256 * 4, s));
+    sel_pass_kernel<2><<<g, kHistThreads, 0, s>>>(d.key, n, sc.state, sc.hist_local);
+    OKV_CUDA_TRY(cudaGetLastError());
+    if (multi && a.reduce(sc.hist_local, hg, 256, s, a.comm_ctx) != ORCHKV_OK)
+        return ORCHKV_ERR_CUDA;
+    sel_scan_kernel<<<1, 1024, 0, s>>>(hg, sc.state, 2, a.k, a.frac, !multi);
+    OKV_CUDA_TRY(cudaGetLastError());
+
+    if (multi) {
+        sel_tie_local_kernel<<<1, 1, 0, s>>>(sc.hist_local, sc.state, sc.state + 8);
+        if (a.gather(sc.state + 8, a.gather_buf, s, a.comm_ctx) != ORCHKV_OK)
+            return ORCHKV_ERR_CUDA;
+        sel_tie_split_kernel<<<1, 1, 0, s>>>(a.gather_buf, a.rank, sc.state);
+        OKV_CUDA_TRY(cudaGetLastError());
+    }
+
+    // ordered compaction
+    const uint32_t tiles = (n + kTile - 1) / kTile;
+    sel_count_kernel<<<tiles, kTileThreads, 0, s>>>(d.key, n, sc.state, sc.tile_counts);
+    sel_offsets_kernel<<<1, 1024, 0, s>>>(sc.tile_counts, tiles, sc.tile_offsets, sc.state,
+                                          a.out_count);
+    sel_write_kernel<<<tiles, kTileThreads, 0, s>>>(d.key, n, sc.state, sc.tile_offsets,
+                                                    a.out_ids, a.max_out);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+}  // namespace okv

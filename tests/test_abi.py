@@ -1,0 +1,115 @@
+"""C-ABI boundary checks that need no GPU: the library loads, exports every
+function declared in include/orchkv/*.h, the struct layouts the reference
+callers compile against are unchanged, and orchkv_core exposes the reference
+binding's names (bindings/orchkv_pybind.cpp:26-416)."""
+import ctypes as C
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+INC = os.path.join(ROOT, "include", "orchkv")
+
+
+def declared_functions():
+    names = set()
+    for f in os.listdir(INC):
+        if not f.endswith(".h"):
+            continue
+        src = open(os.path.join(INC, f)).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        src = re.sub(r"static inline[^{]*\{.*?\n\}", "", src, flags=re.S)
+        for m in re.finditer(r"^[A-Za-z_][\w \*]*?\b(\w+)\s*\([^;{]*\)\s*;", src, flags=re.M):
+            name = m.group(1)
+            if name.startswith(("orchkv_", "tm_")):
+                names.add(name)
+    return sorted(names)
+
+
+def test_library_loads_and_exports_every_declared_function():
+    import orchkv_b200
+    L = orchkv_b200.lib()
+    names = declared_functions()
+    assert len(names) >= 60
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+    # every declared function is also bound by the ctypes layer
+    from orchkv_b200 import _lib
+    assert set(names) <= set(_lib.exported_names())
+
+
+def test_no_gpu_code_path_without_library():
+    # the package refuses to run without the native library (no CPU fallback)
+    import orchkv_b200._lib as lb
+    assert os.path.exists(lb.LIB_PATH)
+
+
+def test_struct_layouts_match_reference_abi():
+    from orchkv_b200 import _lib
+    # sizes of the reference structs on x86-64 (computed from the reference
+    # headers: src/core/kv_types.h, src/core/kv_block.h, src/scheduler/*.h)
+    assert C.sizeof(_lib.OrchkvConfig) == 104
+    assert C.sizeof(_lib.OrchkvStats) == 128
+    assert C.sizeof(_lib.KvBlock) == 152
+    assert C.sizeof(_lib.TmConfig) == 184
+    assert C.sizeof(_lib.TmStats) == 232
+
+
+def test_struct_layouts_against_headers():
+    """Compile the public headers and compare sizeof() with the ctypes mirror."""
+    src = r"""
+#include <stdio.h>
+#include "orchkv/orchkv_api.h"
+int main(void) {
+  printf("%zu %zu %zu %zu %zu %zu\n", sizeof(orchkv_config_t), sizeof(orchkv_stats_t),
+         sizeof(kv_block_t), sizeof(tm_config_t), sizeof(tm_stats_t), sizeof(tiered_manager_t));
+  return 0;
+}
+"""
+    import tempfile
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        open(c, "w").write(src)
+        exe = os.path.join(d, "t")
+        subprocess.run(["gcc", "-std=gnu11", "-I" + os.path.join(ROOT, "include"), c, "-o", exe],
+                       check=True)
+        out = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()
+    from orchkv_b200 import _lib
+    assert [int(x) for x in out] == [C.sizeof(_lib.OrchkvConfig), C.sizeof(_lib.OrchkvStats),
+                                     C.sizeof(_lib.KvBlock), C.sizeof(_lib.TmConfig),
+                                     C.sizeof(_lib.TmStats), C.sizeof(_lib.TieredManager)]
+
+
+REFERENCE_BINDING_NAMES = [
+    "StorageTier", "DataType", "OK", "ERR_OOM", "ERR_INVALID", "ERR_NOT_FOUND",
+    "ERR_TIER_FULL", "ERR_CUDA", "ERR_IO", "Config", "init", "shutdown", "is_initialized",
+    "request_create", "request_destroy", "prefill", "get_kv_block", "evict_to_dram",
+    "promote_to_gpu", "evict_to_storage", "promote_from_storage", "evict_cold",
+    "storage_flush", "get_stats", "tm_create", "tm_destroy", "tm_register_block_id",
+    "tm_set_block_tier", "tm_report_attn", "tm_step_done", "tm_set_usage",
+    "tm_schedule_once", "tm_get_block_score", "tm_get_block_heat", "tm_start", "tm_stop",
+    "tm_set_policy", "tm_get_stats", "GPU_HBM", "HOST_DRAM", "NVM", "SSD", "NONE", "FP16",
+    "BF16", "FP32", "INT8", "INT4",
+]
+
+
+def test_orchkv_core_names_and_defaults():
+    import orchkv_b200
+    m = orchkv_b200.core()
+    import orchkv_core
+    assert orchkv_core is m
+    for n in REFERENCE_BINDING_NAMES:
+        assert hasattr(m, n), n
+    c = m.Config()
+    assert repr(c) == "<orchkv.Config gpu_pool=40960MB dram_pool=65536MB d_head=128>"
+    assert c.tokens_per_block == 64 and c.max_blocks_per_head == 256
+    assert int(m.GPU_HBM) == 0 and int(m.NONE) == 4 and m.ERR_TIER_FULL == -4
+    doc = m.tm_create.__doc__
+    for kw, val in [("tracker_cap", "4096"), ("max_blocks", "8192"), ("cooldown_sec", "0.5"),
+                    ("recency_tau", "50.0"), ("prefetch_budget", "16"),
+                    ("schedule_interval_us", "1000")]:
+        assert re.search(kw + r":[^=,]*= " + re.escape(val) + r"\b", doc), kw
+    assert re.search(r"tier:[^=,]*= 0\b", m.tm_register_block_id.__doc__)
+    assert re.search(r"flags:[^=,]*= 0\b", m.tm_register_block_id.__doc__)

@@ -1,0 +1,333 @@
+"""Data-plane parity on the GPU through the C ABI: slab layout after prefill
+and append, per-block and batched evict/promote against the oracle's
+sequential per-block model (free stacks, block locations and slab bytes
+bit-exact), the GPU -> DRAM -> GPU round trip, and error codes."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TPB, D, E = 16, 128, 2
+ROW = D * E
+SLAB = TPB * ROW * 2
+HALF = SLAB // 2
+
+
+@pytest.fixture
+def dp(cuda):
+    import orchkv_b200 as o
+    L = o.lib()
+    cfg = o.make_config(gpu_pool_bytes=96 * SLAB, dram_pool_bytes=64 * SLAB,
+                        tokens_per_block=TPB, d_head=D, dtype=1, max_blocks_per_head=32)
+    ext = o.OrchkvConfigExt()
+    ext.max_blocks = 512
+    assert L.orchkv_init_ext(C.byref(cfg), C.byref(ext)) == 0
+    yield o, L
+    assert L.orchkv_shutdown() == 0
+
+
+def pool_state(L, which, total):
+    st = np.zeros(total, np.uint32)
+    top = C.c_uint32()
+    assert L.orchkv_read_pool(which, st.ctypes.data, C.byref(top)) == 0
+    return st[: top.value].tolist()
+
+
+def locs(L, n):
+    loc = np.zeros(n, np.uint32)
+    state = np.zeros(n, np.uint8)
+    assert L.orchkv_read_block_locs(loc.ctypes.data, state.ctypes.data) == 0
+    return loc, state
+
+
+_CUDART = None
+
+
+def _cudart():
+    global _CUDART
+    if _CUDART is None:
+        import glob
+        import os
+        import torch
+        cands = glob.glob(os.path.join(os.path.dirname(torch.__file__), "..", "nvidia",
+                                       "cuda_runtime", "lib", "libcudart.so*"))
+        cands += ["libcudart.so.12", "/usr/local/cuda/lib64/libcudart.so"]
+        for c in cands:
+            try:
+                _CUDART = C.CDLL(c)
+                break
+            except OSError:
+                continue
+        _CUDART.cudaMemcpy.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int]
+    return _CUDART
+
+
+def read_dev(ptr, nbytes):
+    out = np.empty(nbytes, np.uint8)
+    assert _cudart().cudaMemcpy(out.ctypes.data, ptr, nbytes, 2) == 0
+    return out
+
+
+def read_host(ptr, nbytes):
+    return np.ctypeslib.as_array((C.c_uint8 * nbytes).from_address(ptr)).copy()
+
+
+def kv_data(rng, H, n):
+    k = rng.integers(0, 255, (H, n, ROW), dtype=np.uint8)
+    v = rng.integers(0, 255, (H, n, ROW), dtype=np.uint8)
+    return k, v
+
+
+def expected_slab(k, v, h, b):
+    """Slab bytes of block b of head h: [K rows | V rows] (src/api/orchkv_api.cu:8-18)."""
+    out = np.zeros(SLAB, np.uint8)
+    n = k.shape[1]
+    rows = range(b * TPB, min((b + 1) * TPB, n))
+    for j, t in enumerate(rows):
+        out[j * ROW:(j + 1) * ROW] = k[h, t]
+        out[HALF + j * ROW:HALF + (j + 1) * ROW] = v[h, t]
+    return out
+
+
+def info(L, ctx, l, h, b):
+    bid, tier, slab, st, tok = C.c_uint64(), C.c_int(), C.c_uint32(), C.c_int(), C.c_uint32()
+    rc = L.orchkv_block_info(ctx, l, h, b, C.byref(bid), C.byref(tier), C.byref(slab),
+                             C.byref(st), C.byref(tok))
+    return rc, bid.value, tier.value, slab.value, st.value, tok.value
+
+
+@pytest.mark.parametrize("src", ["pageable", "device", "pinned"])
+def test_prefill_layout_and_ids(dp, cuda, src):
+    o, L = dp
+    rng = np.random.default_rng(1)
+    H, n = 2, 40                      # 3 blocks per head, last one partial
+    k, v = kv_data(rng, H, n)
+    ctx = L.orchkv_request_create(7, 2, H)
+    assert ctx
+    if src == "pageable":
+        kp, vp = k.ctypes.data, v.ctypes.data
+        keep = (k, v)
+    elif src == "device":
+        kt, vt = cuda.from_numpy(k).cuda(), cuda.from_numpy(v).cuda()
+        kp, vp, keep = kt.data_ptr(), vt.data_ptr(), (kt, vt)
+    else:
+        kt, vt = cuda.from_numpy(k).pin_memory(), cuda.from_numpy(v).pin_memory()
+        kp, vp, keep = kt.data_ptr(), vt.data_ptr(), (kt, vt)
+    assert L.orchkv_prefill(ctx, 0, kp, vp, n) == 0
+    del keep
+    # block ids follow the reference counter order: block-major, then head
+    # (src/core/kv_request.c:177-204); slabs are popped head-major
+    # (src/api/orchkv_api.cu:219-226): head 0 gets slabs 0,1,2
+    base = L.orchkv_gpu_pool_base()
+    for h in range(H):
+        for b in range(3):
+            rc, bid, tier, slab, st, tok = info(L, ctx, 0, h, b)
+            assert rc == 0 and tier == 0 and st == 2
+            assert bid == b * H + h
+            assert slab == h * 3 + b
+            assert tok == (TPB if b < 2 else n - 2 * TPB)
+            got = read_dev(base + slab * SLAB, SLAB)
+            want = expected_slab(k, v, h, b)
+            used = tok * ROW
+            assert np.array_equal(got[:used], want[:used])
+            assert np.array_equal(got[HALF:HALF + used], want[HALF:HALF + used])
+    assert info(L, ctx, 0, 0, 3)[0] == -3       # NOT_FOUND
+    assert info(L, ctx, 1, 0, 0)[0] == -3
+    s = o.OrchkvStats()
+    L.orchkv_get_stats(C.byref(s))
+    assert s.gpu_slabs_used == 6 and s.total_blocks == 6
+    assert L.orchkv_request_destroy(ctx) == 0
+    L.orchkv_get_stats(C.byref(s))
+    assert s.gpu_slabs_used == 0
+
+
+def _model_from_device(L, total_g, total_d, max_blocks):
+    from oracle import oracle as O
+    gp, dp_ = O.Pool(total_g), O.Pool(total_d)
+    gp.stack = pool_state(L, 0, total_g)
+    dp_.stack = pool_state(L, 1, total_d)
+    loc, state = locs(L, max_blocks)
+    return gp, dp_, loc.astype(np.int64).tolist(), state.tolist()
+
+
+def test_per_block_evict_promote_vs_oracle(dp, cuda):
+    from oracle import oracle as O
+    o, L = dp
+    rng = np.random.default_rng(2)
+    H, n = 4, 64
+    k, v = kv_data(rng, H, n)
+    ctx = L.orchkv_request_create(1, 1, H)
+    assert L.orchkv_prefill(ctx, 0, k.ctypes.data, v.ctypes.data, n) == 0
+    gtot, dtot = 96, 64
+    gpool, dpool, loc, state = _model_from_device(L, gtot, dtot, 512)
+    gbytes = read_dev(L.orchkv_gpu_pool_base(), gtot * SLAB)
+    dbytes = np.zeros(dtot * SLAB, np.uint8)
+    ops = [("e", 1, 2), ("e", 0, 0), ("e", 3, 3), ("p", 0, 0), ("e", 2, 1), ("p", 3, 3),
+           ("p", 1, 2), ("e", 1, 2), ("e", 0, 0)]
+    for kind, h, b in ops:
+        bid = info(L, ctx, 0, h, b)[1]
+        if kind == "e":
+            assert L.orchkv_evict_to_dram(ctx, 0, h, b) == 0
+            O.evict_batch(gpool, dpool, loc, state, None, [bid], gbytes, dbytes, SLAB)
+        else:
+            assert L.orchkv_promote_to_gpu(ctx, 0, h, b) == 0
+            O.promote_batch(gpool, dpool, loc, state, [bid], gbytes, dbytes, SLAB)
+    g2, d2, loc2, state2 = _model_from_device(L, gtot, dtot, 512)
+    assert g2.stack == gpool.stack and d2.stack == dpool.stack
+    assert loc2 == loc
+    # every block's bytes, wherever it lives, equal the prefilled data
+    dbase = L.orchkv_dram_pool_base()
+    for h in range(H):
+        for b in range(4):
+            _, bid, tier, slab, _, _ = info(L, ctx, 0, h, b)
+            got = read_dev(L.orchkv_gpu_pool_base() + slab * SLAB, SLAB) if tier == 0 else \
+                read_host(dbase + slab * SLAB, SLAB)
+            assert np.array_equal(got, expected_slab(k, v, h, b))
+    # error codes (src/api/orchkv_api.cu:353-428)
+    h, b = 0, 0
+    t = info(L, ctx, 0, h, b)[2]
+    if t == 1:
+        assert L.orchkv_evict_to_dram(ctx, 0, h, b) == -8       # ERR_STATE
+    else:
+        assert L.orchkv_promote_to_gpu(ctx, 0, h, b) == -8
+    assert L.orchkv_evict_to_dram(ctx, 0, 0, 9) == -3           # ERR_NOT_FOUND
+    assert L.orchkv_set_block_flags(ctx, 0, 2, 2, 0x01) == 0
+    assert L.orchkv_evict_to_dram(ctx, 0, 2, 2) == -7           # ERR_LOCKED
+    kp, vp = C.c_void_p(), C.c_void_p()
+    _, _, tier, _, _, _ = info(L, ctx, 0, 1, 2)
+    assert L.orchkv_get_kv_block(ctx, 0, 1, 2, C.byref(kp), C.byref(vp)) == 0
+    assert info(L, ctx, 0, 1, 2)[2] == 0 and vp.value - kp.value == HALF
+    assert L.orchkv_request_destroy(ctx) == 0
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_batched_migration_equals_sequential(dp, cuda, seed):
+    from oracle import oracle as O
+    o, L = dp
+    rng = np.random.default_rng(seed)
+    H, n = 4, 16 * 12
+    k, v = kv_data(rng, H, n)
+    ctxs = [L.orchkv_request_create(i, 1, H) for i in range(2)]
+    for c in ctxs:
+        assert L.orchkv_prefill(c, 0, k.ctypes.data, v.ctypes.data, n) == 0
+    gtot, dtot = 96, 64
+    # a few single evictions first so the DRAM free stack is not in order
+    for h, b in [(0, 1), (2, 5), (1, 7)]:
+        assert L.orchkv_evict_to_dram(ctxs[0], 0, h, b) == 0
+    gpool, dpool, loc, state = _model_from_device(L, gtot, dtot, 512)
+    gbytes = read_dev(L.orchkv_gpu_pool_base(), gtot * SLAB)
+    dbytes = read_host(L.orchkv_dram_pool_base(), dtot * SLAB)
+    live = [i for i, w in enumerate(loc) if (w >> 29) in (0, 1)]
+    for rnd in range(4):
+        ids = rng.choice(live, int(rng.integers(10, 80)), replace=False).astype(np.uint32)
+        ids = np.concatenate([ids, np.array([511], np.uint32)])     # an id with no block
+        dev_ids = cuda.from_numpy(ids.view(np.int32)).cuda()
+        res = cuda.zeros(2, dtype=cuda.int32, device="cuda")
+        if rnd % 2 == 0:
+            assert L.orchkv_evict_batch_to_dram(dev_ids.data_ptr(), None, len(ids), res.data_ptr()) == 0
+            done, skipped = O.evict_batch(gpool, dpool, loc, state, None, ids.tolist(),
+                                          gbytes, dbytes, SLAB)
+        else:
+            assert L.orchkv_promote_batch_to_gpu(dev_ids.data_ptr(), None, len(ids), res.data_ptr()) == 0
+            done, skipped = O.promote_batch(gpool, dpool, loc, state, ids.tolist(), gbytes,
+                                            dbytes, SLAB)
+        r = res.cpu().numpy()
+        assert (int(r[0]), int(r[1])) == (done, skipped)
+    g2, d2, loc2, _ = _model_from_device(L, gtot, dtot, 512)
+    assert g2.stack == gpool.stack and d2.stack == dpool.stack and loc2 == loc
+    for bid, w in enumerate(loc):
+        t, s = w >> 29, w & 0x1FFFFFFF
+        if t == 0:
+            assert np.array_equal(read_dev(L.orchkv_gpu_pool_base() + s * SLAB, SLAB),
+                                  gbytes[s * SLAB:(s + 1) * SLAB]), bid
+        elif t == 1:
+            assert np.array_equal(read_host(L.orchkv_dram_pool_base() + s * SLAB, SLAB),
+                                  dbytes[s * SLAB:(s + 1) * SLAB]), bid
+    for c in ctxs:
+        assert L.orchkv_request_destroy(c) == 0
+
+
+def test_batch_pool_exhaustion(dp, cuda):
+    from oracle import oracle as O
+    o, L = dp
+    rng = np.random.default_rng(9)
+    H, n = 4, 16 * 20        # 80 GPU slabs; DRAM holds 64
+    k, v = kv_data(rng, H, n)
+    ctx = L.orchkv_request_create(3, 1, H)
+    assert L.orchkv_prefill(ctx, 0, k.ctypes.data, v.ctypes.data, n) == 0
+    gpool, dpool, loc, state = _model_from_device(L, 96, 64, 512)
+    ids = np.arange(80, dtype=np.uint32)[::-1].copy()
+    dev_ids = cuda.from_numpy(ids.view(np.int32)).cuda()
+    cnt = cuda.tensor([75], dtype=cuda.int32, device="cuda")
+    res = cuda.zeros(2, dtype=cuda.int32, device="cuda")
+    assert L.orchkv_evict_batch_to_dram(dev_ids.data_ptr(), cnt.data_ptr(), 80, res.data_ptr()) == 0
+    gb = read_dev(L.orchkv_gpu_pool_base(), 96 * SLAB)
+    db = np.zeros(64 * SLAB, np.uint8)
+    done, skipped = O.evict_batch(gpool, dpool, loc, state, None, ids[:75].tolist(), gb, db, SLAB)
+    assert (done, skipped) == (64, 11)
+    assert res.cpu().tolist() == [64, 11]
+    g2, d2, loc2, _ = _model_from_device(L, 96, 64, 512)
+    assert g2.stack == gpool.stack and d2.stack == dpool.stack and loc2 == loc
+    assert L.orchkv_request_destroy(ctx) == 0
+
+
+def test_append_one_and_batch_agree(dp, cuda):
+    o, L = dp
+    rng = np.random.default_rng(4)
+    H, Lr, n0 = 2, 3, 30
+    reqs = []
+    for _ in range(2):                       # two identical systems: per-call vs batch
+        reqs.append([L.orchkv_request_create(i, Lr, H) for i in range(3)])
+    k0, v0 = kv_data(rng, H, n0)
+    for group in reqs:
+        for c in group:
+            for layer in range(Lr):
+                assert L.orchkv_prefill(c, layer, k0.ctypes.data, v0.ctypes.data, n0) == 0
+    for step in range(5):
+        kt = rng.integers(0, 255, (3, Lr, H, ROW), dtype=np.uint8)
+        vt = rng.integers(0, 255, (3, Lr, H, ROW), dtype=np.uint8)
+        # reference call order: for request, for layer (src/api/orchkv_api.cu:263-317)
+        for i, c in enumerate(reqs[0]):
+            for layer in range(Lr):
+                assert L.orchkv_append_token(c, layer, kt[i, layer].ctypes.data,
+                                             vt[i, layer].ctypes.data) == 0
+        arr = (C.c_void_p * 3)(*reqs[1])
+        kd, vd = cuda.from_numpy(kt).cuda(), cuda.from_numpy(vt).cuda()
+        assert L.orchkv_append_token_batch(arr, 3, kd.data_ptr(), vd.data_ptr()) == 0
+    base = L.orchkv_gpu_pool_base()
+    for i in range(3):
+        for layer in range(Lr):
+            for h in range(H):
+                for b in range(3):
+                    a = info(L, reqs[0][i], layer, h, b)
+                    bb = info(L, reqs[1][i], layer, h, b)
+                    assert a[0] == 0 and bb[0] == 0 and a[5] == bb[5]
+                    ga = read_dev(base + a[3] * SLAB, SLAB)
+                    gb = read_dev(base + bb[3] * SLAB, SLAB)
+                    used = a[5] * ROW
+                    assert np.array_equal(ga[:used], gb[:used])
+                    assert np.array_equal(ga[HALF:HALF + used], gb[HALF:HALF + used])
+    s = o.OrchkvStats()
+    L.orchkv_get_stats(C.byref(s))
+    assert s.gpu_slabs_used == 2 * 3 * Lr * H * 3
+    for group in reqs:
+        for c in group:
+            assert L.orchkv_request_destroy(c) == 0
+
+
+def test_append_state_error(dp, cuda):
+    o, L = dp
+    rng = np.random.default_rng(8)
+    H = 2
+    k, v = kv_data(rng, H, 20)                  # last block partial (4 of 16)
+    ctx = L.orchkv_request_create(1, 1, H)
+    assert L.orchkv_prefill(ctx, 0, k.ctypes.data, v.ctypes.data, 20) == 0
+    assert L.orchkv_evict_to_dram(ctx, 0, 1, 1) == 0
+    row = np.zeros((H, ROW), np.uint8)
+    assert L.orchkv_append_token(ctx, 0, row.ctypes.data, row.ctypes.data) == -8
+    arr = (C.c_void_p * 1)(ctx)
+    kd = cuda.zeros(H * ROW, dtype=cuda.uint8, device="cuda")
+    assert L.orchkv_append_token_batch(arr, 1, kd.data_ptr(), kd.data_ptr()) == -8
+    assert L.orchkv_request_destroy(ctx) == 0
