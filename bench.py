@@ -1,0 +1,576 @@
+#!/usr/bin/env python
+"""Decode-step schedule + migrate benchmark for orchkv_b200 on B200.
+
+Workload (per GPU; weak scaling across ranks): the Qwen2.5-7B-shaped GQA batch
+— 32 requests x 8192-token context, 28 layers, 28 query heads, 4 KV heads,
+d_head 128, bf16 KV, 16-token blocks (8 KiB slabs, 1,835,008 slabs, 14 GiB).
+Synthetic, seeded inputs: attention logits N(0, 2) with 1% heavy-hitter
+tokens +6 per (row, head), softmaxed over the context; KV values N(0, 1).
+
+One step (everything resident in HBM when it starts):
+  append 1 token per (request, layer)       -> paged append kernel
+  per-block attention mass, EMA, hotness    -> scoring + step/classify sweep
+  coldest 25% of GPU blocks                 -> radix select
+  evict them to the pinned DRAM tier        -> pack + copy engine
+  5% prefetch set (top EMA among DRAM)      -> radix select
+  promote it back                           -> fused host-link read + scatter
+  read the step's result counts back to the host.
+Between timed steps the rest of the evicted blocks are promoted back (not
+timed) so every step starts from the same pool state.
+
+value = migrated blocks (evicted + promoted) per second, whole job.
+e2e   = the same step through the C ABI with host inputs: attention
+        probabilities and new tokens copied from pinned host memory inside
+        the timed region.
+--impl reference times the reference's own C scheduler and per-block
+migration path (compiled from its sources into oracle/_ref) on a sample.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode-step schedule+migrate µs and migrated blocks/s per GPU; HBM GB/s % peak"
+WL = dict(name="qwen2.5-7b-gqa-decode-step", B=32, L=28, Hq=28, Hkv=4, D=128, T=8192, tpb=16)
+EVICT_FRAC, PROMOTE_FRAC = 0.25, 0.05
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            p = json.load(fh)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples while the timed region runs."""
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + q,
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) == 7:
+                self.rows.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[3 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+
+class Workload:
+    def __init__(self, torch, okv, rank, world, comm=None, seed=0):
+        self.t, self.okv, self.L = torch, okv, okv.lib()
+        w = WL
+        self.B, self.Ly, self.Hq, self.Hkv, self.D, self.T, self.tpb = (
+            w["B"], w["L"], w["Hq"], w["Hkv"], w["D"], w["T"], w["tpb"])
+        self.nb = self.T // self.tpb
+        self.n_blocks = self.B * self.Ly * self.Hkv * self.nb
+        self.slab = self.tpb * self.D * 2 * 2
+        self.rows = self.B * self.Ly
+        self.k_evict = int(EVICT_FRAC * self.n_blocks)
+        self.k_promote = int(PROMOTE_FRAC * self.n_blocks)
+        # with a communicator, selections are global: the promote k covers all ranks
+        self.k_promote_sel = self.k_promote * world
+        torch_ = torch
+        dev = torch_.cuda.current_device()
+        self.stream = torch_.cuda.current_stream()
+        L = self.L
+        extra = self.B * self.Ly * self.Hkv * 4           # appended blocks over a run
+        cfg = okv.make_config(gpu_pool_bytes=(self.n_blocks + extra + 4096) * self.slab,
+                              dram_pool_bytes=(self.k_evict + 4096) * self.slab,
+                              tokens_per_block=self.tpb, d_head=self.D, dtype=1, device=dev,
+                              max_blocks_per_head=self.nb + 8)
+        ext = okv.OrchkvConfigExt()
+        ext.max_blocks = 1 << 21
+        rc = L.orchkv_init_ext(C.byref(cfg), C.byref(ext))
+        if rc != 0:
+            raise RuntimeError(f"orchkv_init_ext failed: {rc}")
+        L.orchkv_set_stream(C.c_void_p(self.stream.cuda_stream))
+        self.tm = okv.Manager(tracker_cap=1 << 21, max_blocks=1 << 22, ema_lambda=0.9,
+                              alpha=0.5, beta=0.3, gamma=0.2, recency_tau=50.0)
+        assert L.orchkv_attach_scheduler(self.tm.ref) == 0
+        if comm:
+            assert L.tm_set_comm(self.tm.ref, comm) == 0
+        g = torch_.Generator(device="cuda").manual_seed(seed + 1000 * rank)
+        self.ctxs = [L.orchkv_request_create(rank * 1000 + i, self.Ly, self.Hkv)
+                     for i in range(self.B)]
+        assert all(self.ctxs)
+        self.arr = (C.c_void_p * self.B)(*self.ctxs)
+        for c in self.ctxs:
+            for layer in range(self.Ly):
+                kv = torch_.randn(2, self.Hkv, self.T, self.D, generator=g, device="cuda",
+                                  dtype=torch_.bfloat16)
+                assert L.orchkv_prefill(c, layer, kv[0].data_ptr(), kv[1].data_ptr(), self.T) == 0
+        # attention probabilities: logits N(0,2), 1% heavy hitters +6, softmax
+        probs = torch_.randn(self.rows, self.Hq, self.T, generator=g, device="cuda") * 2.0
+        n_hh = max(1, self.T // 100)
+        pos = torch_.randint(0, self.T, (self.rows, self.Hq, n_hh), generator=g, device="cuda")
+        probs.scatter_add_(2, pos, torch_.full(pos.shape, 6.0, device="cuda"))
+        self.probs = torch_.softmax(probs, dim=-1)
+        del probs, pos
+        self.ids = torch_.empty(self.rows * self.Hkv * self.nb, dtype=torch_.int32, device="cuda")
+        self.tok = torch_.randn(2, self.B, self.Ly, self.Hkv, self.D, generator=g, device="cuda",
+                                dtype=torch_.bfloat16)
+        self.victims = torch_.empty(1 << 21, dtype=torch_.int32, device="cuda")
+        self.pref = torch_.empty(1 << 21, dtype=torch_.int32, device="cuda")
+        # counts words: 0 victims, 2-3 evict {done, skipped}, 4 prefetch set,
+        # 5-6 promote {done, skipped}, 8 restore set, 9-10 restore result
+        self.counts = torch_.zeros(16, dtype=torch_.int32, device="cuda")
+        self.h_counts = torch_.zeros(16, dtype=torch_.int32).pin_memory()
+        # host copies for the end-to-end variant
+        self.h_probs = self.probs.cpu().pin_memory()
+        self.h_tok = self.tok.cpu().pin_memory()
+        self.d_probs_e2e = torch_.empty_like(self.probs)
+        torch_.cuda.synchronize()
+        self.ev = [torch_.cuda.Event(enable_timing=True) for _ in range(10)]
+
+    def _ptr(self, t, off=0):
+        return C.c_void_p(t.data_ptr() + off)
+
+    def step(self, e2e=False):
+        """One decode step; returns nothing (results land in self.counts)."""
+        L, t, tm = self.L, self.t, self.tm.ref
+        ev = self.ev
+        ev[0].record()
+        if e2e:
+            self.d_probs_e2e.copy_(self.h_probs, non_blocking=True)
+            probs = self.d_probs_e2e
+            kp, vp = self.h_tok[0].data_ptr(), self.h_tok[1].data_ptr()
+        else:
+            probs = self.probs
+            kp, vp = self.tok[0].data_ptr(), self.tok[1].data_ptr()
+        rc = L.orchkv_append_token_batch(self.arr, self.B, C.c_void_p(kp), C.c_void_p(vp))
+        assert rc == 0, rc
+        ev[1].record()
+        assert L.orchkv_block_id_table(self.arr, self.B, self.T, self._ptr(self.ids)) == 0
+        ev[2].record()
+        assert L.tm_report_attn_probs(tm, self._ptr(probs), self.rows, self.Hq, self.Hkv,
+                                      self.T, self.tpb, None, self._ptr(self.ids)) == 0
+        ev[3].record()
+        assert L.tm_step_and_classify(tm) == 0
+        assert L.tm_select_victims_frac(tm, EVICT_FRAC, self._ptr(self.victims),
+                                        self._ptr(self.counts), 1 << 21) == 0
+        ev[4].record()
+        assert L.orchkv_evict_batch_to_dram(self._ptr(self.victims), self._ptr(self.counts),
+                                            1 << 21, self._ptr(self.counts, 8)) == 0
+        ev[5].record()
+        assert L.tm_select_prefetch(tm, self.k_promote_sel, 0.0, 0.0, self._ptr(self.pref),
+                                    self._ptr(self.counts, 16)) == 0
+        assert L.orchkv_promote_batch_to_gpu(self._ptr(self.pref), self._ptr(self.counts, 16),
+                                             self.k_promote_sel, self._ptr(self.counts, 20)) == 0
+        ev[6].record()
+        self.h_counts.copy_(self.counts, non_blocking=True)
+        ev[7].record()
+
+    def restore(self):
+        """Promote every block still on the DRAM tier (outside the timed region)."""
+        L, tm = self.L, self.tm.ref
+        assert L.tm_select_prefetch(tm, 1 << 21, 0.0, 0.0, self._ptr(self.pref),
+                                    self._ptr(self.counts, 32)) == 0
+        assert L.orchkv_promote_batch_to_gpu(self._ptr(self.pref), self._ptr(self.counts, 32),
+                                             1 << 21, self._ptr(self.counts, 36)) == 0
+        self.t.cuda.synchronize()
+
+    def phases(self):
+        e = self.ev
+        names = ["append", "id_table", "score", "classify+select", "evict", "prefetch+promote",
+                 "readback"]
+        return {n: e[i].elapsed_time(e[i + 1]) for i, n in enumerate(names)}
+
+    def close(self):
+        L = self.L
+        for c in self.ctxs:
+            L.orchkv_request_destroy(c)
+        self.tm.close()
+        L.orchkv_shutdown()
+
+
+def score_bytes(wl):
+    """Algorithmic bytes of one scoring launch: probabilities read once, block
+    id table read, per-block tracker read (active, sum, max) and written (sum,
+    max, last hit)."""
+    probs = wl.rows * wl.Hq * wl.T * 4
+    per_block = 4 + 1 + 4 + 4 + 4 + 4 + 8
+    return probs + wl.n_blocks * per_block
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    import orchkv_b200 as okv
+    okv.lib()
+    comm = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+        uid = (C.c_ubyte * 128)()
+        if rank == 0:
+            assert okv.lib().orchkv_comm_unique_id(uid) == 0
+        buf = torch.tensor(list(bytes(uid)), dtype=torch.uint8, device="cuda")
+        dist.broadcast(buf, 0)
+        uid = (C.c_ubyte * 128)(*buf.cpu().tolist())
+        comm = okv.lib().orchkv_comm_create(rank, world, uid, 60.0)
+        assert comm, "NCCL communicator creation failed"
+
+    # one dedicated stream for torch ops and the library (non-default, so
+    # events and copies order with every kernel the library launches)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    wl = Workload(torch, okv, rank, world, comm)
+    hbm_peak, peak_kind = peaks()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        wl.step()
+        wl.restore()
+    # timed: K steps, each bracketed by barrier + synchronize; the restore of
+    # the DRAM-resident remainder runs outside the brackets
+    step_ms, phase_acc, score_ms = [], {}, []
+    migrated = 0
+    launches0 = okv.lib().orchkv_kernel_launches()
+    with ClockSampler(local_rank) as clk:
+        launches_timed = 0
+        la = launches0
+        for _ in range(args.steps):
+            barrier()
+            la = okv.lib().orchkv_kernel_launches()
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record()
+            wl.step()
+            t1.record()
+            barrier()
+            step_ms.append(t0.elapsed_time(t1))
+            ph = wl.phases()
+            for k, v in ph.items():
+                phase_acc.setdefault(k, []).append(v)
+            score_ms.append(ph["score"])
+            c = wl.h_counts.tolist()
+            migrated += c[2] + c[5]
+            launches_timed += okv.lib().orchkv_kernel_launches() - la
+            wl.restore()
+            la = okv.lib().orchkv_kernel_launches()
+    # e2e through the C ABI with host inputs
+    e2e_ms = []
+    for _ in range(max(1, min(args.steps, 5))):
+        barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        wl.step(e2e=True)
+        t1.record()
+        barrier()
+        e2e_ms.append(t0.elapsed_time(t1))
+        c_e2e = wl.h_counts.tolist()
+        wl.restore()
+    # pack kernel profile of one more evict (device events on its stream)
+    wl.step()
+    pk_ms, pk_bytes, pk_chunks, pr_ms = C.c_float(), C.c_ulonglong(), C.c_uint32(), C.c_float()
+    wl.L.orchkv_last_migration_profile(C.byref(pk_ms), C.byref(pk_bytes), C.byref(pk_chunks),
+                                       C.byref(pr_ms))
+    c_last = wl.h_counts.tolist()
+    wl.restore()
+
+    mean_ms = sum(step_ms) / len(step_ms)
+    per_step_migrated = migrated / args.steps
+    if world > 1:
+        t = torch.tensor([mean_ms, per_step_migrated, sum(e2e_ms) / len(e2e_ms)],
+                         dtype=torch.float64, device="cuda")
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        mean_ms_max, migrated_total, e2e_max = float(mx[0]), float(sm[1]), float(mx[2])
+    else:
+        mean_ms_max, migrated_total, e2e_max = mean_ms, per_step_migrated, sum(e2e_ms) / len(e2e_ms)
+
+    sb = score_bytes(wl)
+    score_avg = sum(score_ms) / len(score_ms)
+    achieved = sb / (score_avg * 1e-3) / 1e9
+    phases = {k: round(sum(v) / len(v), 4) for k, v in phase_acc.items()}
+    evict_bytes = c_last[2] * wl.slab
+    promote_bytes = c_last[5] * wl.slab
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline_sample(args)
+        line = {
+            "metric": METRIC,
+            "value": round(migrated_total / (mean_ms_max * 1e-3), 1),
+            "unit": "blocks/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(mean_ms_max, 4),
+            "us_per_step": round(mean_ms_max * 1e3, 1),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded: logits N(0,2) + 1% heavy hitters, KV N(0,1))",
+            "config": {"workload": WL["name"], "requests": WL["B"], "context": WL["T"],
+                       "layers": WL["L"], "q_heads": WL["Hq"], "kv_heads": WL["Hkv"],
+                       "d_head": WL["D"], "tokens_per_block": WL["tpb"],
+                       "blocks_per_gpu": wl.n_blocks, "evict_frac": EVICT_FRAC,
+                       "promote_frac": PROMOTE_FRAC, "parallelism": f"kv-shard x{world}",
+                       "l2": "inputs larger than L2 (0.82 GB probs, 14 GiB KV pool)"},
+            "gpu_launches": int(launches_timed),
+            "gpu_launches_per_step": round(launches_timed / args.steps, 1),
+            "roofline": {
+                "kernel": "score (per-block attention mass, tm_report_attn_probs)",
+                "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
+                "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                "peak_kind": peak_kind, "bytes_per_launch": sb,
+                "ms_per_launch": round(score_avg, 4), "traffic": None},
+            "pack": {"kernel": "evict pack (HBM gather -> staging)",
+                     "ms": round(pk_ms.value, 4), "bytes": pk_bytes.value,
+                     "achieved_gbs": round(pk_bytes.value / max(pk_ms.value, 1e-9) / 1e6, 1),
+                     "frac": round(pk_bytes.value / max(pk_ms.value, 1e-9) / 1e6 / hbm_peak, 4),
+                     "chunks": pk_chunks.value},
+            "host_link": {"evict_bytes": evict_bytes, "evict_ms": phases.get("evict"),
+                          "evict_gbs": round(evict_bytes / max(phases.get("evict", 1), 1e-9) / 1e6, 1),
+                          "promote_bytes": promote_bytes, "promote_kernel_ms": round(pr_ms.value, 3),
+                          "promote_gbs": round(promote_bytes / max(pr_ms.value, 1e-9) / 1e6, 1)},
+            "phases_ms": phases,
+            "e2e": {"value": round(migrated_total / (e2e_max * 1e-3), 1), "unit": "blocks/s",
+                    "ms_per_step": round(e2e_max, 4),
+                    "h2d_bytes_per_step": int(wl.probs.numel() * 4 + wl.tok.numel() * 2
+                                              + c_e2e[5] * wl.slab),
+                    "d2h_bytes_per_step": int(c_e2e[2] * wl.slab + 32)},
+            "clocks": clk.summary(),
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+    wl.close()
+    if comm:
+        okv.lib().orchkv_comm_destroy(comm)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line:
+        print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# Reference arm: the reference's C scheduler + per-block migration on a sample
+# ---------------------------------------------------------------------------
+
+def _reference_sample(max_seconds=12.0, steps=3, warm=1, sample_requests=1):
+    """Time the reference on `sample_requests` request(s) of the workload:
+    fixed-order C reduction of the attention probabilities (restating the
+    managers' torch reduction), attn_tracker_update_batch + tm_step_done +
+    tm_schedule_once (reference C), the FastKVCacheManager coldest-first order,
+    then orchkv_evict_to_dram / orchkv_promote_to_gpu per block and
+    orchkv_append_token per (request, layer) through the reference's own
+    orchkv_api (real CUDA copies).  Returns blocks/s (migrated) and details."""
+    import numpy as np
+
+    from oracle import oracle as O
+    w = WL
+    B, Ly, Hq, Hkv, D, T, tpb = sample_requests, w["L"], w["Hq"], w["Hkv"], w["D"], w["T"], w["tpb"]
+    nb = T // tpb
+    n = B * Ly * Hkv * nb
+    slab = tpb * D * 4
+    rng = np.random.default_rng(0)
+    logits = rng.normal(0, 2, (B * Ly, Hq, T)).astype(np.float32)
+    for r in range(B * Ly):
+        for h in range(Hq):
+            logits[r, h, rng.choice(T, T // 100, replace=False)] += 6.0
+    logits -= logits.max(-1, keepdims=True)
+    p = np.exp(logits)
+    probs = (p / p.sum(-1, keepdims=True)).astype(np.float32)
+    del logits, p
+    R = O.ref()
+    tm = O.RefTM(tracker_cap=n, max_blocks=n, ema_lambda=0.9, alpha=0.5, beta=0.3, gamma=0.2,
+                 recency_tau=50.0, cooldown_sec=0.0)
+    ids = np.arange(n, dtype=np.uint64)
+    for i in range(n):
+        tm.register(i, 0, 0)
+    gpu_pool = (n + B * Ly * Hkv * 8 + 64) * slab
+    dram_pool = (n // 4 + 64) * slab
+    rc = R.ref_api_init(0, gpu_pool, dram_pool, tpb, D, 1, 4, nb + 8, b"/dev/shm/orchkv_ref_bench")
+    assert rc == 0, rc
+    kv = rng.standard_normal((Hkv, T, D)).astype(np.float16)
+    ctxs = []
+    for b in range(B):
+        c = R.ref_api_request_create(b, Ly, Hkv)
+        for layer in range(Ly):
+            assert R.ref_api_prefill(c, layer, kv.ctypes.data, kv.ctypes.data, T) == 0
+        ctxs.append(c)
+    tok = np.zeros((Hkv, D), np.float16)
+    k_e, k_p = int(EVICT_FRAC * n), int(PROMOTE_FRAC * n)
+    vict = np.zeros(k_e, np.uint64)
+    times = []
+    for s in range(warm + steps):
+        t0 = time.perf_counter()
+        w_ = O.score_blocks(probs, Hq, Hkv, tpb)             # [B*Ly, Hkv, nb]
+        t1 = time.perf_counter()
+        tt = np.zeros(3)
+        c = R.ref_arm_sched_step(tm.h, ids, w_.reshape(-1).copy(), n, 0.95, k_e, vict, tt)
+        t2 = time.perf_counter()
+        # migration: victims are ids -> (request, layer, head, block)
+        lhb = []
+        for v in vict[:c]:
+            v = int(v)
+            b, rem = divmod(v, Ly * Hkv * nb)
+            layer, rem = divmod(rem, Hkv * nb)
+            head, bi = divmod(rem, nb)
+            lhb.append((b, layer, head, bi))
+        t3 = time.perf_counter()
+        by_req = {}
+        for (b, layer, head, bi) in lhb:
+            by_req.setdefault(b, []).append((layer, head, bi))
+        mt = np.zeros(2)
+        n_promote = 0
+        for b, lst in by_req.items():
+            arr = np.array(lst, np.uint32).reshape(-1)
+            npro = max(0, min(len(lst), int(round(k_p * len(lst) / max(c, 1)))))
+            n_promote += npro
+            tmp = np.zeros(2)
+            assert R.ref_api_migrate_list(ctxs[b], arr, len(lst), npro, tmp) == 0
+            mt += tmp
+            # restore the rest (not timed)
+            for (layer, head, bi) in lst[npro:]:
+                R.ref_api_promote(ctxs[b], layer, head, bi)
+        t4 = time.perf_counter()
+        for b in range(B):
+            for layer in range(Ly):
+                R.ref_api_append(ctxs[b], layer, tok.ctypes.data, tok.ctypes.data)
+        t5 = time.perf_counter()
+        step_s = (t1 - t0) + (t2 - t1) + (t3 - t2) + mt[0] + mt[1] + (t5 - t4)
+        if s >= warm:
+            times.append(dict(step_s=step_s, score_s=t1 - t0, sched_s=t2 - t1,
+                              evict_s=mt[0], promote_s=mt[1], append_s=t5 - t4,
+                              migrated=c + n_promote, blocks=n))
+    for cx in ctxs:
+        R.ref_api_request_destroy(cx)
+    R.ref_api_shutdown()
+    tm.close()
+    mean = {k: sum(t[k] for t in times) / len(times) for k in times[0]}
+    return mean
+
+
+def cpu_baseline_sample(args):
+    from oracle import oracle as O
+    if not O.ref_available():
+        return None
+    m = _reference_sample(steps=max(1, min(args.steps, 3)))
+    return {"value": round(m["migrated"] / m["step_s"], 1), "unit": "blocks/s",
+            "cores": 1, "kind": "reference",
+            "sample": f"1 of {WL['B']} requests ({m['blocks']} blocks): reference C scheduler "
+                      f"(attn_tracker_update_batch, tm_step_done, tm_schedule_once) + "
+                      f"coldest-25% order + per-block orchkv_evict_to_dram / "
+                      f"orchkv_promote_to_gpu + orchkv_append_token, mean of "
+                      f"{max(1, min(args.steps, 3))} steps",
+            "us_per_step_sample": round(m["step_s"] * 1e6, 1),
+            "phases_s": {k: round(v, 6) for k, v in m.items() if k.endswith("_s")}}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    if not O.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref was not built (reference sources absent at build time)"}))
+        return
+    import torch
+    torch.cuda.set_device(0)
+    m = _reference_sample(steps=max(1, args.steps), warm=min(args.warmup, 1))
+    v = round(m["migrated"] / m["step_s"], 1)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "blocks/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(m["step_s"] * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32+fp16",
+            "data": "synthetic (seeded)", "config": {"workload": WL["name"],
+                                                     "sample_requests": 1},
+            "cpu_baseline": {"value": v, "unit": "blocks/s", "cores": 1, "kind": "reference",
+                             "sample": "1 request x 28 layers x 4 KV heads x 512 blocks"},
+            "e2e": {"value": v, "unit": "blocks/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "phases_s": {k: round(v_, 6) for k, v_ in m.items() if k.endswith("_s")}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--requests", type=int, default=WL["B"],
+                    help="requests per GPU (32 = the benchmark workload; smaller "
+                         "values only for profiling captures)")
+    args = ap.parse_args()
+    WL["B"] = args.requests
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -135,6 +135,14 @@ int  orchkv_evict_batch_to_dram(const uint32_t *block_ids, const uint32_t *count
 int  orchkv_promote_batch_to_gpu(const uint32_t *block_ids, const uint32_t *count,
                                  uint32_t max_n, uint32_t *result);
 
+/* Device-side timing of the last batched evict / promote (synchronises):
+ * pack_ms sums the pack kernels of a staged (copy-engine) evict, pack_bytes
+ * are the bytes they read and wrote, chunks the staging slots used (0 when the
+ * fused zero-copy kernel ran instead); promote_ms is the last promote
+ * kernel's duration. */
+int  orchkv_last_migration_profile(float *pack_ms, unsigned long long *pack_bytes,
+                                   uint32_t *chunks, float *promote_ms);
+
 /* Device table [n*n_layers][n_kv_heads][ceil(row_len/tpb)] of block ids of
  * the given requests (0xFFFFFFFF where a block does not exist), the layout
  * tm_report_attn_probs takes.  Asynchronous. */
@@ -153,6 +161,8 @@ int  orchkv_read_pool(int which, uint32_t *stack_out, uint32_t *top_out);
 /* Location words ((tier << 29) | slab) and states of all max_blocks ids. */
 int  orchkv_read_block_locs(uint32_t *loc_out, uint8_t *state_out);
 uint32_t orchkv_max_blocks(void);
+/* CUDA kernel launches issued by the library since it was loaded. */
+unsigned long long orchkv_kernel_launches(void);
 void *orchkv_gpu_pool_base(void);
 void *orchkv_dram_pool_base(void);
 

@@ -139,6 +139,8 @@ _SIGS = {
     "orchkv_read_pool": (i32, [i32, vp, P(u32)]),
     "orchkv_read_block_locs": (i32, [vp, vp]),
     "orchkv_max_blocks": (u32, []),
+    "orchkv_kernel_launches": (C.c_ulonglong, []),
+    "orchkv_last_migration_profile": (i32, [P(f32), P(C.c_ulonglong), P(u32), P(f32)]),
     "orchkv_gpu_pool_base": (vp, []),
     "orchkv_dram_pool_base": (vp, []),
     # scheduler

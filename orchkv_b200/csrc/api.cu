@@ -35,6 +35,11 @@ struct kv_request_ctx {
 
 namespace {
 
+constexpr uint32_t kStagedMin = 2048;        // batches this large may use the copy engine
+constexpr size_t kChunkBytes = 256u << 20;   // staging ring slot size
+constexpr int kRing = 3;
+constexpr int kMaxChunks = 1024;
+
 struct Sys {
     std::recursive_mutex mu;
     bool inited = false;
@@ -58,6 +63,18 @@ struct Sys {
     std::vector<uint32_t *> regions_last;
     tiered_manager_t *attached = nullptr;
     uint32_t active_requests = 0;
+    // staged evict: device staging ring drained to the DRAM tier by the copy
+    // engine on its own stream; per-chunk events time the pack kernels
+    cudaStream_t copy = nullptr;
+    char *ring = nullptr;
+    uint32_t ring_slabs = 0;          // slabs per ring slot
+    cudaEvent_t ev_copied[kRing] = {};
+    cudaEvent_t ev_pk[2 * kMaxChunks] = {};
+    cudaEvent_t ev_mig[4] = {};
+    uint32_t *h_meta = nullptr;       // pinned
+    uint32_t last_chunks = 0;
+    int last_evict_staged = 0, last_promote_timed = 0;
+    unsigned long long last_pack_bytes = 0;
     gpu_tier_t gsnap;
     dram_tier_t dsnap;
     std::vector<uint32_t> gsnap_stack, dsnap_stack;
@@ -185,6 +202,7 @@ void region_free(size_t off, size_t words)
 
 void release_all()
 {
+    if (g.copy) cudaStreamSynchronize(g.copy);
     if (g.stream) cudaStreamSynchronize(g.stream);
     cudaFree(g.p.gpu_base);
     if (g.p.dram_base) cudaFreeHost(g.p.dram_base);
@@ -196,6 +214,15 @@ void release_all()
     cudaFreeHost(g.regions_host);
     cudaFreeHost(g.res);
     cudaFreeHost(g.h_ctr);
+    cudaFreeHost(g.h_meta);
+    cudaFree(g.ring);
+    for (auto &e : g.ev_copied) if (e) { cudaEventDestroy(e); e = nullptr; }
+    for (auto &e : g.ev_pk) if (e) { cudaEventDestroy(e); e = nullptr; }
+    for (auto &e : g.ev_mig) if (e) { cudaEventDestroy(e); e = nullptr; }
+    if (g.copy) cudaStreamDestroy(g.copy);
+    g.copy = nullptr;
+    g.ring = nullptr;
+    g.h_meta = nullptr;
     if (g.own) cudaStreamDestroy(g.own);
     g.p = PoolDev();
     g.dev_meta = nullptr;
@@ -329,7 +356,7 @@ int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
     if (cudaMalloc((void **)&g.bt, g.bt_words * 4) != cudaSuccess) { release_all(); return ORCHKV_ERR_CUDA; }
     g.free_regions.clear();
     g.free_regions[0] = g.bt_words;
-    g.scratch_words = (size_t)p.max_blocks * 2 + p.max_blocks / 1024 + 4096 +
+    g.scratch_words = (size_t)p.max_blocks * 3 + p.max_blocks / 1024 + 4096 +
                       (size_t)2 * (ext && ext->max_requests ? ext->max_requests : 4096) * 256;
     if (cudaMalloc((void **)&g.scratch, g.scratch_words * 4) != cudaSuccess) {
         release_all();
@@ -337,7 +364,15 @@ int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
     }
     OKV_CUDA_TRY(cudaMallocHost((void **)&g.res, sizeof(CompatResult)));
     OKV_CUDA_TRY(cudaMallocHost((void **)&g.h_ctr, sizeof(PoolCounters)));
+    OKV_CUDA_TRY(cudaMallocHost((void **)&g.h_meta, 16 * 4));
     memset(g.res, 0, sizeof(CompatResult));
+    OKV_CUDA_TRY(cudaStreamCreateWithFlags(&g.copy, cudaStreamNonBlocking));
+    g.ring_slabs = (uint32_t)(kChunkBytes / slab);
+    if (g.ring_slabs == 0) g.ring_slabs = 1;
+    OKV_CUDA_TRY(cudaMalloc((void **)&g.ring, (size_t)kRing * g.ring_slabs * slab));
+    for (auto &e : g.ev_copied) OKV_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    for (auto &e : g.ev_pk) OKV_CUDA_TRY(cudaEventCreate(&e));
+    for (auto &e : g.ev_mig) OKV_CUDA_TRY(cudaEventCreate(&e));
     g.active_requests = 0;
     g.inited = true;
     return ORCHKV_OK;
@@ -611,8 +646,54 @@ int orchkv_evict_batch_to_dram(const uint32_t *ids, const uint32_t *count, uint3
     std::lock_guard<std::recursive_mutex> lk(g.mu);
     if (!g.inited) return ORCHKV_ERR_INIT;
     if (max_n && !ids) return ORCHKV_ERR_INVALID;
-    if ((size_t)2 * max_n + max_n / 1024 + 32 > g.scratch_words) return ORCHKV_ERR_INVALID;
-    return launch_migrate_batch(g.p, 0, ids, count, max_n, result, g.scratch, g.stream);
+    if ((size_t)3 * max_n + max_n / 1024 + 32 > g.scratch_words) return ORCHKV_ERR_INVALID;
+    g.last_evict_staged = 0;
+    g.last_chunks = 0;
+    g.last_pack_bytes = 0;
+    MigPlan mp = launch_migrate_plan(g.p, 0, ids, count, max_n, result, g.scratch, g.stream);
+    if (mp.rc) return mp.rc;
+    if (max_n >= kStagedMin) {
+        // Large batch: if the DRAM slabs popped for it form one contiguous
+        // range (the LIFO pool hands out ranges), assign them in ascending
+        // order, pack the victims into a device staging ring at HBM speed and
+        // let the copy engine drain each slot into that range while the next
+        // slot is packed.  Pool stacks end exactly as after per-block evicts;
+        // only which victim gets which slab of the range differs.
+        int rc = launch_run_check(g.p, mp, g.stream);
+        if (rc) return rc;
+        OKV_CUDA_TRY(cudaMemcpyAsync(g.h_meta, mp.meta, 8 * 4, cudaMemcpyDeviceToHost, g.stream));
+        OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+        const uint32_t done = g.h_meta[0], run = g.h_meta[4], lo = g.h_meta[5];
+        if (done == 0) return ORCHKV_OK;
+        const uint32_t chunk = g.ring_slabs;
+        const uint32_t nchunks = (done + chunk - 1) / chunk;
+        if (run == 1 && nchunks <= (uint32_t)kMaxChunks) {
+            const size_t slab = g.p.slab;
+            for (uint32_t c = 0; c < nchunks; c++) {
+                const uint32_t slot = c % kRing;
+                const uint32_t pos0 = c * chunk;
+                const uint32_t n = done - pos0 < chunk ? done - pos0 : chunk;
+                char *buf = g.ring + (size_t)slot * chunk * slab;
+                if (c >= (uint32_t)kRing) OKV_CUDA_TRY(cudaStreamWaitEvent(g.stream, g.ev_copied[slot], 0));
+                OKV_CUDA_TRY(cudaEventRecord(g.ev_pk[2 * c], g.stream));
+                rc = launch_pack(g.p, mp, buf, pos0, n, g.stream);
+                if (rc) return rc;
+                OKV_CUDA_TRY(cudaEventRecord(g.ev_pk[2 * c + 1], g.stream));
+                OKV_CUDA_TRY(cudaStreamWaitEvent(g.copy, g.ev_pk[2 * c + 1], 0));
+                OKV_CUDA_TRY(cudaMemcpyAsync(g.p.dram_base + ((size_t)lo + pos0) * slab, buf,
+                                             (size_t)n * slab, cudaMemcpyDeviceToHost, g.copy));
+                OKV_CUDA_TRY(cudaEventRecord(g.ev_copied[slot], g.copy));
+            }
+            // later work on the stream sees the bytes in the DRAM tier
+            OKV_CUDA_TRY(cudaEventRecord(g.ev_mig[0], g.copy));
+            OKV_CUDA_TRY(cudaStreamWaitEvent(g.stream, g.ev_mig[0], 0));
+            g.last_evict_staged = 1;
+            g.last_chunks = nchunks;
+            g.last_pack_bytes = (unsigned long long)done * slab * 2;
+            return ORCHKV_OK;
+        }
+    }
+    return launch_migrate_zero_copy(g.p, 0, mp, g.stream);
 }
 
 int orchkv_promote_batch_to_gpu(const uint32_t *ids, const uint32_t *count, uint32_t max_n,
@@ -621,8 +702,45 @@ int orchkv_promote_batch_to_gpu(const uint32_t *ids, const uint32_t *count, uint
     std::lock_guard<std::recursive_mutex> lk(g.mu);
     if (!g.inited) return ORCHKV_ERR_INIT;
     if (max_n && !ids) return ORCHKV_ERR_INVALID;
-    if ((size_t)2 * max_n + max_n / 1024 + 32 > g.scratch_words) return ORCHKV_ERR_INVALID;
-    return launch_migrate_batch(g.p, 1, ids, count, max_n, result, g.scratch, g.stream);
+    if ((size_t)3 * max_n + max_n / 1024 + 32 > g.scratch_words) return ORCHKV_ERR_INVALID;
+    MigPlan mp = launch_migrate_plan(g.p, 1, ids, count, max_n, result, g.scratch, g.stream);
+    if (mp.rc) return mp.rc;
+    // Promotion sources are scattered DRAM slabs: one fused kernel reads them
+    // over the host link (mapped pinned memory) and scatters into GPU slabs.
+    OKV_CUDA_TRY(cudaEventRecord(g.ev_mig[1], g.stream));
+    int rc = launch_migrate_zero_copy(g.p, 1, mp, g.stream);
+    OKV_CUDA_TRY(cudaEventRecord(g.ev_mig[2], g.stream));
+    g.last_promote_timed = 1;
+    return rc;
+}
+
+/* Timing of the last batched evict / promote (synchronises the stream):
+ * pack_ms = summed device time of the pack kernels (0 if the zero-copy path
+ * ran), pack_bytes = bytes they read + wrote, chunks = staging slots used,
+ * promote_ms = device time of the last promote copy kernel. */
+int orchkv_last_migration_profile(float *pack_ms, unsigned long long *pack_bytes,
+                                  uint32_t *chunks, float *promote_ms)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    float total = 0.f;
+    if (g.last_evict_staged) {
+        for (uint32_t c = 0; c < g.last_chunks; c++) {
+            float ms = 0.f;
+            OKV_CUDA_TRY(cudaEventElapsedTime(&ms, g.ev_pk[2 * c], g.ev_pk[2 * c + 1]));
+            total += ms;
+        }
+    }
+    if (pack_ms) *pack_ms = total;
+    if (pack_bytes) *pack_bytes = g.last_evict_staged ? g.last_pack_bytes : 0;
+    if (chunks) *chunks = g.last_evict_staged ? g.last_chunks : 0;
+    if (promote_ms) {
+        *promote_ms = 0.f;
+        if (g.last_promote_timed)
+            OKV_CUDA_TRY(cudaEventElapsedTime(promote_ms, g.ev_mig[1], g.ev_mig[2]));
+    }
+    return ORCHKV_OK;
 }
 
 int orchkv_block_id_table(kv_request_ctx_t *const *ctxs, uint32_t n, uint32_t row_len,
@@ -690,6 +808,9 @@ int orchkv_read_block_locs(uint32_t *loc_out, uint8_t *state_out)
 }
 
 uint32_t orchkv_max_blocks(void) { return g.inited ? g.p.max_blocks : 0; }
+
+/* Number of CUDA kernel launches this library has issued since it loaded. */
+unsigned long long orchkv_kernel_launches(void) { return launch_count(); }
 void *orchkv_gpu_pool_base(void) { return g.inited ? g.p.gpu_base : nullptr; }
 void *orchkv_dram_pool_base(void) { return g.inited ? g.p.dram_base : nullptr; }
 

@@ -67,6 +67,11 @@ struct ClassCounts {
     uint32_t n_hot, n_warm, n_cold, n_sink;
 };
 
+// Host-side count of kernel launches issued by this library (every launcher
+// adds the launches it enqueues); exported as orchkv_kernel_launches().
+void note_launches(unsigned n);
+unsigned long long launch_count();
+
 // ---- small block-wide helpers ------------------------------------------------
 
 __device__ inline uint32_t warp_incl_scan(uint32_t v)

@@ -75,10 +75,27 @@ int launch_append_batch(const PoolDev &p, uint32_t *const *regions, uint32_t n, 
                         uint32_t H, uint32_t mbph, const char *k, const char *v,
                         uint32_t *scratch, cudaStream_t s);
 // Batched migration.  dir 0 = evict (GPU -> DRAM), 1 = promote (DRAM -> GPU).
-// scratch: >= 2*max_n + 2*tiles + 16 words where tiles = ceil(max_n/1024).
+// scratch: >= 3*max_n + tiles + 16 words where tiles = ceil(max_n/1024).
 int launch_migrate_batch(const PoolDev &p, int dir, const uint32_t *ids,
                          const uint32_t *count, uint32_t max_n, uint32_t *result,
                          uint32_t *scratch, cudaStream_t s);
+
+// Pieces of a batched migration for the staged (copy-engine) evict path.
+// meta words: [0] done, [1] old dst top, [2] old src top, [3] lowest dst slab,
+// [4] 1 if the popped dst slabs form one contiguous range, [5] its first slab.
+// scratch: >= 3*max_n + tiles + 16 words.
+struct MigPlan {
+    uint32_t *meta, *plan_src, *plan_dst, *plan_id;
+    uint32_t tiles, max_n;
+    int rc;
+};
+MigPlan launch_migrate_plan(const PoolDev &p, int dir, const uint32_t *ids,
+                            const uint32_t *count, uint32_t max_n, uint32_t *result,
+                            uint32_t *scratch, cudaStream_t s);
+int launch_migrate_zero_copy(const PoolDev &p, int dir, const MigPlan &mp, cudaStream_t s);
+int launch_run_check(const PoolDev &p, const MigPlan &mp, cudaStream_t s);
+int launch_pack(const PoolDev &p, const MigPlan &mp, char *staging, uint32_t pos0, uint32_t n,
+                cudaStream_t s);
 int launch_id_table(const PoolDev &p, uint32_t *const *regions, uint32_t n, uint32_t L,
                     uint32_t H, uint32_t mbph, uint32_t row_len, uint32_t *out,
                     cudaStream_t s);

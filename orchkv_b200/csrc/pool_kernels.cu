@@ -256,31 +256,22 @@ __global__ void prefill_plan_kernel(PoolDev p, ReqDev r, uint32_t l, uint32_t se
         if (needed > r.mbph || c->id_top < nn * r.H || c->g_top < nn * r.H) {
             rc = ORCHKV_ERR_TIER_FULL;
         } else {
-            uint32_t *tab = req_table(r) + (size_t)l * r.H * r.mbph;
-            // ids: block-major then head (kv_request.c:177-204)
-            for (uint32_t j = 0; j < nn; j++)
-                for (uint32_t hh = 0; hh < r.H; hh++) {
-                    const uint32_t id = p.id_stack[--c->id_top];
-                    tab[(size_t)hh * r.mbph + have + j] = id;
-                    p.flags[id] = 0;
-                }
-            // slabs: head-major then block (orchkv_api.cu:219-226)
-            for (uint32_t hh = 0; hh < r.H; hh++)
-                for (uint32_t j = 0; j < nn; j++) {
-                    const uint32_t id = tab[(size_t)hh * r.mbph + have + j];
-                    const uint32_t g = p.g_stack[--c->g_top];
-                    p.loc[id] = make_loc(TIER_GPU_HBM, g);
-                    p.state[id] = KV_STATE_HOT;
-                    c->live_blocks++;
-                    sched_register(p, id, 0);
-                    const uint32_t ts = (have + j) * p.tpb;
-                    if (ts < seq) {
-                        uint32_t cnt = total - ts < p.tpb ? total - ts : p.tpb;
-                        const unsigned long long bytes = (unsigned long long)cnt * p.row;
-                        if (has_k) { c->transfers_h2d++; c->bytes_h2d += bytes; }
-                        if (has_v) { c->transfers_h2d++; c->bytes_h2d += bytes; }
-                    }
-                }
+            // The per-block pops happen in prefill_copy_kernel from these
+            // saved tops: ids go block-major then head (kv_request.c:177-204),
+            // slabs head-major then block (orchkv_api.cu:219-226).
+            scratch[3] = c->id_top;
+            scratch[4] = c->g_top;
+            c->id_top -= nn * r.H;
+            c->g_top -= nn * r.H;
+            c->live_blocks += nn * r.H;
+            for (uint32_t j = 0; j < nn; j++) {
+                const uint32_t ts = (have + j) * p.tpb;
+                if (ts >= seq) continue;
+                const uint32_t cnt = total - ts < p.tpb ? total - ts : p.tpb;
+                const unsigned long long bytes = (unsigned long long)cnt * p.row * r.H;
+                if (has_k) { c->transfers_h2d += r.H; c->bytes_h2d += bytes; }
+                if (has_v) { c->transfers_h2d += r.H; c->bytes_h2d += bytes; }
+            }
             scratch[0] = nn;
         }
     }
@@ -296,19 +287,28 @@ prefill_copy_kernel(PoolDev p, ReqDev r, uint32_t l, const char *k, const char *
                     uint32_t seq, const uint32_t *scratch)
 {
     const uint32_t nn = scratch[0], have = scratch[1], total = scratch[2];
+    const uint32_t id_top = scratch[3], g_top = scratch[4];
     const uint32_t n_items = nn * r.H;
     const unsigned warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const unsigned lane = threadIdx.x & 31;
     const unsigned nwarps = (gridDim.x * blockDim.x) >> 5;
-    const uint32_t *tab = req_table(r) + (size_t)l * r.H * r.mbph;
+    uint32_t *tab = req_table(r) + (size_t)l * r.H * r.mbph;
     for (uint32_t it = warp; it < n_items; it += nwarps) {
         const uint32_t hh = it / nn, j = it % nn;
+        const uint32_t id = p.id_stack[id_top - 1 - (j * r.H + hh)];
+        const uint32_t g = p.g_stack[g_top - 1 - it];
+        if (lane == 0) {
+            tab[(size_t)hh * r.mbph + have + j] = id;
+            p.flags[id] = 0;
+            p.loc[id] = make_loc(TIER_GPU_HBM, g);
+            p.state[id] = KV_STATE_HOT;
+            sched_register(p, id, 0);
+        }
         const uint32_t ts = (have + j) * p.tpb;
         if (ts >= seq) continue;             // source offset beyond the buffer
         uint32_t cnt = total - ts < p.tpb ? total - ts : p.tpb;
         if (cnt > seq - ts) cnt = seq - ts;  // stay inside this head's rows
-        const uint32_t id = tab[(size_t)hh * r.mbph + have + j];
-        char *dst = p.gpu_base + (unsigned long long)loc_slab(p.loc[id]) * p.slab;
+        char *dst = p.gpu_base + (unsigned long long)g * p.slab;
         const size_t off = ((size_t)hh * seq + ts) * p.row;
         const unsigned long long bytes = (unsigned long long)cnt * p.row;
         if (k) coop_copy(dst, k + off, bytes, lane, 32);
@@ -480,7 +480,11 @@ mig_scan_kernel(PoolDev p, int dir, const uint32_t *count, uint32_t max_n, uint3
         uint32_t *dst_top = dir == 0 ? &c->d_top : &c->g_top;
         uint32_t *src_top = dir == 0 ? &c->g_top : &c->d_top;
         const uint32_t avail = *dst_top;
-        const uint32_t done = valid < avail ? valid : avail;
+        uint32_t done = valid < avail ? valid : avail;
+        // ids must be unique; a repeated id would push its slab twice, so the
+        // pushes are bounded by the source stack's free room
+        const uint32_t src_room = (dir == 0 ? p.g_total : p.d_total) - *src_top;
+        if (done > src_room) done = src_room;
         meta[0] = done;
         meta[1] = *dst_top;
         meta[2] = *src_top;
@@ -497,7 +501,7 @@ mig_scan_kernel(PoolDev p, int dir, const uint32_t *count, uint32_t max_n, uint3
 __global__ void __launch_bounds__(256)
 mig_plan_kernel(PoolDev p, int dir, const uint32_t *ids, const uint32_t *count,
                 uint32_t max_n, const uint32_t *tile_base, const uint32_t *meta,
-                uint32_t *plan_src, uint32_t *plan_dst)
+                uint32_t *plan_src, uint32_t *plan_dst, uint32_t *plan_id)
 {
     __shared__ uint32_t tmp[33];
     const uint32_t n = list_len(count, max_n);
@@ -532,6 +536,7 @@ mig_plan_kernel(PoolDev p, int dir, const uint32_t *ids, const uint32_t *count,
             sched_move(p, id, (uint8_t)dst_tier, new_state);
             plan_src[o] = s;
             plan_dst[o] = d;
+            plan_id[o] = id;
         }
         o++;
     }
@@ -550,6 +555,79 @@ mig_copy_kernel(const char *src_base, char *dst_base, unsigned long long slab,
     for (unsigned long long w = warp0; w < done; w += nwarps) {
         const uint4 *s = reinterpret_cast<const uint4 *>(src_base + plan_src[w] * slab);
         uint4 *d = reinterpret_cast<uint4 *>(dst_base + plan_dst[w] * slab);
+        unsigned long long i = lane;
+        for (; i + 7 * 32 < nvec; i += 8 * 32) {
+            uint4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = s[i + u * 32];
+#pragma unroll
+            for (int u = 0; u < 8; u++) d[i + u * 32] = v[u];
+        }
+        for (; i < nvec; i += 32) d[i] = s[i];
+    }
+}
+
+// Do the DRAM slabs popped for this batch form one contiguous range?  (They
+// are distinct stack entries, so min/max decide it.)  meta[4] = 1 if so,
+// meta[5] = lowest slab of the range.
+__global__ void __launch_bounds__(1024)
+mig_run_check_kernel(const uint32_t *plan_dst, uint32_t *meta)
+{
+    __shared__ uint32_t smin[32], smax[32];
+    const uint32_t done = meta[0];
+    uint32_t mn = 0xFFFFFFFFu, mx = 0;
+    for (uint32_t o = threadIdx.x; o < done; o += blockDim.x) {
+        const uint32_t d = plan_dst[o];
+        mn = d < mn ? d : mn;
+        mx = d > mx ? d : mx;
+    }
+#pragma unroll
+    for (int k = 16; k > 0; k >>= 1) {
+        const uint32_t a = __shfl_xor_sync(0xFFFFFFFFu, mn, k);
+        const uint32_t b = __shfl_xor_sync(0xFFFFFFFFu, mx, k);
+        mn = a < mn ? a : mn;
+        mx = b > mx ? b : mx;
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    if (lane == 0) { smin[wid] = mn; smax[wid] = mx; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) {
+            mn = smin[w] < mn ? smin[w] : mn;
+            mx = smax[w] > mx ? smax[w] : mx;
+        }
+        const bool run = done > 0 && mx - mn + 1 == done;
+        meta[3] = mn;
+        meta[4] = run ? 1u : 0u;
+        meta[5] = run ? mn : 0u;
+    }
+}
+
+// Contiguous batch: hand the range out in ascending slab order (entry o gets
+// lo + o), so the victims packed in list order are byte-for-byte that range.
+__global__ void mig_fixup_kernel(PoolDev p, const uint32_t *meta, const uint32_t *plan_id,
+                                 uint32_t *plan_dst)
+{
+    if (meta[4] != 1u) return;
+    const uint32_t done = meta[0], lo = meta[5];
+    for (uint32_t o = blockIdx.x * blockDim.x + threadIdx.x; o < done; o += gridDim.x * blockDim.x) {
+        plan_dst[o] = lo + o;
+        p.loc[plan_id[o]] = make_loc(TIER_HOST_DRAM, lo + o);
+    }
+}
+
+// Pack list entries [pos0, pos0 + n) into the staging buffer, in list order.
+__global__ void __launch_bounds__(256)
+mig_pack_kernel(const char *src_base, char *staging, unsigned long long slab,
+                const uint32_t *plan_src, uint32_t pos0, uint32_t n)
+{
+    const unsigned lane = threadIdx.x & 31;
+    const unsigned long long nvec = slab >> 4;
+    const unsigned long long warp0 = ((unsigned long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const unsigned long long nwarps = ((unsigned long long)gridDim.x * blockDim.x) >> 5;
+    for (unsigned long long w = warp0; w < n; w += nwarps) {
+        const uint4 *s = reinterpret_cast<const uint4 *>(src_base + plan_src[pos0 + w] * slab);
+        uint4 *d = reinterpret_cast<uint4 *>(staging + w * slab);
         unsigned long long i = lane;
         for (; i + 7 * 32 < nvec; i += 8 * 32) {
             uint4 v[8];
@@ -661,7 +739,7 @@ unsigned copy_grid(uint32_t items, int per_cta)
 int launch_compat_op(const PoolDev &p, const ReqDev &r, int op, uint32_t l, uint32_t h,
                      uint32_t bi, uint32_t arg, CompatResult *res, cudaStream_t s)
 {
-    compat_op_kernel<<<1, 256, 0, s>>>(p, r, op, l, h, bi, arg, res);
+    compat_op_kernel<<<1, 256, 0, s>>>(p, r, op, l, h, bi, arg, res); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }
@@ -670,7 +748,7 @@ int launch_append_one(const PoolDev &p, const ReqDev &r, uint32_t l, const char 
                       const char *v, CompatResult *res, cudaStream_t s)
 {
     if (r.H > (uint32_t)kMaxHeads) return ORCHKV_ERR_INVALID;
-    append_one_kernel<<<1, 256, 0, s>>>(p, r, l, k, v, res);
+    append_one_kernel<<<1, 256, 0, s>>>(p, r, l, k, v, res); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }
@@ -680,9 +758,9 @@ int launch_prefill(const PoolDev &p, const ReqDev &r, uint32_t l, const char *k,
                    cudaStream_t s)
 {
     prefill_plan_kernel<<<1, 1, 0, s>>>(p, r, l, seq_len, k != nullptr, v != nullptr,
-                                        scratch, res);
+                                        scratch, res); note_launches(1);
     const uint32_t items = ((seq_len + p.tpb - 1) / p.tpb + 1) * r.H;
-    prefill_copy_kernel<<<copy_grid(items, 8), 256, 0, s>>>(p, r, l, k, v, seq_len, scratch);
+    prefill_copy_kernel<<<copy_grid(items, 8), 256, 0, s>>>(p, r, l, k, v, seq_len, scratch); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }
@@ -692,10 +770,61 @@ int launch_append_batch(const PoolDev &p, uint32_t *const *regions, uint32_t n, 
                         uint32_t *scratch, cudaStream_t s)
 {
     append_plan_kernel<<<1, 1024, 0, s>>>(p, regions, n, L, H, mbph, k != nullptr,
-                                          v != nullptr, scratch);
+                                          v != nullptr, scratch); note_launches(1);
     const unsigned long long warps = (unsigned long long)n * L * H;
     append_write_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(p, regions, n, L, H, mbph,
-                                                                     k, v, scratch);
+                                                                     k, v, scratch); note_launches(1);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+MigPlan launch_migrate_plan(const PoolDev &p, int dir, const uint32_t *ids,
+                            const uint32_t *count, uint32_t max_n, uint32_t *result,
+                            uint32_t *scratch, cudaStream_t s)
+{
+    MigPlan mp;
+    mp.tiles = (max_n + kTileN - 1) / kTileN;
+    mp.meta = scratch;                         // [16]
+    uint32_t *tile_cnt = scratch + 16;         // [tiles]
+    mp.plan_src = tile_cnt + mp.tiles;         // [max_n]
+    mp.plan_dst = mp.plan_src + max_n;         // [max_n]
+    mp.plan_id = mp.plan_dst + max_n;          // [max_n]
+    mp.max_n = max_n;
+    mp.rc = ORCHKV_OK;
+    if (max_n == 0) return mp;
+    mig_count_kernel<<<mp.tiles, 256, 0, s>>>(p, dir, ids, count, max_n, tile_cnt); note_launches(1);
+    mig_scan_kernel<<<1, 1024, 0, s>>>(p, dir, count, max_n, mp.tiles, tile_cnt, mp.meta, result); note_launches(1);
+    mig_plan_kernel<<<mp.tiles, 256, 0, s>>>(p, dir, ids, count, max_n, tile_cnt, mp.meta,
+                                             mp.plan_src, mp.plan_dst, mp.plan_id); note_launches(1);
+    if (cudaGetLastError() != cudaSuccess) mp.rc = ORCHKV_ERR_CUDA;
+    return mp;
+}
+
+int launch_migrate_zero_copy(const PoolDev &p, int dir, const MigPlan &mp, cudaStream_t s)
+{
+    if (mp.max_n == 0) return ORCHKV_OK;
+    const char *src_base = dir == 0 ? p.gpu_base : p.dram_base;
+    char *dst_base = dir == 0 ? p.dram_base : p.gpu_base;
+    mig_copy_kernel<<<copy_grid(mp.max_n, 8), 256, 0, s>>>(src_base, dst_base, p.slab,
+                                                           mp.plan_src, mp.plan_dst, mp.meta); note_launches(1);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_run_check(const PoolDev &p, const MigPlan &mp, cudaStream_t s)
+{
+    mig_run_check_kernel<<<1, 1024, 0, s>>>(mp.plan_dst, mp.meta); note_launches(1);
+    mig_fixup_kernel<<<copy_grid(mp.max_n, 256), 256, 0, s>>>(p, mp.meta, mp.plan_id, mp.plan_dst); note_launches(1);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_pack(const PoolDev &p, const MigPlan &mp, char *staging, uint32_t pos0, uint32_t n,
+                cudaStream_t s)
+{
+    if (n == 0) return ORCHKV_OK;
+    mig_pack_kernel<<<copy_grid(n, 8), 256, 0, s>>>(p.gpu_base, staging, p.slab, mp.plan_src,
+                                                     pos0, n); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }
@@ -704,22 +833,9 @@ int launch_migrate_batch(const PoolDev &p, int dir, const uint32_t *ids,
                          const uint32_t *count, uint32_t max_n, uint32_t *result,
                          uint32_t *scratch, cudaStream_t s)
 {
-    if (max_n == 0) return ORCHKV_OK;
-    const uint32_t tiles = (max_n + kTileN - 1) / kTileN;
-    uint32_t *meta = scratch;                  // [16]
-    uint32_t *tile_cnt = scratch + 16;         // [tiles]
-    uint32_t *plan_src = tile_cnt + tiles;     // [max_n]
-    uint32_t *plan_dst = plan_src + max_n;     // [max_n]
-    mig_count_kernel<<<tiles, 256, 0, s>>>(p, dir, ids, count, max_n, tile_cnt);
-    mig_scan_kernel<<<1, 1024, 0, s>>>(p, dir, count, max_n, tiles, tile_cnt, meta, result);
-    mig_plan_kernel<<<tiles, 256, 0, s>>>(p, dir, ids, count, max_n, tile_cnt, meta, plan_src,
-                                          plan_dst);
-    const char *src_base = dir == 0 ? p.gpu_base : p.dram_base;
-    char *dst_base = dir == 0 ? p.dram_base : p.gpu_base;
-    mig_copy_kernel<<<copy_grid(max_n, 8), 256, 0, s>>>(src_base, dst_base, p.slab, plan_src,
-                                                        plan_dst, meta);
-    OKV_CUDA_TRY(cudaGetLastError());
-    return ORCHKV_OK;
+    MigPlan mp = launch_migrate_plan(p, dir, ids, count, max_n, result, scratch, s);
+    if (mp.rc) return mp.rc;
+    return launch_migrate_zero_copy(p, dir, mp, s);
 }
 
 int launch_id_table(const PoolDev &p, uint32_t *const *regions, uint32_t n, uint32_t L,
@@ -731,14 +847,14 @@ int launch_id_table(const PoolDev &p, uint32_t *const *regions, uint32_t n, uint
     unsigned g = (unsigned)((total + 255) / 256);
     if (g > 148 * 16) g = 148 * 16;
     if (g == 0) g = 1;
-    id_table_kernel<<<g, 256, 0, s>>>(p, regions, n, L, H, mbph, nb, out);
+    id_table_kernel<<<g, 256, 0, s>>>(p, regions, n, L, H, mbph, nb, out); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }
 
 int launch_request_free(const PoolDev &p, const ReqDev &r, cudaStream_t s)
 {
-    request_free_kernel<<<1, 1024, 0, s>>>(p, r);
+    request_free_kernel<<<1, 1024, 0, s>>>(p, r); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }

@@ -12,9 +12,15 @@
 // __fdiv_rn so no FMA is formed and each operation rounds exactly as the
 // reference's single-precision host code; the recency table is built on the
 // host with libm expf (as the reference does) and only read here.
+#include <atomic>
+
 #include "kernels.h"
 
 namespace okv {
+
+static std::atomic<unsigned long long> g_launches{0};
+void note_launches(unsigned n) { g_launches += n; }
+unsigned long long launch_count() { return g_launches.load(); }
 
 // ---------------------------------------------------------------------------
 // K1: per-block attention mass
@@ -162,7 +168,7 @@ int launch_score(const float *probs, uint32_t R, uint32_t Hq, uint32_t Hkv,
 #define OKV_SCORE_CASE(L)                                                              \
     case L:                                                                            \
         score_vec_kernel<L><<<(unsigned)grid, kScoreWarps * 32, 0, s>>>(               \
-            probs, Hq, Hkv, T, tpb, lens, ids, nb, n_chunks, n_tiles, d, step);        \
+            probs, Hq, Hkv, T, tpb, lens, ids, nb, n_chunks, n_tiles, d, step); note_launches(1);        \
         break;
         switch (log_lpb) {
             OKV_SCORE_CASE(0) OKV_SCORE_CASE(1) OKV_SCORE_CASE(2)
@@ -174,7 +180,7 @@ int launch_score(const float *probs, uint32_t R, uint32_t Hq, uint32_t Hkv,
         const unsigned long long n_items = (unsigned long long)R * Hkv * nb;
         const unsigned grid = (unsigned)((n_items + 255) / 256);
         score_scalar_kernel<<<grid, 256, 0, s>>>(probs, Hq, Hkv, T, tpb, lens, ids, nb,
-                                                 n_items, d, step);
+                                                 n_items, d, step); note_launches(1);
     }
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
@@ -203,7 +209,7 @@ int launch_report_apply(const uint32_t *slots, const float *psum, const float *p
                         cudaStream_t s)
 {
     if (n == 0) return ORCHKV_OK;
-    report_apply_kernel<<<(n + 255) / 256, 256, 0, s>>>(slots, psum, pmax, n, d, step);
+    report_apply_kernel<<<(n + 255) / 256, 256, 0, s>>>(slots, psum, pmax, n, d, step); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }
@@ -221,7 +227,7 @@ int launch_report_batch(const uint32_t *ids, const float *w, uint32_t n,
                         const SchedDev &d, unsigned long long step, cudaStream_t s)
 {
     if (n == 0) return ORCHKV_OK;
-    report_batch_kernel<<<(n + 255) / 256, 256, 0, s>>>(ids, w, n, d, step);
+    report_batch_kernel<<<(n + 255) / 256, 256, 0, s>>>(ids, w, n, d, step); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }
@@ -331,6 +337,7 @@ int launch_sweep(const SchedDev &d, const SchedParams &p, bool step_done, bool c
     else if (step_done) sweep_kernel<true, false><<<g, 256, 0, s>>>(d, p, counts);
     else if (classify) sweep_kernel<false, true><<<g, 256, 0, s>>>(d, p, counts);
     else return ORCHKV_OK;
+    note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }
@@ -368,7 +375,7 @@ int launch_registry_count(const uint32_t *reg_slot, const uint8_t *reg_tier, uin
     if (n == 0) return ORCHKV_OK;
     unsigned g = (n + 255) / 256;
     if (g > 1184) g = 1184;
-    registry_count_kernel<<<g, 256, 0, s>>>(reg_slot, reg_tier, n, d, th_gpu, th_dram, count);
+    registry_count_kernel<<<g, 256, 0, s>>>(reg_slot, reg_tier, n, d, th_gpu, th_dram, count); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }
@@ -414,7 +421,7 @@ int launch_slot_ops(const uint32_t *slots, const uint8_t *b, uint32_t n,
                     const SchedDev &d, cudaStream_t s)
 {
     if (n == 0) return ORCHKV_OK;
-    slot_ops_kernel<<<1, 32, 0, s>>>(slots, b, n, d);
+    slot_ops_kernel<<<1, 32, 0, s>>>(slots, b, n, d); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }

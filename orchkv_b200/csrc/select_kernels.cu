@@ -136,6 +136,7 @@ sel_scan_kernel(const uint32_t *hist, uint32_t *state, int pass, uint32_t k_req,
         state[S_TAKE] = 0;
         state[S_KTH] = 0;
     }
+    if (threadIdx.x == 0) { found_b = 0; found_before = 0; }
     __syncthreads();
     if (state[S_DONE]) return;
     const uint32_t k_rem = state[S_KREM];
@@ -323,43 +324,44 @@ int launch_select(const SchedDev &d, const SelectScratch &sc, const SelectArgs &
         sel_pass0_kernel<kSelectColdest><<<g, kHistThreads, 0, s>>>(d, a.th_gpu, a.th_dram, sc.hist_local);
     else
         sel_pass0_kernel<kSelectPrefetch><<<g, kHistThreads, 0, s>>>(d, a.th_gpu, a.th_dram, sc.hist_local);
+    note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     if (multi && a.reduce(sc.hist_local, hg, kBins + 1, s, a.comm_ctx) != ORCHKV_OK)
         return ORCHKV_ERR_CUDA;
-    sel_scan_kernel<<<1, 1024, 0, s>>>(hg, sc.state, 0, a.k, a.frac, !multi);
+    sel_scan_kernel<<<1, 1024, 0, s>>>(hg, sc.state, 0, a.k, a.frac, !multi); note_launches(1);
 
     // pass 1
     OKV_CUDA_TRY(cudaMemsetAsync(sc.hist_local, 0, kBins * 4, s));
-    sel_pass_kernel<1><<<g, kHistThreads, 0, s>>>(d.key, n, sc.state, sc.hist_local);
+    sel_pass_kernel<1><<<g, kHistThreads, 0, s>>>(d.key, n, sc.state, sc.hist_local); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     if (multi && a.reduce(sc.hist_local, hg, kBins, s, a.comm_ctx) != ORCHKV_OK)
         return ORCHKV_ERR_CUDA;
-    sel_scan_kernel<<<1, 1024, 0, s>>>(hg, sc.state, 1, a.k, a.frac, !multi);
+    sel_scan_kernel<<<1, 1024, 0, s>>>(hg, sc.state, 1, a.k, a.frac, !multi); note_launches(1);
 
     // pass 2
     OKV_CUDA_TRY(cudaMemsetAsync(sc.hist_local, 0, 256 * 4, s));
-    sel_pass_kernel<2><<<g, kHistThreads, 0, s>>>(d.key, n, sc.state, sc.hist_local);
+    sel_pass_kernel<2><<<g, kHistThreads, 0, s>>>(d.key, n, sc.state, sc.hist_local); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     if (multi && a.reduce(sc.hist_local, hg, 256, s, a.comm_ctx) != ORCHKV_OK)
         return ORCHKV_ERR_CUDA;
-    sel_scan_kernel<<<1, 1024, 0, s>>>(hg, sc.state, 2, a.k, a.frac, !multi);
+    sel_scan_kernel<<<1, 1024, 0, s>>>(hg, sc.state, 2, a.k, a.frac, !multi); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
 
     if (multi) {
-        sel_tie_local_kernel<<<1, 1, 0, s>>>(sc.hist_local, sc.state, sc.state + 8);
+        sel_tie_local_kernel<<<1, 1, 0, s>>>(sc.hist_local, sc.state, sc.state + 8); note_launches(1);
         if (a.gather(sc.state + 8, a.gather_buf, s, a.comm_ctx) != ORCHKV_OK)
             return ORCHKV_ERR_CUDA;
-        sel_tie_split_kernel<<<1, 1, 0, s>>>(a.gather_buf, a.rank, sc.state);
+        sel_tie_split_kernel<<<1, 1, 0, s>>>(a.gather_buf, a.rank, sc.state); note_launches(1);
         OKV_CUDA_TRY(cudaGetLastError());
     }
 
     // ordered compaction
     const uint32_t tiles = (n + kTile - 1) / kTile;
-    sel_count_kernel<<<tiles, kTileThreads, 0, s>>>(d.key, n, sc.state, sc.tile_counts);
+    sel_count_kernel<<<tiles, kTileThreads, 0, s>>>(d.key, n, sc.state, sc.tile_counts); note_launches(1);
     sel_offsets_kernel<<<1, 1024, 0, s>>>(sc.tile_counts, tiles, sc.tile_offsets, sc.state,
-                                          a.out_count);
+                                          a.out_count); note_launches(1);
     sel_write_kernel<<<tiles, kTileThreads, 0, s>>>(d.key, n, sc.state, sc.tile_offsets,
-                                                    a.out_ids, a.max_out);
+                                                    a.out_ids, a.max_out); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }

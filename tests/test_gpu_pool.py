@@ -15,11 +15,14 @@ SLAB = TPB * ROW * 2
 HALF = SLAB // 2
 
 
+GPU_SLABS, DRAM_SLABS = 160, 64
+
+
 @pytest.fixture
 def dp(cuda):
     import orchkv_b200 as o
     L = o.lib()
-    cfg = o.make_config(gpu_pool_bytes=96 * SLAB, dram_pool_bytes=64 * SLAB,
+    cfg = o.make_config(gpu_pool_bytes=GPU_SLABS * SLAB, dram_pool_bytes=DRAM_SLABS * SLAB,
                         tokens_per_block=TPB, d_head=D, dtype=1, max_blocks_per_head=32)
     ext = o.OrchkvConfigExt()
     ext.max_blocks = 512
@@ -160,7 +163,7 @@ def test_per_block_evict_promote_vs_oracle(dp, cuda):
     k, v = kv_data(rng, H, n)
     ctx = L.orchkv_request_create(1, 1, H)
     assert L.orchkv_prefill(ctx, 0, k.ctypes.data, v.ctypes.data, n) == 0
-    gtot, dtot = 96, 64
+    gtot, dtot = GPU_SLABS, DRAM_SLABS
     gpool, dpool, loc, state = _model_from_device(L, gtot, dtot, 512)
     gbytes = read_dev(L.orchkv_gpu_pool_base(), gtot * SLAB)
     dbytes = np.zeros(dtot * SLAB, np.uint8)
@@ -212,7 +215,7 @@ def test_batched_migration_equals_sequential(dp, cuda, seed):
     ctxs = [L.orchkv_request_create(i, 1, H) for i in range(2)]
     for c in ctxs:
         assert L.orchkv_prefill(c, 0, k.ctypes.data, v.ctypes.data, n) == 0
-    gtot, dtot = 96, 64
+    gtot, dtot = GPU_SLABS, DRAM_SLABS
     # a few single evictions first so the DRAM free stack is not in order
     for h, b in [(0, 1), (2, 5), (1, 7)]:
         assert L.orchkv_evict_to_dram(ctxs[0], 0, h, b) == 0
@@ -257,18 +260,18 @@ def test_batch_pool_exhaustion(dp, cuda):
     k, v = kv_data(rng, H, n)
     ctx = L.orchkv_request_create(3, 1, H)
     assert L.orchkv_prefill(ctx, 0, k.ctypes.data, v.ctypes.data, n) == 0
-    gpool, dpool, loc, state = _model_from_device(L, 96, 64, 512)
+    gpool, dpool, loc, state = _model_from_device(L, GPU_SLABS, DRAM_SLABS, 512)
     ids = np.arange(80, dtype=np.uint32)[::-1].copy()
     dev_ids = cuda.from_numpy(ids.view(np.int32)).cuda()
     cnt = cuda.tensor([75], dtype=cuda.int32, device="cuda")
     res = cuda.zeros(2, dtype=cuda.int32, device="cuda")
     assert L.orchkv_evict_batch_to_dram(dev_ids.data_ptr(), cnt.data_ptr(), 80, res.data_ptr()) == 0
-    gb = read_dev(L.orchkv_gpu_pool_base(), 96 * SLAB)
-    db = np.zeros(64 * SLAB, np.uint8)
+    gb = read_dev(L.orchkv_gpu_pool_base(), GPU_SLABS * SLAB)
+    db = np.zeros(DRAM_SLABS * SLAB, np.uint8)
     done, skipped = O.evict_batch(gpool, dpool, loc, state, None, ids[:75].tolist(), gb, db, SLAB)
     assert (done, skipped) == (64, 11)
     assert res.cpu().tolist() == [64, 11]
-    g2, d2, loc2, _ = _model_from_device(L, 96, 64, 512)
+    g2, d2, loc2, _ = _model_from_device(L, GPU_SLABS, DRAM_SLABS, 512)
     assert g2.stack == gpool.stack and d2.stack == dpool.stack and loc2 == loc
     assert L.orchkv_request_destroy(ctx) == 0
 
