@@ -255,6 +255,23 @@ int tm_select_victims_frac(tiered_manager_t *m, float frac, uint32_t *out_ids,
 int tm_select_prefetch(tiered_manager_t *m, uint32_t k, float th_gpu,
                        float th_dram, uint32_t *out_ids, uint32_t *out_count);
 
+/* Coldest-k selection that allocates no memory.  No counterpart in the
+ * reference: it is for callers that cannot call cudaMalloc while they run
+ * (engines that reserve device memory for their own allocator up front,
+ * paths that must not take the CUDA allocator's locks).  Same ordering and
+ * output as tm_select_victims, over a caller's arrays: values[i] (device f32)
+ * is eligible where eligible[i] (device u8) is non-zero; the min(k, #eligible)
+ * winners go to out_ids in ascending index order, their number to *out_count
+ * (device u32).  n is at most 1,048,576 (ORCHKV_ERR_INVALID beyond, with a
+ * message).  Scratch is one static device array of ~4.1 MB in each GPU that
+ * loads the library, kept until exit: the first call on a device looks its
+ * address up (make that first call before any stream capture), every call
+ * reuses it, so calls that overlap on the GPU race.  Asynchronous on
+ * `stream` (a cudaStream_t, NULL = default stream). */
+int orchkv_select_coldest_noalloc(const float *values, const uint8_t *eligible,
+                                  uint32_t n, uint32_t k, uint32_t *out_ids,
+                                  uint32_t *out_count, void *stream);
+
 /* Threshold controller state (the fields the reference binding reads from
  * m->threshold, bindings/orchkv_pybind.cpp:408-411). */
 int tm_get_threshold_state(const tiered_manager_t *m, float *threshold_hot,

@@ -173,6 +173,7 @@ _SIGS = {
     "tm_select_victims_frac": (i32, [P(TieredManager), f32, vp, vp, u32]),
     "tm_select_prefetch": (i32, [P(TieredManager), u32, f32, f32, vp, vp]),
     "tm_get_threshold_state": (i32, [P(TieredManager), P(f32), P(f32), P(u64), P(u64)]),
+    "orchkv_select_coldest_noalloc": (i32, [vp, vp, u32, u32, vp, vp, vp]),
     # multi-GPU
     "orchkv_comm_unique_id": (i32, [vp]),
     "orchkv_comm_create": (vp, [i32, i32, vp, f64]),

@@ -30,7 +30,9 @@ int launch_slot_ops(const uint32_t *slots, const uint8_t *b, uint32_t n,
                     const SchedDev &d, cudaStream_t s);
 
 // ---- selection (select_kernels.cu) -------------------------------------------
-enum SelectMode { kSelectColdest = 0, kSelectPrefetch = 1 };
+// kSelectExternal: keys from a caller's value array (SchedDev.hot) where the
+// caller's byte array (SchedDev.tact) is non-zero; ascending value order.
+enum SelectMode { kSelectColdest = 0, kSelectPrefetch = 1, kSelectExternal = 2 };
 
 struct SelectScratch {
     uint32_t *hist_local;    // [4096 + 16]
