@@ -501,6 +501,10 @@ def ref():
         L.ref_api_get.restype = C.c_int
         L.ref_api_migrate_list.argtypes = [vp, _u32p, C.c_uint32, C.c_uint32, _f64p]
         L.ref_api_migrate_list.restype = C.c_int
+        L.ref_storage_read.argtypes = [C.c_char_p, C.c_uint64, C.c_uint32, C.c_uint32,
+                                       C.c_uint32, C.c_size_t, C.c_uint32, C.c_uint32,
+                                       C.c_uint32, vp]
+        L.ref_storage_read.restype = C.c_int
         _REF = L
     return _REF
 

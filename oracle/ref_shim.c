@@ -14,6 +14,7 @@
 #include <stdlib.h>
 #include <string.h>
 #include <time.h>
+#include <unistd.h>
 
 #include "scheduler/tiered_manager.h"
 #include "api/orchkv_api.h"
@@ -205,6 +206,25 @@ int ref_dram_pool_free(void *h, uint32_t idx)
     return dram_tier_free(t, (char *)t->pool_base + (size_t)idx * t->slab_size);
 }
 void ref_dram_pool_destroy(void *h) { dram_tier_destroy(h); free(h); }
+
+/* Read one slab of a request's storage file with the reference's own
+ * orchfs_tier_read (POSIX path, src/tiered_store/orchfs_tier.c:246-317), to
+ * check that files written by another implementation use its layout.  The
+ * file is opened, not removed. */
+int ref_storage_read(const char *base_dir, uint64_t request_id, uint32_t L, uint32_t H,
+                     uint32_t mbph, size_t slab, uint32_t l, uint32_t h, uint32_t bi,
+                     void *buf)
+{
+    orchfs_tier_t t;
+    if (orchfs_tier_init(&t, base_dir, slab) != ORCHKV_OK) return ORCHKV_ERR_INIT;
+    orchfs_file_ctx_t *f = orchfs_file_open(&t, request_id, L, H, mbph);
+    if (!f) { orchfs_tier_destroy(&t); return ORCHKV_ERR_IO; }
+    int rc = orchfs_tier_read(f, l, h, bi, buf, slab);
+    close(f->fd);
+    free(f);
+    orchfs_tier_destroy(&t);
+    return rc;
+}
 
 static double now_s(void)
 {

@@ -13,6 +13,7 @@
 #include <fcntl.h>
 #include <stdlib.h>
 #include <string.h>
+#include <sys/stat.h>
 #include <unistd.h>
 
 #include <map>
@@ -31,6 +32,8 @@ struct kv_request_ctx {
     uint32_t L, H, mbph;
     size_t region_off;     // words into the block-table array
     size_t region_words;
+    int fd = -1;           // storage-tier file (src/tiered_store/orchfs_tier.c:201-244)
+    char path[256] = {0};
 };
 
 namespace {
@@ -78,7 +81,26 @@ struct Sys {
     gpu_tier_t gsnap;
     dram_tier_t dsnap;
     std::vector<uint32_t> gsnap_stack, dsnap_stack;
+    // storage tier
+    char base_dir[256] = {0};
+    uint64_t storage_writes = 0, storage_reads = 0;
+    uint64_t storage_bytes_written = 0, storage_bytes_read = 0;
 };
+
+// mkdir -p (src/tiered_store/orchfs_tier.c:152-165)
+void mkdir_p(const char *path)
+{
+    char tmp[256];
+    snprintf(tmp, sizeof(tmp), "%s", path);
+    for (char *q = tmp + 1; *q; q++) {
+        if (*q == '/') {
+            *q = '\0';
+            mkdir(tmp, 0755);
+            *q = '/';
+        }
+    }
+    mkdir(tmp, 0755);
+}
 
 Sys g;
 
@@ -242,11 +264,12 @@ void release_all()
     g.active_requests = 0;
 }
 
-int compat(kv_request_ctx_t *ctx, int op, uint32_t l, uint32_t h, uint32_t bi, uint32_t arg)
+int compat(kv_request_ctx_t *ctx, int op, uint32_t l, uint32_t h, uint32_t bi, uint32_t arg,
+           uint32_t arg2 = 0)
 {
     if (!g.inited) return ORCHKV_ERR_INIT;
     if (!ctx) return ORCHKV_ERR_NOT_FOUND;
-    int rc = launch_compat_op(g.p, req_dev(ctx), op, l, h, bi, arg, g.res, g.stream);
+    int rc = launch_compat_op(g.p, req_dev(ctx), op, l, h, bi, arg, arg2, g.res, g.stream);
     if (rc) return rc;
     int krc = 0;
     rc = sync_result(&krc);
@@ -272,6 +295,12 @@ int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
         return ORCHKV_ERR_INVALID;
     g.cfg = *cfg;
     g.device = cfg->gpu_device_id;
+    snprintf(g.base_dir, sizeof(g.base_dir), "%s",
+             cfg->orchfs_base_dir && cfg->orchfs_base_dir[0] ? cfg->orchfs_base_dir : "/dev/shm/orchkv");
+    g.cfg.orchfs_base_dir = g.base_dir;
+    mkdir_p(g.base_dir);
+    g.storage_writes = g.storage_reads = 0;
+    g.storage_bytes_written = g.storage_bytes_read = 0;
     OKV_CUDA_TRY(cudaSetDevice(g.device));
     OKV_CUDA_TRY(cudaStreamCreateWithFlags(&g.own, cudaStreamNonBlocking));
     g.stream = g.own;
@@ -415,6 +444,11 @@ kv_request_ctx_t *orchkv_request_create(uint64_t request_id, uint32_t n_layers,
         delete c;
         return nullptr;
     }
+    // one storage file per request, as orchfs_file_open does
+    // (src/tiered_store/orchfs_tier.c:201-230); a request without one still
+    // works, its storage calls return ORCHKV_ERR_INIT
+    snprintf(c->path, sizeof(c->path), "%s/req_%lu", g.base_dir, (unsigned long)request_id);
+    c->fd = open(c->path, O_CREAT | O_RDWR, 0644);
     g.active_requests++;
     return c;
 }
@@ -427,6 +461,10 @@ int orchkv_request_destroy(kv_request_ctx_t *ctx)
     int rc = launch_request_free(g.p, req_dev(ctx), g.stream);
     if (rc) return rc;
     OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    if (ctx->fd >= 0) {                   // orchfs_file_close: close + unlink
+        close(ctx->fd);
+        unlink(ctx->path);
+    }
     region_free(ctx->region_off, ctx->region_words);
     g.regions_last.clear();
     if (g.active_requests) g.active_requests--;
@@ -473,7 +511,15 @@ int orchkv_get_kv_block(kv_request_ctx_t *ctx, uint32_t l, uint32_t h, uint32_t 
                         void **k_out, void **v_out)
 {
     std::lock_guard<std::recursive_mutex> lk(g.mu);
-    const int rc = compat(ctx, OP_GET, l, h, bi, 0);
+    // storage -> DRAM first, then DRAM -> GPU (src/api/orchkv_api.cu:321-349)
+    int rc = compat(ctx, OP_INFO, l, h, bi, 0);
+    if (rc) return rc;
+    const uint32_t tier = loc_tier(g.res->loc);
+    if (tier == TIER_NVM || tier == TIER_SSD) {
+        rc = orchkv_promote_from_storage(ctx, l, h, bi);
+        if (rc) return rc;
+    }
+    rc = compat(ctx, OP_GET, l, h, bi, 0);
     if (rc) return rc;
     if (k_out) *k_out = (void *)g.res->k_ptr;
     if (v_out) *v_out = (void *)g.res->v_ptr;
@@ -492,15 +538,76 @@ int orchkv_promote_to_gpu(kv_request_ctx_t *ctx, uint32_t l, uint32_t h, uint32_
     return compat(ctx, OP_PROMOTE, l, h, bi, 0);
 }
 
-// The file tier (src/tiered_store/orchfs_tier.c) is not part of this build yet.
-int orchkv_evict_to_storage(kv_request_ctx_t *, uint32_t, uint32_t, uint32_t)
+// ---- storage tier: one file per request, POSIX pwrite/pread at the
+// reference's offsets (src/tiered_store/orchfs_tier.h:89-97,
+// orchfs_tier.c:246-317).  The DRAM slab is pinned host memory, so the file
+// IO reads and writes it directly.
+
+static off_t storage_offset(const kv_request_ctx_t *c, uint32_t l, uint32_t h, uint32_t bi)
 {
-    return g.inited ? ORCHKV_ERR_INIT : ORCHKV_ERR_INIT;
+    const uint64_t head_linear = (uint64_t)l * c->H + h;
+    return (off_t)((head_linear * c->mbph + bi) * g.p.slab);
 }
 
-int orchkv_promote_from_storage(kv_request_ctx_t *, uint32_t, uint32_t, uint32_t)
+static bool full_io(bool write, int fd, char *buf, size_t n, off_t off)
 {
-    return ORCHKV_ERR_INIT;
+    while (n > 0) {
+        const ssize_t r = write ? pwrite(fd, buf, n, off) : pread(fd, buf, n, off);
+        if (r < 0) {
+            if (errno == EINTR) continue;
+            return false;
+        }
+        if (r == 0) return false;          // short read: the slab was never written
+        buf += r;
+        off += r;
+        n -= (size_t)r;
+    }
+    return true;
+}
+
+int orchkv_evict_to_storage(kv_request_ctx_t *ctx, uint32_t l, uint32_t h, uint32_t bi)
+{
+    // src/api/orchkv_api.cu:432-466
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    int rc = compat(ctx, OP_INFO, l, h, bi, 0);
+    if (rc) return rc;
+    const uint32_t w = g.res->loc;
+    if (loc_tier(w) != TIER_HOST_DRAM) return ORCHKV_ERR_STATE;
+    if (g.res->flags & KV_FLAG_PIN) return ORCHKV_ERR_LOCKED;
+    if (ctx->fd < 0) return ORCHKV_ERR_INIT;
+    const uint32_t d = loc_slab(w);
+    if (!full_io(true, ctx->fd, g.p.dram_base + (size_t)d * g.p.slab, g.p.slab,
+                 storage_offset(ctx, l, h, bi)))
+        return ORCHKV_ERR_IO;
+    g.storage_writes++;
+    g.storage_bytes_written += g.p.slab;
+    // tier := NVM (the reference records file blocks as TIER_NVM), state COLD,
+    // DRAM slab back to its pool
+    return compat(ctx, OP_SET_LOC, l, h, bi, make_loc(TIER_NVM, 0),
+                  (uint32_t)KV_STATE_COLD | ((d + 1) << 8));
+}
+
+int orchkv_promote_from_storage(kv_request_ctx_t *ctx, uint32_t l, uint32_t h, uint32_t bi)
+{
+    // src/api/orchkv_api.cu:470-504
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    int rc = compat(ctx, OP_INFO, l, h, bi, 0);
+    if (rc) return rc;
+    const uint32_t w = g.res->loc;
+    if (loc_tier(w) != TIER_NVM && loc_tier(w) != TIER_SSD) return ORCHKV_ERR_STATE;
+    if (ctx->fd < 0) return ORCHKV_ERR_INIT;
+    rc = compat(ctx, OP_DRAM_POP, l, h, bi, 0);
+    if (rc) return rc;
+    const uint32_t d = g.res->aux;
+    if (!full_io(false, ctx->fd, g.p.dram_base + (size_t)d * g.p.slab, g.p.slab,
+                 storage_offset(ctx, l, h, bi))) {
+        compat(ctx, OP_SET_LOC, l, h, bi, w, (uint32_t)KV_STATE_COLD | ((d + 1) << 8));
+        return ORCHKV_ERR_IO;
+    }
+    g.storage_reads++;
+    g.storage_bytes_read += g.p.slab;
+    return compat(ctx, OP_SET_LOC, l, h, bi, make_loc(TIER_HOST_DRAM, d),
+                  (uint32_t)KV_STATE_WARM);
 }
 
 int orchkv_evict_cold(kv_request_ctx_t *ctx, uint32_t l, uint32_t h, uint32_t bi)

@@ -50,7 +50,8 @@ struct CompatResult {
     int rc;
     uint32_t id;
     unsigned long long k_ptr, v_ptr;
-    uint32_t loc, state, tok, pad;
+    uint32_t loc, state, tok, flags;
+    uint32_t aux, pad;
 };
 
 enum CompatOp : int {
@@ -59,11 +60,14 @@ enum CompatOp : int {
     OP_GET = 2,          // promote if on DRAM, return pointers
     OP_INFO = 3,
     OP_SET_FLAGS = 4,
+    OP_DRAM_POP = 5,     // pop a DRAM slab into res->aux (storage promotion)
+    OP_SET_LOC = 6,      // loc := arg; state := arg2 & 0xFF; arg2 >> 8 = DRAM slab + 1 to push
 };
 
 // ---- launchers (pool_kernels.cu) -------------------------------------------
 int launch_compat_op(const PoolDev &p, const ReqDev &r, int op, uint32_t l, uint32_t h,
-                     uint32_t bi, uint32_t arg, CompatResult *res, cudaStream_t s);
+                     uint32_t bi, uint32_t arg, uint32_t arg2, CompatResult *res,
+                     cudaStream_t s);
 int launch_append_one(const PoolDev &p, const ReqDev &r, uint32_t l, const char *k,
                       const char *v, CompatResult *res, cudaStream_t s);
 int launch_prefill(const PoolDev &p, const ReqDev &r, uint32_t l, const char *k,

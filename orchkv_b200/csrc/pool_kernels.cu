@@ -84,7 +84,7 @@ __device__ __forceinline__ void coop_copy(char *dst, const char *src, unsigned l
 
 __global__ void __launch_bounds__(256)
 compat_op_kernel(PoolDev p, ReqDev r, int op, uint32_t l, uint32_t h, uint32_t bi,
-                 uint32_t arg, CompatResult *res)
+                 uint32_t arg, uint32_t arg2, CompatResult *res)
 {
     __shared__ int rc, dir;
     __shared__ uint32_t id, src, dst;
@@ -120,6 +120,16 @@ compat_op_kernel(PoolDev p, ReqDev r, int op, uint32_t l, uint32_t h, uint32_t b
             } else if (op == OP_SET_FLAGS) {
                 p.flags[id] = (uint8_t)arg;
                 if (p.attached) p.sd.bflags[id & p.sd.mask] = (uint8_t)arg;
+            } else if (op == OP_DRAM_POP) {
+                if (c->d_top == 0) rc = ORCHKV_ERR_TIER_FULL;
+                else res->aux = p.d_stack[--c->d_top];
+            } else if (op == OP_SET_LOC) {
+                const uint8_t st = (uint8_t)(arg2 & 0xFF);
+                const uint32_t push = arg2 >> 8;
+                p.loc[id] = arg;
+                p.state[id] = st;
+                if (push) p.d_stack[c->d_top++] = push - 1;
+                sched_move(p, id, (uint8_t)loc_tier(arg), st);
             }
         }
     }
@@ -152,6 +162,7 @@ compat_op_kernel(PoolDev p, ReqDev r, int op, uint32_t l, uint32_t h, uint32_t b
             const uint32_t w = p.loc[id];
             res->loc = w;
             res->state = p.state[id];
+            res->flags = p.flags[id];
             if (loc_tier(w) == TIER_GPU_HBM) {
                 res->k_ptr = (unsigned long long)(p.gpu_base + (unsigned long long)loc_slab(w) * p.slab);
                 res->v_ptr = res->k_ptr + p.half;
@@ -737,9 +748,10 @@ unsigned copy_grid(uint32_t items, int per_cta)
 }  // namespace
 
 int launch_compat_op(const PoolDev &p, const ReqDev &r, int op, uint32_t l, uint32_t h,
-                     uint32_t bi, uint32_t arg, CompatResult *res, cudaStream_t s)
+                     uint32_t bi, uint32_t arg, uint32_t arg2, CompatResult *res,
+                     cudaStream_t s)
 {
-    compat_op_kernel<<<1, 256, 0, s>>>(p, r, op, l, h, bi, arg, res); note_launches(1);
+    compat_op_kernel<<<1, 256, 0, s>>>(p, r, op, l, h, bi, arg, arg2, res); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }

@@ -81,18 +81,40 @@ score_vec_kernel(const float *__restrict__ probs, uint32_t Hq, uint32_t Hkv,
     for (int u = 0; u < kScoreU; u++) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
 
     const uint32_t col0 = c * (32 * kScoreU) + lane;
-    for (uint32_t g = 0; g < G; g++) {
-        const float4 *row = base + (unsigned long long)g * T4;
-        float4 v[kScoreU];
+    // two query-head rows per iteration: 8 x 16 B loads in flight per lane
+    // before any accumulation (rows are still added in order g, g+1, ...)
+    uint32_t g = 0;
+    for (; g + 1 < G; g += 2) {
+        const float4 *r0 = base + (unsigned long long)g * T4;
+        const float4 *r1 = r0 + T4;
+        float4 a[kScoreU], b[kScoreU];
 #pragma unroll
         for (int u = 0; u < kScoreU; u++) {
             const uint32_t col = col0 + u * 32;
-            v[u] = col < T4 ? ld_stream(row + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const bool in = col < T4;
+            a[u] = in ? ld_stream(r0 + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+            b[u] = in ? ld_stream(r1 + col) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int u = 0; u < kScoreU; u++) {
-            acc[u].x += v[u].x; acc[u].y += v[u].y;
-            acc[u].z += v[u].z; acc[u].w += v[u].w;
+            acc[u].x += a[u].x; acc[u].y += a[u].y;
+            acc[u].z += a[u].z; acc[u].w += a[u].w;
+            acc[u].x += b[u].x; acc[u].y += b[u].y;
+            acc[u].z += b[u].z; acc[u].w += b[u].w;
+        }
+    }
+    if (g < G) {
+        const float4 *r0 = base + (unsigned long long)g * T4;
+        float4 a[kScoreU];
+#pragma unroll
+        for (int u = 0; u < kScoreU; u++) {
+            const uint32_t col = col0 + u * 32;
+            a[u] = col < T4 ? ld_stream(r0 + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kScoreU; u++) {
+            acc[u].x += a[u].x; acc[u].y += a[u].y;
+            acc[u].z += a[u].z; acc[u].w += a[u].w;
         }
     }
 
