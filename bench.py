@@ -326,6 +326,8 @@ def run_ours(args, rank, world, local_rank):
     pk_ms, pk_bytes, pk_chunks, pr_ms = C.c_float(), C.c_ulonglong(), C.c_uint32(), C.c_float()
     wl.L.orchkv_last_migration_profile(C.byref(pk_ms), C.byref(pk_bytes), C.byref(pk_chunks),
                                        C.byref(pr_ms))
+    lay = [C.c_uint32() for _ in range(3)]
+    wl.L.orchkv_last_evict_layout(*[C.byref(x) for x in lay])
     c_last = wl.h_counts.tolist()
     wl.restore()
 
@@ -385,7 +387,8 @@ def run_ours(args, rank, world, local_rank):
                      "ms": round(pk_ms.value, 4), "bytes": pk_bytes.value,
                      "achieved_gbs": round(pk_bytes.value / max(pk_ms.value, 1e-9) / 1e6, 1),
                      "frac": round(pk_bytes.value / max(pk_ms.value, 1e-9) / 1e6 / hbm_peak, 4),
-                     "chunks": pk_chunks.value},
+                     "chunks": pk_chunks.value, "dram_runs": lay[0].value,
+                     "ce_copies": lay[1].value, "zero_copy_blocks": lay[2].value},
             "host_link": {"evict_bytes": evict_bytes, "evict_ms": phases.get("evict"),
                           "evict_gbs": round(evict_bytes / max(phases.get("evict", 1), 1e-9) / 1e6, 1),
                           "promote_bytes": promote_bytes, "promote_kernel_ms": round(pr_ms.value, 3),

@@ -143,6 +143,14 @@ int  orchkv_promote_batch_to_gpu(const uint32_t *block_ids, const uint32_t *coun
 int  orchkv_last_migration_profile(float *pack_ms, unsigned long long *pack_bytes,
                                    uint32_t *chunks, float *promote_ms);
 
+/* How the last staged evict reached the DRAM tier: `runs` = runs of
+ * consecutive DRAM slabs it filled, `ce_copies` = copy-engine copies issued
+ * (one per run of at least 1 MiB, split at staging-slot boundaries),
+ * `zero_copy_slabs` = blocks in shorter runs, written by a kernel straight
+ * into mapped host memory.  All 0 when the zero-copy kernel ran alone. */
+int  orchkv_last_evict_layout(uint32_t *runs, uint32_t *ce_copies,
+                              uint32_t *zero_copy_slabs);
+
 /* Device table [n*n_layers][n_kv_heads][ceil(row_len/tpb)] of block ids of
  * the given requests (0xFFFFFFFF where a block does not exist), the layout
  * tm_report_attn_probs takes.  Asynchronous. */

@@ -499,12 +499,23 @@ def ref():
         L.ref_api_get.argtypes = [vp, C.c_uint32, C.c_uint32, C.c_uint32,
                                   C.POINTER(vp), C.POINTER(vp)]
         L.ref_api_get.restype = C.c_int
+        L.ref_api_dram_base.restype = vp
+        L.ref_api_gpu_base.restype = vp
+        L.ref_api_block.argtypes = [vp, C.c_uint32, C.c_uint32, C.c_uint32,
+                                    C.POINTER(C.c_int), C.POINTER(vp)]
+        L.ref_api_block.restype = C.c_int
         L.ref_api_migrate_list.argtypes = [vp, _u32p, C.c_uint32, C.c_uint32, _f64p]
         L.ref_api_migrate_list.restype = C.c_int
         L.ref_storage_read.argtypes = [C.c_char_p, C.c_uint64, C.c_uint32, C.c_uint32,
                                        C.c_uint32, C.c_size_t, C.c_uint32, C.c_uint32,
                                        C.c_uint32, vp]
         L.ref_storage_read.restype = C.c_int
+        _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+        L.ref_c4_scenario.argtypes = [C.c_uint32, _u64p, _i32p, _u8p, _u32p, C.c_uint32,
+                                      C.c_uint32, _u64p, _f32p, _u32p, _f32p, _f32p,
+                                      C.c_uint32, C.c_float, C.c_float, C.c_float, _i32p,
+                                      _i32p, _i32p, _f64p]
+        L.ref_c4_scenario.restype = C.c_int
         _REF = L
     return _REF
 

@@ -226,6 +226,86 @@ int ref_storage_read(const char *base_dir, uint64_t request_id, uint32_t L, uint
     return rc;
 }
 
+/* ------------------------------------------------------------------------
+ * Callback scenario for the C4/C7 demotion path (tm_schedule_once with a
+ * transfer callback and an allocator, as test/test_tiered_manager.c:24-60
+ * sets up): memcpy transfer, calloc allocator, free.  Blocks get 64-byte
+ * payloads.  touch[] is a sequence of block indices passed to
+ * tm_notify_access; rep_off[s]..rep_off[s+1] are step s's reports.
+ * Outputs: final tier, state and last payload byte (-1 when data_ptr is
+ * NULL) per block, and stats o[0..15] =
+ * gpu_demotes, dram_demotes, blocks_migrated, op_errors, op_count[6],
+ * op_bytes[6] (bytes / 64).
+ * ------------------------------------------------------------------------ */
+static int sc_transfer(kv_block_t *blk, void *dst, size_t size, MigrateOp op, void *ctx)
+{
+    (void)op; (void)ctx;
+    if (blk->data_ptr && dst) memcpy(dst, blk->data_ptr, size);
+    return ORCHKV_OK;
+}
+static void *sc_alloc(size_t size, StorageTier tier, void *ctx) { (void)tier; (void)ctx; return calloc(1, size); }
+static void sc_free(void *p, StorageTier tier, void *ctx) { (void)tier; (void)ctx; free(p); }
+
+int ref_c4_scenario(uint32_t n, const uint64_t *ids, const int *tiers, const uint8_t *flags,
+                    const uint32_t *touch, uint32_t n_touch, uint32_t steps,
+                    const uint64_t *rep_ids, const float *rep_w, const uint32_t *rep_off,
+                    const float *gpu_ratio, const float *dram_ratio, uint32_t demote_batch,
+                    float alpha, float beta, float gamma, int *out_tier, int *out_state,
+                    int *out_byte, double *o)
+{
+    tiered_manager_t m;
+    tm_config_t cfg;
+    tm_config_default(&cfg);
+    cfg.tracker_capacity = 4096;
+    cfg.max_blocks = 4096;
+    cfg.hcc_params.alpha = alpha;
+    cfg.hcc_params.beta = beta;
+    cfg.hcc_params.gamma = gamma;
+    cfg.transfer_fn = sc_transfer;
+    cfg.alloc_fn = sc_alloc;
+    cfg.free_fn = sc_free;
+    cfg.block_data_size = 64;
+    cfg.demote_batch_size = demote_batch;
+    cfg.athresh_params.cooldown_sec = 0.0;
+    if (tm_init(&m, &cfg) != ORCHKV_OK) return -1;
+    kv_block_t *b = calloc(n, sizeof(kv_block_t));
+    for (uint32_t i = 0; i < n; i++) {
+        b[i].block_id = ids[i];
+        b[i].tier = (StorageTier)tiers[i];
+        b[i].flags = flags[i];
+        b[i].state = tiers[i] == 0 ? KV_STATE_HOT : KV_STATE_WARM;
+        b[i].data_ptr = calloc(1, 64);
+        memset(b[i].data_ptr, (int)(i & 0xFF), 64);
+        tm_register_block(&m, &b[i]);
+    }
+    for (uint32_t t = 0; t < n_touch; t++) tm_notify_access(&m, &b[touch[t]]);
+    for (uint32_t s = 0; s < steps; s++) {
+        for (uint32_t r = rep_off[s]; r < rep_off[s + 1]; r++) tm_notify_attn(&m, rep_ids[r], rep_w[r]);
+        tm_step_done(&m);
+        tm_set_usage(&m, gpu_ratio[s], dram_ratio[s]);
+        tm_schedule_once(&m);
+    }
+    tm_stats_t st;
+    tm_get_stats(&m, &st);
+    o[0] = (double)st.gpu_demotes;
+    o[1] = (double)st.dram_demotes;
+    o[2] = (double)st.migration_stats.blocks_migrated;
+    o[3] = (double)st.migration_stats.op_errors;
+    for (int i = 0; i < 6; i++) {
+        o[4 + i] = (double)st.migration_stats.op_count[i];
+        o[10 + i] = (double)st.migration_stats.op_bytes[i] / 64.0;
+    }
+    for (uint32_t i = 0; i < n; i++) {
+        out_tier[i] = (int)b[i].tier;
+        out_state[i] = (int)b[i].state;
+        out_byte[i] = b[i].data_ptr ? (int)((unsigned char *)b[i].data_ptr)[63] : -1;
+        free(b[i].data_ptr);
+    }
+    tm_destroy(&m);
+    free(b);
+    return 0;
+}
+
 static double now_s(void)
 {
     struct timespec ts;
@@ -315,6 +395,17 @@ int   ref_api_promote(void *c, uint32_t l, uint32_t h, uint32_t b) { return orch
 int   ref_api_evict_cold(void *c, uint32_t l, uint32_t h, uint32_t b) { return orchkv_evict_cold(c, l, h, b); }
 int   ref_api_promote_storage(void *c, uint32_t l, uint32_t h, uint32_t b) { return orchkv_promote_from_storage(c, l, h, b); }
 int   ref_api_get(void *c, uint32_t l, uint32_t h, uint32_t b, void **k, void **v) { return orchkv_get_kv_block(c, l, h, b, k, v); }
+void *ref_api_dram_base(void) { dram_tier_t *d = orchkv_dram_tier(); return d ? d->pool_base : NULL; }
+void *ref_api_gpu_base(void) { gpu_tier_t *g = orchkv_gpu_tier(); return g ? g->pool_base : NULL; }
+/* tier and data pointer of block (l, h, b) of a request, without migrating it */
+int ref_api_block(void *c, uint32_t l, uint32_t h, uint32_t b, int *tier, void **data)
+{
+    kv_block_t *blk = kv_request_get_block((kv_request_ctx_t *)c, l, h, b);
+    if (!blk) return ORCHKV_ERR_NOT_FOUND;
+    *tier = (int)blk->tier;
+    *data = blk->data_ptr;
+    return ORCHKV_OK;
+}
 
 /* Evict then promote a list of (layer, head, block) triples of one request,
  * timing each phase (seconds in t[0], t[1]). */

@@ -141,6 +141,7 @@ _SIGS = {
     "orchkv_max_blocks": (u32, []),
     "orchkv_kernel_launches": (C.c_ulonglong, []),
     "orchkv_last_migration_profile": (i32, [P(f32), P(C.c_ulonglong), P(u32), P(f32)]),
+    "orchkv_last_evict_layout": (i32, [P(u32), P(u32), P(u32)]),
     "orchkv_gpu_pool_base": (vp, []),
     "orchkv_dram_pool_base": (vp, []),
     # scheduler

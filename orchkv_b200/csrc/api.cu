@@ -42,6 +42,8 @@ constexpr uint32_t kStagedMin = 2048;        // batches this large may use the c
 constexpr size_t kChunkBytes = 256u << 20;   // staging ring slot size
 constexpr int kRing = 3;
 constexpr int kMaxChunks = 1024;
+constexpr uint32_t kMaxRuns = 65536;         // DRAM runs per staged evict
+constexpr size_t kCeMinRunBytes = 1u << 20;  // shorter DRAM runs are written zero-copy
 
 struct Sys {
     std::recursive_mutex mu;
@@ -74,10 +76,14 @@ struct Sys {
     cudaEvent_t ev_copied[kRing] = {};
     cudaEvent_t ev_pk[2 * kMaxChunks] = {};
     cudaEvent_t ev_mig[4] = {};
+    char *sort_mem = nullptr;         // SortScratch storage
+    SortScratch ss;
+    uint32_t *h_runs = nullptr;       // pinned: run_o then run_d
     uint32_t *h_meta = nullptr;       // pinned
     uint32_t last_chunks = 0;
     int last_evict_staged = 0, last_promote_timed = 0;
     unsigned long long last_pack_bytes = 0;
+    uint32_t last_runs = 0, last_ce_copies = 0, last_zc_slabs = 0;
     gpu_tier_t gsnap;
     dram_tier_t dsnap;
     std::vector<uint32_t> gsnap_stack, dsnap_stack;
@@ -238,6 +244,10 @@ void release_all()
     cudaFreeHost(g.h_ctr);
     cudaFreeHost(g.h_meta);
     cudaFree(g.ring);
+    cudaFree(g.sort_mem);
+    cudaFreeHost(g.h_runs);
+    g.sort_mem = nullptr;
+    g.h_runs = nullptr;
     for (auto &e : g.ev_copied) if (e) { cudaEventDestroy(e); e = nullptr; }
     for (auto &e : g.ev_pk) if (e) { cudaEventDestroy(e); e = nullptr; }
     for (auto &e : g.ev_mig) if (e) { cudaEventDestroy(e); e = nullptr; }
@@ -402,6 +412,21 @@ int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
     for (auto &e : g.ev_copied) OKV_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     for (auto &e : g.ev_pk) OKV_CUDA_TRY(cudaEventCreate(&e));
     for (auto &e : g.ev_mig) OKV_CUDA_TRY(cudaEventCreate(&e));
+    {
+        const size_t dt = p.d_total, tiles = (dt + 1023) / 1024;
+        const size_t bytes = dt * 2 + (tiles + dt + 2 * (size_t)kMaxRuns) * 4 + 8 * 256;
+        OKV_CUDA_TRY(cudaMalloc((void **)&g.sort_mem, bytes));
+        char *q2 = g.sort_mem;
+        auto take2 = [&](size_t sz) { char *r = q2; q2 += (sz + 255) & ~size_t(255); return r; };
+        g.ss.flags = (uint8_t *)take2(dt);
+        g.ss.run_flag = (uint8_t *)take2(dt);
+        g.ss.tile_cnt = (uint32_t *)take2(tiles * 4);
+        g.ss.sorted = (uint32_t *)take2(dt * 4);
+        g.ss.run_o = (uint32_t *)take2((size_t)kMaxRuns * 4);
+        g.ss.run_d = (uint32_t *)take2((size_t)kMaxRuns * 4);
+        g.ss.max_runs = kMaxRuns;
+        OKV_CUDA_TRY(cudaMallocHost((void **)&g.h_runs, (size_t)kMaxRuns * 8));
+    }
     g.active_requests = 0;
     g.inited = true;
     return ORCHKV_OK;
@@ -757,46 +782,90 @@ int orchkv_evict_batch_to_dram(const uint32_t *ids, const uint32_t *count, uint3
     g.last_evict_staged = 0;
     g.last_chunks = 0;
     g.last_pack_bytes = 0;
+    g.last_runs = g.last_ce_copies = g.last_zc_slabs = 0;
     MigPlan mp = launch_migrate_plan(g.p, 0, ids, count, max_n, result, g.scratch, g.stream);
     if (mp.rc) return mp.rc;
     if (max_n >= kStagedMin) {
-        // Large batch: if the DRAM slabs popped for it form one contiguous
-        // range (the LIFO pool hands out ranges), assign them in ascending
-        // order, pack the victims into a device staging ring at HBM speed and
-        // let the copy engine drain each slot into that range while the next
-        // slot is packed.  Pool stacks end exactly as after per-block evicts;
-        // only which victim gets which slab of the range differs.
-        int rc = launch_run_check(g.p, mp, g.stream);
+        // Large batch: sort the DRAM slabs popped for it and hand them out in
+        // ascending order, pack the victims into a device staging ring at HBM
+        // speed, and let the copy engine drain each slot into the DRAM tier,
+        // one copy per run of consecutive slabs, while the next slot is
+        // packed.  Pool stacks end exactly as after per-block evicts; only
+        // which victim gets which of the popped slabs differs.
+        int rc = launch_sorted_assign(g.p, mp, g.ss, g.stream);
         if (rc) return rc;
         OKV_CUDA_TRY(cudaMemcpyAsync(g.h_meta, mp.meta, 8 * 4, cudaMemcpyDeviceToHost, g.stream));
         OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
-        const uint32_t done = g.h_meta[0], run = g.h_meta[4], lo = g.h_meta[5];
+        const uint32_t done = g.h_meta[0], n_runs = g.h_meta[6];
         if (done == 0) return ORCHKV_OK;
         const uint32_t chunk = g.ring_slabs;
         const uint32_t nchunks = (done + chunk - 1) / chunk;
-        if (run == 1 && nchunks <= (uint32_t)kMaxChunks) {
+        if (n_runs >= 1 && n_runs <= kMaxRuns && nchunks <= (uint32_t)kMaxChunks) {
+            uint32_t *run_o = g.h_runs, *run_d = g.h_runs + kMaxRuns;
+            OKV_CUDA_TRY(cudaMemcpyAsync(run_o, g.ss.run_o, (size_t)n_runs * 4,
+                                         cudaMemcpyDeviceToHost, g.stream));
+            OKV_CUDA_TRY(cudaMemcpyAsync(run_d, g.ss.run_d, (size_t)n_runs * 4,
+                                         cudaMemcpyDeviceToHost, g.stream));
+            OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
             const size_t slab = g.p.slab;
+            uint32_t min_len = (uint32_t)((kCeMinRunBytes + slab - 1) / slab);
+            if (min_len < 2) min_len = 2;
+            if (n_runs == 1 && done >= min_len) min_len = 0;   // one long run: no lookups
+            uint32_t r = 0;                       // first run touching the chunk
+            uint32_t ce_copies = 0, zc_slabs = 0;
             for (uint32_t c = 0; c < nchunks; c++) {
                 const uint32_t slot = c % kRing;
                 const uint32_t pos0 = c * chunk;
                 const uint32_t n = done - pos0 < chunk ? done - pos0 : chunk;
                 char *buf = g.ring + (size_t)slot * chunk * slab;
+                // list positions [pos0, pos0 + n) split into runs of consecutive
+                // slabs; runs of >= min_len slabs go through the copy engine
+                while (r + 1 < n_runs && run_o[r + 1] <= pos0) r++;
+                uint32_t chunk_short = 0, q_end = r;
+                for (uint32_t q = r; q < n_runs && run_o[q] < pos0 + n; q++) {
+                    const uint32_t run_end = q + 1 < n_runs ? run_o[q + 1] : done;
+                    const uint32_t a = run_o[q] > pos0 ? run_o[q] : pos0;
+                    const uint32_t b = run_end < pos0 + n ? run_end : pos0 + n;
+                    if (min_len && run_end - run_o[q] < min_len) chunk_short += b - a;
+                    q_end = q + 1;
+                }
                 if (c >= (uint32_t)kRing) OKV_CUDA_TRY(cudaStreamWaitEvent(g.stream, g.ev_copied[slot], 0));
                 OKV_CUDA_TRY(cudaEventRecord(g.ev_pk[2 * c], g.stream));
-                rc = launch_pack(g.p, mp, buf, pos0, n, g.stream);
-                if (rc) return rc;
+                if (chunk_short < n) {
+                    rc = launch_pack(g.p, mp, buf, pos0, n, g.ss, chunk_short ? min_len : 0,
+                                     g.stream);
+                    if (rc) return rc;
+                }
                 OKV_CUDA_TRY(cudaEventRecord(g.ev_pk[2 * c + 1], g.stream));
                 OKV_CUDA_TRY(cudaStreamWaitEvent(g.copy, g.ev_pk[2 * c + 1], 0));
-                OKV_CUDA_TRY(cudaMemcpyAsync(g.p.dram_base + ((size_t)lo + pos0) * slab, buf,
-                                             (size_t)n * slab, cudaMemcpyDeviceToHost, g.copy));
+                for (uint32_t q = r; q < q_end; q++) {
+                    const uint32_t run_end = q + 1 < n_runs ? run_o[q + 1] : done;
+                    if (min_len && run_end - run_o[q] < min_len) continue;
+                    const uint32_t a = run_o[q] > pos0 ? run_o[q] : pos0;
+                    const uint32_t b = run_end < pos0 + n ? run_end : pos0 + n;
+                    const uint32_t d0 = run_d[q] + (a - run_o[q]);
+                    OKV_CUDA_TRY(cudaMemcpyAsync(g.p.dram_base + (size_t)d0 * slab,
+                                                 buf + (size_t)(a - pos0) * slab,
+                                                 (size_t)(b - a) * slab, cudaMemcpyDeviceToHost,
+                                                 g.copy));
+                    ce_copies++;
+                }
                 OKV_CUDA_TRY(cudaEventRecord(g.ev_copied[slot], g.copy));
+                if (chunk_short) {
+                    rc = launch_drain_short(g.p, mp, pos0, n, g.ss, min_len, g.stream);
+                    if (rc) return rc;
+                    zc_slabs += chunk_short;
+                }
             }
+            g.last_runs = n_runs;
+            g.last_ce_copies = ce_copies;
+            g.last_zc_slabs = zc_slabs;
             // later work on the stream sees the bytes in the DRAM tier
             OKV_CUDA_TRY(cudaEventRecord(g.ev_mig[0], g.copy));
             OKV_CUDA_TRY(cudaStreamWaitEvent(g.stream, g.ev_mig[0], 0));
             g.last_evict_staged = 1;
             g.last_chunks = nchunks;
-            g.last_pack_bytes = (unsigned long long)done * slab * 2;
+            g.last_pack_bytes = (unsigned long long)(done - zc_slabs) * slab * 2;
             return ORCHKV_OK;
         }
     }
@@ -847,6 +916,16 @@ int orchkv_last_migration_profile(float *pack_ms, unsigned long long *pack_bytes
         if (g.last_promote_timed)
             OKV_CUDA_TRY(cudaEventElapsedTime(promote_ms, g.ev_mig[1], g.ev_mig[2]));
     }
+    return ORCHKV_OK;
+}
+
+int orchkv_last_evict_layout(uint32_t *runs, uint32_t *ce_copies, uint32_t *zero_copy_slabs)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (runs) *runs = g.last_evict_staged ? g.last_runs : 0;
+    if (ce_copies) *ce_copies = g.last_evict_staged ? g.last_ce_copies : 0;
+    if (zero_copy_slabs) *zero_copy_slabs = g.last_evict_staged ? g.last_zc_slabs : 0;
     return ORCHKV_OK;
 }
 

@@ -97,9 +97,29 @@ MigPlan launch_migrate_plan(const PoolDev &p, int dir, const uint32_t *ids,
                             const uint32_t *count, uint32_t max_n, uint32_t *result,
                             uint32_t *scratch, cudaStream_t s);
 int launch_migrate_zero_copy(const PoolDev &p, int dir, const MigPlan &mp, cudaStream_t s);
-int launch_run_check(const PoolDev &p, const MigPlan &mp, cudaStream_t s);
+// Staged evict: the popped DRAM slabs are sorted (byte map over the pool),
+// victim o gets the o-th smallest, and the runs of consecutive slabs are
+// listed for the copy engine.  meta[6] receives the number of runs.
+struct SortScratch {
+    uint8_t *flags;      // [d_total]
+    uint32_t *tile_cnt;  // [ceil(d_total / 1024)]
+    uint32_t *sorted;    // [d_total]
+    uint8_t *run_flag;   // [d_total]
+    uint32_t *run_o;     // [max_runs] list position of each run start
+    uint32_t *run_d;     // [max_runs] first slab of each run
+    uint32_t max_runs;
+};
+int launch_sorted_assign(const PoolDev &p, const MigPlan &mp, const SortScratch &ss,
+                         cudaStream_t s);
+// Pack entries [pos0, pos0 + n) into staging (entry w at staging + w*slab).
+// min_len > 0: only entries in DRAM runs of >= min_len slabs (requires the
+// run list of launch_sorted_assign, and meta[6] <= ss.max_runs).
 int launch_pack(const PoolDev &p, const MigPlan &mp, char *staging, uint32_t pos0, uint32_t n,
-                cudaStream_t s);
+                const SortScratch &ss, uint32_t min_len, cudaStream_t s);
+// Entries of [pos0, pos0 + n) in DRAM runs shorter than min_len: written from
+// their GPU slab straight into the DRAM tier (zero-copy).
+int launch_drain_short(const PoolDev &p, const MigPlan &mp, uint32_t pos0, uint32_t n,
+                       const SortScratch &ss, uint32_t min_len, cudaStream_t s);
 int launch_id_table(const PoolDev &p, uint32_t *const *regions, uint32_t n, uint32_t L,
                     uint32_t H, uint32_t mbph, uint32_t row_len, uint32_t *out,
                     cudaStream_t s);

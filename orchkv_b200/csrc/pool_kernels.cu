@@ -578,76 +578,186 @@ mig_copy_kernel(const char *src_base, char *dst_base, unsigned long long slab,
     }
 }
 
-// Do the DRAM slabs popped for this batch form one contiguous range?  (They
-// are distinct stack entries, so min/max decide it.)  meta[4] = 1 if so,
-// meta[5] = lowest slab of the range.
-__global__ void __launch_bounds__(1024)
-mig_run_check_kernel(const uint32_t *plan_dst, uint32_t *meta)
+// ---- sorted assignment of a staged evict's DRAM slabs ---------------------
+// The batch popped `done` distinct slabs of the DRAM pool (bounded by d_total),
+// so a byte map + scan sorts them in O(d_total).  Entry o of the victim list
+// then gets the o-th smallest popped slab, and the copy engine drains the
+// staging buffer run by run (maximal runs of consecutive slabs).
+
+__global__ void mig_mark_kernel(const uint32_t *plan_dst, const uint32_t *meta, uint8_t *flags)
 {
-    __shared__ uint32_t smin[32], smax[32];
     const uint32_t done = meta[0];
-    uint32_t mn = 0xFFFFFFFFu, mx = 0;
-    for (uint32_t o = threadIdx.x; o < done; o += blockDim.x) {
-        const uint32_t d = plan_dst[o];
-        mn = d < mn ? d : mn;
-        mx = d > mx ? d : mx;
-    }
-#pragma unroll
-    for (int k = 16; k > 0; k >>= 1) {
-        const uint32_t a = __shfl_xor_sync(0xFFFFFFFFu, mn, k);
-        const uint32_t b = __shfl_xor_sync(0xFFFFFFFFu, mx, k);
-        mn = a < mn ? a : mn;
-        mx = b > mx ? b : mx;
-    }
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    if (lane == 0) { smin[wid] = mn; smax[wid] = mx; }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); w++) {
-            mn = smin[w] < mn ? smin[w] : mn;
-            mx = smax[w] > mx ? smax[w] : mx;
-        }
-        const bool run = done > 0 && mx - mn + 1 == done;
-        meta[3] = mn;
-        meta[4] = run ? 1u : 0u;
-        meta[5] = run ? mn : 0u;
-    }
+    for (uint32_t o = blockIdx.x * blockDim.x + threadIdx.x; o < done; o += gridDim.x * blockDim.x)
+        flags[plan_dst[o]] = 1;
 }
 
-// Contiguous batch: hand the range out in ascending slab order (entry o gets
-// lo + o), so the victims packed in list order are byte-for-byte that range.
-__global__ void mig_fixup_kernel(PoolDev p, const uint32_t *meta, const uint32_t *plan_id,
-                                 uint32_t *plan_dst)
+__global__ void __launch_bounds__(256)
+mig_flag_count_kernel(const uint8_t *flags, uint32_t n, uint32_t *tile_cnt)
 {
-    if (meta[4] != 1u) return;
-    const uint32_t done = meta[0], lo = meta[5];
-    for (uint32_t o = blockIdx.x * blockDim.x + threadIdx.x; o < done; o += gridDim.x * blockDim.x) {
-        plan_dst[o] = lo + o;
-        p.loc[plan_id[o]] = make_loc(TIER_HOST_DRAM, lo + o);
+    __shared__ uint32_t tmp[33];
+    const uint32_t base = blockIdx.x * kTileN + threadIdx.x * 4;
+    uint32_t c = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) c += (base + j < n) ? flags[base + j] : 0u;
+    uint32_t tot;
+    block_excl_scan(c, tmp, &tot);
+    if (threadIdx.x == 0) tile_cnt[blockIdx.x] = tot;
+}
+
+__global__ void __launch_bounds__(1024)
+mig_tile_scan_kernel(uint32_t *tile_cnt, uint32_t tiles)
+{
+    __shared__ uint32_t tmp[33];
+    __shared__ uint32_t carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (uint32_t b0 = 0; b0 < tiles; b0 += blockDim.x) {
+        const uint32_t t = b0 + threadIdx.x;
+        const uint32_t c = t < tiles ? tile_cnt[t] : 0;
+        uint32_t tot;
+        const uint32_t ex = block_excl_scan(c, tmp, &tot);
+        if (t < tiles) tile_cnt[t] = carry + ex;
+        __syncthreads();
+        if (threadIdx.x == 0) carry += tot;
+        __syncthreads();
     }
 }
 
-// Pack list entries [pos0, pos0 + n) into the staging buffer, in list order.
+__global__ void __launch_bounds__(256)
+mig_flag_write_kernel(const uint8_t *flags, uint32_t n, const uint32_t *tile_base,
+                      uint32_t *sorted)
+{
+    __shared__ uint32_t tmp[33];
+    const uint32_t base = blockIdx.x * kTileN + threadIdx.x * 4;
+    uint8_t f[4];
+    uint32_t c = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        f[j] = (base + j < n) ? flags[base + j] : 0;
+        c += f[j];
+    }
+    uint32_t pos = tile_base[blockIdx.x] + block_excl_scan(c, tmp, nullptr);
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+        if (f[j]) sorted[pos++] = base + j;
+}
+
+__global__ void mig_assign_kernel(PoolDev p, const uint32_t *meta, const uint32_t *sorted,
+                                  const uint32_t *plan_id, uint32_t *plan_dst, uint8_t *run_flag)
+{
+    const uint32_t done = meta[0];
+    for (uint32_t o = blockIdx.x * blockDim.x + threadIdx.x; o < done; o += gridDim.x * blockDim.x) {
+        const uint32_t d = sorted[o];
+        plan_dst[o] = d;
+        p.loc[plan_id[o]] = make_loc(TIER_HOST_DRAM, d);
+        run_flag[o] = (o == 0 || sorted[o - 1] + 1 != d) ? 1 : 0;
+    }
+}
+
+// One CTA: list the run starts (list position, first slab) in order.
+// meta[6] = number of runs (may exceed max_runs; only max_runs are written).
+__global__ void __launch_bounds__(1024)
+mig_runs_kernel(const uint8_t *run_flag, const uint32_t *sorted, uint32_t *meta,
+                uint32_t *run_o, uint32_t *run_d, uint32_t max_runs)
+{
+    __shared__ uint32_t tmp[33];
+    __shared__ uint32_t carry;
+    const uint32_t done = meta[0];
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (uint32_t b0 = 0; b0 < done; b0 += blockDim.x * 4) {
+        const uint32_t e0 = b0 + threadIdx.x * 4;
+        uint32_t c = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) c += (e0 + j < done) ? run_flag[e0 + j] : 0u;
+        uint32_t tot;
+        uint32_t pos = carry + block_excl_scan(c, tmp, &tot);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint32_t e = e0 + j;
+            if (e < done && run_flag[e]) {
+                if (pos < max_runs) { run_o[pos] = e; run_d[pos] = sorted[e]; }
+                pos++;
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) carry += tot;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) meta[6] = carry;
+}
+
+// Length of the run of consecutive DRAM slabs that list position o belongs
+// to.  run_o holds the ascending list positions where runs start (run_o[0] is
+// 0); n_runs of them, the last run ending at done.
+__device__ __forceinline__ uint32_t run_len_at(const uint32_t *run_o, uint32_t n_runs,
+                                               uint32_t done, uint32_t o)
+{
+    uint32_t lo = 0, hi = n_runs;          // last q with run_o[q] <= o
+    while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (__ldg(run_o + mid) <= o) lo = mid; else hi = mid;
+    }
+    const uint32_t end = lo + 1 < n_runs ? __ldg(run_o + lo + 1) : done;
+    return end - __ldg(run_o + lo);
+}
+
+__device__ __forceinline__ void copy_slab_warp(const char *src, char *dst,
+                                               unsigned long long nvec, unsigned lane)
+{
+    const uint4 *s = reinterpret_cast<const uint4 *>(src);
+    uint4 *d = reinterpret_cast<uint4 *>(dst);
+    unsigned long long i = lane;
+    for (; i + 7 * 32 < nvec; i += 8 * 32) {
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) v[u] = s[i + u * 32];
+#pragma unroll
+        for (int u = 0; u < 8; u++) d[i + u * 32] = v[u];
+    }
+    for (; i < nvec; i += 32) d[i] = s[i];
+}
+
+// Pack list entries [pos0, pos0 + n) into the staging buffer, in list order
+// (entry w at staging + w * slab).  With min_len > 0 only entries whose DRAM
+// run is at least min_len slabs long are packed (the copy engine drains
+// those); the rest are left to mig_drain_short_kernel.
 __global__ void __launch_bounds__(256)
 mig_pack_kernel(const char *src_base, char *staging, unsigned long long slab,
-                const uint32_t *plan_src, uint32_t pos0, uint32_t n)
+                const uint32_t *plan_src, uint32_t pos0, uint32_t n, const uint32_t *run_o,
+                const uint32_t *meta, uint32_t min_len)
 {
     const unsigned lane = threadIdx.x & 31;
     const unsigned long long nvec = slab >> 4;
     const unsigned long long warp0 = ((unsigned long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const unsigned long long nwarps = ((unsigned long long)gridDim.x * blockDim.x) >> 5;
+    const uint32_t done = min_len ? meta[0] : 0, n_runs = min_len ? meta[6] : 0;
     for (unsigned long long w = warp0; w < n; w += nwarps) {
-        const uint4 *s = reinterpret_cast<const uint4 *>(src_base + plan_src[pos0 + w] * slab);
-        uint4 *d = reinterpret_cast<uint4 *>(staging + w * slab);
-        unsigned long long i = lane;
-        for (; i + 7 * 32 < nvec; i += 8 * 32) {
-            uint4 v[8];
-#pragma unroll
-            for (int u = 0; u < 8; u++) v[u] = s[i + u * 32];
-#pragma unroll
-            for (int u = 0; u < 8; u++) d[i + u * 32] = v[u];
-        }
-        for (; i < nvec; i += 32) d[i] = s[i];
+        const uint32_t o = pos0 + (uint32_t)w;
+        if (min_len && run_len_at(run_o, n_runs, done, o) < min_len) continue;
+        copy_slab_warp(src_base + plan_src[o] * slab, staging + w * slab, nvec, lane);
+    }
+}
+
+// Entries of [pos0, pos0 + n) whose DRAM run is shorter than min_len go
+// straight from their GPU slab to their DRAM slab over the host link
+// (mapped pinned memory): runs that short would cost the copy engine more in
+// per-copy overhead than in transfer time.
+__global__ void __launch_bounds__(256)
+mig_drain_short_kernel(const char *src_base, char *dram_base, unsigned long long slab,
+                       const uint32_t *plan_src, const uint32_t *plan_dst, uint32_t pos0,
+                       uint32_t n, const uint32_t *run_o, const uint32_t *meta, uint32_t min_len)
+{
+    const unsigned lane = threadIdx.x & 31;
+    const unsigned long long nvec = slab >> 4;
+    const unsigned long long warp0 = ((unsigned long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const unsigned long long nwarps = ((unsigned long long)gridDim.x * blockDim.x) >> 5;
+    const uint32_t done = meta[0], n_runs = meta[6];
+    for (unsigned long long w = warp0; w < n; w += nwarps) {
+        const uint32_t o = pos0 + (uint32_t)w;
+        if (run_len_at(run_o, n_runs, done, o) >= min_len) continue;
+        copy_slab_warp(src_base + plan_src[o] * slab, dram_base + plan_dst[o] * slab, nvec,
+                       lane);
     }
 }
 
@@ -823,20 +933,44 @@ int launch_migrate_zero_copy(const PoolDev &p, int dir, const MigPlan &mp, cudaS
     return ORCHKV_OK;
 }
 
-int launch_run_check(const PoolDev &p, const MigPlan &mp, cudaStream_t s)
+int launch_sorted_assign(const PoolDev &p, const MigPlan &mp, const SortScratch &ss,
+                         cudaStream_t s)
 {
-    mig_run_check_kernel<<<1, 1024, 0, s>>>(mp.plan_dst, mp.meta); note_launches(1);
-    mig_fixup_kernel<<<copy_grid(mp.max_n, 256), 256, 0, s>>>(p, mp.meta, mp.plan_id, mp.plan_dst); note_launches(1);
+    OKV_CUDA_TRY(cudaMemsetAsync(ss.flags, 0, p.d_total, s));
+    const unsigned g = copy_grid(mp.max_n, 256);
+    const uint32_t tiles = (p.d_total + kTileN - 1) / kTileN;
+    mig_mark_kernel<<<g, 256, 0, s>>>(mp.plan_dst, mp.meta, ss.flags);
+    mig_flag_count_kernel<<<tiles, 256, 0, s>>>(ss.flags, p.d_total, ss.tile_cnt);
+    mig_tile_scan_kernel<<<1, 1024, 0, s>>>(ss.tile_cnt, tiles);
+    mig_flag_write_kernel<<<tiles, 256, 0, s>>>(ss.flags, p.d_total, ss.tile_cnt, ss.sorted);
+    mig_assign_kernel<<<g, 256, 0, s>>>(p, mp.meta, ss.sorted, mp.plan_id, mp.plan_dst,
+                                        ss.run_flag);
+    mig_runs_kernel<<<1, 1024, 0, s>>>(ss.run_flag, ss.sorted, mp.meta, ss.run_o, ss.run_d,
+                                       ss.max_runs);
+    note_launches(6);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }
 
 int launch_pack(const PoolDev &p, const MigPlan &mp, char *staging, uint32_t pos0, uint32_t n,
-                cudaStream_t s)
+                const SortScratch &ss, uint32_t min_len, cudaStream_t s)
 {
     if (n == 0) return ORCHKV_OK;
     mig_pack_kernel<<<copy_grid(n, 8), 256, 0, s>>>(p.gpu_base, staging, p.slab, mp.plan_src,
-                                                     pos0, n); note_launches(1);
+                                                     pos0, n, ss.run_o, mp.meta, min_len);
+    note_launches(1);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_drain_short(const PoolDev &p, const MigPlan &mp, uint32_t pos0, uint32_t n,
+                       const SortScratch &ss, uint32_t min_len, cudaStream_t s)
+{
+    if (n == 0 || min_len == 0) return ORCHKV_OK;
+    mig_drain_short_kernel<<<copy_grid(n, 8), 256, 0, s>>>(p.gpu_base, p.dram_base, p.slab,
+                                                            mp.plan_src, mp.plan_dst, pos0, n,
+                                                            ss.run_o, mp.meta, min_len);
+    note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }

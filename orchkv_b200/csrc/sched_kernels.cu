@@ -53,7 +53,9 @@ constexpr int kScoreU = 4;         // float4 columns per lane per row: 512-token
 // loads float4 column (chunk*128 + u*32 + l) of each of the G query-head rows
 // of KV group h: every load instruction is one fully coalesced 512-byte line.
 // Token blocks of tpb tokens cover tpb/4 consecutive lanes and are summed with
-// xor-shuffles; one lane per block records the mass.
+// xor-shuffles.  The tile's blocks are then spread over the lanes (block k of
+// the tile to lane k % 32), whose tracker entries were fetched while the
+// probability rows streamed in, so recording costs no extra round trip.
 template <int LOG_LPB>
 __global__ void __launch_bounds__(kScoreWarps * 32)
 score_vec_kernel(const float *__restrict__ probs, uint32_t Hq, uint32_t Hkv,
@@ -61,7 +63,10 @@ score_vec_kernel(const float *__restrict__ probs, uint32_t Hq, uint32_t Hkv,
                  const uint32_t *__restrict__ ids, uint32_t nb, uint32_t n_chunks,
                  unsigned long long n_tiles, SchedDev d, unsigned long long step)
 {
-    constexpr int LPB = 1 << LOG_LPB;
+    constexpr int LPB = 1 << LOG_LPB;              // lanes per block in one step
+    constexpr int BPU = 32 / LPB;                  // blocks per step
+    constexpr int NBLK = kScoreU * BPU;            // blocks per tile
+    constexpr int K = NBLK > 32 ? NBLK / 32 : 1;   // blocks recorded per lane
     const int lane = threadIdx.x & 31;
     const unsigned long long tile =
         (unsigned long long)blockIdx.x * kScoreWarps + (threadIdx.x >> 5);
@@ -76,40 +81,44 @@ score_vec_kernel(const float *__restrict__ probs, uint32_t Hq, uint32_t Hkv,
     const uint32_t T4 = T >> 2;
     const float4 *base = reinterpret_cast<const float4 *>(probs + (r * Hq + (unsigned long long)h * G) * T);
 
-    float4 acc[kScoreU];
+    // block ids of the blocks this lane records
+    uint32_t bid[K];
 #pragma unroll
-    for (int u = 0; u < kScoreU; u++) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < K; j++) {
+        const uint32_t k = (uint32_t)lane + 32u * j;
+        const uint32_t b = c * NBLK + k;
+        bid[j] = (k < (uint32_t)NBLK && b < nb && b * tpb < len) ? ids[rh * nb + b] : kNoBlock;
+    }
 
     const uint32_t col0 = c * (32 * kScoreU) + lane;
-    // two query-head rows per iteration: 8 x 16 B loads in flight per lane
-    // before any accumulation (rows are still added in order g, g+1, ...)
-    uint32_t g = 0;
-    for (; g + 1 < G; g += 2) {
-        const float4 *r0 = base + (unsigned long long)g * T4;
-        const float4 *r1 = r0 + T4;
-        float4 a[kScoreU], b[kScoreU];
+    // row 0 of the group: its loads are issued first, then the tracker
+    // entries are fetched under them
+    float4 acc[kScoreU];
 #pragma unroll
-        for (int u = 0; u < kScoreU; u++) {
-            const uint32_t col = col0 + u * 32;
-            const bool in = col < T4;
-            a[u] = in ? ld_stream(r0 + col) : make_float4(0.f, 0.f, 0.f, 0.f);
-            b[u] = in ? ld_stream(r1 + col) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+    for (int u = 0; u < kScoreU; u++) {
+        const uint32_t col = col0 + u * 32;
+        acc[u] = col < T4 ? ld_stream(base + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    uint8_t act[K];
+    float old_sum[K], old_max[K];
 #pragma unroll
-        for (int u = 0; u < kScoreU; u++) {
-            acc[u].x += a[u].x; acc[u].y += a[u].y;
-            acc[u].z += a[u].z; acc[u].w += a[u].w;
-            acc[u].x += b[u].x; acc[u].y += b[u].y;
-            acc[u].z += b[u].z; acc[u].w += b[u].w;
+    for (int j = 0; j < K; j++) {
+        act[j] = 0; old_sum[j] = 0.f; old_max[j] = 0.f;
+        if (bid[j] != kNoBlock) {
+            const uint32_t sl = bid[j] & d.mask;
+            act[j] = d.tact[sl];
+            old_sum[j] = d.sum[sl];
+            old_max[j] = d.mx[sl];
         }
     }
-    if (g < G) {
-        const float4 *r0 = base + (unsigned long long)g * T4;
+    // remaining rows in order g = 1, 2, ...
+    for (uint32_t g = 1; g < G; g++) {
+        const float4 *rg = base + (unsigned long long)g * T4;
         float4 a[kScoreU];
 #pragma unroll
         for (int u = 0; u < kScoreU; u++) {
             const uint32_t col = col0 + u * 32;
-            a[u] = col < T4 ? ld_stream(r0 + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+            a[u] = col < T4 ? ld_stream(rg + col) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
         for (int u = 0; u < kScoreU; u++) {
@@ -118,23 +127,37 @@ score_vec_kernel(const float *__restrict__ probs, uint32_t Hq, uint32_t Hkv,
         }
     }
 
-    const uint32_t *idrow = ids + rh * nb;
+    float part[kScoreU];
 #pragma unroll
     for (int u = 0; u < kScoreU; u++) {
-        const uint32_t col = col0 + u * 32;
-        const uint32_t t0 = col * 4;
+        const uint32_t t0 = (col0 + u * 32) * 4;
         // tokens at or beyond the row's valid length contribute nothing
         float4 a = acc[u];
         if (t0 + 0 >= len) a.x = 0.f;
         if (t0 + 1 >= len) a.y = 0.f;
         if (t0 + 2 >= len) a.z = 0.f;
         if (t0 + 3 >= len) a.w = 0.f;
-        float s = (a.x + a.y) + (a.z + a.w);
+        float sv = (a.x + a.y) + (a.z + a.w);
 #pragma unroll
-        for (int o = 1; o < LPB; o <<= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-        if ((lane & (LPB - 1)) == 0 && col < T4 && t0 < len) {
-            const uint32_t b = t0 / tpb;
-            record_mass(d, idrow[b], s, step);
+        for (int o = 1; o < LPB; o <<= 1) sv += __shfl_xor_sync(0xFFFFFFFFu, sv, o);
+        part[u] = sv;                  // block (u, lane / LPB) total, on its lanes
+    }
+#pragma unroll
+    for (int j = 0; j < K; j++) {
+        const uint32_t k = (uint32_t)lane + 32u * j;
+        const uint32_t uk = k / BPU;                 // step holding block k
+        const int src = (int)((k % BPU) * LPB);      // a lane of block k in that step
+        float w = 0.f;
+#pragma unroll
+        for (int u = 0; u < kScoreU; u++) {
+            const float t = __shfl_sync(0xFFFFFFFFu, part[u], src);
+            if (uk == (uint32_t)u) w = t;
+        }
+        if (bid[j] != kNoBlock && act[j]) {
+            const uint32_t sl = bid[j] & d.mask;
+            d.sum[sl] = __fadd_rn(old_sum[j], w);
+            if (w > old_max[j]) d.mx[sl] = w;
+            d.last[sl] = step;
         }
     }
 }

@@ -111,9 +111,58 @@ def fast_manager_ops(rng):
     return list(range(n_blocks)), ops
 
 
+def c4_case(seed=11, n=240, steps=16):
+    """Demotion through the callback path: tm_schedule_once with a memcpy
+    transfer callback, calloc/free allocators and 64-byte payloads (the
+    set-up of test/test_tiered_manager.c), memory pressure varying per step."""
+    rng = np.random.default_rng(seed)
+    ids = [int(x) for x in rng.choice(4096, n, replace=False)]
+    tiers = [int(t) for t in rng.choice([0, 0, 0, 1, 1, 2], n)]
+    flags = [int(f) for f in rng.choice([0, 0, 0, 0, 1, 8], n)]
+    touch = [int(t) for t in rng.integers(0, n, 3 * n)]
+    rep_ids, rep_w, rep_off = [], [], [0]
+    for _ in range(steps):
+        for i in rng.choice(n, 60):
+            rep_ids.append(ids[int(i)])
+            rep_w.append(float(np.float32(rng.random())))
+        rep_off.append(len(rep_ids))
+    gpu = [float(np.float32(x)) for x in rng.uniform(0.6, 1.0, steps)]
+    dram = [float(np.float32(x)) for x in rng.uniform(0.6, 1.0, steps)]
+    return dict(ids=ids, tiers=tiers, flags=flags, touch=touch, steps=steps, rep_ids=rep_ids,
+                rep_w=rep_w, rep_off=rep_off, gpu_ratio=gpu, dram_ratio=dram,
+                demote_batch=8, alpha=0.5, beta=0.3, gamma=0.2)
+
+
+def run_ref_c4(c):
+    n = len(c["ids"])
+    out_tier = np.zeros(n, np.int32)
+    out_state = np.zeros(n, np.int32)
+    out_byte = np.zeros(n, np.int32)
+    o = np.zeros(16, np.float64)
+    rc = O.ref().ref_c4_scenario(
+        n, np.asarray(c["ids"], np.uint64), np.asarray(c["tiers"], np.int32),
+        np.asarray(c["flags"], np.uint8), np.asarray(c["touch"], np.uint32), len(c["touch"]),
+        c["steps"], np.asarray(c["rep_ids"], np.uint64), np.asarray(c["rep_w"], np.float32),
+        np.asarray(c["rep_off"], np.uint32), np.asarray(c["gpu_ratio"], np.float32),
+        np.asarray(c["dram_ratio"], np.float32), c["demote_batch"], c["alpha"], c["beta"],
+        c["gamma"], out_tier, out_state, out_byte, o)
+    assert rc == 0
+    return dict(tier=out_tier.tolist(), state=out_state.tolist(), byte=out_byte.tolist(),
+                stats=[int(x) for x in o])
+
+
 def main():
     if not O.ref_available():
         raise SystemExit("build the reference first: make -C oracle")
+    c = c4_case()
+    fx = {"name": "c4_demote_callbacks", "case": c, "expect": run_ref_c4(c),
+          "stats_order": "gpu_demotes dram_demotes blocks_migrated op_errors op_count[6] "
+                         "op_bytes[6]/64",
+          "source": "reference src/scheduler/*.c compiled by oracle/Makefile, driven like "
+                    "test/test_tiered_manager.c (transfer/alloc/free callbacks)"}
+    with open(os.path.join(HERE, "c4_demote_callbacks.json"), "w") as fh:
+        json.dump(fx, fh, separators=(",", ":"))
+    print("wrote c4_demote_callbacks", fx["expect"]["stats"])
     for name, case in CASES.items():
         rng = np.random.default_rng(case["seed"])
         if case["ops"] is None:

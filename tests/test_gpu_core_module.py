@@ -21,7 +21,7 @@ def core(cuda):
 
 
 def _fixtures():
-    return sorted(f for f in os.listdir(GOLDEN) if f.endswith(".json"))
+    return sorted(f for f in os.listdir(GOLDEN) if f.startswith("sched_") and f.endswith(".json"))
 
 
 def f32bits(x):

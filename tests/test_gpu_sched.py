@@ -25,7 +25,7 @@ def okv(cuda):
 
 
 def _fixtures():
-    return sorted(f for f in os.listdir(GOLDEN) if f.endswith(".json"))
+    return sorted(f for f in os.listdir(GOLDEN) if f.startswith("sched_") and f.endswith(".json"))
 
 
 @pytest.mark.parametrize("name", _fixtures())

@@ -199,7 +199,7 @@ def test_pool_lifo_order(oracle_mod):
 def _fixtures():
     if not os.path.isdir(GOLDEN):
         return []
-    return sorted(f for f in os.listdir(GOLDEN) if f.endswith(".json"))
+    return sorted(f for f in os.listdir(GOLDEN) if f.startswith("sched_") and f.endswith(".json"))
 
 
 @pytest.mark.parametrize("name", _fixtures())
@@ -218,6 +218,18 @@ def test_golden_fixture(oracle_mod, name):
 
 def test_fixtures_present():
     assert len(_fixtures()) >= 3, "tests/golden fixtures missing (run tests/golden/gen_golden.py)"
+    assert os.path.exists(os.path.join(GOLDEN, "c4_demote_callbacks.json"))
+
+
+@pytest.mark.ref
+def test_c4_fixture_regenerates(oracle_mod):
+    """The callback-path fixture is what the compiled reference produces now."""
+    if not oracle_mod.ref_available():
+        pytest.skip("reference not compiled into oracle/_ref on this machine")
+    from tests.golden.gen_golden import run_ref_c4
+    with open(os.path.join(GOLDEN, "c4_demote_callbacks.json")) as fh:
+        fx = json.load(fh)
+    assert run_ref_c4(fx["case"]) == fx["expect"]
 
 
 # ---- live cross-check against the reference compiled from its sources --------
