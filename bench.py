@@ -43,6 +43,10 @@ sys.path.insert(0, ROOT)
 METRIC = "decode-step schedule+migrate µs and migrated blocks/s per GPU; HBM GB/s % peak"
 WL = dict(name="qwen2.5-7b-gqa-decode-step", B=32, L=28, Hq=28, Hkv=4, D=128, T=8192, tpb=16)
 EVICT_FRAC, PROMOTE_FRAC = 0.25, 0.05
+# DRAM bytes (read + write) of one score launch per request of this workload:
+# 215.9 MB measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum) on one
+# 8-request launch; the launch streams each request's rows once, so it scales
+SCORE_TRAFFIC_PER_REQUEST = 215.91e6 / 8
 
 
 def peaks():
@@ -278,6 +282,7 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize()
 
+    link = host_link_probe(torch)
     for _ in range(args.warmup):
         wl.step()
         wl.restore()
@@ -382,7 +387,10 @@ def run_ours(args, rank, world, local_rank):
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
                 "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                 "peak_kind": peak_kind, "bytes_per_launch": sb,
-                "ms_per_launch": round(score_avg, 4), "traffic": None},
+                "ms_per_launch": round(score_avg, 4),
+                "traffic": round(SCORE_TRAFFIC_PER_REQUEST * WL["B"]),
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                  "8-request launch, scaled by requests"},
             "pack": {"kernel": "evict pack (HBM gather -> staging)",
                      "ms": round(pk_ms.value, 4), "bytes": pk_bytes.value,
                      "achieved_gbs": round(pk_bytes.value / max(pk_ms.value, 1e-9) / 1e6, 1),
@@ -392,7 +400,10 @@ def run_ours(args, rank, world, local_rank):
             "host_link": {"evict_bytes": evict_bytes, "evict_ms": phases.get("evict"),
                           "evict_gbs": round(evict_bytes / max(phases.get("evict", 1), 1e-9) / 1e6, 1),
                           "promote_bytes": promote_bytes, "promote_kernel_ms": round(pr_ms.value, 3),
-                          "promote_gbs": round(promote_bytes / max(pr_ms.value, 1e-9) / 1e6, 1)},
+                          "promote_gbs": round(promote_bytes / max(pr_ms.value, 1e-9) / 1e6, 1),
+                          "measured_ce_d2h_gbs": link["d2h"], "measured_ce_h2d_gbs": link["h2d"],
+                          "evict_frac": round(evict_bytes / max(phases.get("evict", 1), 1e-9) / 1e6 / link["d2h"], 4),
+                          "promote_frac": round(promote_bytes / max(pr_ms.value, 1e-9) / 1e6 / link["h2d"], 4)},
             "phases_ms": phases,
             "e2e": {"value": round(migrated_total / (e2e_max * 1e-3), 1), "unit": "blocks/s",
                     "ms_per_step": round(e2e_max, 4),
@@ -411,6 +422,27 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
     if line:
         print(json.dumps(line), flush=True)
+
+
+def host_link_probe(torch, nbytes=512 << 20, reps=3):
+    """Copy-engine bandwidth of this GPU's host link, pinned memory, one
+    direction at a time (best of `reps` copies of `nbytes`), in GB/s."""
+    h = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    out = {}
+    for name, dst, src in (("h2d", d, h), ("d2h", h, d)):
+        best = 0.0
+        for _ in range(reps):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            dst.copy_(src, non_blocking=True)
+            b.record()
+            b.synchronize()
+            best = max(best, nbytes / (a.elapsed_time(b) * 1e-3) / 1e9)
+        out[name] = round(best, 1)
+    del h, d
+    return out
 
 
 # ---------------------------------------------------------------------------

@@ -134,36 +134,51 @@ int sync_result(int *rc_out)
     return ORCHKV_OK;
 }
 
-// Resolve a caller pointer to something kernels can read: device and mapped
-// pinned memory are used in place, pageable memory is staged with one copy.
-int resolve_input(const void *ptr, size_t bytes, size_t stage_off, const char **out)
+// A caller pointer kernels can read in place: device, managed or mapped
+// pinned memory.  nullptr for pageable host memory.
+const char *direct_ptr(const void *ptr)
 {
-    *out = nullptr;
-    if (!ptr) return ORCHKV_OK;
     cudaPointerAttributes a;
     cudaError_t e = cudaPointerGetAttributes(&a, ptr);
-    if (e == cudaSuccess && (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged)) {
-        *out = (const char *)ptr;
-        return ORCHKV_OK;
-    }
-    if (e == cudaSuccess && a.type == cudaMemoryTypeHost && a.devicePointer) {
-        *out = (const char *)a.devicePointer;
-        return ORCHKV_OK;
-    }
+    if (e == cudaSuccess && (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged))
+        return (const char *)ptr;
+    if (e == cudaSuccess && a.type == cudaMemoryTypeHost && a.devicePointer)
+        return (const char *)a.devicePointer;
     cudaGetLastError();   // clear a failed attribute query
-    const size_t need = stage_off + bytes;
+    return nullptr;
+}
+
+// Resolve the K and V inputs of one call (`bytes` each): used in place when
+// kernels can read them, else copied into the staging buffer.  The buffer is
+// grown for both before either copy is queued, so a growth never strands a
+// pointer handed out for the first.
+int resolve_kv(const void *k, const void *v, size_t bytes, const char **kd, const char **vd)
+{
+    *kd = k ? direct_ptr(k) : nullptr;
+    *vd = v ? direct_ptr(v) : nullptr;
+    const bool stage_k = k && !*kd, stage_v = v && !*vd;
+    const size_t need = (stage_k ? bytes : 0) + (stage_v ? bytes : 0);
+    if (need == 0) return ORCHKV_OK;
     if (need > g.stage_cap) {
         size_t cap = g.stage_cap ? g.stage_cap : (1 << 20);
         while (cap < need) cap *= 2;
-        OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+        OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));   // earlier copies may still read it
         cudaFree(g.stage);
         g.stage = nullptr;
         g.stage_cap = 0;
         OKV_CUDA_TRY(cudaMalloc((void **)&g.stage, cap));
         g.stage_cap = cap;
     }
-    OKV_CUDA_TRY(cudaMemcpyAsync(g.stage + stage_off, ptr, bytes, cudaMemcpyHostToDevice, g.stream));
-    *out = g.stage + stage_off;
+    size_t off = 0;
+    if (stage_k) {
+        OKV_CUDA_TRY(cudaMemcpyAsync(g.stage, k, bytes, cudaMemcpyHostToDevice, g.stream));
+        *kd = g.stage;
+        off = bytes;
+    }
+    if (stage_v) {
+        OKV_CUDA_TRY(cudaMemcpyAsync(g.stage + off, v, bytes, cudaMemcpyHostToDevice, g.stream));
+        *vd = g.stage + off;
+    }
     return ORCHKV_OK;
 }
 
@@ -230,6 +245,13 @@ void region_free(size_t off, size_t words)
 
 void release_all()
 {
+    if (g.attached) {
+        // the manager outlives the data plane: give it back its own stream
+        // and stop data-plane kernels from writing its slots
+        tm_set_stream(g.attached, nullptr);
+        g.attached = nullptr;
+        g.p.attached = 0;
+    }
     if (g.copy) cudaStreamSynchronize(g.copy);
     if (g.stream) cudaStreamSynchronize(g.stream);
     cudaFree(g.p.gpu_base);
@@ -505,8 +527,7 @@ int orchkv_prefill(kv_request_ctx_t *ctx, uint32_t layer, const void *k, const v
     if (!ctx || layer >= ctx->L) return ORCHKV_ERR_INVALID;
     const size_t bytes = (size_t)ctx->H * seq_len * g.p.row;
     const char *kd, *vd;
-    int rc = resolve_input(k, bytes, 0, &kd);
-    if (!rc) rc = resolve_input(v, bytes, bytes, &vd);
+    int rc = resolve_kv(k, v, bytes, &kd, &vd);
     if (rc) return rc;
     rc = launch_prefill(g.p, req_dev(ctx), layer, kd, vd, seq_len, g.scratch, g.res, g.stream);
     if (rc) return rc;
@@ -522,8 +543,7 @@ int orchkv_append_token(kv_request_ctx_t *ctx, uint32_t layer, const void *k, co
     if (!ctx || layer >= ctx->L) return ORCHKV_ERR_INVALID;
     const size_t bytes = (size_t)ctx->H * g.p.row;
     const char *kd, *vd;
-    int rc = resolve_input(k, bytes, 0, &kd);
-    if (!rc) rc = resolve_input(v, bytes, bytes, &vd);
+    int rc = resolve_kv(k, v, bytes, &kd, &vd);
     if (rc) return rc;
     rc = launch_append_one(g.p, req_dev(ctx), layer, kd, vd, g.res, g.stream);
     if (rc) return rc;
@@ -727,6 +747,17 @@ int orchkv_sync(void)
     return ORCHKV_OK;
 }
 
+// Called by tm_destroy: a manager that goes away while attached is detached
+// first, after the data-plane work queued against its slots has finished.
+void okv_manager_destroyed(tiered_manager_t *tm)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited || g.attached != tm) return;
+    tm_set_stream(tm, nullptr);
+    g.attached = nullptr;
+    g.p.attached = 0;
+}
+
 int orchkv_attach_scheduler(tiered_manager_t *tm)
 {
     std::lock_guard<std::recursive_mutex> lk(g.mu);
@@ -759,8 +790,7 @@ int orchkv_append_token_batch(kv_request_ctx_t *const *ctxs, uint32_t n, const v
     if (2 * P + 16 > g.scratch_words) return ORCHKV_ERR_INVALID;
     const size_t bytes = P * H * g.p.row;
     const char *kd, *vd;
-    rc = resolve_input(k, bytes, 0, &kd);
-    if (!rc) rc = resolve_input(v, bytes, bytes, &vd);
+    rc = resolve_kv(k, v, bytes, &kd, &vd);
     if (rc) return rc;
     rc = launch_append_batch(g.p, g.regions_dev, n, L, H, mbph, kd, vd, g.scratch, g.stream);
     if (rc) return rc;

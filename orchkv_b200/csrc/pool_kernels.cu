@@ -591,10 +591,13 @@ __global__ void mig_mark_kernel(const uint32_t *plan_dst, const uint32_t *meta, 
         flags[plan_dst[o]] = 1;
 }
 
+// Per-tile count of set bytes in flags[0 .. n) (n capped at *n_dev if given).
 __global__ void __launch_bounds__(256)
-mig_flag_count_kernel(const uint8_t *flags, uint32_t n, uint32_t *tile_cnt)
+mig_flag_count_kernel(const uint8_t *flags, uint32_t n, const uint32_t *n_dev,
+                      uint32_t *tile_cnt)
 {
     __shared__ uint32_t tmp[33];
+    if (n_dev && *n_dev < n) n = *n_dev;
     const uint32_t base = blockIdx.x * kTileN + threadIdx.x * 4;
     uint32_t c = 0;
 #pragma unroll
@@ -604,8 +607,9 @@ mig_flag_count_kernel(const uint8_t *flags, uint32_t n, uint32_t *tile_cnt)
     if (threadIdx.x == 0) tile_cnt[blockIdx.x] = tot;
 }
 
+// Exclusive scan of the tile counts in place; the total goes to *total if given.
 __global__ void __launch_bounds__(1024)
-mig_tile_scan_kernel(uint32_t *tile_cnt, uint32_t tiles)
+mig_tile_scan_kernel(uint32_t *tile_cnt, uint32_t tiles, uint32_t *total)
 {
     __shared__ uint32_t tmp[33];
     __shared__ uint32_t carry;
@@ -621,6 +625,7 @@ mig_tile_scan_kernel(uint32_t *tile_cnt, uint32_t tiles)
         if (threadIdx.x == 0) carry += tot;
         __syncthreads();
     }
+    if (total && threadIdx.x == 0) *total = carry;
 }
 
 __global__ void __launch_bounds__(256)
@@ -654,37 +659,32 @@ __global__ void mig_assign_kernel(PoolDev p, const uint32_t *meta, const uint32_
     }
 }
 
-// One CTA: list the run starts (list position, first slab) in order.
-// meta[6] = number of runs (may exceed max_runs; only max_runs are written).
-__global__ void __launch_bounds__(1024)
-mig_runs_kernel(const uint8_t *run_flag, const uint32_t *sorted, uint32_t *meta,
-                uint32_t *run_o, uint32_t *run_d, uint32_t max_runs)
+// List the run starts in order: run_o[r] = list position, run_d[r] = its
+// first DRAM slab, for run_flag[o] set, o < meta[0].  Tiles of kTileN list
+// entries, placed by the scanned tile counts; only the first max_runs runs are
+// written (meta[6], the total, may be larger).
+__global__ void __launch_bounds__(256)
+mig_run_write_kernel(const uint8_t *run_flag, const uint32_t *meta, const uint32_t *tile_base,
+                     const uint32_t *sorted, uint32_t *run_o, uint32_t *run_d,
+                     uint32_t max_runs)
 {
     __shared__ uint32_t tmp[33];
-    __shared__ uint32_t carry;
-    const uint32_t done = meta[0];
-    if (threadIdx.x == 0) carry = 0;
-    __syncthreads();
-    for (uint32_t b0 = 0; b0 < done; b0 += blockDim.x * 4) {
-        const uint32_t e0 = b0 + threadIdx.x * 4;
-        uint32_t c = 0;
+    const uint32_t n = meta[0];
+    const uint32_t base = blockIdx.x * kTileN + threadIdx.x * 4;
+    uint8_t f[4];
+    uint32_t c = 0;
 #pragma unroll
-        for (int j = 0; j < 4; j++) c += (e0 + j < done) ? run_flag[e0 + j] : 0u;
-        uint32_t tot;
-        uint32_t pos = carry + block_excl_scan(c, tmp, &tot);
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const uint32_t e = e0 + j;
-            if (e < done && run_flag[e]) {
-                if (pos < max_runs) { run_o[pos] = e; run_d[pos] = sorted[e]; }
-                pos++;
-            }
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) carry += tot;
-        __syncthreads();
+    for (int j = 0; j < 4; j++) {
+        f[j] = (base + j < n) ? run_flag[base + j] : 0;
+        c += f[j];
     }
-    if (threadIdx.x == 0) meta[6] = carry;
+    uint32_t pos = tile_base[blockIdx.x] + block_excl_scan(c, tmp, nullptr);
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+        if (f[j]) {
+            if (pos < max_runs) { run_o[pos] = base + j; run_d[pos] = sorted[base + j]; }
+            pos++;
+        }
 }
 
 // Length of the run of consecutive DRAM slabs that list position o belongs
@@ -940,14 +940,24 @@ int launch_sorted_assign(const PoolDev &p, const MigPlan &mp, const SortScratch 
     const unsigned g = copy_grid(mp.max_n, 256);
     const uint32_t tiles = (p.d_total + kTileN - 1) / kTileN;
     mig_mark_kernel<<<g, 256, 0, s>>>(mp.plan_dst, mp.meta, ss.flags);
-    mig_flag_count_kernel<<<tiles, 256, 0, s>>>(ss.flags, p.d_total, ss.tile_cnt);
-    mig_tile_scan_kernel<<<1, 1024, 0, s>>>(ss.tile_cnt, tiles);
+    mig_flag_count_kernel<<<tiles, 256, 0, s>>>(ss.flags, p.d_total, nullptr, ss.tile_cnt);
+    mig_tile_scan_kernel<<<1, 1024, 0, s>>>(ss.tile_cnt, tiles, nullptr);
     mig_flag_write_kernel<<<tiles, 256, 0, s>>>(ss.flags, p.d_total, ss.tile_cnt, ss.sorted);
     mig_assign_kernel<<<g, 256, 0, s>>>(p, mp.meta, ss.sorted, mp.plan_id, mp.plan_dst,
                                         ss.run_flag);
-    mig_runs_kernel<<<1, 1024, 0, s>>>(ss.run_flag, ss.sorted, mp.meta, ss.run_o, ss.run_d,
-                                       ss.max_runs);
-    note_launches(6);
+    // runs of consecutive slabs among list positions [0, done), done <= min(max_n, d_total)
+    const uint32_t span = mp.max_n < p.d_total ? mp.max_n : p.d_total;
+    const uint32_t rtiles = (span + kTileN - 1) / kTileN;
+    if (rtiles) {
+        mig_flag_count_kernel<<<rtiles, 256, 0, s>>>(ss.run_flag, span, mp.meta, ss.tile_cnt);
+        mig_tile_scan_kernel<<<1, 1024, 0, s>>>(ss.tile_cnt, rtiles, mp.meta + 6);
+        mig_run_write_kernel<<<rtiles, 256, 0, s>>>(ss.run_flag, mp.meta, ss.tile_cnt, ss.sorted,
+                                                    ss.run_o, ss.run_d, ss.max_runs);
+        note_launches(3);
+    } else {
+        OKV_CUDA_TRY(cudaMemsetAsync(mp.meta + 6, 0, 4, s));
+    }
+    note_launches(5);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }

@@ -596,6 +596,7 @@ void tm_destroy(tiered_manager_t *m)
     TmImpl *t = tm_impl(m);
     if (!t) return;
     tm_stop(m);
+    okv_manager_destroyed(m);
     free_device(t);
     delete t;
     m->impl = nullptr;

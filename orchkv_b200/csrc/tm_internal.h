@@ -109,5 +109,7 @@ struct TmImpl {
 };
 
 TmImpl *tm_impl(const tiered_manager_t *m);
+// data plane hook (api.cu): detach m if it is the attached manager
+extern "C" __attribute__((visibility("hidden"))) void okv_manager_destroyed(tiered_manager_t *m);
 int tm_flush_locked(TmImpl *t);
 int tm_refresh_mirror_locked(TmImpl *t);

@@ -334,3 +334,75 @@ def test_append_state_error(dp, cuda):
     kd = cuda.zeros(H * ROW, dtype=cuda.uint8, device="cuda")
     assert L.orchkv_append_token_batch(arr, 1, kd.data_ptr(), kd.data_ptr()) == -8
     assert L.orchkv_request_destroy(ctx) == 0
+
+
+def test_attached_manager_lifetimes(cuda):
+    """A manager attached to the data plane may be destroyed first (the data
+    plane stops touching its slots) or last (it gets its own stream back when
+    the data plane shuts down); both orders leave every call valid."""
+    import orchkv_b200 as o
+    L = o.lib()
+    rng = np.random.default_rng(9)
+    for destroy_manager_first in (True, False):
+        cfg = o.make_config(gpu_pool_bytes=GPU_SLABS * SLAB, dram_pool_bytes=DRAM_SLABS * SLAB,
+                            tokens_per_block=TPB, d_head=D, dtype=1, max_blocks_per_head=32)
+        ext = o.OrchkvConfigExt()
+        ext.max_blocks = 512
+        assert L.orchkv_init_ext(C.byref(cfg), C.byref(ext)) == 0
+        m = o.Manager(tracker_cap=512, max_blocks=4096)
+        assert L.orchkv_attach_scheduler(m.ref) == 0
+        k, v = kv_data(rng, 2, 40)
+        c1 = L.orchkv_request_create(1, 2, 2)
+        assert L.orchkv_prefill(c1, 0, k.ctypes.data, v.ctypes.data, 40) == 0
+        assert L.orchkv_sync() == 0
+        assert m.state()["c_active"].sum() == 6              # 2 heads x 3 blocks registered
+        if destroy_manager_first:
+            m.close()
+            # data-plane work after the manager is gone
+            c2 = L.orchkv_request_create(2, 2, 2)
+            assert L.orchkv_prefill(c2, 1, k.ctypes.data, v.ctypes.data, 40) == 0
+            assert L.orchkv_evict_to_dram(c2, 1, 0, 0) == 0
+            assert L.orchkv_request_destroy(c2) == 0
+            assert L.orchkv_request_destroy(c1) == 0
+            assert L.orchkv_sync() == 0
+            assert L.orchkv_shutdown() == 0
+        else:
+            assert L.orchkv_request_destroy(c1) == 0
+            assert L.orchkv_shutdown() == 0
+            # the manager keeps working on its own stream, then goes away
+            m.report(0, 0.5)
+            m.step_done()
+            assert m.state()["t_active"].sum() == 0          # request teardown unregistered
+            m.close()
+
+
+@pytest.mark.parametrize("kv_src", ["pageable", "pageable_k_device_v"])
+def test_prefill_stages_large_host_inputs(cuda, kv_src):
+    """Pageable K and V larger than the staging buffer of a fresh system: both
+    are staged before the buffer can move (K bytes used to be lost when the
+    buffer grew for V)."""
+    import orchkv_b200 as o
+    L = o.lib()
+    H, n = 4, 16 * 100                                # 1.6 MB each of K and V
+    cfg = o.make_config(gpu_pool_bytes=(H * 100 + 8) * SLAB, dram_pool_bytes=8 * SLAB,
+                        tokens_per_block=TPB, d_head=D, dtype=1, max_blocks_per_head=128)
+    ext = o.OrchkvConfigExt()
+    ext.max_blocks = 512
+    assert L.orchkv_init_ext(C.byref(cfg), C.byref(ext)) == 0
+    try:
+        rng = np.random.default_rng(21)
+        k, v = kv_data(rng, H, n)
+        ctx = L.orchkv_request_create(1, 1, H)
+        vt = cuda.from_numpy(v).cuda() if kv_src == "pageable_k_device_v" else None
+        vp = vt.data_ptr() if vt is not None else v.ctypes.data
+        assert L.orchkv_prefill(ctx, 0, k.ctypes.data, vp, n) == 0
+        base = L.orchkv_gpu_pool_base()
+        for h in range(H):
+            for b in (0, 57, 99):
+                rc, bid, tier, slab, st, tok = info(L, ctx, 0, h, b)
+                assert rc == 0 and tier == 0
+                assert np.array_equal(read_dev(base + slab * SLAB, SLAB),
+                                      expected_slab(k, v, h, b)), (h, b)
+        assert L.orchkv_request_destroy(ctx) == 0
+    finally:
+        assert L.orchkv_shutdown() == 0
