@@ -101,7 +101,11 @@ typedef struct orchkv_config_ext {
     uint32_t max_requests;    /* concurrent requests; default 4096             */
     uint64_t table_entries;   /* block-table entries for all requests; default
                                  max_blocks * 2                                 */
-    uint32_t reserved[12];
+    uint32_t staging_mb;      /* device staging for batched evicts, in MiB;
+                                 default 768 (three 256 MiB slots).  A swap
+                                 overlaps its evict and promote only when the
+                                 whole evict fits.                             */
+    uint32_t reserved[11];
 } orchkv_config_ext_t;
 
 int  orchkv_init_ext(const orchkv_config_t *config, const orchkv_config_ext_t *ext);
@@ -150,6 +154,25 @@ int  orchkv_last_migration_profile(float *pack_ms, unsigned long long *pack_byte
  * into mapped host memory.  All 0 when the zero-copy kernel ran alone. */
 int  orchkv_last_evict_layout(uint32_t *runs, uint32_t *ce_copies,
                               uint32_t *zero_copy_slabs);
+
+/* The same for the promote half of the last batched promote or swap (runs of
+ * consecutive source slabs, copy-engine H2D copies, blocks read zero-copy),
+ * and whether the last swap overlapped its evict and promote. */
+int  orchkv_last_promote_layout(uint32_t *runs, uint32_t *ce_copies,
+                                uint32_t *zero_copy_slabs, int *overlapped);
+
+/* B200: evict one list and promote another in one call, with exactly the
+ * effect of orchkv_evict_batch_to_dram(evict list) followed by
+ * orchkv_promote_batch_to_gpu(promote list).  When the evict fits the
+ * staging buffer (orchkv_config_ext_t.staging_mb) and no promoted block sits
+ * in a DRAM slab this evict fills, the evict's device-to-host and the
+ * promote's host-to-device transfers run at the same time on the two copy
+ * engines.  `result` (device uint32[4], may be NULL) receives {evicted,
+ * evict skipped, promoted, promote skipped}.  Asynchronous. */
+int  orchkv_swap_batch(const uint32_t *evict_ids, const uint32_t *evict_count,
+                       uint32_t max_evict, const uint32_t *promote_ids,
+                       const uint32_t *promote_count, uint32_t max_promote,
+                       uint32_t *result);
 
 /* Device table [n*n_layers][n_kv_heads][ceil(row_len/tpb)] of block ids of
  * the given requests (0xFFFFFFFF where a block does not exist), the layout

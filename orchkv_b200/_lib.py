@@ -30,7 +30,7 @@ class OrchkvConfig(C.Structure):
 
 class OrchkvConfigExt(C.Structure):
     _fields_ = [("max_blocks", u32), ("max_requests", u32), ("table_entries", u64),
-                ("reserved", u32 * 12)]
+                ("staging_mb", u32), ("reserved", u32 * 11)]
 
 
 class OrchkvStats(C.Structure):
@@ -142,6 +142,8 @@ _SIGS = {
     "orchkv_kernel_launches": (C.c_ulonglong, []),
     "orchkv_last_migration_profile": (i32, [P(f32), P(C.c_ulonglong), P(u32), P(f32)]),
     "orchkv_last_evict_layout": (i32, [P(u32), P(u32), P(u32)]),
+    "orchkv_last_promote_layout": (i32, [P(u32), P(u32), P(u32), P(i32)]),
+    "orchkv_swap_batch": (i32, [vp, vp, u32, vp, vp, u32, vp]),
     "orchkv_gpu_pool_base": (vp, []),
     "orchkv_dram_pool_base": (vp, []),
     # scheduler

@@ -71,19 +71,33 @@ struct Sys {
     // staged evict: device staging ring drained to the DRAM tier by the copy
     // engine on its own stream; per-chunk events time the pack kernels
     cudaStream_t copy = nullptr;
-    char *ring = nullptr;
+    char *ring = nullptr;             // ev_copied.size() slots of ring_slabs slabs
     uint32_t ring_slabs = 0;          // slabs per ring slot
-    cudaEvent_t ev_copied[kRing] = {};
+    std::vector<cudaEvent_t> ev_copied;
     cudaEvent_t ev_pk[2 * kMaxChunks] = {};
     cudaEvent_t ev_mig[4] = {};
-    char *sort_mem = nullptr;         // SortScratch storage
-    SortScratch ss;
-    uint32_t *h_runs = nullptr;       // pinned: run_o then run_d
+    cudaEvent_t ev_packed = nullptr;  // all of a swap's victims packed
+    char *sort_mem = nullptr;         // SortScratch storage (evict, then promote)
+    SortScratch ss, ss2;
+    uint32_t *h_runs = nullptr;       // pinned: run_o then run_d (evict)
+    uint32_t *h_runs2 = nullptr;      // pinned: run_o then run_d (promote)
     uint32_t *h_meta = nullptr;       // pinned
+    // staged promote: copy-engine H2D on copy_in into its own ring, unpack
+    // kernels on their own stream
+    cudaStream_t copy_in = nullptr, unpack = nullptr;
+    char *pring = nullptr;            // kRing slots of ring_slabs slabs
+    cudaEvent_t ev_h2d[kMaxChunks] = {};
+    cudaEvent_t ev_unpacked[kRing] = {};
+    cudaEvent_t ev_in_done = nullptr;
+    uint32_t *scratch2 = nullptr;     // the promote plan of a swap
+    size_t scratch2_words = 0;
     uint32_t last_chunks = 0;
     int last_evict_staged = 0, last_promote_timed = 0;
     unsigned long long last_pack_bytes = 0;
     uint32_t last_runs = 0, last_ce_copies = 0, last_zc_slabs = 0;
+    uint32_t last_p_runs = 0, last_p_ce_copies = 0, last_p_zc_slabs = 0;
+    int last_swap_overlapped = 0;
+    uint32_t last_swap_conflicts = 0;
     gpu_tier_t gsnap;
     dram_tier_t dsnap;
     std::vector<uint32_t> gsnap_stack, dsnap_stack;
@@ -253,6 +267,8 @@ void release_all()
         g.p.attached = 0;
     }
     if (g.copy) cudaStreamSynchronize(g.copy);
+    if (g.copy_in) cudaStreamSynchronize(g.copy_in);
+    if (g.unpack) cudaStreamSynchronize(g.unpack);
     if (g.stream) cudaStreamSynchronize(g.stream);
     cudaFree(g.p.gpu_base);
     if (g.p.dram_base) cudaFreeHost(g.p.dram_base);
@@ -266,16 +282,29 @@ void release_all()
     cudaFreeHost(g.h_ctr);
     cudaFreeHost(g.h_meta);
     cudaFree(g.ring);
+    cudaFree(g.pring);
+    cudaFree(g.scratch2);
     cudaFree(g.sort_mem);
     cudaFreeHost(g.h_runs);
+    cudaFreeHost(g.h_runs2);
     g.sort_mem = nullptr;
-    g.h_runs = nullptr;
-    for (auto &e : g.ev_copied) if (e) { cudaEventDestroy(e); e = nullptr; }
+    g.h_runs = g.h_runs2 = nullptr;
+    g.scratch2 = nullptr;
+    g.scratch2_words = 0;
+    for (auto &e : g.ev_copied) if (e) cudaEventDestroy(e);
+    g.ev_copied.clear();
     for (auto &e : g.ev_pk) if (e) { cudaEventDestroy(e); e = nullptr; }
     for (auto &e : g.ev_mig) if (e) { cudaEventDestroy(e); e = nullptr; }
+    for (auto &e : g.ev_h2d) if (e) { cudaEventDestroy(e); e = nullptr; }
+    for (auto &e : g.ev_unpacked) if (e) { cudaEventDestroy(e); e = nullptr; }
+    if (g.ev_in_done) cudaEventDestroy(g.ev_in_done);
+    if (g.ev_packed) cudaEventDestroy(g.ev_packed);
+    g.ev_in_done = g.ev_packed = nullptr;
     if (g.copy) cudaStreamDestroy(g.copy);
-    g.copy = nullptr;
-    g.ring = nullptr;
+    if (g.copy_in) cudaStreamDestroy(g.copy_in);
+    if (g.unpack) cudaStreamDestroy(g.unpack);
+    g.copy = g.copy_in = g.unpack = nullptr;
+    g.ring = g.pring = nullptr;
     g.h_meta = nullptr;
     if (g.own) cudaStreamDestroy(g.own);
     g.p = PoolDev();
@@ -428,26 +457,58 @@ int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
     OKV_CUDA_TRY(cudaMallocHost((void **)&g.h_meta, 16 * 4));
     memset(g.res, 0, sizeof(CompatResult));
     OKV_CUDA_TRY(cudaStreamCreateWithFlags(&g.copy, cudaStreamNonBlocking));
+    OKV_CUDA_TRY(cudaStreamCreateWithFlags(&g.copy_in, cudaStreamNonBlocking));
+    OKV_CUDA_TRY(cudaStreamCreateWithFlags(&g.unpack, cudaStreamNonBlocking));
     g.ring_slabs = (uint32_t)(kChunkBytes / slab);
     if (g.ring_slabs == 0) g.ring_slabs = 1;
-    OKV_CUDA_TRY(cudaMalloc((void **)&g.ring, (size_t)kRing * g.ring_slabs * slab));
+    {
+        // evict staging: kRing slots by default; ext->staging_mb enlarges it so
+        // a whole batch can be packed at once (what lets a swap overlap)
+        const size_t slot_bytes = (size_t)g.ring_slabs * slab;
+        size_t slots = ext && ext->staging_mb ? ((size_t)ext->staging_mb << 20) / slot_bytes : 0;
+        if (slots < (size_t)kRing) slots = kRing;
+        if (slots > (size_t)kMaxChunks) slots = kMaxChunks;
+        if (cudaMalloc((void **)&g.ring, slots * slot_bytes) != cudaSuccess) {
+            fprintf(stderr, "[orchkv] staging ring of %zu MB could not be allocated\n",
+                    (slots * slot_bytes) >> 20);
+            g.ring = nullptr;
+            release_all();
+            return ORCHKV_ERR_CUDA;
+        }
+        g.ev_copied.assign(slots, nullptr);
+        OKV_CUDA_TRY(cudaMalloc((void **)&g.pring, (size_t)kRing * slot_bytes));
+    }
     for (auto &e : g.ev_copied) OKV_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     for (auto &e : g.ev_pk) OKV_CUDA_TRY(cudaEventCreate(&e));
     for (auto &e : g.ev_mig) OKV_CUDA_TRY(cudaEventCreate(&e));
+    for (auto &e : g.ev_h2d) OKV_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    for (auto &e : g.ev_unpacked) OKV_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    OKV_CUDA_TRY(cudaEventCreateWithFlags(&g.ev_in_done, cudaEventDisableTiming));
+    OKV_CUDA_TRY(cudaEventCreateWithFlags(&g.ev_packed, cudaEventDisableTiming));
+    g.scratch2_words = (size_t)p.max_blocks * 3 + p.max_blocks / 1024 + 4096;
+    OKV_CUDA_TRY(cudaMalloc((void **)&g.scratch2, g.scratch2_words * 4));
     {
+        // two sort scratches over the DRAM pool: the evict's assignment and
+        // the promote's source order (with its slab -> position map)
         const size_t dt = p.d_total, tiles = (dt + 1023) / 1024;
-        const size_t bytes = dt * 2 + (tiles + dt + 2 * (size_t)kMaxRuns) * 4 + 8 * 256;
+        const size_t one = dt * 2 + (tiles + dt + 2 * (size_t)kMaxRuns) * 4 + 8 * 256;
+        const size_t bytes = 2 * one + dt * 4 + 256;
         OKV_CUDA_TRY(cudaMalloc((void **)&g.sort_mem, bytes));
         char *q2 = g.sort_mem;
         auto take2 = [&](size_t sz) { char *r = q2; q2 += (sz + 255) & ~size_t(255); return r; };
-        g.ss.flags = (uint8_t *)take2(dt);
-        g.ss.run_flag = (uint8_t *)take2(dt);
-        g.ss.tile_cnt = (uint32_t *)take2(tiles * 4);
-        g.ss.sorted = (uint32_t *)take2(dt * 4);
-        g.ss.run_o = (uint32_t *)take2((size_t)kMaxRuns * 4);
-        g.ss.run_d = (uint32_t *)take2((size_t)kMaxRuns * 4);
-        g.ss.max_runs = kMaxRuns;
+        for (SortScratch *x : {&g.ss, &g.ss2}) {
+            x->flags = (uint8_t *)take2(dt);
+            x->run_flag = (uint8_t *)take2(dt);
+            x->tile_cnt = (uint32_t *)take2(tiles * 4);
+            x->sorted = (uint32_t *)take2(dt * 4);
+            x->run_o = (uint32_t *)take2((size_t)kMaxRuns * 4);
+            x->run_d = (uint32_t *)take2((size_t)kMaxRuns * 4);
+            x->max_runs = kMaxRuns;
+            x->pos_of = nullptr;
+        }
+        g.ss2.pos_of = (uint32_t *)take2(dt * 4);
         OKV_CUDA_TRY(cudaMallocHost((void **)&g.h_runs, (size_t)kMaxRuns * 8));
+        OKV_CUDA_TRY(cudaMallocHost((void **)&g.h_runs2, (size_t)kMaxRuns * 8));
     }
     g.active_requests = 0;
     g.inited = true;
@@ -802,104 +863,274 @@ int orchkv_append_token_batch(kv_request_ctx_t *const *ctxs, uint32_t n, const v
     return (int)err;
 }
 
+}  // extern "C"
+
+namespace {
+
+// Pinned copies of a staged migration's metadata and run list.  false when
+// nothing moved, or the runs do not fit kMaxRuns (the caller falls back).
+bool read_runs(const MigPlan &mp, const SortScratch &ss, uint32_t *h_runs, uint32_t *done,
+               uint32_t *n_runs, int *rc)
+{
+    *rc = ORCHKV_OK;
+    if (cudaMemcpyAsync(g.h_meta, mp.meta, 8 * 4, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess ||
+        cudaStreamSynchronize(g.stream) != cudaSuccess) {
+        *rc = ORCHKV_ERR_CUDA;
+        return false;
+    }
+    *done = g.h_meta[0];
+    *n_runs = g.h_meta[6];
+    if (*done == 0 || *n_runs == 0 || *n_runs > kMaxRuns) return false;
+    if (cudaMemcpyAsync(h_runs, ss.run_o, (size_t)*n_runs * 4, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess ||
+        cudaMemcpyAsync(h_runs + kMaxRuns, ss.run_d, (size_t)*n_runs * 4, cudaMemcpyDeviceToHost, g.stream) != cudaSuccess ||
+        cudaStreamSynchronize(g.stream) != cudaSuccess) {
+        *rc = ORCHKV_ERR_CUDA;
+        return false;
+    }
+    return true;
+}
+
+// Runs shorter than this many slabs move zero-copy: per-copy overhead of the
+// copy engine would exceed their transfer time.
+uint32_t min_run_slabs(uint32_t done, uint32_t n_runs)
+{
+    uint32_t m = (uint32_t)((kCeMinRunBytes + g.p.slab - 1) / g.p.slab);
+    if (m < 2) m = 2;
+    return (n_runs == 1 && done >= m) ? 0 : m;   // 0: one long run, no per-entry lookups
+}
+
+// Drain a staged evict (after launch_sorted_assign and read_runs).  Runs of
+// >= min_len slabs: pack into the ring at HBM speed, copy-engine D2H per run
+// on g.copy.  Shorter runs: written zero-copy.  With pack_all (the whole
+// batch fits the ring) every entry is packed before any drain and `packed`
+// is recorded on g.stream after the last pack: from then on the victims' GPU
+// slabs may be reused.  Returns with g.stream ordered after every drain.
+int evict_drain(const MigPlan &mp, uint32_t done, uint32_t n_runs, bool pack_all,
+                cudaEvent_t packed)
+{
+    const uint32_t *run_o = g.h_runs, *run_d = g.h_runs + kMaxRuns;
+    const size_t slab = g.p.slab;
+    const uint32_t min_len = min_run_slabs(done, n_runs);
+    const uint32_t chunk = g.ring_slabs;
+    const uint32_t nchunks = (done + chunk - 1) / chunk;
+    const uint32_t slots = (uint32_t)g.ev_copied.size();
+    if (nchunks > (uint32_t)kMaxChunks) return launch_migrate_zero_copy(g.p, 0, mp, g.stream);
+    int rc;
+    if (pack_all) {
+        for (uint32_t c = 0; c < nchunks; c++) {
+            const uint32_t pos0 = c * chunk, n = done - pos0 < chunk ? done - pos0 : chunk;
+            OKV_CUDA_TRY(cudaEventRecord(g.ev_pk[2 * c], g.stream));
+            rc = launch_pack(g.p, mp, g.ring + (size_t)c * chunk * slab, pos0, n, g.ss, 0, g.stream);
+            if (rc) return rc;
+            OKV_CUDA_TRY(cudaEventRecord(g.ev_pk[2 * c + 1], g.stream));
+        }
+        OKV_CUDA_TRY(cudaEventRecord(packed, g.stream));
+    }
+    uint32_t r = 0, ce_copies = 0, zc_slabs = 0;
+    for (uint32_t c = 0; c < nchunks; c++) {
+        const uint32_t slot = pack_all ? c : c % slots;
+        const uint32_t pos0 = c * chunk;
+        const uint32_t n = done - pos0 < chunk ? done - pos0 : chunk;
+        char *buf = g.ring + (size_t)slot * chunk * slab;
+        // list positions [pos0, pos0 + n) split into runs of consecutive slabs
+        while (r + 1 < n_runs && run_o[r + 1] <= pos0) r++;
+        uint32_t chunk_short = 0, q_end = r;
+        for (uint32_t q = r; q < n_runs && run_o[q] < pos0 + n; q++) {
+            const uint32_t run_end = q + 1 < n_runs ? run_o[q + 1] : done;
+            const uint32_t a = run_o[q] > pos0 ? run_o[q] : pos0;
+            const uint32_t b = run_end < pos0 + n ? run_end : pos0 + n;
+            if (min_len && run_end - run_o[q] < min_len) chunk_short += b - a;
+            q_end = q + 1;
+        }
+        if (!pack_all) {
+            if (c >= slots) OKV_CUDA_TRY(cudaStreamWaitEvent(g.stream, g.ev_copied[slot], 0));
+            OKV_CUDA_TRY(cudaEventRecord(g.ev_pk[2 * c], g.stream));
+            if (chunk_short < n) {
+                rc = launch_pack(g.p, mp, buf, pos0, n, g.ss, chunk_short ? min_len : 0, g.stream);
+                if (rc) return rc;
+            }
+            OKV_CUDA_TRY(cudaEventRecord(g.ev_pk[2 * c + 1], g.stream));
+        }
+        OKV_CUDA_TRY(cudaStreamWaitEvent(g.copy, g.ev_pk[2 * c + 1], 0));
+        for (uint32_t q = r; q < q_end; q++) {
+            const uint32_t run_end = q + 1 < n_runs ? run_o[q + 1] : done;
+            if (min_len && run_end - run_o[q] < min_len) continue;
+            const uint32_t a = run_o[q] > pos0 ? run_o[q] : pos0;
+            const uint32_t b = run_end < pos0 + n ? run_end : pos0 + n;
+            const uint32_t d0 = run_d[q] + (a - run_o[q]);
+            OKV_CUDA_TRY(cudaMemcpyAsync(g.p.dram_base + (size_t)d0 * slab,
+                                         buf + (size_t)(a - pos0) * slab,
+                                         (size_t)(b - a) * slab, cudaMemcpyDeviceToHost, g.copy));
+            ce_copies++;
+        }
+        if (!pack_all) OKV_CUDA_TRY(cudaEventRecord(g.ev_copied[slot], g.copy));
+        if (chunk_short) {
+            rc = launch_drain_short(g.p, mp, pos0, n, g.ss, min_len, pack_all ? buf : nullptr,
+                                    g.stream);
+            if (rc) return rc;
+            zc_slabs += chunk_short;
+        }
+    }
+    // later work on the stream sees the bytes in the DRAM tier
+    OKV_CUDA_TRY(cudaEventRecord(g.ev_mig[0], g.copy));
+    OKV_CUDA_TRY(cudaStreamWaitEvent(g.stream, g.ev_mig[0], 0));
+    g.last_evict_staged = 1;
+    g.last_chunks = nchunks;
+    g.last_pack_bytes = (unsigned long long)(pack_all ? done : done - zc_slabs) * slab * 2;
+    g.last_runs = n_runs;
+    g.last_ce_copies = ce_copies;
+    g.last_zc_slabs = zc_slabs;
+    return ORCHKV_OK;
+}
+
+// Zero-copy promote of a planned batch, timed by ev_mig[1..2].
+int promote_zero_copy(const MigPlan &mp)
+{
+    OKV_CUDA_TRY(cudaEventRecord(g.ev_mig[1], g.stream));
+    int rc = launch_migrate_zero_copy(g.p, 1, mp, g.stream);
+    OKV_CUDA_TRY(cudaEventRecord(g.ev_mig[2], g.stream));
+    g.last_promote_timed = 1;
+    return rc;
+}
+
+// Drain a staged promote (after launch_sorted_sources on g.ss2 and
+// read_runs into g.h_runs2).  Runs of >= min_len source slabs: copy-engine
+// H2D into the promote ring on g.copy_in, scattered by unpack kernels on
+// g.unpack; shorter runs: one zero-copy kernel.  `dram_ready` (may be null)
+// gates every read of the DRAM tier, `gpu_ready` (may be null) every write
+// into GPU slabs.  Returns with g.stream ordered after the whole promote.
+int promote_drain(const MigPlan &mp, uint32_t done, uint32_t n_runs, cudaEvent_t dram_ready,
+                  cudaEvent_t gpu_ready)
+{
+    const uint32_t *run_o = g.h_runs2, *run_d = g.h_runs2 + kMaxRuns;
+    const size_t slab = g.p.slab;
+    const uint32_t min_len = min_run_slabs(done, n_runs);
+    const uint32_t chunk = g.ring_slabs;
+    const uint32_t nchunks = (done + chunk - 1) / chunk;
+    if (nchunks > (uint32_t)kMaxChunks) return promote_zero_copy(mp);
+    if (dram_ready) {
+        OKV_CUDA_TRY(cudaStreamWaitEvent(g.copy_in, dram_ready, 0));
+        OKV_CUDA_TRY(cudaStreamWaitEvent(g.unpack, dram_ready, 0));
+    }
+    if (gpu_ready) OKV_CUDA_TRY(cudaStreamWaitEvent(g.unpack, gpu_ready, 0));
+    OKV_CUDA_TRY(cudaEventRecord(g.ev_mig[1], g.copy_in));
+    int rc;
+    uint32_t r = 0, ce_copies = 0, zc_slabs = 0;
+    for (uint32_t c = 0; c < nchunks; c++) {
+        const uint32_t slot = c % kRing;
+        const uint32_t j0 = c * chunk;
+        const uint32_t n = done - j0 < chunk ? done - j0 : chunk;
+        char *buf = g.pring + (size_t)slot * chunk * slab;
+        while (r + 1 < n_runs && run_o[r + 1] <= j0) r++;
+        uint32_t chunk_long = 0, q_end = r;
+        for (uint32_t q = r; q < n_runs && run_o[q] < j0 + n; q++) {
+            const uint32_t run_end = q + 1 < n_runs ? run_o[q + 1] : done;
+            const uint32_t a = run_o[q] > j0 ? run_o[q] : j0;
+            const uint32_t b = run_end < j0 + n ? run_end : j0 + n;
+            if (min_len && run_end - run_o[q] < min_len) zc_slabs += b - a;
+            else chunk_long += b - a;
+            q_end = q + 1;
+        }
+        if (chunk_long == 0) continue;
+        if (c >= (uint32_t)kRing) OKV_CUDA_TRY(cudaStreamWaitEvent(g.copy_in, g.ev_unpacked[slot], 0));
+        for (uint32_t q = r; q < q_end; q++) {
+            const uint32_t run_end = q + 1 < n_runs ? run_o[q + 1] : done;
+            if (min_len && run_end - run_o[q] < min_len) continue;
+            const uint32_t a = run_o[q] > j0 ? run_o[q] : j0;
+            const uint32_t b = run_end < j0 + n ? run_end : j0 + n;
+            const uint32_t s0 = run_d[q] + (a - run_o[q]);
+            OKV_CUDA_TRY(cudaMemcpyAsync(buf + (size_t)(a - j0) * slab,
+                                         g.p.dram_base + (size_t)s0 * slab,
+                                         (size_t)(b - a) * slab, cudaMemcpyHostToDevice, g.copy_in));
+            ce_copies++;
+        }
+        OKV_CUDA_TRY(cudaEventRecord(g.ev_h2d[c], g.copy_in));
+        OKV_CUDA_TRY(cudaStreamWaitEvent(g.unpack, g.ev_h2d[c], 0));
+        rc = launch_unpack(g.p, mp, g.ss2, buf, j0, n, min_len, g.unpack);
+        if (rc) return rc;
+        OKV_CUDA_TRY(cudaEventRecord(g.ev_unpacked[slot], g.unpack));
+    }
+    if (zc_slabs) {
+        rc = launch_promote_short(g.p, mp, g.ss2, min_len, g.unpack);
+        if (rc) return rc;
+    }
+    OKV_CUDA_TRY(cudaEventRecord(g.ev_in_done, g.copy_in));
+    OKV_CUDA_TRY(cudaStreamWaitEvent(g.unpack, g.ev_in_done, 0));
+    OKV_CUDA_TRY(cudaEventRecord(g.ev_mig[2], g.unpack));
+    OKV_CUDA_TRY(cudaStreamWaitEvent(g.stream, g.ev_mig[2], 0));
+    g.last_promote_timed = 1;
+    g.last_p_runs = n_runs;
+    g.last_p_ce_copies = ce_copies;
+    g.last_p_zc_slabs = zc_slabs;
+    return ORCHKV_OK;
+}
+
+void reset_profile()
+{
+    g.last_evict_staged = 0;
+    g.last_chunks = 0;
+    g.last_pack_bytes = 0;
+    g.last_runs = g.last_ce_copies = g.last_zc_slabs = 0;
+    g.last_p_runs = g.last_p_ce_copies = g.last_p_zc_slabs = 0;
+    g.last_swap_overlapped = 0;
+    g.last_swap_conflicts = 0;
+}
+
+bool scratch_fits(uint32_t max_n)
+{
+    return (size_t)3 * max_n + max_n / 1024 + 32 <= g.scratch_words;
+}
+
+// Evict a planned batch: staged when large, else the fused zero-copy kernel.
+int evict_planned(const MigPlan &mp, uint32_t max_n)
+{
+    if (max_n >= kStagedMin) {
+        int rc = launch_sorted_assign(g.p, mp, g.ss, g.stream);
+        if (rc) return rc;
+        uint32_t done = 0, n_runs = 0;
+        if (read_runs(mp, g.ss, g.h_runs, &done, &n_runs, &rc))
+            return evict_drain(mp, done, n_runs, false, nullptr);
+        if (rc || done == 0) return rc;
+    }
+    return launch_migrate_zero_copy(g.p, 0, mp, g.stream);
+}
+
+// Promote a planned batch: staged when large (copy engine for long source
+// runs), else the fused zero-copy kernel.
+int promote_planned(const MigPlan &mp, uint32_t max_n, cudaEvent_t ready)
+{
+    if (max_n >= kStagedMin) {
+        int rc = launch_sorted_sources(g.p, mp, g.ss2, g.stream);
+        if (rc) return rc;
+        uint32_t done = 0, n_runs = 0;
+        if (read_runs(mp, g.ss2, g.h_runs2, &done, &n_runs, &rc))
+            return promote_drain(mp, done, n_runs, ready, ready);
+        if (rc || done == 0) return rc;
+    }
+    return promote_zero_copy(mp);
+}
+
+}  // namespace
+
+extern "C" {
+
 int orchkv_evict_batch_to_dram(const uint32_t *ids, const uint32_t *count, uint32_t max_n,
                                uint32_t *result)
 {
     std::lock_guard<std::recursive_mutex> lk(g.mu);
     if (!g.inited) return ORCHKV_ERR_INIT;
     if (max_n && !ids) return ORCHKV_ERR_INVALID;
-    if ((size_t)3 * max_n + max_n / 1024 + 32 > g.scratch_words) return ORCHKV_ERR_INVALID;
-    g.last_evict_staged = 0;
-    g.last_chunks = 0;
-    g.last_pack_bytes = 0;
-    g.last_runs = g.last_ce_copies = g.last_zc_slabs = 0;
+    if (!scratch_fits(max_n)) return ORCHKV_ERR_INVALID;
+    reset_profile();
     MigPlan mp = launch_migrate_plan(g.p, 0, ids, count, max_n, result, g.scratch, g.stream);
     if (mp.rc) return mp.rc;
-    if (max_n >= kStagedMin) {
-        // Large batch: sort the DRAM slabs popped for it and hand them out in
-        // ascending order, pack the victims into a device staging ring at HBM
-        // speed, and let the copy engine drain each slot into the DRAM tier,
-        // one copy per run of consecutive slabs, while the next slot is
-        // packed.  Pool stacks end exactly as after per-block evicts; only
-        // which victim gets which of the popped slabs differs.
-        int rc = launch_sorted_assign(g.p, mp, g.ss, g.stream);
-        if (rc) return rc;
-        OKV_CUDA_TRY(cudaMemcpyAsync(g.h_meta, mp.meta, 8 * 4, cudaMemcpyDeviceToHost, g.stream));
-        OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
-        const uint32_t done = g.h_meta[0], n_runs = g.h_meta[6];
-        if (done == 0) return ORCHKV_OK;
-        const uint32_t chunk = g.ring_slabs;
-        const uint32_t nchunks = (done + chunk - 1) / chunk;
-        if (n_runs >= 1 && n_runs <= kMaxRuns && nchunks <= (uint32_t)kMaxChunks) {
-            uint32_t *run_o = g.h_runs, *run_d = g.h_runs + kMaxRuns;
-            OKV_CUDA_TRY(cudaMemcpyAsync(run_o, g.ss.run_o, (size_t)n_runs * 4,
-                                         cudaMemcpyDeviceToHost, g.stream));
-            OKV_CUDA_TRY(cudaMemcpyAsync(run_d, g.ss.run_d, (size_t)n_runs * 4,
-                                         cudaMemcpyDeviceToHost, g.stream));
-            OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
-            const size_t slab = g.p.slab;
-            uint32_t min_len = (uint32_t)((kCeMinRunBytes + slab - 1) / slab);
-            if (min_len < 2) min_len = 2;
-            if (n_runs == 1 && done >= min_len) min_len = 0;   // one long run: no lookups
-            uint32_t r = 0;                       // first run touching the chunk
-            uint32_t ce_copies = 0, zc_slabs = 0;
-            for (uint32_t c = 0; c < nchunks; c++) {
-                const uint32_t slot = c % kRing;
-                const uint32_t pos0 = c * chunk;
-                const uint32_t n = done - pos0 < chunk ? done - pos0 : chunk;
-                char *buf = g.ring + (size_t)slot * chunk * slab;
-                // list positions [pos0, pos0 + n) split into runs of consecutive
-                // slabs; runs of >= min_len slabs go through the copy engine
-                while (r + 1 < n_runs && run_o[r + 1] <= pos0) r++;
-                uint32_t chunk_short = 0, q_end = r;
-                for (uint32_t q = r; q < n_runs && run_o[q] < pos0 + n; q++) {
-                    const uint32_t run_end = q + 1 < n_runs ? run_o[q + 1] : done;
-                    const uint32_t a = run_o[q] > pos0 ? run_o[q] : pos0;
-                    const uint32_t b = run_end < pos0 + n ? run_end : pos0 + n;
-                    if (min_len && run_end - run_o[q] < min_len) chunk_short += b - a;
-                    q_end = q + 1;
-                }
-                if (c >= (uint32_t)kRing) OKV_CUDA_TRY(cudaStreamWaitEvent(g.stream, g.ev_copied[slot], 0));
-                OKV_CUDA_TRY(cudaEventRecord(g.ev_pk[2 * c], g.stream));
-                if (chunk_short < n) {
-                    rc = launch_pack(g.p, mp, buf, pos0, n, g.ss, chunk_short ? min_len : 0,
-                                     g.stream);
-                    if (rc) return rc;
-                }
-                OKV_CUDA_TRY(cudaEventRecord(g.ev_pk[2 * c + 1], g.stream));
-                OKV_CUDA_TRY(cudaStreamWaitEvent(g.copy, g.ev_pk[2 * c + 1], 0));
-                for (uint32_t q = r; q < q_end; q++) {
-                    const uint32_t run_end = q + 1 < n_runs ? run_o[q + 1] : done;
-                    if (min_len && run_end - run_o[q] < min_len) continue;
-                    const uint32_t a = run_o[q] > pos0 ? run_o[q] : pos0;
-                    const uint32_t b = run_end < pos0 + n ? run_end : pos0 + n;
-                    const uint32_t d0 = run_d[q] + (a - run_o[q]);
-                    OKV_CUDA_TRY(cudaMemcpyAsync(g.p.dram_base + (size_t)d0 * slab,
-                                                 buf + (size_t)(a - pos0) * slab,
-                                                 (size_t)(b - a) * slab, cudaMemcpyDeviceToHost,
-                                                 g.copy));
-                    ce_copies++;
-                }
-                OKV_CUDA_TRY(cudaEventRecord(g.ev_copied[slot], g.copy));
-                if (chunk_short) {
-                    rc = launch_drain_short(g.p, mp, pos0, n, g.ss, min_len, g.stream);
-                    if (rc) return rc;
-                    zc_slabs += chunk_short;
-                }
-            }
-            g.last_runs = n_runs;
-            g.last_ce_copies = ce_copies;
-            g.last_zc_slabs = zc_slabs;
-            // later work on the stream sees the bytes in the DRAM tier
-            OKV_CUDA_TRY(cudaEventRecord(g.ev_mig[0], g.copy));
-            OKV_CUDA_TRY(cudaStreamWaitEvent(g.stream, g.ev_mig[0], 0));
-            g.last_evict_staged = 1;
-            g.last_chunks = nchunks;
-            g.last_pack_bytes = (unsigned long long)(done - zc_slabs) * slab * 2;
-            return ORCHKV_OK;
-        }
-    }
-    return launch_migrate_zero_copy(g.p, 0, mp, g.stream);
+    // Large batch: the DRAM slabs popped for it are sorted and handed out in
+    // ascending order; victims are packed into a device staging ring at HBM
+    // speed and the copy engine drains each slot into the DRAM tier, one copy
+    // per run of consecutive slabs, while the next slot is packed.  Pool
+    // stacks end exactly as after per-block evicts; only which victim gets
+    // which of the popped slabs differs.
+    return evict_planned(mp, max_n);
 }
 
 int orchkv_promote_batch_to_gpu(const uint32_t *ids, const uint32_t *count, uint32_t max_n,
@@ -908,22 +1139,90 @@ int orchkv_promote_batch_to_gpu(const uint32_t *ids, const uint32_t *count, uint
     std::lock_guard<std::recursive_mutex> lk(g.mu);
     if (!g.inited) return ORCHKV_ERR_INIT;
     if (max_n && !ids) return ORCHKV_ERR_INVALID;
-    if ((size_t)3 * max_n + max_n / 1024 + 32 > g.scratch_words) return ORCHKV_ERR_INVALID;
+    if (!scratch_fits(max_n)) return ORCHKV_ERR_INVALID;
+    reset_profile();
     MigPlan mp = launch_migrate_plan(g.p, 1, ids, count, max_n, result, g.scratch, g.stream);
     if (mp.rc) return mp.rc;
-    // Promotion sources are scattered DRAM slabs: one fused kernel reads them
-    // over the host link (mapped pinned memory) and scatters into GPU slabs.
-    OKV_CUDA_TRY(cudaEventRecord(g.ev_mig[1], g.stream));
-    int rc = launch_migrate_zero_copy(g.p, 1, mp, g.stream);
-    OKV_CUDA_TRY(cudaEventRecord(g.ev_mig[2], g.stream));
-    g.last_promote_timed = 1;
-    return rc;
+    // Sources are wherever the blocks sit in the DRAM tier: sorted, long runs
+    // of consecutive slabs go through the copy engine (H2D + unpack), the
+    // rest is read zero-copy by one kernel.
+    return promote_planned(mp, max_n, nullptr);
 }
 
-/* Timing of the last batched evict / promote (synchronises the stream):
- * pack_ms = summed device time of the pack kernels (0 if the zero-copy path
- * ran), pack_bytes = bytes they read + wrote, chunks = staging slots used,
- * promote_ms = device time of the last promote copy kernel. */
+int orchkv_swap_batch(const uint32_t *evict_ids, const uint32_t *evict_count, uint32_t max_e,
+                      const uint32_t *promote_ids, const uint32_t *promote_count,
+                      uint32_t max_p, uint32_t *result)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if ((max_e && !evict_ids) || (max_p && !promote_ids)) return ORCHKV_ERR_INVALID;
+    if (!scratch_fits(max_e) || (size_t)3 * max_p + max_p / 1024 + 32 > g.scratch2_words)
+        return ORCHKV_ERR_INVALID;
+    reset_profile();
+    // Plans in call order: the evict's pops and pushes (and its sorted DRAM
+    // assignment) first, then the promote's, so stacks and locations end as
+    // after the evict list followed by the promote list, block by block.
+    MigPlan me = launch_migrate_plan(g.p, 0, evict_ids, evict_count, max_e, result, g.scratch,
+                                     g.stream);
+    if (me.rc) return me.rc;
+    const bool staged_e = max_e >= kStagedMin;
+    int rc;
+    if (staged_e) {
+        rc = launch_sorted_assign(g.p, me, g.ss, g.stream);
+        if (rc) return rc;
+    }
+    MigPlan mq = launch_migrate_plan(g.p, 1, promote_ids, promote_count, max_p,
+                                     result ? result + 2 : nullptr, g.scratch2, g.stream);
+    if (mq.rc) return mq.rc;
+    const bool staged_p = max_p >= kStagedMin;
+    if (staged_p) {
+        rc = launch_sorted_sources(g.p, mq, g.ss2, g.stream);
+        if (rc) return rc;
+    }
+    uint32_t de = 0, re = 0, dq = 0, rq = 0;
+    bool runs_e = false, runs_p = false;
+    if (staged_e) {
+        runs_e = read_runs(me, g.ss, g.h_runs, &de, &re, &rc);
+        if (rc) return rc;
+    }
+    if (staged_p) {
+        runs_p = read_runs(mq, g.ss2, g.h_runs2, &dq, &rq, &rc);
+        if (rc) return rc;
+    }
+    // Overlap needs (a) every victim packed before the promote writes GPU
+    // slabs the evict freed (the batch fits the ring) and (b) no promoted
+    // block read from a DRAM slab this evict is still filling.
+    bool overlap = runs_e && runs_p && (de + g.ring_slabs - 1) / g.ring_slabs <= g.ev_copied.size();
+    if (overlap) {
+        rc = launch_conflicts(mq, g.ss, g.h_meta + 8, g.stream);
+        if (rc) return rc;
+        OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+        g.last_swap_conflicts = g.h_meta[8];
+        overlap = g.h_meta[8] == 0;
+    }
+    if (overlap) {
+        // evict D2H and promote H2D run at once on the two copy engines
+        rc = evict_drain(me, de, re, true, g.ev_packed);
+        if (rc) return rc;
+        rc = promote_drain(mq, dq, rq, nullptr, g.ev_packed);
+        if (rc) return rc;
+        g.last_swap_overlapped = 1;
+        return ORCHKV_OK;
+    }
+    // one after the other
+    if (runs_e) rc = evict_drain(me, de, re, false, nullptr);
+    else rc = launch_migrate_zero_copy(g.p, 0, me, g.stream);
+    if (rc) return rc;
+    OKV_CUDA_TRY(cudaEventRecord(g.ev_packed, g.stream));
+    if (runs_p) return promote_drain(mq, dq, rq, g.ev_packed, g.ev_packed);
+    return promote_zero_copy(mq);
+}
+
+/* Timing of the last batched evict / promote / swap (synchronises the
+ * stream): pack_ms = summed device time of the evict's pack kernels (0 if
+ * the zero-copy path ran), pack_bytes = bytes they read + wrote, chunks =
+ * staging slots used, promote_ms = device time of the promote, from its
+ * first copy or kernel to its last. */
 int orchkv_last_migration_profile(float *pack_ms, unsigned long long *pack_bytes,
                                   uint32_t *chunks, float *promote_ms)
 {
@@ -956,6 +1255,18 @@ int orchkv_last_evict_layout(uint32_t *runs, uint32_t *ce_copies, uint32_t *zero
     if (runs) *runs = g.last_evict_staged ? g.last_runs : 0;
     if (ce_copies) *ce_copies = g.last_evict_staged ? g.last_ce_copies : 0;
     if (zero_copy_slabs) *zero_copy_slabs = g.last_evict_staged ? g.last_zc_slabs : 0;
+    return ORCHKV_OK;
+}
+
+int orchkv_last_promote_layout(uint32_t *runs, uint32_t *ce_copies, uint32_t *zero_copy_slabs,
+                               int *overlapped)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (runs) *runs = g.last_p_runs;
+    if (ce_copies) *ce_copies = g.last_p_ce_copies;
+    if (zero_copy_slabs) *zero_copy_slabs = g.last_p_zc_slabs;
+    if (overlapped) *overlapped = g.last_swap_overlapped;
     return ORCHKV_OK;
 }
 

@@ -108,6 +108,7 @@ struct SortScratch {
     uint32_t *run_o;     // [max_runs] list position of each run start
     uint32_t *run_d;     // [max_runs] first slab of each run
     uint32_t max_runs;
+    uint32_t *pos_of;    // [d_total] DRAM slab -> list position (staged promote only)
 };
 int launch_sorted_assign(const PoolDev &p, const MigPlan &mp, const SortScratch &ss,
                          cudaStream_t s);
@@ -118,8 +119,28 @@ int launch_pack(const PoolDev &p, const MigPlan &mp, char *staging, uint32_t pos
                 const SortScratch &ss, uint32_t min_len, cudaStream_t s);
 // Entries of [pos0, pos0 + n) in DRAM runs shorter than min_len: written from
 // their GPU slab straight into the DRAM tier (zero-copy).
+// `staged` (may be null): the packed copies of entries [pos0, pos0 + n), read
+// instead of the GPU slabs.
 int launch_drain_short(const PoolDev &p, const MigPlan &mp, uint32_t pos0, uint32_t n,
-                       const SortScratch &ss, uint32_t min_len, cudaStream_t s);
+                       const SortScratch &ss, uint32_t min_len, const char *staged,
+                       cudaStream_t s);
+
+// Staged promote (dir 1 plan): sort the source DRAM slabs (ss.sorted, with
+// ss.pos_of mapping slab -> list position) and list their runs (meta[6]).
+int launch_sorted_sources(const PoolDev &p, const MigPlan &mp, const SortScratch &ss,
+                          cudaStream_t s);
+// Sorted positions [j0, j0 + n) in runs of >= min_len slabs (all if 0):
+// staging entry j - j0 -> the block's GPU slab.
+int launch_unpack(const PoolDev &p, const MigPlan &mp, const SortScratch &ss,
+                  const char *staging, uint32_t j0, uint32_t n, uint32_t min_len, cudaStream_t s);
+// Sorted positions in runs shorter than min_len: DRAM slab -> GPU slab over
+// the host link (no-op when min_len is 0).
+int launch_promote_short(const PoolDev &p, const MigPlan &mp, const SortScratch &ss,
+                         uint32_t min_len, cudaStream_t s);
+// *conflicts = promote sources among the slabs an evict's sorted assignment
+// popped (evict_ss.flags).
+int launch_conflicts(const MigPlan &promote, const SortScratch &evict_ss, uint32_t *conflicts,
+                     cudaStream_t s);
 int launch_id_table(const PoolDev &p, uint32_t *const *regions, uint32_t n, uint32_t L,
                     uint32_t H, uint32_t mbph, uint32_t row_len, uint32_t *out,
                     cudaStream_t s);

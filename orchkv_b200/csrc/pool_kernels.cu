@@ -743,10 +743,13 @@ mig_pack_kernel(const char *src_base, char *staging, unsigned long long slab,
 // straight from their GPU slab to their DRAM slab over the host link
 // (mapped pinned memory): runs that short would cost the copy engine more in
 // per-copy overhead than in transfer time.
+// With `staged` set, entry w is read from staged + w * slab (its packed copy)
+// instead of its GPU slab, which a concurrent promote may already reuse.
 __global__ void __launch_bounds__(256)
 mig_drain_short_kernel(const char *src_base, char *dram_base, unsigned long long slab,
                        const uint32_t *plan_src, const uint32_t *plan_dst, uint32_t pos0,
-                       uint32_t n, const uint32_t *run_o, const uint32_t *meta, uint32_t min_len)
+                       uint32_t n, const uint32_t *run_o, const uint32_t *meta, uint32_t min_len,
+                       const char *staged)
 {
     const unsigned lane = threadIdx.x & 31;
     const unsigned long long nvec = slab >> 4;
@@ -756,9 +759,88 @@ mig_drain_short_kernel(const char *src_base, char *dram_base, unsigned long long
     for (unsigned long long w = warp0; w < n; w += nwarps) {
         const uint32_t o = pos0 + (uint32_t)w;
         if (run_len_at(run_o, n_runs, done, o) >= min_len) continue;
-        copy_slab_warp(src_base + plan_src[o] * slab, dram_base + plan_dst[o] * slab, nvec,
-                       lane);
+        const char *src = staged ? staged + w * slab : src_base + plan_src[o] * slab;
+        copy_slab_warp(src, dram_base + plan_dst[o] * slab, nvec, lane);
     }
+}
+
+// ---- staged promote --------------------------------------------------------
+// The promoted blocks' DRAM slabs are sorted (byte map over the DRAM pool);
+// sorted position j holds slab sorted[j], which list position pos_of[slab]
+// promotes into GPU slab plan_dst[pos_of[slab]].  Runs of consecutive slabs
+// are copied host-to-device by the copy engine into a staging ring and
+// scattered by mig_unpack_kernel; short runs are read zero-copy.
+
+__global__ void mig_src_mark_kernel(const uint32_t *plan_src, const uint32_t *meta,
+                                    uint8_t *flags, uint32_t *pos_of)
+{
+    const uint32_t done = meta[0];
+    for (uint32_t o = blockIdx.x * blockDim.x + threadIdx.x; o < done; o += gridDim.x * blockDim.x) {
+        flags[plan_src[o]] = 1;
+        pos_of[plan_src[o]] = o;
+    }
+}
+
+__global__ void mig_runflag_kernel(const uint32_t *meta, const uint32_t *sorted, uint8_t *run_flag)
+{
+    const uint32_t done = meta[0];
+    for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < done; j += gridDim.x * blockDim.x)
+        run_flag[j] = (j == 0 || sorted[j - 1] + 1 != sorted[j]) ? 1 : 0;
+}
+
+// Sorted positions [j0, j0 + n) in DRAM runs of >= min_len slabs: staging
+// entry (j - j0) goes to its block's GPU slab.
+__global__ void __launch_bounds__(256)
+mig_unpack_kernel(const char *staging, char *gpu_base, unsigned long long slab,
+                  const uint32_t *sorted, const uint32_t *pos_of, const uint32_t *plan_dst,
+                  uint32_t j0, uint32_t n, const uint32_t *run_o, const uint32_t *meta,
+                  uint32_t min_len)
+{
+    const unsigned lane = threadIdx.x & 31;
+    const unsigned long long nvec = slab >> 4;
+    const unsigned long long warp0 = ((unsigned long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const unsigned long long nwarps = ((unsigned long long)gridDim.x * blockDim.x) >> 5;
+    const uint32_t done = meta[0], n_runs = meta[6];
+    for (unsigned long long w = warp0; w < n; w += nwarps) {
+        const uint32_t j = j0 + (uint32_t)w;
+        if (min_len && run_len_at(run_o, n_runs, done, j) < min_len) continue;
+        const uint32_t d = plan_dst[pos_of[sorted[j]]];
+        copy_slab_warp(staging + w * slab, gpu_base + d * slab, nvec, lane);
+    }
+}
+
+// Sorted positions in DRAM runs shorter than min_len: read over the host link
+// (mapped pinned memory) straight into their GPU slabs.
+__global__ void __launch_bounds__(256)
+mig_promote_short_kernel(const char *dram_base, char *gpu_base, unsigned long long slab,
+                         const uint32_t *sorted, const uint32_t *pos_of, const uint32_t *plan_dst,
+                         const uint32_t *run_o, const uint32_t *meta, uint32_t min_len)
+{
+    const unsigned lane = threadIdx.x & 31;
+    const unsigned long long nvec = slab >> 4;
+    const unsigned long long warp0 = ((unsigned long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const unsigned long long nwarps = ((unsigned long long)gridDim.x * blockDim.x) >> 5;
+    const uint32_t done = meta[0], n_runs = meta[6];
+    for (unsigned long long w = warp0; w < done; w += nwarps) {
+        const uint32_t j = (uint32_t)w;
+        if (run_len_at(run_o, n_runs, done, j) >= min_len) continue;
+        const uint32_t s = sorted[j];
+        copy_slab_warp(dram_base + s * slab, gpu_base + plan_dst[pos_of[s]] * slab, nvec, lane);
+    }
+}
+
+// Promote sources that are among the DRAM slabs an evict of the same call
+// just popped (evict_flags, its byte map): the promote must then wait for
+// the evict's bytes to land.  Counted into *conflicts.
+__global__ void mig_conflict_kernel(const uint32_t *plan_src, const uint32_t *meta,
+                                    const uint8_t *evict_flags, uint32_t *conflicts)
+{
+    const uint32_t done = meta[0];
+    uint32_t c = 0;
+    for (uint32_t o = blockIdx.x * blockDim.x + threadIdx.x; o < done; o += gridDim.x * blockDim.x)
+        c += evict_flags[plan_src[o]];
+    c = __reduce_add_sync(0xFFFFFFFFu, c);
+    if ((threadIdx.x & 31) == 0 && c) atomicAdd(conflicts, c);
 }
 
 // ---------------------------------------------------------------------------
@@ -974,12 +1056,76 @@ int launch_pack(const PoolDev &p, const MigPlan &mp, char *staging, uint32_t pos
 }
 
 int launch_drain_short(const PoolDev &p, const MigPlan &mp, uint32_t pos0, uint32_t n,
-                       const SortScratch &ss, uint32_t min_len, cudaStream_t s)
+                       const SortScratch &ss, uint32_t min_len, const char *staged,
+                       cudaStream_t s)
 {
     if (n == 0 || min_len == 0) return ORCHKV_OK;
     mig_drain_short_kernel<<<copy_grid(n, 8), 256, 0, s>>>(p.gpu_base, p.dram_base, p.slab,
                                                             mp.plan_src, mp.plan_dst, pos0, n,
-                                                            ss.run_o, mp.meta, min_len);
+                                                            ss.run_o, mp.meta, min_len, staged);
+    note_launches(1);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_sorted_sources(const PoolDev &p, const MigPlan &mp, const SortScratch &ss,
+                          cudaStream_t s)
+{
+    if (!ss.pos_of) return ORCHKV_ERR_INVALID;
+    OKV_CUDA_TRY(cudaMemsetAsync(ss.flags, 0, p.d_total, s));
+    const unsigned g = copy_grid(mp.max_n, 256);
+    const uint32_t tiles = (p.d_total + kTileN - 1) / kTileN;
+    mig_src_mark_kernel<<<g, 256, 0, s>>>(mp.plan_src, mp.meta, ss.flags, ss.pos_of);
+    mig_flag_count_kernel<<<tiles, 256, 0, s>>>(ss.flags, p.d_total, nullptr, ss.tile_cnt);
+    mig_tile_scan_kernel<<<1, 1024, 0, s>>>(ss.tile_cnt, tiles, nullptr);
+    mig_flag_write_kernel<<<tiles, 256, 0, s>>>(ss.flags, p.d_total, ss.tile_cnt, ss.sorted);
+    mig_runflag_kernel<<<g, 256, 0, s>>>(mp.meta, ss.sorted, ss.run_flag);
+    note_launches(5);
+    const uint32_t span = mp.max_n < p.d_total ? mp.max_n : p.d_total;
+    const uint32_t rtiles = (span + kTileN - 1) / kTileN;
+    if (rtiles) {
+        mig_flag_count_kernel<<<rtiles, 256, 0, s>>>(ss.run_flag, span, mp.meta, ss.tile_cnt);
+        mig_tile_scan_kernel<<<1, 1024, 0, s>>>(ss.tile_cnt, rtiles, mp.meta + 6);
+        mig_run_write_kernel<<<rtiles, 256, 0, s>>>(ss.run_flag, mp.meta, ss.tile_cnt, ss.sorted,
+                                                    ss.run_o, ss.run_d, ss.max_runs);
+        note_launches(3);
+    } else {
+        OKV_CUDA_TRY(cudaMemsetAsync(mp.meta + 6, 0, 4, s));
+    }
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_unpack(const PoolDev &p, const MigPlan &mp, const SortScratch &ss,
+                  const char *staging, uint32_t j0, uint32_t n, uint32_t min_len, cudaStream_t s)
+{
+    if (n == 0) return ORCHKV_OK;
+    mig_unpack_kernel<<<copy_grid(n, 8), 256, 0, s>>>(staging, p.gpu_base, p.slab, ss.sorted,
+                                                       ss.pos_of, mp.plan_dst, j0, n, ss.run_o,
+                                                       mp.meta, min_len);
+    note_launches(1);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_promote_short(const PoolDev &p, const MigPlan &mp, const SortScratch &ss,
+                         uint32_t min_len, cudaStream_t s)
+{
+    if (min_len == 0) return ORCHKV_OK;
+    mig_promote_short_kernel<<<copy_grid(mp.max_n, 8), 256, 0, s>>>(
+        p.dram_base, p.gpu_base, p.slab, ss.sorted, ss.pos_of, mp.plan_dst, ss.run_o, mp.meta,
+        min_len);
+    note_launches(1);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_conflicts(const MigPlan &promote, const SortScratch &evict_ss, uint32_t *conflicts,
+                     cudaStream_t s)
+{
+    OKV_CUDA_TRY(cudaMemsetAsync(conflicts, 0, 4, s));
+    mig_conflict_kernel<<<copy_grid(promote.max_n, 256), 256, 0, s>>>(
+        promote.plan_src, promote.meta, evict_ss.flags, conflicts);
     note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;

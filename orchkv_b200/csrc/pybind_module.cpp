@@ -322,6 +322,17 @@ PYBIND11_MODULE(orchkv_core, m)
                                                  max_n, P<uint32_t>(result));
           },
           py::arg("ids_ptr"), py::arg("count_ptr"), py::arg("max_n"), py::arg("result_ptr") = 0);
+    m.def("swap_batch",
+          [](uintptr_t evict_ids, uintptr_t evict_count, uint32_t max_evict, uintptr_t promote_ids,
+             uintptr_t promote_count, uint32_t max_promote, uintptr_t result) {
+              return orchkv_swap_batch(P<const uint32_t>(evict_ids), P<const uint32_t>(evict_count),
+                                       max_evict, P<const uint32_t>(promote_ids),
+                                       P<const uint32_t>(promote_count), max_promote,
+                                       P<uint32_t>(result));
+          },
+          py::arg("evict_ids_ptr"), py::arg("evict_count_ptr"), py::arg("max_evict"),
+          py::arg("promote_ids_ptr"), py::arg("promote_count_ptr"), py::arg("max_promote"),
+          py::arg("result_ptr") = 0);
     m.def("attach_scheduler",
           [](uintptr_t tm) { return orchkv_attach_scheduler(P<tiered_manager_t>(tm)); },
           py::arg("tm"));
