@@ -174,6 +174,23 @@ int  orchkv_swap_batch(const uint32_t *evict_ids, const uint32_t *evict_count,
                        const uint32_t *promote_count, uint32_t max_promote,
                        uint32_t *result);
 
+/* B200: copy token blocks between a caller's own contiguous KV buffers and
+ * a packed store in one launch.  bufs: host array of n_bufs (<= 1024)
+ * buffer pointers (device memory), each laid out [n_heads][tokens][row_bytes]
+ * with heads head_stride_bytes apart -- e.g. K and V of every layer of the
+ * managers' persistent buffers (python/orchkv/fast_kvcache_manager.py:79-88).
+ * blocks: device array of n_blocks block indices; block b covers tokens
+ * [b*block_tokens, min((b+1)*block_tokens, n_tokens)).  The store (device or
+ * pinned host memory) is laid out [n_blocks][n_bufs][n_heads][block_tokens]
+ * [row_bytes]; rows past n_tokens are left untouched.  dir 0: buffers ->
+ * store, 1: store -> buffers.  row_bytes, head_stride_bytes and every
+ * pointer must be 16-byte aligned.  Asynchronous on `stream` (cudaStream_t). */
+int  orchkv_copy_token_blocks(void *const *bufs, uint32_t n_bufs, uint32_t n_heads,
+                              uint64_t head_stride_bytes, uint32_t row_bytes,
+                              uint32_t block_tokens, uint32_t n_tokens,
+                              const uint32_t *blocks, uint32_t n_blocks, void *store,
+                              int dir, void *stream);
+
 /* Device table [n*n_layers][n_kv_heads][ceil(row_len/tpb)] of block ids of
  * the given requests (0xFFFFFFFF where a block does not exist), the layout
  * tm_report_attn_probs takes.  Asynchronous. */
@@ -186,8 +203,8 @@ int  orchkv_block_info(kv_request_ctx_t *ctx, uint32_t layer_id, uint32_t head_i
                        uint32_t *slab, int *state, uint32_t *token_count);
 int  orchkv_set_block_flags(kv_request_ctx_t *ctx, uint32_t layer_id,
                             uint32_t head_id, uint32_t block_idx, uint8_t flags);
-/* which: 0 = GPU pool, 1 = DRAM pool.  Copies the free stack (total entries)
- * and its top. */
+/* which: 0 = GPU pool, 1 = DRAM pool, 2 = block-id stack.  Copies the free
+ * stack (all entries: pool slabs, or max_blocks ids) and its top. */
 int  orchkv_read_pool(int which, uint32_t *stack_out, uint32_t *top_out);
 /* Location words ((tier << 29) | slab) and states of all max_blocks ids. */
 int  orchkv_read_block_locs(uint32_t *loc_out, uint8_t *state_out);

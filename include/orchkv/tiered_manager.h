@@ -244,6 +244,13 @@ int tm_step_and_classify(tiered_manager_t *m);
 int tm_select_victims(tiered_manager_t *m, uint32_t k, uint32_t *out_ids,
                       uint32_t *out_count);
 
+/* Same, restricted further to slots whose eligible[slot] (device uint8,
+ * tm_capacity() entries, slot = block_id & (capacity - 1)) is non-zero: for
+ * callers that keep their own evicted set, as FastKVCacheManager does
+ * (python/orchkv/fast_kvcache_manager.py:300-318). */
+int tm_select_victims_masked(tiered_manager_t *m, uint32_t k, const uint8_t *eligible,
+                             uint32_t *out_ids, uint32_t *out_count);
+
 /* Same, with k = floor(frac * #candidates) computed on the device. */
 int tm_select_victims_frac(tiered_manager_t *m, float frac, uint32_t *out_ids,
                            uint32_t *out_count, uint32_t max_out);

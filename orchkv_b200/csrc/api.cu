@@ -566,7 +566,8 @@ int orchkv_request_destroy(kv_request_ctx_t *ctx)
     std::lock_guard<std::recursive_mutex> lk(g.mu);
     if (!ctx) return ORCHKV_ERR_INVALID;
     if (!g.inited) { delete ctx; return ORCHKV_ERR_INIT; }
-    int rc = launch_request_free(g.p, req_dev(ctx), g.stream);
+    if ((size_t)3 * ((ctx->region_words + 1023) / 1024) > g.scratch_words) return ORCHKV_ERR_INVALID;
+    int rc = launch_request_free(g.p, req_dev(ctx), g.scratch, g.stream);
     if (rc) return rc;
     OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
     if (ctx->fd >= 0) {                   // orchfs_file_close: close + unlink
@@ -1309,14 +1310,16 @@ int orchkv_read_pool(int which, uint32_t *stack_out, uint32_t *top_out)
 {
     std::lock_guard<std::recursive_mutex> lk(g.mu);
     if (!g.inited) return ORCHKV_ERR_INIT;
-    if (which != 0 && which != 1) return ORCHKV_ERR_INVALID;
+    if (which < 0 || which > 2) return ORCHKV_ERR_INVALID;
     OKV_CUDA_TRY(cudaMemcpyAsync(g.h_ctr, g.p.ctr, sizeof(PoolCounters), cudaMemcpyDeviceToHost, g.stream));
-    const uint32_t total = which == 0 ? g.p.g_total : g.p.d_total;
+    const uint32_t total = which == 0 ? g.p.g_total : which == 1 ? g.p.d_total : g.p.max_blocks;
+    const uint32_t *stack = which == 0 ? g.p.g_stack : which == 1 ? g.p.d_stack : g.p.id_stack;
     if (stack_out)
-        OKV_CUDA_TRY(cudaMemcpyAsync(stack_out, which == 0 ? g.p.g_stack : g.p.d_stack,
-                                     (size_t)total * 4, cudaMemcpyDeviceToHost, g.stream));
+        OKV_CUDA_TRY(cudaMemcpyAsync(stack_out, stack, (size_t)total * 4, cudaMemcpyDeviceToHost,
+                                     g.stream));
     OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
-    if (top_out) *top_out = which == 0 ? g.h_ctr->g_top : g.h_ctr->d_top;
+    if (top_out)
+        *top_out = which == 0 ? g.h_ctr->g_top : which == 1 ? g.h_ctr->d_top : g.h_ctr->id_top;
     return ORCHKV_OK;
 }
 

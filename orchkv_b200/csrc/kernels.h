@@ -63,6 +63,7 @@ struct SelectArgs {
     void *comm_ctx;
     int rank, world;
     uint32_t *gather_buf;  // device [world]
+    const uint8_t *mask;   // coldest mode: optional device [cap]; 0 excludes slot
 };
 
 int launch_select(const SchedDev &d, const SelectScratch &sc, const SelectArgs &a,

@@ -144,6 +144,7 @@ int launch_conflicts(const MigPlan &promote, const SortScratch &evict_ss, uint32
 int launch_id_table(const PoolDev &p, uint32_t *const *regions, uint32_t n, uint32_t L,
                     uint32_t H, uint32_t mbph, uint32_t row_len, uint32_t *out,
                     cudaStream_t s);
-int launch_request_free(const PoolDev &p, const ReqDev &r, cudaStream_t s);
+// scratch: >= 3 * ceil(L*H*mbph / 1024) words.
+int launch_request_free(const PoolDev &p, const ReqDev &r, uint32_t *scratch, cudaStream_t s);
 
 }  // namespace okv

@@ -870,55 +870,109 @@ __global__ void id_table_kernel(PoolDev p, uint32_t *const *regions, uint32_t n,
 // (layer, head, block) order.  One CTA, contiguous chunks per thread.
 // ---------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(1024)
-request_free_kernel(PoolDev p, ReqDev r)
+// Request teardown (src/api/orchkv_api.cu:149-183): every existing block of
+// the request, in table order (layer, head, block), returns its slab to the
+// stack of its tier and its id to the id stack.  Tiles of kTileN table
+// entries: count per tile, scan the three counts, then write in order.
+__device__ __forceinline__ bool req_entry(const PoolDev &p, const ReqDev &r, size_t e, size_t E,
+                                          uint32_t *id)
+{
+    if (e >= E) return false;
+    const uint32_t bi = (uint32_t)(e % r.mbph);
+    const uint32_t l = (uint32_t)(e / ((size_t)r.H * r.mbph));
+    if (bi >= (req_tok(r)[l] + p.tpb - 1) / p.tpb) return false;
+    *id = req_table(r)[e];
+    return *id < p.max_blocks;
+}
+
+__global__ void __launch_bounds__(256)
+req_free_count_kernel(PoolDev p, ReqDev r, uint32_t *tile_cnt)
 {
     __shared__ uint32_t tmp[33];
     const size_t E = (size_t)r.L * r.H * r.mbph;
-    const size_t per = (E + blockDim.x - 1) / blockDim.x;
-    const size_t e0 = threadIdx.x * per;
-    const uint32_t *tok = req_tok(r);
-    const uint32_t *tab = req_table(r);
+    const size_t e0 = (size_t)blockIdx.x * kTileN + threadIdx.x * 4;
     uint32_t ng = 0, nd = 0, ni = 0;
-    for (size_t e = e0; e < e0 + per && e < E; e++) {
-        const uint32_t bi = (uint32_t)(e % r.mbph);
-        const uint32_t l = (uint32_t)(e / ((size_t)r.H * r.mbph));
-        if (bi >= (tok[l] + p.tpb - 1) / p.tpb) continue;
-        const uint32_t id = tab[e];
-        if (id >= p.max_blocks) continue;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        uint32_t id;
+        if (!req_entry(p, r, e0 + j, E, &id)) continue;
         ni++;
         const uint32_t t = loc_tier(p.loc[id]);
         ng += t == TIER_GPU_HBM;
         nd += t == TIER_HOST_DRAM;
     }
     uint32_t tg, td, ti;
-    uint32_t og = block_excl_scan(ng, tmp, &tg);
-    uint32_t od = block_excl_scan(nd, tmp, &td);
-    uint32_t oi = block_excl_scan(ni, tmp, &ti);
+    block_excl_scan(ng, tmp, &tg);
+    block_excl_scan(nd, tmp, &td);
+    block_excl_scan(ni, tmp, &ti);
+    if (threadIdx.x == 0) {
+        tile_cnt[3 * blockIdx.x + 0] = tg;
+        tile_cnt[3 * blockIdx.x + 1] = td;
+        tile_cnt[3 * blockIdx.x + 2] = ti;
+    }
+}
+
+// One CTA: exclusive scan of the per-tile counts into stack positions (old
+// top + offset), then the stack tops move past the pushes.
+__global__ void __launch_bounds__(1024)
+req_free_scan_kernel(PoolDev p, uint32_t *tile_cnt, uint32_t tiles)
+{
+    __shared__ uint32_t tmp[33];
+    __shared__ uint32_t carry[3];
     PoolCounters *c = p.ctr;
-    const uint32_t gtop = c->g_top, dtop = c->d_top, itop = c->id_top;
+    if (threadIdx.x == 0) { carry[0] = c->g_top; carry[1] = c->d_top; carry[2] = c->id_top; }
     __syncthreads();
-    for (size_t e = e0; e < e0 + per && e < E; e++) {
-        const uint32_t bi = (uint32_t)(e % r.mbph);
-        const uint32_t l = (uint32_t)(e / ((size_t)r.H * r.mbph));
-        if (bi >= (tok[l] + p.tpb - 1) / p.tpb) continue;
-        const uint32_t id = tab[e];
-        if (id >= p.max_blocks) continue;
-        const uint32_t w = p.loc[id];
-        if (loc_tier(w) == TIER_GPU_HBM) p.g_stack[gtop + og++] = loc_slab(w);
-        else if (loc_tier(w) == TIER_HOST_DRAM) p.d_stack[dtop + od++] = loc_slab(w);
-        p.id_stack[itop + oi++] = id;
+    for (uint32_t b0 = 0; b0 < tiles; b0 += blockDim.x) {
+        const uint32_t t = b0 + threadIdx.x;
+        for (int k = 0; k < 3; k++) {
+            const uint32_t v = t < tiles ? tile_cnt[3 * t + k] : 0;
+            uint32_t tot;
+            const uint32_t ex = block_excl_scan(v, tmp, &tot);
+            if (t < tiles) tile_cnt[3 * t + k] = carry[k] + ex;
+            __syncthreads();
+            if (threadIdx.x == 0) carry[k] += tot;
+            __syncthreads();
+        }
+    }
+    if (threadIdx.x == 0) {
+        c->live_blocks -= carry[2] - c->id_top;
+        c->g_top = carry[0];
+        c->d_top = carry[1];
+        c->id_top = carry[2];
+    }
+}
+
+__global__ void __launch_bounds__(256)
+req_free_write_kernel(PoolDev p, ReqDev r, const uint32_t *tile_pos)
+{
+    __shared__ uint32_t tmp[33];
+    const size_t E = (size_t)r.L * r.H * r.mbph;
+    const size_t e0 = (size_t)blockIdx.x * kTileN + threadIdx.x * 4;
+    uint32_t ids[4], ws[4];
+    bool ok[4];
+    uint32_t ng = 0, nd = 0, ni = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        ok[j] = req_entry(p, r, e0 + j, E, &ids[j]);
+        ws[j] = ok[j] ? p.loc[ids[j]] : 0;
+        ni += ok[j];
+        ng += ok[j] && loc_tier(ws[j]) == TIER_GPU_HBM;
+        nd += ok[j] && loc_tier(ws[j]) == TIER_HOST_DRAM;
+    }
+    uint32_t og = tile_pos[3 * blockIdx.x + 0] + block_excl_scan(ng, tmp, nullptr);
+    uint32_t od = tile_pos[3 * blockIdx.x + 1] + block_excl_scan(nd, tmp, nullptr);
+    uint32_t oi = tile_pos[3 * blockIdx.x + 2] + block_excl_scan(ni, tmp, nullptr);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        if (!ok[j]) continue;
+        const uint32_t id = ids[j], w = ws[j];
+        if (loc_tier(w) == TIER_GPU_HBM) p.g_stack[og++] = loc_slab(w);
+        else if (loc_tier(w) == TIER_HOST_DRAM) p.d_stack[od++] = loc_slab(w);
+        p.id_stack[oi++] = id;
         p.loc[id] = make_loc(TIER_NONE, 0);
         p.state[id] = KV_STATE_EVICTED;
         p.flags[id] = 0;
         sched_unregister(p, id);
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        c->g_top = gtop + tg;
-        c->d_top = dtop + td;
-        c->id_top = itop + ti;
-        c->live_blocks -= ti;
     }
 }
 
@@ -1154,9 +1208,15 @@ int launch_id_table(const PoolDev &p, uint32_t *const *regions, uint32_t n, uint
     return ORCHKV_OK;
 }
 
-int launch_request_free(const PoolDev &p, const ReqDev &r, cudaStream_t s)
+int launch_request_free(const PoolDev &p, const ReqDev &r, uint32_t *scratch, cudaStream_t s)
 {
-    request_free_kernel<<<1, 1024, 0, s>>>(p, r); note_launches(1);
+    const size_t E = (size_t)r.L * r.H * r.mbph;
+    const uint32_t tiles = (uint32_t)((E + kTileN - 1) / kTileN);
+    if (tiles == 0) return ORCHKV_OK;
+    req_free_count_kernel<<<tiles, 256, 0, s>>>(p, r, scratch);
+    req_free_scan_kernel<<<1, 1024, 0, s>>>(p, scratch, tiles);
+    req_free_write_kernel<<<tiles, 256, 0, s>>>(p, r, scratch);
+    note_launches(3);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }

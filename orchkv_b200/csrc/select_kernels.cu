@@ -62,7 +62,7 @@ __device__ __forceinline__ uint32_t key_prefetch(const SchedDev &d, uint32_t i,
 
 template <int MODE>
 __global__ void __launch_bounds__(kHistThreads)
-sel_pass0_kernel(SchedDev d, float th_gpu, float th_dram, uint32_t *hist)
+sel_pass0_kernel(SchedDev d, float th_gpu, float th_dram, const uint8_t *mask, uint32_t *hist)
 {
     __shared__ uint32_t sh[kBins];
     for (int b = threadIdx.x; b < kBins; b += blockDim.x) sh[b] = 0;
@@ -70,9 +70,10 @@ sel_pass0_kernel(SchedDev d, float th_gpu, float th_dram, uint32_t *hist)
     uint32_t n_el = 0;
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < d.cap;
          i += gridDim.x * blockDim.x) {
-        const uint32_t k = MODE == kSelectColdest   ? key_coldest(d, i)
-                           : MODE == kSelectPrefetch ? key_prefetch(d, i, th_gpu, th_dram)
-                           : (d.tact[i] ? orderable(d.hot[i]) : kKeyInvalid);
+        uint32_t k = MODE == kSelectColdest   ? key_coldest(d, i)
+                     : MODE == kSelectPrefetch ? key_prefetch(d, i, th_gpu, th_dram)
+                     : (d.tact[i] ? orderable(d.hot[i]) : kKeyInvalid);
+        if (MODE == kSelectColdest && mask && !mask[i]) k = kKeyInvalid;
         d.key[i] = k;
         if (k != kKeyInvalid) {
             atomicAdd(&sh[k >> 20], 1u);
@@ -322,11 +323,11 @@ int launch_select(const SchedDev &d, const SelectScratch &sc, const SelectArgs &
     // pass 0: keys + top-12-bit histogram + eligible count
     OKV_CUDA_TRY(cudaMemsetAsync(sc.hist_local, 0, (kBins + 16) * 4, s));
     if (a.mode == kSelectColdest)
-        sel_pass0_kernel<kSelectColdest><<<g, kHistThreads, 0, s>>>(d, a.th_gpu, a.th_dram, sc.hist_local);
+        sel_pass0_kernel<kSelectColdest><<<g, kHistThreads, 0, s>>>(d, a.th_gpu, a.th_dram, a.mask, sc.hist_local);
     else if (a.mode == kSelectPrefetch)
-        sel_pass0_kernel<kSelectPrefetch><<<g, kHistThreads, 0, s>>>(d, a.th_gpu, a.th_dram, sc.hist_local);
+        sel_pass0_kernel<kSelectPrefetch><<<g, kHistThreads, 0, s>>>(d, a.th_gpu, a.th_dram, nullptr, sc.hist_local);
     else
-        sel_pass0_kernel<kSelectExternal><<<g, kHistThreads, 0, s>>>(d, a.th_gpu, a.th_dram, sc.hist_local);
+        sel_pass0_kernel<kSelectExternal><<<g, kHistThreads, 0, s>>>(d, a.th_gpu, a.th_dram, nullptr, sc.hist_local);
     note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     if (multi && a.reduce(sc.hist_local, hg, kBins + 1, s, a.comm_ctx) != ORCHKV_OK)

@@ -918,7 +918,8 @@ int tm_step_and_classify(tiered_manager_t *m)
 }
 
 static int select_common(TmImpl *t, SelectMode mode, uint32_t k, float frac, float thg,
-                         float thd, uint32_t *out_ids, uint32_t *out_count, uint32_t max_out)
+                         float thd, uint32_t *out_ids, uint32_t *out_count, uint32_t max_out,
+                         const uint8_t *mask = nullptr)
 {
     if (!out_ids || !out_count) return ORCHKV_ERR_INVALID;
     std::lock_guard<std::mutex> g(t->mu);
@@ -935,6 +936,7 @@ static int select_common(TmImpl *t, SelectMode mode, uint32_t k, float frac, flo
     a.max_out = max_out;
     a.out_ids = out_ids;
     a.out_count = out_count;
+    a.mask = mask;
     a.world = 1;
     if (t->comm_reduce) {
         a.reduce = t->comm_reduce;
@@ -952,6 +954,15 @@ int tm_select_victims(tiered_manager_t *m, uint32_t k, uint32_t *out_ids, uint32
     TmImpl *t = tm_impl(m);
     if (!t) return ORCHKV_ERR_INVALID;
     return select_common(t, kSelectColdest, k, -1.0f, 0.f, 0.f, out_ids, out_count, k);
+}
+
+int tm_select_victims_masked(tiered_manager_t *m, uint32_t k, const uint8_t *eligible,
+                             uint32_t *out_ids, uint32_t *out_count)
+{
+    TmImpl *t = tm_impl(m);
+    if (!t || !eligible) return ORCHKV_ERR_INVALID;
+    return select_common(t, kSelectColdest, k, -1.0f, 0.f, 0.f, out_ids, out_count, k,
+                         eligible);
 }
 
 int tm_select_victims_frac(tiered_manager_t *m, float frac, uint32_t *out_ids,

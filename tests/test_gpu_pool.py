@@ -406,3 +406,42 @@ def test_prefill_stages_large_host_inputs(cuda, kv_src):
         assert L.orchkv_request_destroy(ctx) == 0
     finally:
         assert L.orchkv_shutdown() == 0
+
+
+def test_request_destroy_returns_slabs_in_table_order(dp, cuda):
+    """Teardown (src/api/orchkv_api.cu:149-183) pushes each existing block's
+    slab onto its tier's stack and its id onto the id stack in (layer, head,
+    block) order; blocks on both tiers, two layers, a partial last block."""
+    o, L = dp
+    rng = np.random.default_rng(17)
+    H, n = 2, 16 * 5 + 7                       # 6 blocks per head, the last partial
+    ctxs = []
+    for r in range(2):
+        c = L.orchkv_request_create(r, 2, H)
+        for layer in range(2):
+            k, v = kv_data(rng, H, n)
+            assert L.orchkv_prefill(c, layer, k.ctypes.data, v.ctypes.data, n) == 0
+        ctxs.append(c)
+    c = ctxs[0]
+    for (l, h, b) in [(0, 1, 2), (1, 0, 0), (1, 1, 5), (0, 0, 4)]:
+        assert L.orchkv_evict_to_dram(c, l, h, b) == 0
+    g0, d0 = pool_state(L, 0, GPU_SLABS), pool_state(L, 1, DRAM_SLABS)
+    want_g, want_d, want_i = list(g0), list(d0), []
+    for l in range(2):
+        for h in range(H):
+            for b in range(6):
+                rc, bid, tier, slab, st, tok = info(L, c, l, h, b)
+                assert rc == 0
+                (want_g if tier == 0 else want_d).append(slab)
+                want_i.append(bid)
+    st = o.OrchkvStats()
+    L.orchkv_get_stats(C.byref(st))
+    blocks_before = st.total_blocks
+    assert L.orchkv_request_destroy(c) == 0
+    assert pool_state(L, 0, GPU_SLABS) == want_g
+    assert pool_state(L, 1, DRAM_SLABS) == want_d
+    ids_top = pool_state(L, 2, 512)
+    assert ids_top[-len(want_i):] == want_i
+    L.orchkv_get_stats(C.byref(st))
+    assert st.total_blocks == blocks_before - 24
+    assert L.orchkv_request_destroy(ctxs[1]) == 0
