@@ -181,15 +181,18 @@ int  orchkv_swap_batch(const uint32_t *evict_ids, const uint32_t *evict_count,
  * managers' persistent buffers (python/orchkv/fast_kvcache_manager.py:79-88).
  * blocks: device array of n_blocks block indices; block b covers tokens
  * [b*block_tokens, min((b+1)*block_tokens, n_tokens)).  The store (device or
- * pinned host memory) is laid out [n_blocks][n_bufs][n_heads][block_tokens]
- * [row_bytes]; rows past n_tokens are left untouched.  dir 0: buffers ->
- * store, 1: store -> buffers.  row_bytes, head_stride_bytes and every
- * pointer must be 16-byte aligned.  Asynchronous on `stream` (cudaStream_t). */
+ * pinned host memory) is laid out [slot][n_bufs][n_heads][block_tokens]
+ * [row_bytes]; the j-th listed block uses slot store_slots[j] (device array,
+ * may be NULL for slot j).  Rows past n_tokens are left untouched.  dir 0:
+ * buffers -> store, 1: store -> buffers.  row_bytes, head_stride_bytes and
+ * every pointer must be 16-byte aligned.  Asynchronous on `stream`
+ * (cudaStream_t).  With n_heads = 1, block_tokens = 1 and row_bytes = one
+ * block's bytes it moves whole blocks of a [num_blocks, ...] cache tensor. */
 int  orchkv_copy_token_blocks(void *const *bufs, uint32_t n_bufs, uint32_t n_heads,
                               uint64_t head_stride_bytes, uint32_t row_bytes,
                               uint32_t block_tokens, uint32_t n_tokens,
                               const uint32_t *blocks, uint32_t n_blocks, void *store,
-                              int dir, void *stream);
+                              const uint32_t *store_slots, int dir, void *stream);
 
 /* Device table [n*n_layers][n_kv_heads][ceil(row_len/tpb)] of block ids of
  * the given requests (0xFFFFFFFF where a block does not exist), the layout

@@ -175,7 +175,7 @@ _SIGS = {
     "tm_select_victims": (i32, [P(TieredManager), u32, vp, vp]),
     "tm_select_victims_frac": (i32, [P(TieredManager), f32, vp, vp, u32]),
     "tm_select_victims_masked": (i32, [P(TieredManager), u32, vp, vp, vp]),
-    "orchkv_copy_token_blocks": (i32, [vp, u32, u32, u64, u32, u32, u32, vp, u32, vp, i32, vp]),
+    "orchkv_copy_token_blocks": (i32, [vp, u32, u32, u64, u32, u32, u32, vp, u32, vp, vp, i32, vp]),
     "tm_select_prefetch": (i32, [P(TieredManager), u32, f32, f32, vp, vp]),
     "tm_get_threshold_state": (i32, [P(TieredManager), P(f32), P(f32), P(u64), P(u64)]),
     "orchkv_select_coldest_noalloc": (i32, [vp, vp, u32, u32, vp, vp, vp]),

@@ -25,7 +25,7 @@ __global__ void __launch_bounds__(256)
 token_block_copy_kernel(const __grid_constant__ BufTable bufs, uint32_t n_bufs, uint32_t n_heads,
                         unsigned long long head_stride, uint32_t row_bytes,
                         uint32_t block_tokens, uint32_t n_tokens, const uint32_t *blocks,
-                        uint32_t n_blocks, char *store, int dir)
+                        uint32_t n_blocks, char *store, const uint32_t *slots, int dir)
 {
     const unsigned lane = threadIdx.x & 31;
     const unsigned long long chunks = (unsigned long long)n_blocks * n_bufs * n_heads;
@@ -41,7 +41,8 @@ token_block_copy_kernel(const __grid_constant__ BufTable bufs, uint32_t n_bufs, 
         if (t0 >= n_tokens) continue;
         const unsigned long long rows = n_tokens - t0 < block_tokens ? n_tokens - t0 : block_tokens;
         char *buf = bufs.p[bi] + h * head_stride + t0 * row_bytes;
-        char *st = store + c * chunk_bytes;
+        const unsigned long long slot = slots ? slots[j] : j;
+        char *st = store + ((slot * n_bufs + bi) * n_heads + h) * chunk_bytes;
         const uint4 *s = reinterpret_cast<const uint4 *>(dir == 0 ? buf : st);
         uint4 *d = reinterpret_cast<uint4 *>(dir == 0 ? st : buf);
         const unsigned long long nvec = rows * row_bytes / 16;
@@ -78,7 +79,7 @@ extern "C" int orchkv_copy_token_blocks(void *const *bufs, uint32_t n_bufs, uint
                                         uint64_t head_stride_bytes, uint32_t row_bytes,
                                         uint32_t block_tokens, uint32_t n_tokens,
                                         const uint32_t *blocks, uint32_t n_blocks, void *store,
-                                        int dir, void *stream)
+                                        const uint32_t *store_slots, int dir, void *stream)
 {
     using namespace okv;
     if (n_blocks == 0) return ORCHKV_OK;
@@ -93,12 +94,13 @@ extern "C" int orchkv_copy_token_blocks(void *const *bufs, uint32_t n_bufs, uint
     }
     char *st = kernel_ptr(store);
     if (!st || (uintptr_t)st % 16 || !kernel_ptr((void *)blocks)) return ORCHKV_ERR_INVALID;
+    if (store_slots && !kernel_ptr((void *)store_slots)) return ORCHKV_ERR_INVALID;
     const unsigned long long chunks = (unsigned long long)n_blocks * n_bufs * n_heads;
     unsigned grid = (unsigned)((chunks + 7) / 8);
     if (grid > 148 * 16) grid = 148 * 16;
     token_block_copy_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
         t, n_bufs, n_heads, head_stride_bytes, row_bytes, block_tokens, n_tokens, blocks,
-        n_blocks, st, dir);
+        n_blocks, st, store_slots, dir);
     note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;

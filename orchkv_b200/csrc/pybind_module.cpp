@@ -370,17 +370,18 @@ PYBIND11_MODULE(orchkv_core, m)
     m.def("copy_token_blocks",
           [](const std::vector<uintptr_t> &bufs, uint32_t n_heads, uint64_t head_stride,
              uint32_t row_bytes, uint32_t block_tokens, uint32_t n_tokens, uintptr_t blocks,
-             uint32_t n_blocks, uintptr_t store, int dir, uintptr_t stream) {
+             uint32_t n_blocks, uintptr_t store, int dir, uintptr_t stream, uintptr_t slots) {
               std::vector<void *> b(bufs.size());
               for (size_t i = 0; i < bufs.size(); i++) b[i] = reinterpret_cast<void *>(bufs[i]);
               return orchkv_copy_token_blocks(b.data(), (uint32_t)b.size(), n_heads, head_stride,
                                               row_bytes, block_tokens, n_tokens,
                                               P<const uint32_t>(blocks), n_blocks, P<void>(store),
-                                              dir, P<void>(stream));
+                                              P<const uint32_t>(slots), dir, P<void>(stream));
           },
           py::arg("bufs"), py::arg("n_heads"), py::arg("head_stride_bytes"), py::arg("row_bytes"),
           py::arg("block_tokens"), py::arg("n_tokens"), py::arg("blocks_ptr"),
-          py::arg("n_blocks"), py::arg("store_ptr"), py::arg("dir"), py::arg("stream") = 0);
+          py::arg("n_blocks"), py::arg("store_ptr"), py::arg("dir"), py::arg("stream") = 0,
+          py::arg("slots_ptr") = 0);
     m.def("tm_select_prefetch",
           [](uintptr_t tm, uint32_t k, float thg, float thd, uintptr_t out, uintptr_t count) {
               return tm_select_prefetch(P<tiered_manager_t>(tm), k, thg, thd, P<uint32_t>(out),
