@@ -50,6 +50,7 @@ EVICT_FRAC, PROMOTE_FRAC = 0.25, 0.05
 # 215.9 MB measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum) on one
 # 8-request launch; the launch streams each request's rows once, so it scales
 SCORE_TRAFFIC_PER_REQUEST = 215.91e6 / 8
+NOMINAL_HBM_GBS = 7700.0          # B200 HBM3e, HGX figure
 
 
 def peaks():
@@ -313,6 +314,10 @@ def run_ours(args, rank, world, local_rank):
     step_ms, phase_acc, score_ms = [], {}, []
     migrated = 0
     launches0 = okv.lib().orchkv_kernel_launches()
+    xch_ms, xch_calls = C.c_float(), C.c_uint32()
+    if comm:                                  # drop the warm-up's exchanges
+        okv.lib().orchkv_comm_exchange_time(comm, C.byref(xch_ms), C.byref(xch_calls))
+    xch = [0.0, 0]
     with ClockSampler(local_rank) as clk:
         launches_timed = 0
         la = launches0
@@ -333,6 +338,10 @@ def run_ours(args, rank, world, local_rank):
             c = wl.h_counts.tolist()
             migrated += c[2] + c[4]
             launches_timed += okv.lib().orchkv_kernel_launches() - la
+            if comm:
+                okv.lib().orchkv_comm_exchange_time(comm, C.byref(xch_ms), C.byref(xch_calls))
+                xch[0] += xch_ms.value
+                xch[1] += xch_calls.value
             wl.restore()
             la = okv.lib().orchkv_kernel_launches()
     # e2e through the C ABI with host inputs
@@ -410,7 +419,8 @@ def run_ours(args, rank, world, local_rank):
                 "kernel": "score (per-block attention mass, tm_report_attn_probs)",
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
                 "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-                "peak_kind": peak_kind, "bytes_per_launch": sb,
+                "peak_kind": peak_kind, "nominal_peak": NOMINAL_HBM_GBS,
+                "frac_nominal": round(achieved / NOMINAL_HBM_GBS, 4), "bytes_per_launch": sb,
                 "ms_per_launch": round(score_avg, 4),
                 "traffic": round(SCORE_TRAFFIC_PER_REQUEST * WL["B"]),
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
@@ -443,6 +453,11 @@ def run_ours(args, rank, world, local_rank):
                                         (evict_bytes + promote_bytes) / (link["both"] * 1e9))
                               / max(phases.get("swap", 1), 1e-9), 4)},
             "phases_ms": phases,
+            "collective": ({"kind": "ncclAllReduce of 16 KB key histograms + ncclAllGather "
+                                    "of tie counts inside each global selection",
+                            "exchanges_per_step": round(xch[1] / args.steps, 1),
+                            "device_ms_per_step": round(xch[0] / args.steps, 4)}
+                           if comm else None),
             "e2e": {"value": round(migrated_total / (e2e_max * 1e-3), 1), "unit": "blocks/s",
                     "ms_per_step": round(e2e_max, 4),
                     "h2d_bytes_per_step": int(wl.probs.numel() * 4 + wl.tok.numel() * 2
@@ -622,7 +637,27 @@ def cpu_baseline_sample(args):
                       f"orchkv_promote_to_gpu of the 5% DRAM reserve + orchkv_append_token, "
                       f"mean of {max(1, min(args.steps, 3))} steps",
             "us_per_step_sample": round(m["step_s"] * 1e6, 1),
-            "phases_s": {k: round(v, 6) for k, v in m.items() if k.endswith("_s")}}
+            "phases_s": {k: round(v, 6) for k, v in m.items() if k.endswith("_s")},
+            "cpu_pack_gbs": cpu_pack_gbs()}
+
+
+def cpu_pack_gbs(n_slabs=1 << 15, pool_slabs=1 << 16):
+    """The CPU form of the evict pack: gather n_slabs random 8 KiB slabs of a
+    host pool (512 MiB) into a pinned buffer with numpy, one thread; GB/s
+    moved (read + written), best of three."""
+    import numpy as np
+    import torch
+    slab = WL["tpb"] * WL["D"] * 4
+    rng = np.random.default_rng(1)
+    pool = np.full((pool_slabs, slab), 7, dtype=np.uint8)
+    dst = torch.zeros(n_slabs, slab, dtype=torch.uint8).pin_memory().numpy()
+    idx = np.sort(rng.choice(pool_slabs, n_slabs, replace=False))
+    best = float("inf")
+    for _ in range(3):
+        t0 = time.perf_counter()
+        dst[:] = pool[idx]
+        best = min(best, time.perf_counter() - t0)
+    return round(2 * n_slabs * slab / best / 1e9, 2)
 
 
 def run_reference(args, rank, world):

@@ -297,6 +297,9 @@ void *orchkv_comm_create(int rank, int world, const unsigned char *id128, double
 int   orchkv_comm_destroy(void *comm);
 int   orchkv_comm_allreduce_u32(void *comm, const uint32_t *send, uint32_t *recv,
                                 uint32_t n, void *stream);
+/* Device time of the communicator's exchanges since the previous call (the
+ * first 64 timed, waits for slower ranks included) and their number; resets. */
+int   orchkv_comm_exchange_time(void *comm, float *ms, uint32_t *calls);
 int   tm_set_comm(tiered_manager_t *m, void *comm);
 
 #ifdef __cplusplus

@@ -184,6 +184,7 @@ _SIGS = {
     "orchkv_comm_create": (vp, [i32, i32, vp, f64]),
     "orchkv_comm_destroy": (i32, [vp]),
     "orchkv_comm_allreduce_u32": (i32, [vp, vp, vp, u32, vp]),
+    "orchkv_comm_exchange_time": (i32, [vp, P(f32), P(u32)]),
     "tm_set_comm": (i32, [P(TieredManager), vp]),
 }
 

@@ -72,12 +72,36 @@ double now_s()
     return (double)ts.tv_sec + ts.tv_nsec * 1e-9;
 }
 
+constexpr int kTimedExchanges = 64;
+
 struct Comm {
     ncclComm_t comm = nullptr;
     int rank = 0, world = 1;
     double timeout = 30.0;
     bool broken = false;
+    // device time of the exchanges since the last read: events around each
+    // NCCL call on its stream (the first kTimedExchanges of them)
+    cudaEvent_t ev[2 * kTimedExchanges] = {};
+    uint32_t n_timed = 0, n_calls = 0;
 };
+
+void time_begin(Comm *c, cudaStream_t s)
+{
+    if (c->n_timed >= (uint32_t)kTimedExchanges) return;
+    cudaEvent_t &e = c->ev[2 * c->n_timed];
+    if (!e && cudaEventCreate(&e) != cudaSuccess) { e = nullptr; return; }
+    cudaEventRecord(e, s);
+}
+
+void time_end(Comm *c, cudaStream_t s)
+{
+    c->n_calls++;
+    if (c->n_timed >= (uint32_t)kTimedExchanges || !c->ev[2 * c->n_timed]) return;
+    cudaEvent_t &e = c->ev[2 * c->n_timed + 1];
+    if (!e && cudaEventCreate(&e) != cudaSuccess) { e = nullptr; return; }
+    cudaEventRecord(e, s);
+    c->n_timed++;
+}
 
 // Wait until a non-blocking NCCL call has been accepted; abort on timeout.
 int settle(Comm *c, ncclResult_t r)
@@ -111,14 +135,20 @@ int reduce_hist(const uint32_t *local, uint32_t *global, uint32_t n, cudaStream_
 {
     Comm *c = (Comm *)ctx;
     if (!c || c->broken || !c->comm) return ORCHKV_ERR_CUDA;
-    return settle(c, nccl.allReduce(local, global, n, ncclUint32, ncclSum, c->comm, s));
+    time_begin(c, s);
+    const int rc = settle(c, nccl.allReduce(local, global, n, ncclUint32, ncclSum, c->comm, s));
+    time_end(c, s);
+    return rc;
 }
 
 int gather_one(const uint32_t *one, uint32_t *all, cudaStream_t s, void *ctx)
 {
     Comm *c = (Comm *)ctx;
     if (!c || c->broken || !c->comm) return ORCHKV_ERR_CUDA;
-    return settle(c, nccl.allGather(one, all, 1, ncclUint32, c->comm, s));
+    time_begin(c, s);
+    const int rc = settle(c, nccl.allGather(one, all, 1, ncclUint32, c->comm, s));
+    time_end(c, s);
+    return rc;
 }
 
 }  // namespace
@@ -160,10 +190,34 @@ void *orchkv_comm_create(int rank, int world, const unsigned char *id_bytes, dou
     return c;
 }
 
+/* Device time spent in this communicator's exchanges (histogram all-reduces
+ * and tie all-gathers, each timed on its stream, waits for slower ranks
+ * included) since the previous call, and how many there were; then starts
+ * over.  Synchronises on the timed events. */
+int orchkv_comm_exchange_time(void *h, float *ms, uint32_t *calls)
+{
+    Comm *c = (Comm *)h;
+    if (!c) return ORCHKV_ERR_INVALID;
+    float total = 0.f;
+    for (uint32_t i = 0; i < c->n_timed; i++) {
+        float x = 0.f;
+        if (cudaEventSynchronize(c->ev[2 * i + 1]) != cudaSuccess ||
+            cudaEventElapsedTime(&x, c->ev[2 * i], c->ev[2 * i + 1]) != cudaSuccess)
+            return ORCHKV_ERR_CUDA;
+        total += x;
+    }
+    if (ms) *ms = total;
+    if (calls) *calls = c->n_calls;
+    c->n_timed = 0;
+    c->n_calls = 0;
+    return ORCHKV_OK;
+}
+
 int orchkv_comm_destroy(void *h)
 {
     Comm *c = (Comm *)h;
     if (!c) return ORCHKV_ERR_INVALID;
+    for (auto &e : c->ev) if (e) cudaEventDestroy(e);
     if (c->comm) {
         if (c->broken) nccl.abort(c->comm);
         else nccl.destroy(c->comm);
