@@ -111,7 +111,8 @@ typedef struct orchkv_config_ext {
 int  orchkv_init_ext(const orchkv_config_t *config, const orchkv_config_ext_t *ext);
 
 /* All data-plane GPU work runs on this stream (cudaStream_t; NULL restores
- * the library's own stream). */
+ * the library's own stream, which is ordered with the legacy default
+ * stream). */
 int  orchkv_set_stream(void *stream);
 int  orchkv_sync(void);
 
@@ -130,8 +131,9 @@ int  orchkv_append_token_batch(kv_request_ctx_t *const *ctxs, uint32_t n,
 
 /* Batched orchkv_evict_to_dram / orchkv_promote_to_gpu over a device list of
  * block ids, with exactly the per-block semantics applied in list order:
- * blocks in the wrong tier (or pinned, for evict) are skipped; once the
- * destination pool is empty the rest fail with TIER_FULL.  `count` (device
+ * blocks in the wrong tier (or pinned, for evict) are skipped, as are
+ * repeats of an id already listed and ids outside the block-id space; once
+ * the destination pool is empty the rest fail with TIER_FULL.  `count` (device
  * uint32*) may be NULL to use max_n.  `result` (device uint32[2], may be NULL)
  * receives {migrated, skipped}.  Asynchronous. */
 int  orchkv_evict_batch_to_dram(const uint32_t *block_ids, const uint32_t *count,

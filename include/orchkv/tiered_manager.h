@@ -187,7 +187,8 @@ void      tm_get_stats(const tiered_manager_t *m, tm_stats_t *out);
 /* ---- B200: stream binding and state access ------------------------------ */
 
 /* Run the manager's GPU work on `stream` (a cudaStream_t; NULL = the
- * manager's own stream).  Replaces tm_notify_attn's implicit ordering. */
+ * manager's own stream, which is ordered with the legacy default stream).
+ * Replaces tm_notify_attn's implicit ordering. */
 int       tm_set_stream(tiered_manager_t *m, void *stream);
 /* Block until all GPU work queued by the manager has finished. */
 int       tm_sync(tiered_manager_t *m);

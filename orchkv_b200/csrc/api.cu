@@ -363,7 +363,10 @@ int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
     g.storage_writes = g.storage_reads = 0;
     g.storage_bytes_written = g.storage_bytes_read = 0;
     OKV_CUDA_TRY(cudaSetDevice(g.device));
-    OKV_CUDA_TRY(cudaStreamCreateWithFlags(&g.own, cudaStreamNonBlocking));
+    // the library's own stream is a blocking one: unless the caller sets a
+    // stream, its work is ordered with the legacy default stream (buffers a
+    // caller fills or reads there need no extra synchronisation)
+    OKV_CUDA_TRY(cudaStreamCreate(&g.own));
     g.stream = g.own;
 
     PoolDev &p = g.p;
@@ -403,7 +406,7 @@ int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
         return ORCHKV_ERR_CUDA;
     }
 
-    const size_t meta = ((size_t)p.g_total + p.d_total + p.max_blocks) * 4 +
+    const size_t meta = ((size_t)p.g_total + p.d_total + 2 * (size_t)p.max_blocks) * 4 +
                         (size_t)p.max_blocks * 6 + sizeof(PoolCounters) + 8 * 256;
     if (cudaMalloc((void **)&g.dev_meta, meta) != cudaSuccess) { release_all(); return ORCHKV_ERR_CUDA; }
     char *q = g.dev_meta;
@@ -412,6 +415,7 @@ int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
     p.d_stack = (uint32_t *)take((size_t)p.d_total * 4);
     p.id_stack = (uint32_t *)take((size_t)p.max_blocks * 4);
     p.loc = (uint32_t *)take((size_t)p.max_blocks * 4);
+    p.first = (uint32_t *)take((size_t)p.max_blocks * 4);
     p.state = (uint8_t *)take(p.max_blocks);
     p.flags = (uint8_t *)take(p.max_blocks);
     p.ctr = (PoolCounters *)take(sizeof(PoolCounters));
@@ -433,6 +437,7 @@ int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
         if (rc) { release_all(); return rc; }
     }
     OKV_CUDA_TRY(cudaMemset(p.loc, 0xFF, (size_t)p.max_blocks * 4));  // tier 7: no block
+    OKV_CUDA_TRY(cudaMemset(p.first, 0xFF, (size_t)p.max_blocks * 4));
     OKV_CUDA_TRY(cudaMemset(p.state, KV_STATE_EVICTED, p.max_blocks));
     OKV_CUDA_TRY(cudaMemset(p.flags, 0, p.max_blocks));
     PoolCounters c0;

@@ -22,6 +22,7 @@ struct PoolDev {
     uint32_t g_total, d_total, max_blocks;
     uint32_t *g_stack, *d_stack, *id_stack;
     uint32_t *loc;                   // (tier << 29) | slab, per block id
+    uint32_t *first;                 // per block id: first list position in a batch (else ~0)
     uint8_t *state, *flags;          // per block id
     PoolCounters *ctr;
     SchedDev sd;                     // attached scheduler (valid if attached)

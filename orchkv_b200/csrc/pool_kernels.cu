@@ -434,9 +434,12 @@ append_write_kernel(PoolDev p, uint32_t *const *regions, uint32_t n, uint32_t L,
 // per-entry plan (metadata + free-stack pushes), then the slab copy.
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ bool mig_valid(const PoolDev &p, int dir, uint32_t id)
+// An entry moves only if it is the first occurrence of its id in the list
+// (a repeat finds the block already on the destination tier, as the
+// per-block loop would) and the block is on the source tier.
+__device__ __forceinline__ bool mig_valid(const PoolDev &p, int dir, uint32_t id, uint32_t e)
 {
-    if (id >= p.max_blocks) return false;
+    if (id >= p.max_blocks || p.first[id] != e) return false;
     const uint32_t w = p.loc[id];
     if (dir == 0) return loc_tier(w) == TIER_GPU_HBM && !(p.flags[id] & KV_FLAG_PIN);
     return loc_tier(w) == TIER_HOST_DRAM;
@@ -459,7 +462,7 @@ mig_count_kernel(PoolDev p, int dir, const uint32_t *ids, const uint32_t *count,
     uint32_t c = 0;
     for (uint32_t j = threadIdx.x; j < kTileN; j += blockDim.x) {
         const uint32_t e = base + j;
-        if (e < n && mig_valid(p, dir, ids[e])) c++;
+        if (e < n && mig_valid(p, dir, ids[e], e)) c++;
     }
     uint32_t tot;
     block_excl_scan(c, tmp, &tot);
@@ -492,8 +495,8 @@ mig_scan_kernel(PoolDev p, int dir, const uint32_t *count, uint32_t max_n, uint3
         uint32_t *src_top = dir == 0 ? &c->g_top : &c->d_top;
         const uint32_t avail = *dst_top;
         uint32_t done = valid < avail ? valid : avail;
-        // ids must be unique; a repeated id would push its slab twice, so the
-        // pushes are bounded by the source stack's free room
+        // repeated ids count once (mig_valid); the pushes stay bounded by
+        // the source stack's free room all the same
         const uint32_t src_room = (dir == 0 ? p.g_total : p.d_total) - *src_top;
         if (done > src_room) done = src_room;
         meta[0] = done;
@@ -526,7 +529,7 @@ mig_plan_kernel(PoolDev p, int dir, const uint32_t *ids, const uint32_t *count,
     for (int j = 0; j < 4; j++) {
         const uint32_t e = e0 + j;
         idv[j] = e < n ? ids[e] : kNoBlock;
-        val[j] = e < n && mig_valid(p, dir, idv[j]);
+        val[j] = e < n && mig_valid(p, dir, idv[j], e);
         c += val[j];
     }
     uint32_t o = tile_base[blockIdx.x] + block_excl_scan(c, tmp, nullptr);
@@ -1036,6 +1039,19 @@ int launch_append_batch(const PoolDev &p, uint32_t *const *regions, uint32_t n, 
     return ORCHKV_OK;
 }
 
+// First list position of every id of a batch (p.first), and its reset.
+__global__ void mig_first_kernel(PoolDev p, const uint32_t *ids, const uint32_t *count,
+                                 uint32_t max_n, int reset)
+{
+    const uint32_t n = list_len(count, max_n);
+    for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) {
+        const uint32_t id = ids[e];
+        if (id >= p.max_blocks) continue;
+        if (reset) p.first[id] = 0xFFFFFFFFu;
+        else atomicMin(&p.first[id], e);
+    }
+}
+
 MigPlan launch_migrate_plan(const PoolDev &p, int dir, const uint32_t *ids,
                             const uint32_t *count, uint32_t max_n, uint32_t *result,
                             uint32_t *scratch, cudaStream_t s)
@@ -1049,11 +1065,18 @@ MigPlan launch_migrate_plan(const PoolDev &p, int dir, const uint32_t *ids,
     mp.plan_id = mp.plan_dst + max_n;          // [max_n]
     mp.max_n = max_n;
     mp.rc = ORCHKV_OK;
-    if (max_n == 0) return mp;
+    if (max_n == 0) {                           // nothing listed: {0 done, 0 skipped}
+        if (result && cudaMemsetAsync(result, 0, 2 * sizeof(uint32_t), s) != cudaSuccess)
+            mp.rc = ORCHKV_ERR_CUDA;
+        return mp;
+    }
+    const unsigned g = copy_grid(max_n, 256);
+    mig_first_kernel<<<g, 256, 0, s>>>(p, ids, count, max_n, 0); note_launches(1);
     mig_count_kernel<<<mp.tiles, 256, 0, s>>>(p, dir, ids, count, max_n, tile_cnt); note_launches(1);
     mig_scan_kernel<<<1, 1024, 0, s>>>(p, dir, count, max_n, mp.tiles, tile_cnt, mp.meta, result); note_launches(1);
     mig_plan_kernel<<<mp.tiles, 256, 0, s>>>(p, dir, ids, count, max_n, tile_cnt, mp.meta,
                                              mp.plan_src, mp.plan_dst, mp.plan_id); note_launches(1);
+    mig_first_kernel<<<g, 256, 0, s>>>(p, ids, count, max_n, 1); note_launches(1);
     if (cudaGetLastError() != cudaSuccess) mp.rc = ORCHKV_ERR_CUDA;
     return mp;
 }

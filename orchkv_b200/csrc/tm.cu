@@ -575,7 +575,8 @@ int tm_init(tiered_manager_t *m, const tm_config_t *cfg)
     t->demote_batch_size = cfg->demote_batch_size;
     t->prefetch_batch_size = cfg->prefetch_batch_size;
     t->max_blocks = cfg->max_blocks > 0 ? cfg->max_blocks : 4096;
-    if (cudaStreamCreateWithFlags(&t->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+    // blocking: ordered with the legacy default stream until tm_set_stream
+    if (cudaStreamCreate(&t->own_stream) != cudaSuccess) {
         delete t;
         return ORCHKV_ERR_CUDA;
     }

@@ -89,6 +89,12 @@ CASES = {
                          threshold_to_dram=0.1, prefetch_budget=5),
         ops=dict(n_ids=180, id_space=256, steps=25, reports=70, tiers=(0, 0, 1, 2, 4),
                  flags=(0, 8), dup_frac=0.3, tier_changes=3)),
+    "sched_slot_collisions": dict(
+        # ids far beyond the tracker capacity: several ids share a slot
+        # (slot = id & (capacity - 1), src/scheduler/attention_tracker.c:27-33)
+        seed=5, cfg=dict(tracker_cap=64, max_blocks=8192),
+        ops=dict(n_ids=200, id_space=2000, steps=20, reports=80, flags=(0, 0, 8),
+                 dup_frac=0.1)),
     "sched_fast_manager_pattern": dict(
         # FastKVCacheManager: ids = block index, sinks registered with tier 1
         # (positional quirk, python/orchkv/fast_kvcache_manager.py:155), every

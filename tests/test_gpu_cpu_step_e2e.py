@@ -155,6 +155,7 @@ def test_cpu_step_end_to_end(cuda, oracle_mod):
         out = cuda.zeros(N, dtype=cuda.int32, device="cuda")
         cnt = cuda.zeros(1, dtype=cuda.int32, device="cuda")
         assert L.tm_select_victims(tm.ref, k, out.data_ptr(), cnt.data_ptr()) == 0
+        assert L.orchkv_sync() == 0
         assert int(cnt.item()) == k
         victims = out[:k].cpu().numpy().view(np.uint32).copy()
         elig = got["c_active"].copy()

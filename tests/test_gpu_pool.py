@@ -226,6 +226,9 @@ def test_batched_migration_equals_sequential(dp, cuda, seed):
     for rnd in range(4):
         ids = rng.choice(live, int(rng.integers(10, 80)), replace=False).astype(np.uint32)
         ids = np.concatenate([ids, np.array([511], np.uint32)])     # an id with no block
+        if seed == 2:                                               # repeated ids
+            ids = np.concatenate([ids, rng.choice(ids, 12)]).astype(np.uint32)
+            rng.shuffle(ids)
         dev_ids = cuda.from_numpy(ids.view(np.int32)).cuda()
         res = cuda.zeros(2, dtype=cuda.int32, device="cuda")
         if rnd % 2 == 0:
@@ -445,3 +448,40 @@ def test_request_destroy_returns_slabs_in_table_order(dp, cuda):
     L.orchkv_get_stats(C.byref(st))
     assert st.total_blocks == blocks_before - 24
     assert L.orchkv_request_destroy(ctxs[1]) == 0
+
+
+def test_batched_edge_cases(dp, cuda):
+    """Empty lists, a device count below max_n, ids past the block-id space
+    and repeated ids: skipped exactly as the per-block calls would skip them
+    (unknown id -> not on the tier), nothing else moves."""
+    o, L = dp
+    rng = np.random.default_rng(23)
+    H, n = 2, 16 * 4
+    k, v = kv_data(rng, H, n)
+    c = L.orchkv_request_create(1, 1, H)
+    assert L.orchkv_prefill(c, 0, k.ctypes.data, v.ctypes.data, n) == 0
+    g0, d0 = pool_state(L, 0, GPU_SLABS), pool_state(L, 1, DRAM_SLABS)
+    res = cuda.full((4,), -1, dtype=cuda.int32, device="cuda")
+    empty = cuda.zeros(1, dtype=cuda.int32, device="cuda")
+    assert L.orchkv_evict_batch_to_dram(empty.data_ptr(), None, 0, res.data_ptr()) == 0
+    assert L.orchkv_promote_batch_to_gpu(empty.data_ptr(), None, 0, res.data_ptr()) == 0
+    assert L.orchkv_swap_batch(empty.data_ptr(), None, 0, empty.data_ptr(), None, 0,
+                               res.data_ptr()) == 0
+    assert L.orchkv_sync() == 0
+    assert res.cpu().tolist() == [0, 0, 0, 0]
+    assert pool_state(L, 0, GPU_SLABS) == g0 and pool_state(L, 1, DRAM_SLABS) == d0
+    # count 2 of a 5-entry list; then unknown and repeated ids
+    ids = cuda.tensor([0, 1, 2, 3, 4], dtype=cuda.int32, device="cuda")
+    cnt = cuda.tensor([2], dtype=cuda.int32, device="cuda")
+    assert L.orchkv_evict_batch_to_dram(ids.data_ptr(), cnt.data_ptr(), 5, res.data_ptr()) == 0
+    assert L.orchkv_sync() == 0
+    assert res.cpu().tolist()[:2] == [2, 0]
+    odd = cuda.tensor([1 << 30, 0, 0, 511, 5], dtype=cuda.int32, device="cuda")
+    assert L.orchkv_promote_batch_to_gpu(odd.data_ptr(), None, 5, res.data_ptr()) == 0
+    assert L.orchkv_sync() == 0
+    # id 0 (on DRAM) comes back once; its repeat, the unknown ids and id 5
+    # (on the GPU) are skipped
+    assert res.cpu().tolist()[:2] == [1, 4]
+    rc, bid, tier, slab, st, tok = info(L, c, 0, 0, 0)
+    assert bid == 0 and tier == 0
+    assert L.orchkv_request_destroy(c) == 0

@@ -151,6 +151,7 @@ def _select(okv, cuda, m, k, mode="victims", thg=0.0, thd=0.0):
     else:
         rc = okv.lib().tm_select_prefetch(m.ref, k, thg, thd, out.data_ptr(), cnt.data_ptr())
     assert rc == 0
+    assert okv.lib().tm_sync(m.ref) == 0
     c = int(cnt.item())
     return out[:c].cpu().numpy().view(np.uint32).copy()
 
