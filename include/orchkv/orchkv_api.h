@@ -141,6 +141,24 @@ int  orchkv_evict_batch_to_dram(const uint32_t *block_ids, const uint32_t *count
 int  orchkv_promote_batch_to_gpu(const uint32_t *block_ids, const uint32_t *count,
                                  uint32_t max_n, uint32_t *result);
 
+/* B200: orchkv_evict_to_storage / orchkv_promote_from_storage /
+ * orchkv_evict_cold over a host list of n (layer, head, block) triples of one
+ * request (lhb[3*i .. 3*i+2]), with the per-block semantics applied in list
+ * order: entries not on the source tier (DRAM; storage; GPU for
+ * evict_cold), pinned (evicts), repeated or naming no block are skipped, and
+ * a promote that finds the DRAM pool empty skips the rest.  File I/O goes in
+ * offset order; entries at consecutive offsets of the reference's file layout
+ * move in one pwritev / preadv of up to 1 MiB straight from / into their
+ * DRAM slabs.  result (host uint32[2], may be NULL) = {moved, skipped}.
+ * Synchronous.  ORCHKV_ERR_IO when a write or read fails: no entry of the
+ * call is committed (the file may hold part of the data). */
+int  orchkv_evict_batch_to_storage(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t n,
+                                   uint32_t *result);
+int  orchkv_promote_batch_from_storage(kv_request_ctx_t *ctx, const uint32_t *lhb,
+                                       uint32_t n, uint32_t *result);
+int  orchkv_evict_cold_batch(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t n,
+                             uint32_t *result);
+
 /* Device-side timing of the last batched evict / promote (synchronises):
  * pack_ms sums the pack kernels of a staged (copy-engine) evict, pack_bytes
  * are the bytes they read and wrote, chunks the staging slots used (0 when the

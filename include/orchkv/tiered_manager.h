@@ -213,7 +213,9 @@ int       tm_read_state(tiered_manager_t *m, float *sum, float *ema,
  *   lens       device uint32 [n_rows] valid tokens per row, or NULL (= row_len)
  *   block_ids  device uint32 [n_rows][n_kv_heads][ceil(row_len/tpb)]: the block
  *              id receiving the mass of (row, kv head, token block);
- *              0xFFFFFFFF = none.  Ids must be unique within one call.
+ *              0xFFFFFFFF = none.  Within one call the ids must map to
+ *              distinct tracker slots (slot = id & (capacity - 1)): unique
+ *              ids below the tracker capacity do; aliasing ids would race.
  *
  * mass(row,h,b) = sum over the n_q_heads/n_kv_heads query heads of KV group h
  * and the tokens of block b of probs.  A block's per-step sum, max and last

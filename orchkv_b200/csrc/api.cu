@@ -14,7 +14,11 @@
 #include <stdlib.h>
 #include <string.h>
 #include <sys/stat.h>
+#include <sys/uio.h>
 #include <unistd.h>
+
+#include <algorithm>
+#include <unordered_set>
 
 #include <map>
 #include <mutex>
@@ -81,6 +85,7 @@ struct Sys {
     SortScratch ss, ss2;
     uint32_t *h_runs = nullptr;       // pinned: run_o then run_d (evict)
     uint32_t *h_runs2 = nullptr;      // pinned: run_o then run_d (promote)
+    char *h_cold = nullptr;           // pinned, mapped: staging of batched cold evicts
     uint32_t *h_meta = nullptr;       // pinned
     // staged promote: copy-engine H2D on copy_in into its own ring, unpack
     // kernels on their own stream
@@ -287,6 +292,8 @@ void release_all()
     cudaFree(g.sort_mem);
     cudaFreeHost(g.h_runs);
     cudaFreeHost(g.h_runs2);
+    if (g.h_cold) cudaFreeHost(g.h_cold);
+    g.h_cold = nullptr;
     g.sort_mem = nullptr;
     g.h_runs = g.h_runs2 = nullptr;
     g.scratch2 = nullptr;
@@ -362,6 +369,11 @@ int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
     mkdir_p(g.base_dir);
     g.storage_writes = g.storage_reads = 0;
     g.storage_bytes_written = g.storage_bytes_read = 0;
+    // any early return below releases what was allocated so far
+    struct InitGuard {
+        bool ok = false;
+        ~InitGuard() { if (!ok) release_all(); }
+    } guard;
     OKV_CUDA_TRY(cudaSetDevice(g.device));
     // the library's own stream is a blocking one: unless the caller sets a
     // stream, its work is ordered with the legacy default stream (buffers a
@@ -517,6 +529,7 @@ int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
     }
     g.active_requests = 0;
     g.inited = true;
+    guard.ok = true;
     return ORCHKV_OK;
 }
 
@@ -1273,6 +1286,256 @@ int orchkv_last_promote_layout(uint32_t *runs, uint32_t *ce_copies, uint32_t *ze
     if (ce_copies) *ce_copies = g.last_p_ce_copies;
     if (zero_copy_slabs) *zero_copy_slabs = g.last_p_zc_slabs;
     if (overlapped) *overlapped = g.last_swap_overlapped;
+    return ORCHKV_OK;
+}
+
+// ---- batched storage moves ----------------------------------------------------
+
+namespace {
+
+constexpr size_t kStorageRunBytes = 1u << 20;   // one pwritev / preadv moves up to 1 MiB
+
+struct LhbEntry {
+    uint32_t pos;        // list position
+    uint32_t id, slab;   // block id, DRAM slab
+    off_t off;           // file offset (reference layout)
+};
+
+// Look up a request's (layer, head, block) triples: host out[3n] =
+// {id, loc word, flags} per entry.
+int lookup_lhb(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t n, std::vector<uint32_t> &out)
+{
+    if ((size_t)6 * n + 32 > g.scratch_words) return ORCHKV_ERR_INVALID;
+    uint32_t *d_in = g.scratch, *d_out = g.scratch + (size_t)3 * n;
+    OKV_CUDA_TRY(cudaMemcpyAsync(d_in, lhb, (size_t)12 * n, cudaMemcpyHostToDevice, g.stream));
+    int rc = launch_lhb_lookup(g.p, req_dev(ctx), d_in, n, d_out, g.stream);
+    if (rc) return rc;
+    out.resize((size_t)3 * n);
+    OKV_CUDA_TRY(cudaMemcpyAsync(out.data(), d_out, (size_t)12 * n, cudaMemcpyDeviceToHost, g.stream));
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    return ORCHKV_OK;
+}
+
+// Write (evict) or read (promote) entries between their DRAM slabs and the
+// request's file: sorted by file offset, consecutive offsets go out in one
+// pwritev / preadv of up to kStorageRunBytes, straight from / into the slabs.
+bool storage_io(bool write, int fd, std::vector<LhbEntry> e)
+{
+    std::sort(e.begin(), e.end(), [](const LhbEntry &a, const LhbEntry &b) { return a.off < b.off; });
+    const size_t slab = g.p.slab;
+    size_t per_call = kStorageRunBytes / slab;
+    if (per_call < 1) per_call = 1;
+    if (per_call > (size_t)IOV_MAX) per_call = IOV_MAX;
+    std::vector<iovec> iov(per_call);
+    size_t i = 0;
+    while (i < e.size()) {
+        size_t k = 0;
+        const off_t off0 = e[i].off;
+        while (i + k < e.size() && k < per_call &&
+               e[i + k].off == off0 + (off_t)(k * slab)) {
+            iov[k].iov_base = g.p.dram_base + (size_t)e[i + k].slab * slab;
+            iov[k].iov_len = slab;
+            k++;
+        }
+        // move all k slabs, resuming after short transfers
+        size_t done = 0, left = k * slab;
+        iovec *v = iov.data();
+        int cnt = (int)k;
+        while (left > 0) {
+            const ssize_t r = write ? pwritev(fd, v, cnt, off0 + (off_t)done)
+                                    : preadv(fd, v, cnt, off0 + (off_t)done);
+            if (r < 0) {
+                if (errno == EINTR) continue;
+                return false;
+            }
+            if (r == 0) return false;      // short read: a slab that was never written
+            done += (size_t)r;
+            left -= (size_t)r;
+            size_t adv = (size_t)r;
+            while (cnt > 0 && adv >= v->iov_len) { adv -= v->iov_len; v++; cnt--; }
+            if (cnt > 0 && adv) {
+                v->iov_base = (char *)v->iov_base + adv;
+                v->iov_len -= adv;
+            }
+        }
+        i += k;
+    }
+    return true;
+}
+
+// Upload the committed entries (list order) and apply them on the device.
+int storage_commit(const std::vector<LhbEntry> &e, int dir)
+{
+    const size_t n = e.size();
+    if (n == 0) return ORCHKV_OK;
+    std::vector<uint32_t> h(2 * n);
+    for (size_t j = 0; j < n; j++) {
+        h[j] = e[j].id;
+        h[n + j] = e[j].slab;
+    }
+    OKV_CUDA_TRY(cudaMemcpyAsync(g.scratch, h.data(), 8 * n, cudaMemcpyHostToDevice, g.stream));
+    int rc = launch_storage_commit(g.p, g.scratch, g.scratch + n, (uint32_t)n, dir, g.stream);
+    if (rc) return rc;
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    return ORCHKV_OK;
+}
+
+// Entries of `lhb` on `tier` (and not pinned, for evicts), first occurrence
+// of each block only, in list order.
+std::vector<LhbEntry> pick(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t n,
+                           const std::vector<uint32_t> &look, bool from_dram)
+{
+    std::vector<LhbEntry> v;
+    std::unordered_set<uint32_t> seen;
+    for (uint32_t i = 0; i < n; i++) {
+        const uint32_t id = look[3 * i], w = look[3 * i + 1], f = look[3 * i + 2];
+        if (id == kNoBlock || !seen.insert(id).second) continue;
+        const uint32_t t = loc_tier(w);
+        if (from_dram ? (t != TIER_HOST_DRAM || (f & KV_FLAG_PIN))
+                      : (t != TIER_NVM && t != TIER_SSD))
+            continue;
+        v.push_back(LhbEntry{i, id, loc_slab(w),
+                             storage_offset(ctx, lhb[3 * i], lhb[3 * i + 1], lhb[3 * i + 2])});
+    }
+    return v;
+}
+
+int evict_batch_to_storage_locked(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t n,
+                                  uint32_t *result)
+{
+    if (result) { result[0] = 0; result[1] = n; }
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (!ctx || (n && !lhb)) return ORCHKV_ERR_INVALID;
+    if (n == 0) return ORCHKV_OK;
+    if (ctx->fd < 0) return ORCHKV_ERR_INIT;
+    std::vector<uint32_t> look;
+    int rc = lookup_lhb(ctx, lhb, n, look);
+    if (rc) return rc;
+    std::vector<LhbEntry> e = pick(ctx, lhb, n, look, true);
+    if (!storage_io(true, ctx->fd, e)) return ORCHKV_ERR_IO;
+    rc = storage_commit(e, 0);
+    if (rc) return rc;
+    g.storage_writes += e.size();
+    g.storage_bytes_written += e.size() * g.p.slab;
+    if (result) { result[0] = (uint32_t)e.size(); result[1] = n - (uint32_t)e.size(); }
+    return ORCHKV_OK;
+}
+
+}  // namespace
+
+int orchkv_evict_batch_to_storage(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t n,
+                                  uint32_t *result)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    return evict_batch_to_storage_locked(ctx, lhb, n, result);
+}
+
+int orchkv_promote_batch_from_storage(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t n,
+                                      uint32_t *result)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (result) { result[0] = 0; result[1] = n; }
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (!ctx || (n && !lhb)) return ORCHKV_ERR_INVALID;
+    if (n == 0) return ORCHKV_OK;
+    if (ctx->fd < 0) return ORCHKV_ERR_INIT;
+    std::vector<uint32_t> look;
+    int rc = lookup_lhb(ctx, lhb, n, look);
+    if (rc) return rc;
+    std::vector<LhbEntry> e = pick(ctx, lhb, n, look, false);
+    // each promote pops the DRAM stack's top slab, in list order; once it is
+    // empty the rest are skipped (ORCHKV_ERR_TIER_FULL per block)
+    OKV_CUDA_TRY(cudaMemcpyAsync(g.h_ctr, g.p.ctr, sizeof(PoolCounters), cudaMemcpyDeviceToHost,
+                                 g.stream));
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    const uint32_t top = g.h_ctr->d_top;
+    if (e.size() > top) e.resize(top);
+    if (!e.empty()) {
+        std::vector<uint32_t> pops(e.size());
+        OKV_CUDA_TRY(cudaMemcpyAsync(pops.data(), g.p.d_stack + (top - e.size()),
+                                     4 * e.size(), cudaMemcpyDeviceToHost, g.stream));
+        OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+        for (size_t j = 0; j < e.size(); j++) e[j].slab = pops[e.size() - 1 - j];
+    }
+    if (!storage_io(false, ctx->fd, e)) return ORCHKV_ERR_IO;
+    rc = storage_commit(e, 1);
+    if (rc) return rc;
+    g.storage_reads += e.size();
+    g.storage_bytes_read += e.size() * g.p.slab;
+    if (result) { result[0] = (uint32_t)e.size(); result[1] = n - (uint32_t)e.size(); }
+    return ORCHKV_OK;
+}
+
+int orchkv_evict_cold_batch(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t n,
+                            uint32_t *result)
+{
+    // per block, orchkv_evict_cold = orchkv_evict_to_dram then
+    // orchkv_evict_to_storage (src/api/orchkv_api.cu:508-516): a GPU block
+    // passes through the DRAM stack's top slab and the slab goes back, so a
+    // run of them leaves the DRAM stack as it was and pushes the GPU slabs in
+    // list order.  Here the victims are gathered (zero-copy) into a pinned
+    // staging buffer and written from there.
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (result) { result[0] = 0; result[1] = n; }
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (!ctx || (n && !lhb)) return ORCHKV_ERR_INVALID;
+    if (n == 0) return ORCHKV_OK;
+    std::vector<uint32_t> look;
+    int rc = lookup_lhb(ctx, lhb, n, look);
+    if (rc) return rc;
+    std::vector<LhbEntry> e;
+    std::unordered_set<uint32_t> seen;
+    for (uint32_t i = 0; i < n; i++) {
+        const uint32_t id = look[3 * i], w = look[3 * i + 1], f = look[3 * i + 2];
+        if (id == kNoBlock || !seen.insert(id).second) continue;
+        if (loc_tier(w) != TIER_GPU_HBM || (f & KV_FLAG_PIN)) continue;
+        e.push_back(LhbEntry{i, id, loc_slab(w),
+                             storage_offset(ctx, lhb[3 * i], lhb[3 * i + 1], lhb[3 * i + 2])});
+    }
+    if (e.empty()) return ORCHKV_OK;
+    if (ctx->fd < 0) return ORCHKV_ERR_INIT;
+    OKV_CUDA_TRY(cudaMemcpyAsync(g.h_ctr, g.p.ctr, sizeof(PoolCounters), cudaMemcpyDeviceToHost,
+                                 g.stream));
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    if (g.h_ctr->d_top == 0) return ORCHKV_OK;      // no DRAM slab to pass through: TIER_FULL
+    // stage in file-offset order, in chunks of the pinned staging buffer
+    std::vector<LhbEntry> io = e;
+    std::sort(io.begin(), io.end(), [](const LhbEntry &a, const LhbEntry &b) { return a.off < b.off; });
+    const size_t slab = g.p.slab;
+    const uint32_t chunk = g.ring_slabs;
+    if (!g.h_cold) OKV_CUDA_TRY(cudaHostAlloc((void **)&g.h_cold, (size_t)chunk * slab,
+                                              cudaHostAllocMapped | cudaHostAllocPortable));
+    char *h_cold_dev = nullptr;
+    OKV_CUDA_TRY(cudaHostGetDevicePointer((void **)&h_cold_dev, g.h_cold, 0));
+    std::vector<uint32_t> src(chunk);
+    for (size_t c0 = 0; c0 < io.size(); c0 += chunk) {
+        const uint32_t k = (uint32_t)std::min<size_t>(chunk, io.size() - c0);
+        for (uint32_t j = 0; j < k; j++) src[j] = io[c0 + j].slab;
+        OKV_CUDA_TRY(cudaMemcpyAsync(g.scratch, src.data(), (size_t)4 * k,
+                                     cudaMemcpyHostToDevice, g.stream));
+        MigPlan gp{};
+        gp.plan_src = g.scratch;
+        gp.max_n = k;
+        rc = launch_pack(g.p, gp, h_cold_dev, 0, k, g.ss, 0, g.stream);
+        if (rc) return rc;
+        OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+        // write the chunk: consecutive file offsets in one pwritev each
+        size_t i = 0;
+        while (i < k) {
+            size_t m = 1;
+            while (i + m < k && io[c0 + i + m].off == io[c0 + i].off + (off_t)(m * slab) &&
+                   m * slab < kStorageRunBytes)
+                m++;
+            if (!full_io(true, ctx->fd, g.h_cold + i * slab, m * slab, io[c0 + i].off))
+                return ORCHKV_ERR_IO;
+            i += m;
+        }
+    }
+    rc = storage_commit(e, 2);
+    if (rc) return rc;
+    g.storage_writes += e.size();
+    g.storage_bytes_written += e.size() * slab;
+    if (result) { result[0] = (uint32_t)e.size(); result[1] = n - (uint32_t)e.size(); }
     return ORCHKV_OK;
 }
 

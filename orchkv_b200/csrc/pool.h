@@ -145,6 +145,14 @@ int launch_conflicts(const MigPlan &promote, const SortScratch &evict_ss, uint32
 int launch_id_table(const PoolDev &p, uint32_t *const *regions, uint32_t n, uint32_t L,
                     uint32_t H, uint32_t mbph, uint32_t row_len, uint32_t *out,
                     cudaStream_t s);
+// Batched storage moves: triples lhb[3n] -> out[3n] = {id, loc word, flags}.
+int launch_lhb_lookup(const PoolDev &p, const ReqDev &r, const uint32_t *lhb, uint32_t n,
+                      uint32_t *out, cudaStream_t s);
+// Commit n storage moves in list order (dir 0: DRAM -> storage, pushing
+// DRAM slabs[j]; dir 1: storage -> DRAM, popping the DRAM stack's top n
+// slabs; dir 2: GPU -> storage, pushing GPU slabs[j]).
+int launch_storage_commit(const PoolDev &p, const uint32_t *ids, const uint32_t *slabs,
+                          uint32_t n, int dir, cudaStream_t s);
 // scratch: >= 3 * ceil(L*H*mbph / 1024) words.
 int launch_request_free(const PoolDev &p, const ReqDev &r, uint32_t *scratch, cudaStream_t s);
 

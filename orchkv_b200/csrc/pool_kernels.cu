@@ -1039,6 +1039,64 @@ int launch_append_batch(const PoolDev &p, uint32_t *const *regions, uint32_t n, 
     return ORCHKV_OK;
 }
 
+// ---- batched storage moves ---------------------------------------------------
+
+// (layer, head, block) triples of one request -> block id, location word and
+// flags (kNoBlock / ~0 / 0 where the triple names no existing block).
+__global__ void lhb_lookup_kernel(PoolDev p, ReqDev r, const uint32_t *lhb, uint32_t n,
+                                  uint32_t *out)
+{
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const uint32_t l = lhb[3 * i], h = lhb[3 * i + 1], bi = lhb[3 * i + 2];
+        uint32_t id = kNoBlock, w = 0xFFFFFFFFu, f = 0;
+        if (l < r.L && h < r.H && bi < r.mbph && bi < (req_tok(r)[l] + p.tpb - 1) / p.tpb) {
+            const uint32_t x = req_table(r)[((size_t)l * r.H + h) * r.mbph + bi];
+            if (x < p.max_blocks) { id = x; w = p.loc[x]; f = p.flags[x]; }
+        }
+        out[3 * i] = id;
+        out[3 * i + 1] = w;
+        out[3 * i + 2] = f;
+    }
+}
+
+// Commit n storage moves in list order.  dir 0 (DRAM -> storage): block ->
+// TIER_NVM, COLD, its DRAM slab pushed onto the DRAM stack in list order.
+// dir 1 (storage -> DRAM): block -> DRAM slab d_stack[top-1-j] (WARM),
+// popped.  dir 2 (GPU -> storage through one DRAM slab, as consecutive
+// orchkv_evict_cold calls leave it): block -> TIER_NVM, COLD, its GPU slab
+// pushed onto the GPU stack in list order, counted as a device-to-host
+// transfer; the DRAM stack ends where it began.
+__global__ void __launch_bounds__(1024)
+storage_commit_kernel(PoolDev p, const uint32_t *ids, const uint32_t *slabs, uint32_t n, int dir)
+{
+    PoolCounters *c = p.ctr;
+    const uint32_t top = dir == 2 ? c->g_top : c->d_top;
+    for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
+        const uint32_t id = ids[j];
+        if (dir == 1) {
+            p.loc[id] = make_loc(TIER_HOST_DRAM, p.d_stack[top - 1 - j]);
+            p.state[id] = KV_STATE_WARM;
+            sched_move(p, id, (uint8_t)TIER_HOST_DRAM, KV_STATE_WARM);
+            continue;
+        }
+        if (dir == 0) p.d_stack[top + j] = slabs[j];
+        else p.g_stack[top + j] = slabs[j];
+        p.loc[id] = make_loc(TIER_NVM, 0);
+        p.state[id] = KV_STATE_COLD;
+        sched_move(p, id, (uint8_t)TIER_NVM, KV_STATE_COLD);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (dir == 0) c->d_top = top + n;
+        else if (dir == 1) c->d_top = top - n;
+        else {
+            c->g_top = top + n;
+            c->transfers_d2h += n;
+            c->bytes_d2h += (unsigned long long)n * p.slab;
+        }
+    }
+}
+
 // First list position of every id of a batch (p.first), and its reset.
 __global__ void mig_first_kernel(PoolDev p, const uint32_t *ids, const uint32_t *count,
                                  uint32_t max_n, int reset)
@@ -1227,6 +1285,24 @@ int launch_id_table(const PoolDev &p, uint32_t *const *regions, uint32_t n, uint
     if (g > 148 * 16) g = 148 * 16;
     if (g == 0) g = 1;
     id_table_kernel<<<g, 256, 0, s>>>(p, regions, n, L, H, mbph, nb, out); note_launches(1);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_lhb_lookup(const PoolDev &p, const ReqDev &r, const uint32_t *lhb, uint32_t n,
+                      uint32_t *out, cudaStream_t s)
+{
+    if (n == 0) return ORCHKV_OK;
+    lhb_lookup_kernel<<<copy_grid(n, 256), 256, 0, s>>>(p, r, lhb, n, out); note_launches(1);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+int launch_storage_commit(const PoolDev &p, const uint32_t *ids, const uint32_t *slabs,
+                          uint32_t n, int dir, cudaStream_t s)
+{
+    if (n == 0) return ORCHKV_OK;
+    storage_commit_kernel<<<1, 1024, 0, s>>>(p, ids, slabs, n, dir); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }

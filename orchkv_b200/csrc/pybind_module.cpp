@@ -322,6 +322,19 @@ PYBIND11_MODULE(orchkv_core, m)
                                                  max_n, P<uint32_t>(result));
           },
           py::arg("ids_ptr"), py::arg("count_ptr"), py::arg("max_n"), py::arg("result_ptr") = 0);
+#define OKV_STORAGE_BATCH(name, fn)                                                     \
+    m.def(name,                                                                         \
+          [](uintptr_t c, const std::vector<uint32_t> &lhb) -> py::tuple {              \
+              uint32_t res[2] = {0, 0};                                                 \
+              const uint32_t n = (uint32_t)(lhb.size() / 3);                            \
+              int rc = fn(P<kv_request_ctx_t>(c), lhb.data(), n, res);                  \
+              return py::make_tuple(rc, res[0], res[1]);                                \
+          },                                                                            \
+          py::arg("ctx"), py::arg("lhb"))
+    OKV_STORAGE_BATCH("evict_batch_to_storage", orchkv_evict_batch_to_storage);
+    OKV_STORAGE_BATCH("promote_batch_from_storage", orchkv_promote_batch_from_storage);
+    OKV_STORAGE_BATCH("evict_cold_batch", orchkv_evict_cold_batch);
+#undef OKV_STORAGE_BATCH
     m.def("swap_batch",
           [](uintptr_t evict_ids, uintptr_t evict_count, uint32_t max_evict, uintptr_t promote_ids,
              uintptr_t promote_count, uint32_t max_promote, uintptr_t result) {

@@ -97,3 +97,79 @@ def test_storage_error_codes(sp, cuda):
     assert L.orchkv_evict_to_storage(ctx, 0, 1, 1) == 0
     assert L.orchkv_evict_cold(ctx, 0, 1, 1) == -8             # already cold
     assert L.orchkv_request_destroy(ctx) == 0
+
+
+def _storage_scenario(o, L, batched):
+    """One run of evict-to-storage / evict_cold / promote-from-storage lists,
+    as batches or as the per-block calls in list order; returns everything
+    observable."""
+    rng = np.random.default_rng(31)
+    H, n, rid = 2, 16 * 12, 777
+    ctx = L.orchkv_request_create(rid, 2, H)
+    for layer in range(2):
+        k, v = kv_data(rng, H, n)
+        assert L.orchkv_prefill(ctx, layer, k.ctypes.data, v.ctypes.data, n) == 0
+    for (l, h, b) in [(0, 0, 3), (0, 0, 4), (1, 1, 7), (1, 0, 2), (0, 1, 9)]:
+        assert L.orchkv_evict_to_dram(ctx, l, h, b) == 0
+    assert L.orchkv_set_block_flags(ctx, 1, 0, 2, 1) == 0          # pinned, on DRAM
+
+    def run(fn_batch, fn_one, triples):
+        if batched:
+            arr = np.array(triples, np.uint32).reshape(-1)
+            res = (C.c_uint32 * 2)()
+            assert fn_batch(ctx, arr.ctypes.data, len(triples), res) == 0
+            return [res[0], res[1]]
+        ok = sum(1 for t in triples if fn_one(ctx, *t) == 0)
+        return [ok, len(triples) - ok]
+
+    out = []
+    # DRAM blocks go; a GPU block, a repeat, a missing block, a pinned one do not
+    out.append(run(L.orchkv_evict_batch_to_storage, L.orchkv_evict_to_storage,
+                   [(0, 0, 4), (1, 1, 7), (0, 0, 5), (0, 0, 4), (1, 1, 30), (1, 0, 2),
+                    (0, 0, 3), (0, 1, 9)]))
+    # two hops for GPU blocks, 8 consecutive ones of (0, 1) among them
+    out.append(run(L.orchkv_evict_cold_batch, L.orchkv_evict_cold,
+                   [(0, 1, i) for i in range(8)] + [(1, 0, 2), (0, 0, 3), (1, 1, 11),
+                                                    (0, 1, 3)]))
+    # back from storage: some of them, a repeat, a DRAM block, a GPU block
+    out.append(run(L.orchkv_promote_batch_from_storage, L.orchkv_promote_from_storage,
+                   [(0, 1, 5), (0, 0, 4), (0, 1, 2), (0, 1, 5), (1, 0, 2), (0, 0, 0),
+                    (1, 1, 7), (0, 1, 0)]))
+    g = np.zeros(GPU_SLABS, np.uint32)
+    d = np.zeros(DRAM_SLABS, np.uint32)
+    tg, td = C.c_uint32(), C.c_uint32()
+    assert L.orchkv_read_pool(0, g.ctypes.data, C.byref(tg)) == 0
+    assert L.orchkv_read_pool(1, d.ctypes.data, C.byref(td)) == 0
+    blocks = [info(L, ctx, l, h, b) for l in range(2) for h in range(H) for b in range(12)]
+    dram = read_host(L.orchkv_dram_pool_base(), DRAM_SLABS * SLAB)
+    dram_used = {s: dram[s * SLAB:(s + 1) * SLAB].tobytes() for (_, _, t, s, _, _) in blocks
+                 if t == 1}
+    with open(os.path.join(BASE, f"req_{rid}"), "rb") as fh:
+        data = fh.read()
+    files = {(l, h, b): data[((l * H + h) * MBPH + b) * SLAB:((l * H + h) * MBPH + b + 1) * SLAB]
+             for l in range(2) for h in range(H) for b in range(12)
+             if blocks[(l * H + h) * 12 + b][2] == 2}
+    assert L.orchkv_request_destroy(ctx) == 0
+    return out, g[:tg.value].tolist(), d[:td.value].tolist(), blocks, dram_used, files
+
+
+def test_storage_batches_equal_per_block_calls(cuda):
+    import orchkv_b200 as o
+    L = o.lib()
+    results = []
+    for batched in (True, False):
+        cfg = o.make_config(gpu_pool_bytes=GPU_SLABS * SLAB, dram_pool_bytes=DRAM_SLABS * SLAB,
+                            tokens_per_block=TPB, d_head=128, dtype=1, max_blocks_per_head=MBPH)
+        cfg.orchfs_base_dir = BASE.encode()
+        ext = o.OrchkvConfigExt()
+        ext.max_blocks = 512
+        assert L.orchkv_init_ext(C.byref(cfg), C.byref(ext)) == 0
+        try:
+            results.append(_storage_scenario(o, L, batched))
+        finally:
+            assert L.orchkv_shutdown() == 0
+    b, p = results
+    assert b[0] == p[0]
+    assert b[0] == [[4, 4], [9, 3], [5, 3]]
+    for x, y in zip(b[1:], p[1:]):
+        assert x == y
