@@ -514,7 +514,7 @@ def ref():
         L.ref_c4_scenario.argtypes = [C.c_uint32, _u64p, _i32p, _u8p, _u32p, C.c_uint32,
                                       C.c_uint32, _u64p, _f32p, _u32p, _f32p, _f32p,
                                       C.c_uint32, C.c_float, C.c_float, C.c_float, _i32p,
-                                      _i32p, _i32p, _f64p]
+                                      _i32p, _i32p, _f64p, C.c_uint32]
         L.ref_c4_scenario.restype = C.c_int
         _REF = L
     return _REF

@@ -237,9 +237,16 @@ int ref_storage_read(const char *base_dir, uint64_t request_id, uint32_t L, uint
  * gpu_demotes, dram_demotes, blocks_migrated, op_errors, op_count[6],
  * op_bytes[6] (bytes / 64).
  * ------------------------------------------------------------------------ */
+/* ctx: {calls, fail_every}; every fail_every-th transfer fails with
+ * ORCHKV_ERR_IO, as test/test_migration_engine.c:43-48's failing mock does */
 static int sc_transfer(kv_block_t *blk, void *dst, size_t size, MigrateOp op, void *ctx)
 {
-    (void)op; (void)ctx;
+    (void)op;
+    uint32_t *c = ctx;
+    if (c) {
+        c[0]++;
+        if (c[1] && c[0] % c[1] == 0) return ORCHKV_ERR_IO;
+    }
     if (blk->data_ptr && dst) memcpy(dst, blk->data_ptr, size);
     return ORCHKV_OK;
 }
@@ -251,8 +258,9 @@ int ref_c4_scenario(uint32_t n, const uint64_t *ids, const int *tiers, const uin
                     const uint64_t *rep_ids, const float *rep_w, const uint32_t *rep_off,
                     const float *gpu_ratio, const float *dram_ratio, uint32_t demote_batch,
                     float alpha, float beta, float gamma, int *out_tier, int *out_state,
-                    int *out_byte, double *o)
+                    int *out_byte, double *o, uint32_t fail_every)
 {
+    uint32_t xfer_ctx[2] = {0, fail_every};
     tiered_manager_t m;
     tm_config_t cfg;
     tm_config_default(&cfg);
@@ -262,6 +270,7 @@ int ref_c4_scenario(uint32_t n, const uint64_t *ids, const int *tiers, const uin
     cfg.hcc_params.beta = beta;
     cfg.hcc_params.gamma = gamma;
     cfg.transfer_fn = sc_transfer;
+    cfg.transfer_ctx = xfer_ctx;
     cfg.alloc_fn = sc_alloc;
     cfg.free_fn = sc_free;
     cfg.block_data_size = 64;

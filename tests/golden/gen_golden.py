@@ -151,7 +151,7 @@ def run_ref_c4(c):
         c["steps"], np.asarray(c["rep_ids"], np.uint64), np.asarray(c["rep_w"], np.float32),
         np.asarray(c["rep_off"], np.uint32), np.asarray(c["gpu_ratio"], np.float32),
         np.asarray(c["dram_ratio"], np.float32), c["demote_batch"], c["alpha"], c["beta"],
-        c["gamma"], out_tier, out_state, out_byte, o)
+        c["gamma"], out_tier, out_state, out_byte, o, c.get("fail_every", 0))
     assert rc == 0
     return dict(tier=out_tier.tolist(), state=out_state.tolist(), byte=out_byte.tolist(),
                 stats=[int(x) for x in o])
@@ -160,15 +160,18 @@ def run_ref_c4(c):
 def main():
     if not O.ref_available():
         raise SystemExit("build the reference first: make -C oracle")
-    c = c4_case()
-    fx = {"name": "c4_demote_callbacks", "case": c, "expect": run_ref_c4(c),
-          "stats_order": "gpu_demotes dram_demotes blocks_migrated op_errors op_count[6] "
-                         "op_bytes[6]/64",
-          "source": "reference src/scheduler/*.c compiled by oracle/Makefile, driven like "
-                    "test/test_tiered_manager.c (transfer/alloc/free callbacks)"}
-    with open(os.path.join(HERE, "c4_demote_callbacks.json"), "w") as fh:
-        json.dump(fx, fh, separators=(",", ":"))
-    print("wrote c4_demote_callbacks", fx["expect"]["stats"])
+    for name, c in (("c4_demote_callbacks", c4_case()),
+                    ("c4_demote_callbacks_failing", dict(c4_case(seed=12), fail_every=3))):
+        fx = {"name": name, "case": c, "expect": run_ref_c4(c),
+              "stats_order": "gpu_demotes dram_demotes blocks_migrated op_errors op_count[6] "
+                             "op_bytes[6]/64",
+              "source": "reference src/scheduler/*.c compiled by oracle/Makefile, driven like "
+                        "test/test_tiered_manager.c (transfer/alloc/free callbacks; with "
+                        "fail_every, every n-th transfer fails with ORCHKV_ERR_IO as "
+                        "test/test_migration_engine.c's failing mock)"}
+        with open(os.path.join(HERE, name + ".json"), "w") as fh:
+            json.dump(fx, fh, separators=(",", ":"))
+        print("wrote", name, fx["expect"]["stats"])
     for name, case in CASES.items():
         rng = np.random.default_rng(case["seed"])
         if case["ops"] is None:

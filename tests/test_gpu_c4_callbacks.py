@@ -3,8 +3,10 @@ alloc_fn and free_fn set): victim choice by the LRU-tail scan
 (src/scheduler/eviction_policy.c:55-143), the migration bookkeeping
 (src/scheduler/migration_engine.c:111-190) and the demote loops
 (src/scheduler/tiered_manager.c:215-281), compared with the reference run on
-the same scenario (tests/golden/c4_demote_callbacks.json): final tier, state
-and payload of every block, and every demotion/migration counter."""
+the same scenarios (tests/golden/c4_demote_callbacks*.json, one with every
+third transfer failing like test/test_migration_engine.c's failing mock):
+final tier, state and payload of every block, and every demotion/migration
+counter."""
 import ctypes as C
 import json
 import os
@@ -34,7 +36,13 @@ def run_b200(c):
     ALLOC = C.CFUNCTYPE(C.c_void_p, C.c_size_t, C.c_int, C.c_void_p)
     FREE = C.CFUNCTYPE(None, C.c_void_p, C.c_int, C.c_void_p)
 
+    calls = [0]
+    fail_every = c.get("fail_every", 0)
+
     def transfer(blk, dst, size, op, ctx):
+        calls[0] += 1
+        if fail_every and calls[0] % fail_every == 0:
+            return -6                                    # ORCHKV_ERR_IO
         if blk.contents.data_ptr and dst:
             _libc.memmove(dst, blk.contents.data_ptr, size)
         return 0
@@ -99,8 +107,9 @@ def run_b200(c):
     return dict(tier=tier, state=state, byte=byte, stats=[int(x) for x in stats])
 
 
-def test_c4_demotion_matches_reference(cuda):
-    with open(os.path.join(HERE, "golden", "c4_demote_callbacks.json")) as fh:
+@pytest.mark.parametrize("name", ["c4_demote_callbacks", "c4_demote_callbacks_failing"])
+def test_c4_demotion_matches_reference(cuda, name):
+    with open(os.path.join(HERE, "golden", name + ".json")) as fh:
         fx = json.load(fh)
     got = run_b200(fx["case"])
     exp = fx["expect"]
@@ -110,3 +119,5 @@ def test_c4_demotion_matches_reference(cuda):
     assert got["byte"] == exp["byte"]
     assert exp["stats"][0] > 0 and exp["stats"][1] > 0     # both demote loops exercised
     assert np.count_nonzero(np.asarray(exp["tier"]) == 2) > 0
+    if fx["case"].get("fail_every"):
+        assert exp["stats"][3] > 0                         # failed transfers rolled back

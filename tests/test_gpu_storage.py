@@ -99,6 +99,60 @@ def test_storage_error_codes(sp, cuda):
     assert L.orchkv_request_destroy(ctx) == 0
 
 
+def test_storage_io_failures_leave_state_unchanged(sp, cuda):
+    """Host-side fault injection (no GPU fault): the request's file is a link
+    to /dev/full (every write fails with ENOSPC), then a truncated file
+    (every read comes up short).  The failed calls return ORCHKV_ERR_IO and
+    leave the blocks, the stacks and the counters as they were
+    (src/api/orchkv_api.cu:432-504 restores the same way)."""
+    o, L = sp
+    rng = np.random.default_rng(8)
+    H, rid = 2, 9191
+    os.makedirs(BASE, exist_ok=True)
+    path = os.path.join(BASE, f"req_{rid}")
+    if os.path.lexists(path):
+        os.unlink(path)
+    os.symlink("/dev/full", path)
+    k, v = kv_data(rng, H, 64)
+    ctx = L.orchkv_request_create(rid, 1, H)
+    assert ctx
+    assert L.orchkv_prefill(ctx, 0, k.ctypes.data, v.ctypes.data, 64) == 0
+    assert L.orchkv_evict_to_dram(ctx, 0, 0, 1) == 0
+    assert L.orchkv_evict_to_dram(ctx, 0, 1, 2) == 0
+
+    def snap():
+        g = np.zeros(GPU_SLABS, np.uint32)
+        d = np.zeros(DRAM_SLABS, np.uint32)
+        tg, td = C.c_uint32(), C.c_uint32()
+        assert L.orchkv_read_pool(0, g.ctypes.data, C.byref(tg)) == 0
+        assert L.orchkv_read_pool(1, d.ctypes.data, C.byref(td)) == 0
+        return (g[:tg.value].tolist(), d[:td.value].tolist(),
+                [info(L, ctx, 0, h, b) for h in range(H) for b in range(4)])
+
+    before = snap()
+    assert L.orchkv_evict_to_storage(ctx, 0, 0, 1) == -6          # ERR_IO
+    lhb = np.array([0, 0, 1, 0, 1, 2], np.uint32)
+    res = (C.c_uint32 * 2)()
+    assert L.orchkv_evict_batch_to_storage(ctx, lhb.ctypes.data, 2, res) == -6
+    cold = np.array([0, 0, 3], np.uint32)
+    assert L.orchkv_evict_cold_batch(ctx, cold.ctypes.data, 1, res) == -6
+    assert snap() == before
+    assert L.orchkv_request_destroy(ctx) == 0
+
+    # reads: a real file, evicted, then cut short under the library
+    ctx = L.orchkv_request_create(rid + 1, 1, H)
+    assert L.orchkv_prefill(ctx, 0, k.ctypes.data, v.ctypes.data, 64) == 0
+    assert L.orchkv_evict_cold(ctx, 0, 0, 1) == 0
+    assert L.orchkv_evict_cold(ctx, 0, 1, 3) == 0
+    before = snap()
+    os.truncate(os.path.join(BASE, f"req_{rid + 1}"), 0)
+    assert L.orchkv_promote_from_storage(ctx, 0, 0, 1) == -6
+    lhb = np.array([0, 0, 1, 0, 1, 3], np.uint32)
+    assert L.orchkv_promote_batch_from_storage(ctx, lhb.ctypes.data, 2, res) == -6
+    assert snap() == before
+    assert L.orchkv_request_destroy(ctx) == 0
+
+
 def _storage_scenario(o, L, batched):
     """One run of evict-to-storage / evict_cold / promote-from-storage lists,
     as batches or as the per-block calls in list order; returns everything

@@ -222,12 +222,13 @@ def test_fixtures_present():
 
 
 @pytest.mark.ref
-def test_c4_fixture_regenerates(oracle_mod):
-    """The callback-path fixture is what the compiled reference produces now."""
+@pytest.mark.parametrize("name", ["c4_demote_callbacks", "c4_demote_callbacks_failing"])
+def test_c4_fixture_regenerates(oracle_mod, name):
+    """The callback-path fixtures are what the compiled reference produces now."""
     if not oracle_mod.ref_available():
         pytest.skip("reference not compiled into oracle/_ref on this machine")
     from tests.golden.gen_golden import run_ref_c4
-    with open(os.path.join(GOLDEN, "c4_demote_callbacks.json")) as fh:
+    with open(os.path.join(GOLDEN, name + ".json")) as fh:
         fx = json.load(fh)
     assert run_ref_c4(fx["case"]) == fx["expect"]
 
