@@ -130,6 +130,7 @@ class Workload:
         # with a communicator, selections are global: the promote k covers all ranks
         self.k_promote_sel = self.k_promote * world
         self.k_evict_sel = self.k_evict * world
+        self.world = world
         torch_ = torch
         dev = torch_.cuda.current_device()
         self.stream = torch_.cuda.current_stream()
@@ -242,7 +243,8 @@ class Workload:
         """Promote the step's victims back and evict the reserve again (outside
         the timed region)."""
         L, tm = self.L, self.tm.ref
-        assert L.tm_select_prefetch(tm, 1 << 21, 0.0, 0.0, self._ptr(self.pref),
+        # every block off the GPU on every rank (selections are global over ranks)
+        assert L.tm_select_prefetch(tm, (1 << 21) * self.world, 0.0, 0.0, self._ptr(self.pref),
                                     self._ptr(self.counts, 32)) == 0
         assert L.orchkv_promote_batch_to_gpu(self._ptr(self.pref), self._ptr(self.counts, 32),
                                              1 << 21, self._ptr(self.counts, 36)) == 0
