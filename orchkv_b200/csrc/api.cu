@@ -861,6 +861,7 @@ int orchkv_attach_scheduler(tiered_manager_t *tm)
 int orchkv_append_token_batch(kv_request_ctx_t *const *ctxs, uint32_t n, const void *k,
                               const void *v)
 {
+    OKV_RANGE("orchkv_append_token_batch");
     std::lock_guard<std::recursive_mutex> lk(g.mu);
     if (!g.inited) return ORCHKV_ERR_INIT;
     uint32_t L, H, mbph;
@@ -1136,6 +1137,7 @@ extern "C" {
 int orchkv_evict_batch_to_dram(const uint32_t *ids, const uint32_t *count, uint32_t max_n,
                                uint32_t *result)
 {
+    OKV_RANGE("orchkv_evict_batch_to_dram");
     std::lock_guard<std::recursive_mutex> lk(g.mu);
     if (!g.inited) return ORCHKV_ERR_INIT;
     if (max_n && !ids) return ORCHKV_ERR_INVALID;
@@ -1155,6 +1157,7 @@ int orchkv_evict_batch_to_dram(const uint32_t *ids, const uint32_t *count, uint3
 int orchkv_promote_batch_to_gpu(const uint32_t *ids, const uint32_t *count, uint32_t max_n,
                                 uint32_t *result)
 {
+    OKV_RANGE("orchkv_promote_batch_to_gpu");
     std::lock_guard<std::recursive_mutex> lk(g.mu);
     if (!g.inited) return ORCHKV_ERR_INIT;
     if (max_n && !ids) return ORCHKV_ERR_INVALID;
@@ -1172,6 +1175,7 @@ int orchkv_swap_batch(const uint32_t *evict_ids, const uint32_t *evict_count, ui
                       const uint32_t *promote_ids, const uint32_t *promote_count,
                       uint32_t max_p, uint32_t *result)
 {
+    OKV_RANGE("orchkv_swap_batch");
     std::lock_guard<std::recursive_mutex> lk(g.mu);
     if (!g.inited) return ORCHKV_ERR_INIT;
     if ((max_e && !evict_ids) || (max_p && !promote_ids)) return ORCHKV_ERR_INVALID;
@@ -1426,6 +1430,7 @@ int evict_batch_to_storage_locked(kv_request_ctx_t *ctx, const uint32_t *lhb, ui
 int orchkv_evict_batch_to_storage(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t n,
                                   uint32_t *result)
 {
+    OKV_RANGE("orchkv_evict_batch_to_storage");
     std::lock_guard<std::recursive_mutex> lk(g.mu);
     return evict_batch_to_storage_locked(ctx, lhb, n, result);
 }
@@ -1433,6 +1438,7 @@ int orchkv_evict_batch_to_storage(kv_request_ctx_t *ctx, const uint32_t *lhb, ui
 int orchkv_promote_batch_from_storage(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t n,
                                       uint32_t *result)
 {
+    OKV_RANGE("orchkv_promote_batch_from_storage");
     std::lock_guard<std::recursive_mutex> lk(g.mu);
     if (result) { result[0] = 0; result[1] = n; }
     if (!g.inited) return ORCHKV_ERR_INIT;
@@ -1469,6 +1475,7 @@ int orchkv_promote_batch_from_storage(kv_request_ctx_t *ctx, const uint32_t *lhb
 int orchkv_evict_cold_batch(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t n,
                             uint32_t *result)
 {
+    OKV_RANGE("orchkv_evict_cold_batch");
     // per block, orchkv_evict_cold = orchkv_evict_to_dram then
     // orchkv_evict_to_storage (src/api/orchkv_api.cu:508-516): a GPU block
     // passes through the DRAM stack's top slab and the slab goes back, so a
@@ -1542,6 +1549,7 @@ int orchkv_evict_cold_batch(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t
 int orchkv_block_id_table(kv_request_ctx_t *const *ctxs, uint32_t n, uint32_t row_len,
                           uint32_t *out)
 {
+    OKV_RANGE("orchkv_block_id_table");
     std::lock_guard<std::recursive_mutex> lk(g.mu);
     if (!g.inited) return ORCHKV_ERR_INIT;
     if (!out || row_len == 0) return ORCHKV_ERR_INVALID;

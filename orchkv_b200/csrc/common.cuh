@@ -6,6 +6,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "orchkv/kv_types.h"
 
 namespace okv {
@@ -107,7 +109,16 @@ __device__ inline uint32_t block_excl_scan(uint32_t v, uint32_t *tmp, uint32_t *
     return r;
 }
 
+// A named range on the profiler timeline (Nsight Systems, ncu's NVTX
+// filters) for the duration of a host call; a no-op unless a tool is attached.
+struct OkvRange {
+    explicit OkvRange(const char *name) { nvtxRangePushA(name); }
+    ~OkvRange() { nvtxRangePop(); }
+};
+
 }  // namespace okv
+
+#define OKV_RANGE(name) okv::OkvRange okv_range_(name)
 
 #define OKV_CUDA_TRY(call)                                                      \
     do {                                                                        \

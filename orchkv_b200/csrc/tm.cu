@@ -677,6 +677,7 @@ void tm_step_done(tiered_manager_t *m)
 
 void tm_schedule_once(tiered_manager_t *m)
 {
+    OKV_RANGE("tm_schedule_once");
     TmImpl *t = tm_impl(m);
     if (!t) return;
     std::lock_guard<std::mutex> g(t->mu);
@@ -879,6 +880,7 @@ int tm_report_attn_probs(tiered_manager_t *m, const float *probs, uint32_t n_row
                          uint32_t n_q_heads, uint32_t n_kv_heads, uint32_t row_len,
                          uint32_t tpb, const uint32_t *lens, const uint32_t *block_ids)
 {
+    OKV_RANGE("tm_report_attn_probs");
     TmImpl *t = tm_impl(m);
     if (!t) return ORCHKV_ERR_INVALID;
     std::lock_guard<std::mutex> g(t->mu);
@@ -903,6 +905,7 @@ int tm_report_attn_batch_dev(tiered_manager_t *m, const uint32_t *ids, const flo
 
 int tm_step_and_classify(tiered_manager_t *m)
 {
+    OKV_RANGE("tm_step_and_classify");
     TmImpl *t = tm_impl(m);
     if (!t) return ORCHKV_ERR_INVALID;
     std::lock_guard<std::mutex> g(t->mu);
@@ -952,6 +955,7 @@ static int select_common(TmImpl *t, SelectMode mode, uint32_t k, float frac, flo
 
 int tm_select_victims(tiered_manager_t *m, uint32_t k, uint32_t *out_ids, uint32_t *out_count)
 {
+    OKV_RANGE("tm_select_victims");
     TmImpl *t = tm_impl(m);
     if (!t) return ORCHKV_ERR_INVALID;
     return select_common(t, kSelectColdest, k, -1.0f, 0.f, 0.f, out_ids, out_count, k);
@@ -960,6 +964,7 @@ int tm_select_victims(tiered_manager_t *m, uint32_t k, uint32_t *out_ids, uint32
 int tm_select_victims_masked(tiered_manager_t *m, uint32_t k, const uint8_t *eligible,
                              uint32_t *out_ids, uint32_t *out_count)
 {
+    OKV_RANGE("tm_select_victims_masked");
     TmImpl *t = tm_impl(m);
     if (!t || !eligible) return ORCHKV_ERR_INVALID;
     return select_common(t, kSelectColdest, k, -1.0f, 0.f, 0.f, out_ids, out_count, k,
@@ -969,6 +974,7 @@ int tm_select_victims_masked(tiered_manager_t *m, uint32_t k, const uint8_t *eli
 int tm_select_victims_frac(tiered_manager_t *m, float frac, uint32_t *out_ids,
                            uint32_t *out_count, uint32_t max_out)
 {
+    OKV_RANGE("tm_select_victims_frac");
     TmImpl *t = tm_impl(m);
     if (!t || !(frac >= 0.0f) || frac > 1.0f) return ORCHKV_ERR_INVALID;
     return select_common(t, kSelectColdest, 0, frac, 0.f, 0.f, out_ids, out_count, max_out);
@@ -977,6 +983,7 @@ int tm_select_victims_frac(tiered_manager_t *m, float frac, uint32_t *out_ids,
 int tm_select_prefetch(tiered_manager_t *m, uint32_t k, float th_gpu, float th_dram,
                        uint32_t *out_ids, uint32_t *out_count)
 {
+    OKV_RANGE("tm_select_prefetch");
     TmImpl *t = tm_impl(m);
     if (!t) return ORCHKV_ERR_INVALID;
     return select_common(t, kSelectPrefetch, k, -1.0f, th_gpu, th_dram, out_ids, out_count, k);
