@@ -47,9 +47,9 @@ METRIC = "decode-step schedule+migrate µs and migrated blocks/s per GPU; HBM GB
 WL = dict(name="qwen2.5-7b-gqa-decode-step", B=32, L=28, Hq=28, Hkv=4, D=128, T=8192, tpb=16)
 EVICT_FRAC, PROMOTE_FRAC = 0.25, 0.05
 # DRAM bytes (read + write) of one score launch per request of this workload:
-# 215.9 MB measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum) on one
+# 216.95 MB measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum) on one
 # 8-request launch; the launch streams each request's rows once, so it scales
-SCORE_TRAFFIC_PER_REQUEST = 215.91e6 / 8
+SCORE_TRAFFIC_PER_REQUEST = 216.95e6 / 8
 NOMINAL_HBM_GBS = 7700.0          # B200 HBM3e, HGX figure
 
 
