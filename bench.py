@@ -26,7 +26,8 @@ e2e   = the same step through the C ABI with host inputs: attention
         probabilities and new tokens copied from pinned host memory inside
         the timed region.
 --impl reference times the reference's own C scheduler and per-block
-migration path (compiled from its sources into oracle/_ref) on a sample.
+migration path (compiled from its sources into oracle/_ref) on a sample of
+the requests, one request per host thread.
 """
 from __future__ import annotations
 
@@ -514,21 +515,38 @@ def host_link_probe(torch, nbytes=512 << 20, reps=3):
 # Reference arm: the reference's C scheduler + per-block migration on a sample
 # ---------------------------------------------------------------------------
 
-def _reference_sample(max_seconds=12.0, steps=3, warm=1, sample_requests=1):
-    """Time the reference on `sample_requests` request(s) of the workload, in
-    the same steady state: 5% of the blocks (the coldest at the start) held in
-    DRAM.  A step: fixed-order C reduction of the attention probabilities
-    (restating the managers' torch reduction), attn_tracker_update_batch +
-    tm_step_done + tm_schedule_once (reference C), the FastKVCacheManager
-    coldest-first order over the blocks on the GPU, then orchkv_evict_to_dram
-    per victim (25% of the blocks), orchkv_promote_to_gpu per reserve block
-    and orchkv_append_token per (request, layer), through the reference's own
-    orchkv_api (real CUDA copies).  Returns blocks/s (migrated) and details."""
+def host_threads():
+    """Host cores this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def _reference_sample(steps=3, warm=1, threads=1):
+    """Time the reference on `threads` request(s) of the workload, one request
+    per host thread, in the same steady state: 5% of the blocks (the coldest
+    at the start) held in DRAM.  A step: fixed-order C reduction of the
+    attention probabilities (restating the managers' torch reduction; one
+    request per thread), attn_tracker_update_batch + tm_step_done +
+    tm_schedule_once (reference C; one manager, so one thread), the
+    FastKVCacheManager coldest-first order over the blocks on the GPU, then
+    orchkv_evict_to_dram per victim (25% of the blocks), orchkv_promote_to_gpu
+    per reserve block and orchkv_append_token per (request, layer), through
+    the reference's own orchkv_api (real CUDA copies).  The reference's data
+    plane takes a lock around each shared pool and its transfer engine, and
+    its per-request state belongs to one request, so the threads migrate
+    their own requests concurrently (src/tiered_store/gpu_tier.cu:65-93,
+    src/tiered_store/transfer.cu:62-92); the transfer engine gets one CUDA
+    stream per thread (its num_cuda_streams setting).  Each phase is timed by
+    the wall clock.  Returns blocks/s (migrated) and details."""
+    from concurrent.futures import ThreadPoolExecutor
+
     import numpy as np
 
     from oracle import oracle as O
     w = WL
-    B, Ly, Hq, Hkv, D, T, tpb = sample_requests, w["L"], w["Hq"], w["Hkv"], w["D"], w["T"], w["tpb"]
+    B, Ly, Hq, Hkv, D, T, tpb = threads, w["L"], w["Hq"], w["Hkv"], w["D"], w["T"], w["tpb"]
     nb = T // tpb
     n = B * Ly * Hkv * nb
     slab = tpb * D * 4
@@ -538,18 +556,31 @@ def _reference_sample(max_seconds=12.0, steps=3, warm=1, sample_requests=1):
         for h in range(Hq):
             logits[r, h, rng.choice(T, T // 100, replace=False)] += 6.0
     logits -= logits.max(-1, keepdims=True)
-    p = np.exp(logits)
-    probs = (p / p.sum(-1, keepdims=True)).astype(np.float32)
-    del logits, p
+    np.exp(logits, out=logits)
+    logits /= logits.sum(-1, keepdims=True)
+    probs = logits
+    del logits
     R = O.ref()
     tm = O.RefTM(tracker_cap=n, max_blocks=n, ema_lambda=0.9, alpha=0.5, beta=0.3, gamma=0.2,
                  recency_tau=50.0, cooldown_sec=0.0)
     ids = np.arange(n, dtype=np.uint64)
-    for i in range(n):
-        tm.register(i, 0, 0)
+    tm.register_range(n)
+    # tm_schedule_once's prefetch scan takes n_blocks x 16 bytes with alloca
+    # (src/scheduler/tiered_manager.c:283-291): past ~500k blocks that is more
+    # than a default 8 MiB stack, so the scheduler runs on one thread whose
+    # stack holds it.
+    old_stack = threading.stack_size(max(64 << 20, 2 * 16 * n + (32 << 20)))
+    sched_pool = ThreadPoolExecutor(1)
+    sched_pool.submit(lambda: None).result()
+    threading.stack_size(old_stack)
+
+    def sched(wts, k, out):
+        return sched_pool.submit(R.ref_arm_sched_step, tm.h, ids, wts, n, 0.95, k, out,
+                                 np.zeros(3)).result()
     gpu_pool = (n + B * Ly * Hkv * 8 + 64) * slab
     dram_pool = (n // 4 + n // 20 + 128) * slab
-    rc = R.ref_api_init(0, gpu_pool, dram_pool, tpb, D, 1, 4, nb + 8, b"/dev/shm/orchkv_ref_bench")
+    rc = R.ref_api_init(0, gpu_pool, dram_pool, tpb, D, 1, max(4, threads), nb + 8,
+                        b"/dev/shm/orchkv_ref_bench")
     assert rc == 0, rc
     kv = rng.standard_normal((Hkv, T, D)).astype(np.float16)
     ctxs = []
@@ -560,55 +591,67 @@ def _reference_sample(max_seconds=12.0, steps=3, warm=1, sample_requests=1):
         ctxs.append(c)
     tok = np.zeros((Hkv, D), np.float16)
     k_e, k_p = int(EVICT_FRAC * n), int(PROMOTE_FRAC * n)
+    pool = ThreadPoolExecutor(threads) if threads > 1 else None
+
+    def pmap(fn, items):
+        items = list(items)
+        return list(pool.map(fn, items)) if pool else [fn(x) for x in items]
 
     def by_request(id_list):
-        """block ids -> {request: [(layer, head, block), ...]} in list order"""
-        out = {}
-        for v in id_list:
-            b, rem = divmod(int(v), Ly * Hkv * nb)
-            layer, rem = divmod(rem, Hkv * nb)
-            head, bi = divmod(rem, nb)
-            out.setdefault(b, []).append((layer, head, bi))
-        return out
+        """block ids -> {request: uint32 [(layer, head, block), ...]} in list order"""
+        v = np.asarray(id_list, np.int64)
+        b, rem = np.divmod(v, Ly * Hkv * nb)
+        layer, rem = np.divmod(rem, Hkv * nb)
+        head, bi = np.divmod(rem, nb)
+        lhb = np.stack([layer, head, bi], axis=1).astype(np.uint32)
+        order = np.argsort(b, kind="stable")
+        bs, starts = np.unique(b[order], return_index=True)
+        ends = list(starts[1:]) + [len(order)]
+        return {int(r): np.ascontiguousarray(lhb[order[s:e]]) for r, s, e in zip(bs, starts, ends)}
 
     def migrate(groups, evict):
-        tsum = np.zeros(2)
-        for b, lst in groups.items():
-            arr = np.array(lst, np.uint32).reshape(-1)
+        def one(item):
+            b, arr = item
             tmp = np.zeros(2)
-            assert R.ref_api_migrate_list(ctxs[b], arr, len(lst) if evict else 0,
-                                          0 if evict else len(lst), tmp) == 0
-            tsum += tmp
-        return tsum[0] if evict else tsum[1]
+            k = len(arr)
+            rc = R.ref_api_migrate_list(ctxs[b], arr.reshape(-1), k if evict else 0,
+                                        0 if evict else k, tmp)
+            assert rc == 0, rc
+        t0 = time.perf_counter()
+        pmap(one, groups.items())
+        return time.perf_counter() - t0
+
+    def score():
+        return np.concatenate(pmap(
+            lambda b: O.score_blocks(probs[b * Ly:(b + 1) * Ly], Hq, Hkv, tpb), range(B)))
+
+    def append(b):
+        for layer in range(Ly):
+            assert R.ref_api_append(ctxs[b], layer, tok.ctypes.data, tok.ctypes.data) == 0
 
     # the DRAM-resident reserve: one scheduler pass, the coldest 5% evicted
     # and marked as off the GPU (the manager's tm_set_block_tier bookkeeping)
     reserve = np.zeros(k_p, np.uint64)
-    w0 = O.score_blocks(probs, Hq, Hkv, tpb)
-    c_p = R.ref_arm_sched_step(tm.h, ids, w0.reshape(-1).copy(), n, 0.95, k_p, reserve,
-                               np.zeros(3))
+    w0 = score()
+    c_p = sched(w0.reshape(-1).copy(), k_p, reserve)
     reserve = reserve[:c_p].copy()
-    for v in reserve:
-        tm.set_block_tier(int(v), 1)
+    tm.set_tiers(reserve, 1)
     res_groups = by_request(reserve)
     migrate(res_groups, evict=True)
     vict = np.zeros(k_e, np.uint64)
     times = []
     for s in range(warm + steps):
         t0 = time.perf_counter()
-        w_ = O.score_blocks(probs, Hq, Hkv, tpb)             # [B*Ly, Hkv, nb]
+        w_ = score()                                          # [B*Ly, Hkv, nb]
         t1 = time.perf_counter()
-        tt = np.zeros(3)
-        c = R.ref_arm_sched_step(tm.h, ids, w_.reshape(-1).copy(), n, 0.95, k_e, vict, tt)
+        c = sched(w_.reshape(-1).copy(), k_e, vict)
         t2 = time.perf_counter()
         groups = by_request(vict[:c])
         t3 = time.perf_counter()
         evict_s = migrate(groups, evict=True)
         promote_s = migrate(res_groups, evict=False)
         t4 = time.perf_counter()
-        for b in range(B):
-            for layer in range(Ly):
-                R.ref_api_append(ctxs[b], layer, tok.ctypes.data, tok.ctypes.data)
+        pmap(append, range(B))
         t5 = time.perf_counter()
         # back to the starting state (not timed)
         migrate(groups, evict=False)
@@ -616,8 +659,11 @@ def _reference_sample(max_seconds=12.0, steps=3, warm=1, sample_requests=1):
         step_s = (t1 - t0) + (t2 - t1) + (t3 - t2) + evict_s + promote_s + (t5 - t4)
         if s >= warm:
             times.append(dict(step_s=step_s, score_s=t1 - t0, sched_s=t2 - t1,
-                              evict_s=evict_s, promote_s=promote_s, append_s=t5 - t4,
-                              migrated=c + len(reserve), blocks=n))
+                              group_s=t3 - t2, evict_s=evict_s, promote_s=promote_s,
+                              append_s=t5 - t4, migrated=c + len(reserve), blocks=n))
+    if pool:
+        pool.shutdown()
+    sched_pool.shutdown()
     for cx in ctxs:
         R.ref_api_request_destroy(cx)
     R.ref_api_shutdown()
@@ -633,7 +679,7 @@ def cpu_baseline_sample(args):
     m = _reference_sample(steps=max(1, min(args.steps, 3)))
     return {"value": round(m["migrated"] / m["step_s"], 1), "unit": "blocks/s",
             "cores": 1, "kind": "reference",
-            "sample": f"1 of {WL['B']} requests ({m['blocks']} blocks): reference C scheduler "
+            "sample": f"1 of {WL['B']} requests ({int(m['blocks'])} blocks): reference C scheduler "
                       f"(attn_tracker_update_batch, tm_step_done, tm_schedule_once) + "
                       f"coldest-25% order + per-block orchkv_evict_to_dram of the victims / "
                       f"orchkv_promote_to_gpu of the 5% DRAM reserve + orchkv_append_token, "
@@ -672,16 +718,20 @@ def run_reference(args, rank, world):
         return
     import torch
     torch.cuda.set_device(0)
-    m = _reference_sample(steps=max(1, args.steps), warm=min(args.warmup, 1))
+    threads = max(1, min(host_threads(), WL["B"]))
+    m = _reference_sample(steps=max(1, args.steps), warm=min(args.warmup, 1), threads=threads)
     v = round(m["migrated"] / m["step_s"], 1)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "blocks/s",
             "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(m["step_s"] * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32+fp16",
             "data": "synthetic (seeded)", "config": {"workload": WL["name"],
-                                                     "sample_requests": 1},
-            "cpu_baseline": {"value": v, "unit": "blocks/s", "cores": 1, "kind": "reference",
-                             "sample": "1 request x 28 layers x 4 KV heads x 512 blocks"},
+                                                     "sample_requests": threads},
+            "cpu_baseline": {"value": v, "unit": "blocks/s", "cores": threads,
+                             "kind": "reference",
+                             "sample": f"{threads} of {WL['B']} requests x 28 layers x 4 KV "
+                                       f"heads x 512 blocks ({int(m['blocks'])} blocks), one "
+                                       f"request per host thread; scheduler on one thread"},
             "e2e": {"value": v, "unit": "blocks/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
             "phases_s": {k: round(v_, 6) for k, v_ in m.items() if k.endswith("_s")}}

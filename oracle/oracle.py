@@ -449,6 +449,9 @@ def ref():
         L.ref_tm_register_id.argtypes = [vp, C.c_uint64, C.c_int, C.c_uint8]
         L.ref_tm_register_id.restype = C.c_int
         L.ref_tm_set_block_tier.argtypes = [vp, C.c_uint64, C.c_int]
+        L.ref_tm_register_range.argtypes = [vp, C.c_uint32]
+        L.ref_tm_register_range.restype = C.c_int
+        L.ref_tm_set_tiers.argtypes = [vp, _u64p, C.c_uint32, C.c_int]
         L.ref_tm_notify_access.argtypes = [vp, C.c_uint64]
         L.ref_tm_report.argtypes = [vp, C.c_uint64, C.c_float]
         L.ref_tm_report_batch.argtypes = [vp, _u64p, _f32p, C.c_uint32]
@@ -558,6 +561,16 @@ class RefTM:
 
     def set_block_tier(self, bid, tier):
         ref().ref_tm_set_block_tier(self.h, bid, tier)
+
+    def register_range(self, n):
+        """Register ids 0..n-1 (tier GPU, no flags) in order."""
+        rc = ref().ref_tm_register_range(self.h, n)
+        if rc != 0:
+            raise RuntimeError(f"ref_tm_register_range: {rc}")
+
+    def set_tiers(self, ids, tier):
+        ids = np.ascontiguousarray(ids, np.uint64)
+        ref().ref_tm_set_tiers(self.h, ids, len(ids), tier)
 
     def notify_access(self, bid):
         ref().ref_tm_notify_access(self.h, bid)

@@ -94,6 +94,30 @@ void ref_tm_set_block_tier(void *h, uint64_t id, int tier)
         if (w->blks[i]->block_id == id) { w->blks[i]->tier = (StorageTier)tier; return; }
 }
 
+/* Bulk forms for large samples: register ids 0..n-1 in order, and set the
+ * tier of a list of ids (direct index when ids were registered in order,
+ * a scan otherwise). */
+int ref_tm_register_range(void *h, uint32_t n)
+{
+    for (uint32_t i = 0; i < n; i++) {
+        int rc = ref_tm_register_id(h, i, 0, 0);
+        if (rc != ORCHKV_OK) return rc;
+    }
+    return ORCHKV_OK;
+}
+
+void ref_tm_set_tiers(void *h, const uint64_t *ids, uint32_t n, int tier)
+{
+    ref_tm_t *w = h;
+    for (uint32_t i = 0; i < n; i++) {
+        uint64_t id = ids[i];
+        if (id < w->n && w->blks[id]->block_id == id)
+            w->blks[id]->tier = (StorageTier)tier;
+        else
+            ref_tm_set_block_tier(h, id, tier);
+    }
+}
+
 void ref_tm_notify_access(void *h, uint64_t id)
 {
     ref_tm_t *w = h;
