@@ -168,8 +168,8 @@ def test_select_victims_vs_oracle(okv, oracle_mod, cuda, n, k):
     # quantised weights produce many exact hotness ties
     ids = rng.choice(n, n // 2, replace=False).astype(np.uint32)
     w = (rng.integers(0, 7, len(ids)) / 8).astype(np.float32)
-    okv.lib().tm_report_attn_batch_dev(m.ref, _dev(cuda, ids).data_ptr(),
-                                       _dev(cuda, w).data_ptr(), len(ids))
+    ids_d, w_d = _dev(cuda, ids), _dev(cuda, w)        # held until the launch has run
+    okv.lib().tm_report_attn_batch_dev(m.ref, ids_d.data_ptr(), w_d.data_ptr(), len(ids))
     okv.lib().tm_step_and_classify(m.ref)
     st = m.state()
     cap = m.cap
@@ -191,8 +191,8 @@ def test_select_prefetch_vs_oracle(okv, oracle_mod, cuda):
     for _ in range(3):
         ids = rng.choice(n, n // 2, replace=False).astype(np.uint32)
         w = (rng.integers(0, 9, len(ids)) / 4).astype(np.float32)
-        okv.lib().tm_report_attn_batch_dev(m.ref, _dev(cuda, ids).data_ptr(),
-                                           _dev(cuda, w).data_ptr(), len(ids))
+        ids_d, w_d = _dev(cuda, ids), _dev(cuda, w)
+        okv.lib().tm_report_attn_batch_dev(m.ref, ids_d.data_ptr(), w_d.data_ptr(), len(ids))
         okv.lib().tm_step_and_classify(m.ref)
     st = m.state()
     tier_full = np.full(m.cap, 4, np.uint8)

@@ -122,7 +122,8 @@ def promote_layout(L):
 def test_staged_promote_matches_sequential_model(sysm, cuda, order):
     o, L, rng = sysm
     victims = sorted(rng.choice(on_tier(L, 0), 4200, replace=False).tolist())
-    assert L.orchkv_evict_batch_to_dram(dev_ids(cuda, victims).data_ptr(), None, 4200, None) == 0
+    vd = dev_ids(cuda, victims)
+    assert L.orchkv_evict_batch_to_dram(vd.data_ptr(), None, 4200, None) == 0
     assert L.orchkv_sync() == 0
     m = Model(L)
     if order == "same":           # evicted together, promoted together: long source runs
@@ -130,7 +131,8 @@ def test_staged_promote_matches_sequential_model(sysm, cuda, order):
     else:                         # a scattered subset in random order: short runs
         back = rng.permutation(victims)[:2600].tolist()
     res = cuda.zeros(2, dtype=cuda.int32, device="cuda")
-    assert L.orchkv_promote_batch_to_gpu(dev_ids(cuda, back).data_ptr(), None, len(back),
+    bd = dev_ids(cuda, back)
+    assert L.orchkv_promote_batch_to_gpu(bd.data_ptr(), None, len(back),
                                          res.data_ptr()) == 0
     assert L.orchkv_sync() == 0
     done, skipped = m.promote(back)
@@ -148,7 +150,8 @@ def test_swap_equals_evict_then_promote(sysm, cuda, case):
     o, L, rng = sysm
     # blocks evicted earlier, to be promoted by the swap
     first = sorted(rng.choice(on_tier(L, 0), 2500, replace=False).tolist())
-    assert L.orchkv_evict_batch_to_dram(dev_ids(cuda, first).data_ptr(), None, len(first),
+    fd = dev_ids(cuda, first)
+    assert L.orchkv_evict_batch_to_dram(fd.data_ptr(), None, len(first),
                                         None) == 0
     assert L.orchkv_sync() == 0
     m = Model(L)
@@ -162,8 +165,10 @@ def test_swap_equals_evict_then_promote(sysm, cuda, case):
         if case == "overlapping":   # some blocks evicted and promoted in the same call
             pr = pr[:2000] + ev[:300]
     res = cuda.zeros(4, dtype=cuda.int32, device="cuda")
-    assert L.orchkv_swap_batch(dev_ids(cuda, ev).data_ptr(), None, len(ev),
-                               dev_ids(cuda, pr).data_ptr(), None, len(pr),
+    # both lists held in their own tensors: a temporary freed after
+    # data_ptr() could hand its memory to the next list before the call reads it
+    ed, pd = dev_ids(cuda, ev), dev_ids(cuda, pr)
+    assert L.orchkv_swap_batch(ed.data_ptr(), None, len(ev), pd.data_ptr(), None, len(pr),
                                res.data_ptr()) == 0
     assert L.orchkv_sync() == 0
     de, se = m.evict(ev)
