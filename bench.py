@@ -274,6 +274,19 @@ def score_bytes(wl):
     return probs + wl.n_blocks * per_block
 
 
+def pack_first_chunk(chunk_ms, total_bytes, chunks, hbm_peak):
+    """The first staging chunk's pack, timed before the copy engine starts
+    draining the evict (full chunks carry equal bytes): ms, GB/s and the
+    fraction of the measured HBM peak."""
+    if not chunk_ms or chunks < 2:
+        return None
+    nbytes = total_bytes / chunks
+    gbs = nbytes / max(chunk_ms[0], 1e-9) / 1e6
+    return {"ms": round(chunk_ms[0], 4), "achieved_gbs": round(gbs, 1),
+            "frac": round(gbs / hbm_peak, 4),
+            "later_chunks_ms_mean": round(sum(chunk_ms[1:]) / (len(chunk_ms) - 1), 4)}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -365,6 +378,12 @@ def run_ours(args, rank, world, local_rank):
     pk_ms, pk_bytes, pk_chunks, pr_ms = C.c_float(), C.c_ulonglong(), C.c_uint32(), C.c_float()
     wl.L.orchkv_last_migration_profile(C.byref(pk_ms), C.byref(pk_bytes), C.byref(pk_chunks),
                                        C.byref(pr_ms))
+    # per-chunk pack times: chunk 0 is packed before any device-to-host copy
+    # of the evict is in flight, the later ones while the copy engine drains
+    chunk_ms = (C.c_float * 64)()
+    n_chunk_ms = C.c_uint32()
+    wl.L.orchkv_last_pack_chunks(chunk_ms, 64, C.byref(n_chunk_ms))
+    chunk_ms = [chunk_ms[i] for i in range(min(64, n_chunk_ms.value))]
     lay = [C.c_uint32() for _ in range(3)]
     wl.L.orchkv_last_evict_layout(*[C.byref(x) for x in lay])
     play = [C.c_uint32() for _ in range(3)] + [C.c_int()]
@@ -432,6 +451,8 @@ def run_ours(args, rank, world, local_rank):
                      "ms": round(pk_ms.value, 4), "bytes": pk_bytes.value,
                      "achieved_gbs": round(pk_bytes.value / max(pk_ms.value, 1e-9) / 1e6, 1),
                      "frac": round(pk_bytes.value / max(pk_ms.value, 1e-9) / 1e6 / hbm_peak, 4),
+                     "first_chunk": pack_first_chunk(chunk_ms, pk_bytes.value, pk_chunks.value,
+                                                     hbm_peak),
                      "chunks": pk_chunks.value, "dram_runs": lay[0].value,
                      "ce_copies": lay[1].value, "zero_copy_blocks": lay[2].value},
             "host_link": {

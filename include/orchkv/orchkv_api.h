@@ -167,6 +167,11 @@ int  orchkv_evict_cold_batch(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_
 int  orchkv_last_migration_profile(float *pack_ms, unsigned long long *pack_bytes,
                                    uint32_t *chunks, float *promote_ms);
 
+/* Per-chunk device time of the last staged evict's pack kernels, in chunk
+ * order: ms[c] for c < min(*chunks, max_chunks) (synchronises).  *chunks = the
+ * staging slots the evict used (0 when the zero-copy kernel ran alone). */
+int  orchkv_last_pack_chunks(float *ms, uint32_t max_chunks, uint32_t *chunks);
+
 /* How the last staged evict reached the DRAM tier: `runs` = runs of
  * consecutive DRAM slabs it filled, `ce_copies` = copy-engine copies issued
  * (one per run of at least 1 MiB, split at staging-slot boundaries),

@@ -1271,6 +1271,18 @@ int orchkv_last_migration_profile(float *pack_ms, unsigned long long *pack_bytes
     return ORCHKV_OK;
 }
 
+int orchkv_last_pack_chunks(float *ms, uint32_t max_chunks, uint32_t *chunks)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    const uint32_t n = g.last_evict_staged ? g.last_chunks : 0;
+    if (chunks) *chunks = n;
+    for (uint32_t c = 0; ms && c < n && c < max_chunks; c++)
+        OKV_CUDA_TRY(cudaEventElapsedTime(&ms[c], g.ev_pk[2 * c], g.ev_pk[2 * c + 1]));
+    return ORCHKV_OK;
+}
+
 int orchkv_last_evict_layout(uint32_t *runs, uint32_t *ce_copies, uint32_t *zero_copy_slabs)
 {
     std::lock_guard<std::recursive_mutex> lk(g.mu);
