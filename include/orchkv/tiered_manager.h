@@ -232,6 +232,32 @@ int tm_report_attn_probs(tiered_manager_t *m, const float *probs,
 int tm_report_attn_batch_dev(tiered_manager_t *m, const uint32_t *block_ids,
                              const float *weights, uint32_t n);
 
+/* The vLLM attention hook's reduction and reports in one call
+ * (python/orchkv/vllm_integration/attention_hook.py:105-115,118-140,155-189:
+ * _blockwise_reduce, then tm_report_attn per (head, block)), without the
+ * device-to-host copy and the per-block calls.
+ *
+ *   weights    device [batch][heads][q_len][kv_len], contiguous, of dtype
+ *              0 = fp16, 1 = bf16, 2 = fp32 (the softmax output)
+ *   scores     device fp32 [heads][n_blocks], n_blocks = ceil(kv_len /
+ *              block_size), receives score(h, b) = the mean of weights over
+ *              batch, q_len and the block_size positions of block b, positions
+ *              at or past kv_len counting as zeros (the hook pads the last
+ *              block), computed in fp32 and rounded to the weights' type (the
+ *              type a mean over such a tensor returns)
+ *   block_ids  device uint32 [heads][n_blocks]: the id each (h, b) is
+ *              reported to, 0xFFFFFFFF = none; or NULL to compute the scores
+ *              only.  Reports are recorded as tm_notify_attn would, the heads
+ *              of one block b in order h = 0, 1, ...: ids of one block may
+ *              share a tracker slot (the hook's block-table mode gives every
+ *              head the same id); ids of different blocks must map to
+ *              different slots (slot = id & (capacity - 1)).
+ *
+ * block_size <= 4096.  Asynchronous. */
+int tm_report_attn_blockmean(tiered_manager_t *m, const void *weights, int dtype,
+                             uint32_t batch, uint32_t heads, uint32_t q_len, uint32_t kv_len,
+                             uint32_t block_size, const uint32_t *block_ids, float *scores);
+
 /* step_done + classification fused into one sweep: equivalent to
  * tm_step_done followed by the classification pass of tm_schedule_once
  * (src/scheduler/tiered_manager.c:205-213,318), without the threshold update,

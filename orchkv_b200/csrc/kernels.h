@@ -18,6 +18,12 @@ int launch_report_apply(const uint32_t *slots, const float *psum, const float *p
                         cudaStream_t s);
 int launch_report_batch(const uint32_t *ids, const float *w, uint32_t n,
                         const SchedDev &d, unsigned long long step, cudaStream_t s);
+// Block means of attention weights [batch][heads][q_len][kv_len] (dtype 0
+// fp16, 1 bf16, 2 fp32) into scores [heads][ceil(kv_len/bs)]; with ids and d,
+// each (h, b) is then recorded in the tracker, heads of one block in order.
+int launch_blockmean(const void *w, int dtype, uint32_t batch, uint32_t heads, uint32_t q_len,
+                     uint32_t kv_len, uint32_t bs, const uint32_t *ids, float *scores,
+                     const SchedDev *d, unsigned long long step, cudaStream_t s);
 int launch_sweep(const SchedDev &d, const SchedParams &p, bool step_done,
                  bool classify, ClassCounts *counts, cudaStream_t s);
 int launch_registry_count(const uint32_t *reg_slot, const uint8_t *reg_tier,

@@ -355,6 +355,8 @@ PYBIND11_MODULE(orchkv_core, m)
           [](uintptr_t tm, uintptr_t s) { return tm_set_stream(P<tiered_manager_t>(tm), P<void>(s)); },
           py::arg("tm"), py::arg("stream"));
     m.def("tm_sync", [](uintptr_t tm) { return tm_sync(P<tiered_manager_t>(tm)); }, py::arg("tm"));
+    m.def("tm_capacity", [](uintptr_t tm) { return tm_capacity(P<tiered_manager_t>(tm)); },
+          py::arg("tm"));
     m.def("tm_report_attn_probs",
           [](uintptr_t tm, uintptr_t probs, uint32_t n_rows, uint32_t hq, uint32_t hkv,
              uint32_t row_len, uint32_t tpb, uintptr_t ids, uintptr_t lens) {
@@ -365,6 +367,17 @@ PYBIND11_MODULE(orchkv_core, m)
           py::arg("tm"), py::arg("probs_ptr"), py::arg("n_rows"), py::arg("n_q_heads"),
           py::arg("n_kv_heads"), py::arg("row_len"), py::arg("tokens_per_block"),
           py::arg("block_ids_ptr"), py::arg("lens_ptr") = 0);
+    m.def("tm_report_attn_blockmean",
+          [](uintptr_t tm, uintptr_t weights, int dtype, uint32_t batch, uint32_t heads,
+             uint32_t q_len, uint32_t kv_len, uint32_t block_size, uintptr_t ids,
+             uintptr_t scores) {
+              return tm_report_attn_blockmean(P<tiered_manager_t>(tm), P<const void>(weights),
+                                              dtype, batch, heads, q_len, kv_len, block_size,
+                                              P<const uint32_t>(ids), P<float>(scores));
+          },
+          py::arg("tm"), py::arg("weights_ptr"), py::arg("dtype"), py::arg("batch"),
+          py::arg("heads"), py::arg("q_len"), py::arg("kv_len"), py::arg("block_size"),
+          py::arg("block_ids_ptr"), py::arg("scores_ptr"));
     m.def("tm_step_and_classify",
           [](uintptr_t tm) { return tm_step_and_classify(P<tiered_manager_t>(tm)); }, py::arg("tm"));
     m.def("tm_select_victims",

@@ -14,6 +14,9 @@
 // host with libm expf (as the reference does) and only read here.
 #include <atomic>
 
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
 #include "kernels.h"
 
 namespace okv {
@@ -276,6 +279,118 @@ int launch_report_batch(const uint32_t *ids, const float *w, uint32_t n,
 {
     if (n == 0) return ORCHKV_OK;
     report_batch_kernel<<<(n + 255) / 256, 256, 0, s>>>(ids, w, n, d, step); note_launches(1);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Block-mean scores of attention weights [batch][heads][q_len][kv_len] (the
+// vLLM hook's reduction), then their reports in (head, block) order
+// ---------------------------------------------------------------------------
+
+constexpr int kMeanThreads = 256;
+constexpr uint32_t kMeanMaxBlock = 4096;   // tokens per block the kernel accepts
+
+template <typename T> __device__ __forceinline__ float to_f32(T x);
+template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x)
+{
+    return __bfloat162float(x);
+}
+
+// The mean rounded to the weights' type, as a reduction over a tensor of that
+// type returns it.
+template <typename T> __device__ __forceinline__ float round_to(float x);
+template <> __device__ __forceinline__ float round_to<float>(float x) { return x; }
+template <> __device__ __forceinline__ float round_to<__half>(float x)
+{
+    return __half2float(__float2half_rn(x));
+}
+template <> __device__ __forceinline__ float round_to<__nv_bfloat16>(float x)
+{
+    return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// One CTA per (head h, tile of `bpc` consecutive blocks).  Each thread sums
+// its tokens over the batch x q_len rows (coalesced along tokens; batch, then
+// query position, in order), the per-token sums go to shared memory, and one
+// thread per block adds its block's tokens in order and divides by
+// batch * q_len * block_size: tokens past kv_len count as zeros, as in the
+// hook's padded view.
+template <typename T>
+__global__ void __launch_bounds__(kMeanThreads)
+blockmean_kernel(const T *__restrict__ w, uint32_t batch, uint32_t heads, uint32_t q_len,
+                 uint32_t kv_len, uint32_t bs, uint32_t nb, uint32_t bpc, float denom,
+                 float *scores)
+{
+    extern __shared__ float tok_sum[];
+    const uint32_t h = blockIdx.y;
+    const uint32_t b0 = blockIdx.x * bpc;
+    const uint32_t nblk = nb - b0 < bpc ? nb - b0 : bpc;
+    const uint32_t t0 = b0 * bs, ntok = nblk * bs;
+    const size_t row_stride = (size_t)q_len * kv_len;            // next query position
+    const size_t batch_stride = (size_t)heads * row_stride;      // next batch entry
+    for (uint32_t j = threadIdx.x; j < ntok; j += kMeanThreads) {
+        const uint32_t t = t0 + j;
+        float acc = 0.f;
+        if (t < kv_len) {
+            const T *p = w + (size_t)h * row_stride + t;
+            for (uint32_t bi = 0; bi < batch; bi++, p += batch_stride)
+                for (uint32_t q = 0; q < q_len; q++)
+                    acc = __fadd_rn(acc, to_f32<T>(p[(size_t)q * kv_len]));
+        }
+        tok_sum[j] = acc;
+    }
+    __syncthreads();
+    for (uint32_t k = threadIdx.x; k < nblk; k += kMeanThreads) {
+        float s = 0.f;
+        for (uint32_t j = 0; j < bs; j++) s = __fadd_rn(s, tok_sum[k * bs + j]);
+        scores[(size_t)h * nb + b0 + k] = round_to<T>(__fdiv_rn(s, denom));
+    }
+}
+
+// One thread per block column b: the reports (h, b) for h = 0 .. heads-1 in
+// that order, so a column whose heads share an id (or a tracker slot) adds
+// them in the order the per-block calls would.
+__global__ void blockmean_apply_kernel(const float *__restrict__ scores,
+                                       const uint32_t *__restrict__ ids, uint32_t heads,
+                                       uint32_t nb, SchedDev d, unsigned long long step)
+{
+    const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nb) return;
+    for (uint32_t h = 0; h < heads; h++)
+        record_mass(d, ids[(size_t)h * nb + b], scores[(size_t)h * nb + b], step);
+}
+
+int launch_blockmean(const void *w, int dtype, uint32_t batch, uint32_t heads, uint32_t q_len,
+                     uint32_t kv_len, uint32_t bs, const uint32_t *ids, float *scores,
+                     const SchedDev *d, unsigned long long step, cudaStream_t s)
+{
+    if (!w || !scores || batch == 0 || heads == 0 || q_len == 0 || kv_len == 0 || bs == 0 ||
+        bs > kMeanMaxBlock || dtype < 0 || dtype > 2)
+        return ORCHKV_ERR_INVALID;
+    const unsigned long long count = (unsigned long long)batch * q_len * bs;
+    const float denom = (float)count;         // elements averaged per block
+    const uint32_t nb = (kv_len + bs - 1) / bs;
+    const uint32_t bpc = bs >= (uint32_t)kMeanThreads ? 1 : kMeanThreads / bs;
+    const size_t smem = (size_t)bpc * bs * sizeof(float);
+    const dim3 grid((nb + bpc - 1) / bpc, heads);
+    if (grid.y > 65535) return ORCHKV_ERR_INVALID;
+    if (dtype == 0)
+        blockmean_kernel<__half><<<grid, kMeanThreads, smem, s>>>(
+            (const __half *)w, batch, heads, q_len, kv_len, bs, nb, bpc, denom, scores);
+    else if (dtype == 1)
+        blockmean_kernel<__nv_bfloat16><<<grid, kMeanThreads, smem, s>>>(
+            (const __nv_bfloat16 *)w, batch, heads, q_len, kv_len, bs, nb, bpc, denom, scores);
+    else
+        blockmean_kernel<float><<<grid, kMeanThreads, smem, s>>>(
+            (const float *)w, batch, heads, q_len, kv_len, bs, nb, bpc, denom, scores);
+    note_launches(1);
+    if (ids && d) {
+        blockmean_apply_kernel<<<(nb + 255) / 256, 256, 0, s>>>(scores, ids, heads, nb, *d, step);
+        note_launches(1);
+    }
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }

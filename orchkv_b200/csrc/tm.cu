@@ -903,6 +903,21 @@ int tm_report_attn_batch_dev(tiered_manager_t *m, const uint32_t *ids, const flo
     return launch_report_batch(ids, w, n, t->d, t->step, t->stream);
 }
 
+int tm_report_attn_blockmean(tiered_manager_t *m, const void *weights, int dtype,
+                             uint32_t batch, uint32_t heads, uint32_t q_len, uint32_t kv_len,
+                             uint32_t block_size, const uint32_t *block_ids, float *scores)
+{
+    OKV_RANGE("tm_report_attn_blockmean");
+    TmImpl *t = tm_impl(m);
+    if (!t) return ORCHKV_ERR_INVALID;
+    std::lock_guard<std::mutex> g(t->mu);
+    int rc = tm_flush_locked(t);
+    if (rc) return rc;
+    if (block_ids) t->mirror_dirty = true;
+    return launch_blockmean(weights, dtype, batch, heads, q_len, kv_len, block_size, block_ids,
+                            scores, block_ids ? &t->d : nullptr, t->step, t->stream);
+}
+
 int tm_step_and_classify(tiered_manager_t *m)
 {
     OKV_RANGE("tm_step_and_classify");

@@ -1,0 +1,240 @@
+"""orchkv_b200.attention_hook against the reference's
+python/orchkv/vllm_integration/attention_hook.py: the collector's sampling
+schedule and statistics, the block-mean scores (checked against torch's own
+mean over the same padded view, the reduction the reference runs), and the
+reports: after collecting several layers in each block-id mode (the default
+layer/head/block ids, a block_id_fn, a block table whose ids every head
+shares, and a mapping that puts two blocks on one tracker slot), the device
+tracker equals the oracle tracker fed the reference's per-block
+tm_report_attn sequence -- hits and last-hit steps exact, sums and EMA
+within 1e-5 relative (the mean is summed in another order).  Also the hook
+manager's wrapping of a model's self-attention modules."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+REL = 1e-5
+
+
+@pytest.fixture
+def hook_mod(cuda):
+    from orchkv_b200 import attention_hook
+    return attention_hook
+
+
+@pytest.fixture
+def tm(cuda):
+    import orchkv_b200 as o
+    core = o.core()
+    h = core.tm_create(tracker_cap=1024, ema_lambda=0.9)
+    yield h
+    core.tm_destroy(h)
+
+
+def torch_block_mean(torch, aw, n_blocks, block_size):
+    """The reference's reduction (attention_hook.py:118-140): zero-pad kv to
+    n_blocks * block_size, view as blocks, mean over batch, q and tokens."""
+    bs, h, q, kv = aw.shape
+    pad = n_blocks * block_size - kv
+    if pad:
+        aw = torch.nn.functional.pad(aw, (0, pad))
+    return aw.view(bs, h, q, n_blocks, block_size).mean(dim=(0, 2, 4))
+
+
+def softmax_weights(torch, g, shape, dtype=None):
+    w = torch.softmax(torch.randn(*shape, generator=g, device="cuda") * 2.0, dim=-1)
+    return w if dtype is None else w.to(dtype)
+
+
+# ---- sampling schedule and statistics -------------------------------------
+
+def test_sampling_schedule(hook_mod, tm):
+    c = hook_mod.AttentionScoreCollector(tm, block_size=16, sample_interval=5)
+    assert (c.block_size, c.sample_interval, c._step) == (16, 5, 0)
+    c.sample_interval = 3
+    seen = []
+    for _ in range(9):
+        seen.append(c.should_sample())
+        c.on_step_done()
+    assert seen == [True, False, False] * 3
+    c.set_enabled(False)
+    assert not c.should_sample()
+    c.set_enabled(True)
+    c.sample_interval = 0
+    assert c.sample_interval == 1
+
+
+def test_stats_count_like_the_reference(hook_mod, tm, cuda):
+    torch = cuda
+    c = hook_mod.AttentionScoreCollector(tm, block_size=4, sample_interval=2)
+    aw = torch.rand(1, 1, 1, 4, device="cuda")
+    calls = []
+    for _ in range(3):
+        c.collect(0, aw, block_id_fn=lambda l, h, bi: calls.append(bi) or bi)
+        c.on_step_done()
+    st = c.get_stats()
+    # steps 0 and 2 sampled; on_step_done counts the step it moves to
+    assert len(calls) == 2 and st["blocks_reported"] == 2
+    assert st["current_step"] == 3
+    assert (st["samples_taken"], st["steps_skipped"]) == (1, 2)
+
+
+# ---- the block-mean reduction ---------------------------------------------
+
+def test_block_mean_known_values(hook_mod, tm, cuda):
+    torch = cuda
+    c = hook_mod.AttentionScoreCollector(tm, block_size=4, sample_interval=1)
+    s = c._blockwise_reduce(torch.full((1, 2, 1, 8), 0.5, device="cuda"), 2)
+    assert s.shape == (2, 2) and torch.allclose(s, torch.full_like(s, 0.5))
+    s = c._blockwise_reduce(torch.ones(1, 1, 1, 6, device="cuda"), 2)      # padded tail
+    assert s[0].tolist() == [1.0, 0.5]
+    aw = torch.zeros(2, 4, 3, 12, device="cuda")
+    for h in range(4):
+        aw[:, h] = (h + 1) * 0.1
+    s = c._blockwise_reduce(aw, 3)
+    for h in range(4):
+        assert torch.allclose(s[h], torch.full_like(s[h], (h + 1) * 0.1), atol=1e-6)
+
+
+@pytest.mark.parametrize("shape,block_size", [((3, 8, 1, 1000), 16), ((2, 4, 5, 4096), 64),
+                                              ((1, 2, 2, 77), 32), ((4, 3, 1, 300), 512)])
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
+def test_block_mean_matches_torch(hook_mod, tm, cuda, shape, block_size, dtype):
+    torch = cuda
+    dt = getattr(torch, dtype)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    aw = softmax_weights(torch, g, shape, dt)
+    c = hook_mod.AttentionScoreCollector(tm, block_size=block_size, sample_interval=1)
+    nb = (shape[3] + block_size - 1) // block_size
+    got = c._blockwise_reduce(aw, nb)
+    want = torch_block_mean(torch, aw, nb, block_size)
+    assert got.dtype == want.dtype and got.shape == want.shape
+    a, b = got.float(), want.float()
+    if dt == torch.float32:
+        assert torch.all((a - b).abs() <= REL * b.abs().clamp_min(1e-30))
+    else:
+        # rounded to the weights' type: equal, or one unit in the last place
+        # where the fp32 means straddle a rounding boundary
+        ulp = 2.0 ** -7 if dt == torch.bfloat16 else 2.0 ** -10
+        assert torch.all((a - b).abs() <= ulp * b.abs().clamp_min(1e-30))
+        assert (a == b).float().mean().item() > 0.98
+
+
+# ---- reports against the oracle tracker ------------------------------------
+
+def _state(tm_handle):
+    import orchkv_b200 as o
+    from orchkv_b200._lib import TieredManager
+    L = o.lib()
+    m = C.cast(C.c_void_p(tm_handle), C.POINTER(TieredManager))
+    n = L.tm_capacity(m)
+    out = {"sum": np.zeros(n, np.float32), "ema": np.zeros(n, np.float32),
+           "hits": np.zeros(n, np.uint32), "last": np.zeros(n, np.uint64)}
+    assert L.tm_read_state(m, out["sum"].ctypes.data, out["ema"].ctypes.data,
+                           out["hits"].ctypes.data, out["last"].ctypes.data,
+                           None, None, None, None) == 0
+    return out
+
+
+def test_reports_match_reference_sequence(hook_mod, cuda, oracle_mod):
+    torch = cuda
+    import orchkv_b200 as o
+    core = o.core()
+    cap = 4096
+    tm = core.tm_create(tracker_cap=cap, ema_lambda=0.9)
+    try:
+        orc = oracle_mod.OracleSched(cap, 0.9, 0.5, 0.3, 0.2, 50.0)
+        H, bsz, kv, blk = 4, 2, 100, 16
+        nb = (kv + blk - 1) // blk
+        for bid in range(3000):
+            assert core.tm_register_block_id(tm, bid, 0, 0) == 0
+            orc.register(bid)
+        c = hook_mod.AttentionScoreCollector(tm, block_size=blk, sample_interval=1)
+        g = torch.Generator(device="cuda").manual_seed(3)
+        table = torch.tensor([[2000 + 7 * i for i in range(nb - 2)]], device="cuda")
+        modes = [
+            ("default", {}, lambda layer, h, bi: layer * H * nb + h * nb + bi),
+            ("fn", {"block_id_fn": lambda layer, h, bi: 1000 + 31 * h + bi}, None),
+            ("table", {"block_table": table}, None),
+            # blocks 0, 3 and 6 all report to id 2500: one tracker slot, three columns
+            ("shared", {"block_id_fn": lambda layer, h, bi: 2500 + (bi % 3) + 4 * h}, None),
+        ]
+        for step in range(3):
+            for layer, (name, kw, default) in enumerate(modes):
+                aw = softmax_weights(torch, g, (bsz, H, 1, kv))
+                c.collect(layer, aw, **kw)
+                ref_scores = torch_block_mean(torch, aw, nb, blk).cpu()
+                for h in range(H):
+                    for bi in range(nb):
+                        if name == "default":
+                            bid = default(layer, h, bi)
+                        elif name == "table":
+                            bid = int(table[0, bi]) if bi < table.shape[1] else \
+                                layer * H * nb + h * nb + bi
+                        else:
+                            bid = kw["block_id_fn"](layer, h, bi)
+                        orc.update(bid, float(ref_scores[h, bi]))
+            c.on_step_done()
+            orc.step_done()
+        core.tm_sync(tm)
+        got, want = _state(tm), orc.state()
+        for key in ("hits", "last"):
+            assert np.array_equal(got[key], want[key]), key
+        for key in ("sum", "ema"):
+            a, b = got[key], want[key]
+            assert np.all(np.abs(a - b) <= REL * np.maximum(np.abs(b), 1e-30)), key
+        assert np.count_nonzero(want["hits"]) > 60          # every mode touched its slots
+        assert c.get_stats()["blocks_reported"] == 3 * len(modes) * H * nb
+    finally:
+        core.tm_destroy(tm)
+
+
+# ---- the hook manager -------------------------------------------------------
+
+def _mock_model(torch, n_layers, heads, kv_len):
+    class SelfAttn(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.calls = 0
+
+        def forward(self, x, output_attentions=False, **kwargs):
+            self.calls += 1
+            out = torch.zeros(1, heads, 1, 8, device="cuda")
+            if output_attentions:
+                w = torch.rand(1, heads, 1, kv_len, device="cuda")
+                return out, w / w.sum(-1, keepdim=True)
+            return (out,)
+
+    model = torch.nn.Module()
+    model.layers = torch.nn.ModuleList()
+    for _ in range(n_layers):
+        layer = torch.nn.Module()
+        layer.self_attn = SelfAttn()
+        model.layers.append(layer)
+    return model
+
+
+def test_hook_manager_wraps_and_feeds(hook_mod, tm, cuda):
+    torch = cuda
+    c = hook_mod.AttentionScoreCollector(tm, block_size=4, sample_interval=5)
+    mgr = hook_mod.AttentionHookManager(c)
+    assert mgr.collector is c
+    model = _mock_model(torch, 2, 2, 16)
+    mgr.install(model)
+    st = mgr.get_stats()
+    assert st["installed"] and st["n_layers_hooked"] == 2
+    x = torch.zeros(1, 1, 8, device="cuda")
+    for step in range(20):
+        for layer in model.layers:
+            res = layer.self_attn(x)
+            assert len(res) == (2 if step % 5 == 0 else 1)
+        mgr.on_step_done()
+    cs = c.get_stats()
+    assert cs["current_step"] == 20 and cs["samples_taken"] == 4
+    assert cs["blocks_reported"] == 4 * 2 * 2 * 4       # samples x layers x heads x blocks
+    mgr.uninstall()
+    assert not mgr.get_stats()["installed"]
+    assert len(model.layers[0].self_attn(x, output_attentions=False)) == 1
