@@ -85,6 +85,7 @@ def test_stats_count_like_the_reference(hook_mod, tm, cuda):
 # ---- the block-mean reduction ---------------------------------------------
 
 def test_block_mean_known_values(hook_mod, tm, cuda):
+    """The reference's reduction known answers (test/test_attention_hook.py:67-99)."""
     torch = cuda
     c = hook_mod.AttentionScoreCollector(tm, block_size=4, sample_interval=1)
     s = c._blockwise_reduce(torch.full((1, 2, 1, 8), 0.5, device="cuda"), 2)

@@ -485,3 +485,65 @@ def test_batched_edge_cases(dp, cuda):
     rc, bid, tier, slab, st, tok = info(L, c, 0, 0, 0)
     assert bid == 0 and tier == 0
     assert L.orchkv_request_destroy(c) == 0
+
+
+@pytest.mark.parametrize("tpb,seed", [(64, 0xCAFEBABE), (8192, 0xDEADBEEF)])
+def test_seed_pattern_round_trips(cuda, tpb, seed):
+    """The reference's data-integrity known answers (test/test_gpu_dram.cu:40-55,
+    151-243): slabs of 32 KB and 4 MB (fp16, d_head 128, 64- and 8192-token
+    blocks) holding u32 words seed ^ i, GPU -> DRAM -> GPU by the batched and
+    by the per-block calls, every word checked after each hop."""
+    import orchkv_b200 as o
+    L = o.lib()
+    d, e = 128, 2
+    slab = tpb * d * e * 2
+    half, H, nblk = slab // 2, 2, 2
+    cfg = o.make_config(gpu_pool_bytes=8 * slab, dram_pool_bytes=8 * slab, tokens_per_block=tpb,
+                        d_head=d, dtype=0, max_blocks_per_head=4)
+    ext = o.OrchkvConfigExt()
+    ext.max_blocks = 64
+    assert L.orchkv_init_ext(C.byref(cfg), C.byref(ext)) == 0
+    try:
+        # slab (h, b) holds seed' ^ i with seed' = seed + 16 * h + b: K half
+        # first, V half second, as the slab layout puts them
+        pats = {(h, b): (np.uint32(seed + 16 * h + b) ^
+                         np.arange(slab // 4, dtype=np.uint32)).view(np.uint8)
+                for h in range(H) for b in range(nblk)}
+        k = np.empty((H, nblk * tpb, d * e), np.uint8)
+        v = np.empty_like(k)
+        for (h, b), p in pats.items():
+            k[h, b * tpb:(b + 1) * tpb] = p[:half].reshape(tpb, d * e)
+            v[h, b * tpb:(b + 1) * tpb] = p[half:].reshape(tpb, d * e)
+        c = L.orchkv_request_create(9, 1, H)
+        assert L.orchkv_prefill(c, 0, k.ctypes.data, v.ctypes.data, nblk * tpb) == 0
+
+        def check(tier_want):
+            for (h, b), p in pats.items():
+                rc, bid, tier, s, st, tok = info(L, c, 0, h, b)
+                assert rc == 0 and tier == tier_want
+                got = (read_dev(L.orchkv_gpu_pool_base() + s * slab, slab) if tier == 0 else
+                       read_host(L.orchkv_dram_pool_base() + s * slab, slab))
+                assert np.array_equal(got, p), (h, b)
+
+        check(0)
+        bids = cuda.tensor([info(L, c, 0, h, b)[1] for h in range(H) for b in range(nblk)],
+                           dtype=cuda.int32, device="cuda")
+        res = cuda.zeros(2, dtype=cuda.int32, device="cuda")
+        assert L.orchkv_evict_batch_to_dram(bids.data_ptr(), None, len(bids), res.data_ptr()) == 0
+        assert L.orchkv_sync() == 0
+        assert res.cpu().tolist() == [len(bids), 0]
+        check(1)
+        assert L.orchkv_promote_batch_to_gpu(bids.data_ptr(), None, len(bids), res.data_ptr()) == 0
+        assert L.orchkv_sync() == 0
+        check(0)
+        for h in range(H):
+            for b in range(nblk):
+                assert L.orchkv_evict_to_dram(c, 0, h, b) == 0
+        check(1)
+        for h in range(H):
+            for b in range(nblk):
+                assert L.orchkv_promote_to_gpu(c, 0, h, b) == 0
+        check(0)
+        assert L.orchkv_request_destroy(c) == 0
+    finally:
+        L.orchkv_shutdown()
