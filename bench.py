@@ -321,7 +321,7 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize()
 
-    link = host_link_probe(torch)
+    link = host_link_probe(torch, barrier=barrier if world > 1 else None)
     for _ in range(args.warmup):
         wl.step()
         wl.restore()
@@ -501,10 +501,12 @@ def run_ours(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
-def host_link_probe(torch, nbytes=512 << 20, reps=3):
+def host_link_probe(torch, nbytes=512 << 20, reps=3, barrier=None):
     """Copy-engine bandwidth of this GPU's host link with pinned memory, in
     GB/s: each direction alone, and both at once on two streams (bytes moved
-    in both directions over the time of the pair).  Best of `reps`."""
+    in both directions over the time of the pair).  Best of `reps`.  With
+    several ranks, `barrier` starts every rep on all ranks together, so each
+    rep measures this rank's share while every rank copies."""
     h = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
     d = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
     h2 = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
@@ -514,6 +516,8 @@ def host_link_probe(torch, nbytes=512 << 20, reps=3):
     for name, pairs in (("h2d", [(d, h)]), ("d2h", [(h, d)]), ("both", [(d, h), (h2, d2)])):
         best = 0.0
         for _ in range(reps):
+            if barrier:
+                barrier()
             torch.cuda.synchronize()
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
