@@ -547,3 +547,59 @@ def test_seed_pattern_round_trips(cuda, tpb, seed):
         assert L.orchkv_request_destroy(c) == 0
     finally:
         L.orchkv_shutdown()
+
+
+def test_concurrent_batches_from_threads(dp, cuda):
+    """Batched evicts and promotes issued from two host threads at once (two
+    requests, each thread its own): whichever order the library serialises
+    them in, every block moves once, its bytes are intact where it lands, and
+    the free stacks hold exactly the slabs not in use."""
+    import threading
+    o, L = dp
+    rng = np.random.default_rng(41)
+    H, n = 2, 16 * 8                                  # 16 blocks per request
+    data, ctxs, ids = [], [], []
+    for r in range(2):
+        k, v = kv_data(rng, H, n)
+        c = L.orchkv_request_create(50 + r, 1, H)
+        assert L.orchkv_prefill(c, 0, k.ctypes.data, v.ctypes.data, n) == 0
+        data.append((k, v))
+        ctxs.append(c)
+        ids.append([info(L, c, 0, h, b)[1] for h in range(H) for b in range(8)])
+    g_free0 = len(pool_state(L, 0, GPU_SLABS))
+    dev = [cuda.tensor(i, dtype=cuda.int32, device="cuda") for i in ids]
+    res = [cuda.zeros(2, dtype=cuda.int32, device="cuda") for _ in range(2)]
+    errors = []
+
+    def worker(r, fn):
+        try:
+            for _ in range(3):
+                rc = fn(dev[r].data_ptr(), None, len(ids[r]), res[r].data_ptr())
+                if rc != 0:
+                    errors.append(rc)
+        except Exception as e:                         # pragma: no cover - reported below
+            errors.append(repr(e))
+
+    for fn, tier in ((L.orchkv_evict_batch_to_dram, 1), (L.orchkv_promote_batch_to_gpu, 0)):
+        ts = [threading.Thread(target=worker, args=(r, fn)) for r in range(2)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+        assert L.orchkv_sync() == 0 and not errors
+        for r in range(2):
+            k, v = data[r]
+            for h in range(H):
+                for b in range(8):
+                    rc, bid, t_, slab, st, tok = info(L, ctxs[r], 0, h, b)
+                    assert rc == 0 and t_ == tier
+                    base = L.orchkv_dram_pool_base() if tier == 1 else L.orchkv_gpu_pool_base()
+                    got = (read_host if tier == 1 else read_dev)(base + slab * SLAB, SLAB)
+                    assert np.array_equal(got, expected_slab(k, v, h, b)), (r, h, b)
+        g_free, d_free = len(pool_state(L, 0, GPU_SLABS)), len(pool_state(L, 1, DRAM_SLABS))
+        if tier == 1:
+            assert g_free == g_free0 + 32 and d_free == DRAM_SLABS - 32
+        else:
+            assert g_free == g_free0 and d_free == DRAM_SLABS
+    for c in ctxs:
+        assert L.orchkv_request_destroy(c) == 0

@@ -61,6 +61,39 @@ def test_known_answers_gpu(okv):
     m.close()
 
 
+def test_concurrent_reports_from_threads(okv):
+    """The reference's concurrency case (test/test_attention_tracker.c:309-343):
+    4 threads each report weight 0.01 to one block 10,000 times; the sum ends
+    within 0.1 of 400.  ctypes drops the GIL for each call, so the threads run
+    the library's report path at the same time; a second block fed by the
+    same threads with weight 1.0 must end at exactly 40,000 hits of mass."""
+    import threading
+    L = okv.lib()
+    m = okv.Manager(tracker_cap=256, ema_lambda=0.9)
+    m.register_id(1)
+    m.register_id(2)
+
+    def worker():
+        for _ in range(10000):
+            L.tm_notify_attn(m.ref, 1, C.c_float(0.01))
+            L.tm_notify_attn(m.ref, 2, C.c_float(1.0))
+
+    threads = [threading.Thread(target=worker) for _ in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    st = m.state()
+    # all addends equal, so any interleaving gives the sequential fp32 sum
+    want = np.float32(0.0)
+    for _ in range(40000):
+        want = np.float32(want + np.float32(0.01))
+    assert st["sum"][1] == want and abs(float(want) - 400.0) < 0.1
+    assert float(st["sum"][2]) == 40000.0                # exact in fp32
+    assert st["hits"][1] == 0 and st["t_active"][1] == 1
+    m.close()
+
+
 def _dev(cuda, arr):
     return cuda.from_numpy(np.ascontiguousarray(arr)).cuda()
 
