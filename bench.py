@@ -191,7 +191,6 @@ class Workload:
         # host copies for the end-to-end variant
         self.h_probs = self.probs.cpu().pin_memory()
         self.h_tok = self.tok.cpu().pin_memory()
-        self.d_probs_e2e = torch_.empty_like(self.probs)
         torch_.cuda.synchronize()
         self.ev = [torch_.cuda.Event(enable_timing=True) for _ in range(10)]
         # the DRAM-resident reserve: one scoring pass, then the coldest 5%
@@ -214,8 +213,8 @@ class Workload:
         ev = self.ev
         ev[0].record()
         if e2e:
-            self.d_probs_e2e.copy_(self.h_probs, non_blocking=True)
-            probs = self.d_probs_e2e
+            # host buffers straight into the C ABI: the library copies them in
+            probs = self.h_probs
             kp, vp = self.h_tok[0].data_ptr(), self.h_tok[1].data_ptr()
         else:
             probs = self.probs
@@ -406,7 +405,10 @@ def run_ours(args, rank, world, local_rank):
                 xch[1] += xch_calls.value
             wl.restore()
             la = okv.lib().orchkv_kernel_launches()
-    # e2e through the C ABI with host inputs
+    # e2e through the C ABI with host inputs (one untimed step first: the
+    # library sizes its staging for host inputs on first use)
+    wl.step(e2e=True)
+    wl.restore()
     e2e_ms = []
     for _ in range(max(1, min(args.steps, 5))):
         barrier()

@@ -208,10 +208,10 @@ int       tm_read_state(tiered_manager_t *m, float *sum, float *ema,
  * Reduce per-token attention probabilities to per-block attention mass and
  * record it as tm_notify_attn would, for every block in one launch.
  *
- *   probs      device fp32 [n_rows][n_q_heads][row_len]  (row = request*L+layer,
+ *   probs      fp32 [n_rows][n_q_heads][row_len]  (row = request*L+layer,
  *              decode q_len = 1)
- *   lens       device uint32 [n_rows] valid tokens per row, or NULL (= row_len)
- *   block_ids  device uint32 [n_rows][n_kv_heads][ceil(row_len/tpb)]: the block
+ *   lens       uint32 [n_rows] valid tokens per row, or NULL (= row_len)
+ *   block_ids  uint32 [n_rows][n_kv_heads][ceil(row_len/tpb)]: the block
  *              id receiving the mass of (row, kv head, token block);
  *              0xFFFFFFFF = none.  Within one call the ids must map to
  *              distinct tracker slots (slot = id & (capacity - 1)): unique
@@ -220,7 +220,9 @@ int       tm_read_state(tiered_manager_t *m, float *sum, float *ema,
  * mass(row,h,b) = sum over the n_q_heads/n_kv_heads query heads of KV group h
  * and the tokens of block b of probs.  A block's per-step sum, max and last
  * hit then update exactly as attn_tracker_update
- * (src/scheduler/attention_tracker.c:27-33,75-92).  Asynchronous. */
+ * (src/scheduler/attention_tracker.c:27-33,75-92).  Each array may be in
+ * device memory (read in place) or in host memory, pinned or pageable
+ * (copied once to the device on the manager's stream).  Asynchronous. */
 int tm_report_attn_probs(tiered_manager_t *m, const float *probs,
                          uint32_t n_rows, uint32_t n_q_heads, uint32_t n_kv_heads,
                          uint32_t row_len, uint32_t tokens_per_block,

@@ -117,6 +117,7 @@ static void free_device(TmImpl *t)
     cudaFree(t->dev_block);
     cudaFree(t->up_dev);
     cudaFree(t->reg_dev);
+    cudaFree(t->in_stage);
     cudaFreeHost(t->m_hot);
     cudaFreeHost(t->m_heat);
     cudaFreeHost(t->m_cact);
@@ -876,6 +877,52 @@ int tm_read_state(tiered_manager_t *m, float *sum, float *ema, uint32_t *hits,
     return ORCHKV_OK;
 }
 
+// Inputs of tm_report_attn_probs in host memory (pinned or pageable) are
+// copied once into the manager's staging buffer on its stream; device and
+// managed memory is read in place.  The buffer grows before any copy is
+// queued, so no pointer handed out earlier in the same call is stranded.
+static bool on_device(const void *p)
+{
+    cudaPointerAttributes a;
+    const cudaError_t e = cudaPointerGetAttributes(&a, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+static int stage_inputs(TmImpl *t, const void **ptrs, const size_t *bytes, int n)
+{
+    size_t off[4] = {0}, need = 0;
+    bool host[4] = {false};
+    for (int i = 0; i < n; i++) {
+        host[i] = ptrs[i] && bytes[i] && !on_device(ptrs[i]);
+        if (host[i]) {
+            off[i] = need;
+            need += (bytes[i] + 255) & ~size_t(255);
+        }
+    }
+    if (need == 0) return ORCHKV_OK;
+    if (need > t->in_stage_cap) {
+        size_t cap = t->in_stage_cap ? t->in_stage_cap : (1 << 20);
+        while (cap < need) cap *= 2;
+        OKV_CUDA_TRY(cudaStreamSynchronize(t->stream));   // earlier launches may still read it
+        cudaFree(t->in_stage);
+        t->in_stage = nullptr;
+        t->in_stage_cap = 0;
+        OKV_CUDA_TRY(cudaMalloc((void **)&t->in_stage, cap));
+        t->in_stage_cap = cap;
+    }
+    for (int i = 0; i < n; i++) {
+        if (!host[i]) continue;
+        OKV_CUDA_TRY(cudaMemcpyAsync(t->in_stage + off[i], ptrs[i], bytes[i],
+                                     cudaMemcpyHostToDevice, t->stream));
+        ptrs[i] = t->in_stage + off[i];
+    }
+    return ORCHKV_OK;
+}
+
 int tm_report_attn_probs(tiered_manager_t *m, const float *probs, uint32_t n_rows,
                          uint32_t n_q_heads, uint32_t n_kv_heads, uint32_t row_len,
                          uint32_t tpb, const uint32_t *lens, const uint32_t *block_ids)
@@ -883,12 +930,23 @@ int tm_report_attn_probs(tiered_manager_t *m, const float *probs, uint32_t n_row
     OKV_RANGE("tm_report_attn_probs");
     TmImpl *t = tm_impl(m);
     if (!t) return ORCHKV_ERR_INVALID;
+    if (!probs || !block_ids || n_rows == 0 || n_q_heads == 0 || n_kv_heads == 0 ||
+        row_len == 0 || tpb == 0 || n_q_heads % n_kv_heads != 0)
+        return ORCHKV_ERR_INVALID;
     std::lock_guard<std::mutex> g(t->mu);
     int rc = tm_flush_locked(t);
     if (rc) return rc;
+    const size_t nb = (row_len + tpb - 1) / tpb;
+    const void *in[3] = {probs, lens, block_ids};
+    const size_t bytes[3] = {(size_t)n_rows * n_q_heads * row_len * sizeof(float),
+                             lens ? (size_t)n_rows * sizeof(uint32_t) : 0,
+                             (size_t)n_rows * n_kv_heads * nb * sizeof(uint32_t)};
+    rc = stage_inputs(t, in, bytes, 3);
+    if (rc) return rc;
     t->mirror_dirty = true;
-    return launch_score(probs, n_rows, n_q_heads, n_kv_heads, row_len, tpb, lens, block_ids,
-                        t->d, t->step, t->stream);
+    return launch_score((const float *)in[0], n_rows, n_q_heads, n_kv_heads, row_len, tpb,
+                        (const uint32_t *)in[1], (const uint32_t *)in[2], t->d, t->step,
+                        t->stream);
 }
 
 int tm_report_attn_batch_dev(tiered_manager_t *m, const uint32_t *ids, const float *w,

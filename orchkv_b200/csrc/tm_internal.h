@@ -100,6 +100,8 @@ struct TmImpl {
     std::vector<RegEntry> reg_tmp;
     char *reg_host = nullptr, *reg_dev = nullptr;
     size_t reg_cap = 0;
+    char *in_stage = nullptr;     // device copies of host inputs to tm_report_attn_probs
+    size_t in_stage_cap = 0;
 
     // multi-GPU selection hooks (set by the comm layer)
     okv::hist_reduce_fn comm_reduce = nullptr;

@@ -61,6 +61,40 @@ def test_known_answers_gpu(okv):
     m.close()
 
 
+@pytest.mark.parametrize("where", ["pinned", "pageable"])
+def test_tensor_scoring_host_inputs(okv, cuda, where):
+    """tm_report_attn_probs reading host buffers (probabilities, lengths and
+    ids, pinned or pageable) records exactly what it records from device
+    copies of the same arrays, over two calls (the second grows nothing)."""
+    rng = np.random.default_rng(77)
+    R, Hq, Hkv, T, tpb = 5, 8, 2, 1024, 16
+    nb = T // tpb
+    ids = np.arange(R * Hkv * nb, dtype=np.uint32)
+    states = []
+    for mode in ("device", where):
+        m = okv.Manager(tracker_cap=R * Hkv * nb, max_blocks=1 << 20)
+        for i in range(R * Hkv * nb):
+            m.register_id(i)
+        for call in range(2):
+            r2 = np.random.default_rng(call)
+            probs = _mk_probs(r2, R, Hq, T)
+            lens = r2.integers(1, T + 1, R).astype(np.uint32)
+            if mode == "device":
+                bufs = [_dev(cuda, a) for a in (probs, lens, ids)]
+            else:
+                bufs = [cuda.from_numpy(a.copy()) for a in (probs, lens, ids)]
+                if where == "pinned":
+                    bufs = [b.pin_memory() for b in bufs]
+            assert okv.lib().tm_report_attn_probs(m.ref, bufs[0].data_ptr(), R, Hq, Hkv, T, tpb,
+                                                  bufs[1].data_ptr(), bufs[2].data_ptr()) == 0
+            m.step_done()
+        states.append(m.state())
+        m.close()
+    for key in ("sum", "ema", "hits", "last"):
+        assert np.array_equal(states[0][key], states[1][key]), key
+    assert np.count_nonzero(states[0]["hits"]) > R * Hkv * 8
+
+
 def test_concurrent_reports_from_threads(okv):
     """The reference's concurrency case (test/test_attention_tracker.c:309-343):
     4 threads each report weight 0.01 to one block 10,000 times; the sum ends
