@@ -239,3 +239,31 @@ def test_hook_manager_wraps_and_feeds(hook_mod, tm, cuda):
     mgr.uninstall()
     assert not mgr.get_stats()["installed"]
     assert len(model.layers[0].self_attn(x, output_attentions=False)) == 1
+
+
+def test_blockmean_rejects_bad_arguments(hook_mod, tm, cuda):
+    """Invalid shapes, types, block sizes and null buffers return
+    ORCHKV_ERR_INVALID (-2)."""
+    torch = cuda
+    import orchkv_b200 as o
+    core = o.core()
+    w = torch.rand(1, 2, 1, 64, device="cuda")
+    s = torch.zeros(2, 4, device="cuda")
+    ids = torch.zeros(2, 4, dtype=torch.int32, device="cuda")
+    ok = (tm, w.data_ptr(), 2, 1, 2, 1, 64, 16, ids.data_ptr(), s.data_ptr())
+    assert core.tm_report_attn_blockmean(*ok) == 0
+    bad = [
+        dict(i=2, v=3),            # dtype
+        dict(i=3, v=0),            # batch
+        dict(i=4, v=0),            # heads
+        dict(i=5, v=0),            # q_len
+        dict(i=6, v=0),            # kv_len
+        dict(i=7, v=0),            # block_size
+        dict(i=7, v=8192),         # block_size above 4096
+        dict(i=1, v=0),            # weights
+        dict(i=9, v=0),            # scores
+    ]
+    for b in bad:
+        args = list(ok)
+        args[b["i"]] = b["v"]
+        assert core.tm_report_attn_blockmean(*args) == -2, b
