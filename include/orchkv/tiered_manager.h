@@ -228,6 +228,24 @@ int tm_report_attn_probs(tiered_manager_t *m, const float *probs,
                          uint32_t row_len, uint32_t tokens_per_block,
                          const uint32_t *lens, const uint32_t *block_ids);
 
+/* The original KVCacheManager's per-block report in one call
+ * (python/orchkv/kvcache_manager.py:317-347: one float(avg[:, s:e].sum()) and
+ * one tm_report_attn per block).
+ *
+ *   avg        fp32 [heads][kv_len]: the attention weights averaged over batch
+ *              and query positions (the manager's own mean)
+ *   starts, ends, block_ids   uint32 [n]: block i covers tokens
+ *              [starts[i], ends[i]) and reports to block_ids[i]
+ *
+ * Block i records sum over h and t in [starts[i], min(ends[i], kv_len)) of
+ * avg[h][t] as tm_notify_attn would; a block whose range is empty is not
+ * reported.  The ids must map to different tracker slots.  Each array may
+ * be in device or host memory (host arrays are copied once on the manager's
+ * stream).  Asynchronous. */
+int tm_report_attn_ranges(tiered_manager_t *m, const float *avg, uint32_t heads,
+                          uint32_t kv_len, const uint32_t *starts, const uint32_t *ends,
+                          const uint32_t *block_ids, uint32_t n);
+
 /* Report a batch of (id, weight) pairs already on the device, applied in
  * array order per block (attn_tracker_update_batch semantics,
  * src/scheduler/attention_tracker.c:95-118) provided ids are unique. */

@@ -175,6 +175,7 @@ _SIGS = {
     "tm_read_state": (i32, [P(TieredManager), vp, vp, vp, vp, vp, vp, vp, vp]),
     "tm_report_attn_probs": (i32, [P(TieredManager), vp, u32, u32, u32, u32, u32, vp, vp]),
     "tm_report_attn_batch_dev": (i32, [P(TieredManager), vp, vp, u32]),
+    "tm_report_attn_ranges": (i32, [P(TieredManager), vp, u32, u32, vp, vp, vp, u32]),
     "tm_report_attn_blockmean": (i32, [P(TieredManager), vp, i32, u32, u32, u32, u32, u32, vp,
                                        vp]),
     "tm_step_and_classify": (i32, [P(TieredManager)]),

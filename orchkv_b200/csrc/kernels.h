@@ -18,6 +18,11 @@ int launch_report_apply(const uint32_t *slots, const float *psum, const float *p
                         cudaStream_t s);
 int launch_report_batch(const uint32_t *ids, const float *w, uint32_t n,
                         const SchedDev &d, unsigned long long step, cudaStream_t s);
+// Per-block mass over token ranges: sum over heads and tokens [start, min(end,
+// kv_len)) of avg [heads][kv_len], recorded for ids[i]; empty ranges skipped.
+int launch_range_mass(const float *avg, uint32_t heads, uint32_t kv_len, const uint32_t *start,
+                      const uint32_t *end, const uint32_t *ids, uint32_t n, const SchedDev &d,
+                      unsigned long long step, cudaStream_t s);
 // Block means of attention weights [batch][heads][q_len][kv_len] (dtype 0
 // fp16, 1 bf16, 2 fp32) into scores [heads][ceil(kv_len/bs)]; with ids and d,
 // each (h, b) is then recorded in the tracker, heads of one block in order.

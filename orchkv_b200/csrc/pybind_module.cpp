@@ -367,6 +367,15 @@ PYBIND11_MODULE(orchkv_core, m)
           py::arg("tm"), py::arg("probs_ptr"), py::arg("n_rows"), py::arg("n_q_heads"),
           py::arg("n_kv_heads"), py::arg("row_len"), py::arg("tokens_per_block"),
           py::arg("block_ids_ptr"), py::arg("lens_ptr") = 0);
+    m.def("tm_report_attn_ranges",
+          [](uintptr_t tm, uintptr_t avg, uint32_t heads, uint32_t kv_len, uintptr_t starts,
+             uintptr_t ends, uintptr_t ids, uint32_t n) {
+              return tm_report_attn_ranges(P<tiered_manager_t>(tm), P<const float>(avg), heads,
+                                           kv_len, P<const uint32_t>(starts),
+                                           P<const uint32_t>(ends), P<const uint32_t>(ids), n);
+          },
+          py::arg("tm"), py::arg("avg_ptr"), py::arg("heads"), py::arg("kv_len"),
+          py::arg("starts_ptr"), py::arg("ends_ptr"), py::arg("block_ids_ptr"), py::arg("n"));
     m.def("tm_report_attn_blockmean",
           [](uintptr_t tm, uintptr_t weights, int dtype, uint32_t batch, uint32_t heads,
              uint32_t q_len, uint32_t kv_len, uint32_t block_size, uintptr_t ids,

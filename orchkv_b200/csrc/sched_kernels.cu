@@ -396,6 +396,52 @@ int launch_blockmean(const void *w, int dtype, uint32_t batch, uint32_t heads, u
 }
 
 // ---------------------------------------------------------------------------
+// Token-range mass (the original KVCacheManager's report): block i gets the
+// sum over all heads h and tokens t in [start_i, min(end_i, kv_len)) of
+// avg[h][t]; blocks whose range is empty are not reported
+// ---------------------------------------------------------------------------
+
+// One warp per block: heads in order, lanes strided over the block's tokens
+// (coalesced), a warp sum, one tracker record by lane 0.
+__global__ void range_mass_kernel(const float *__restrict__ avg, uint32_t heads,
+                                  uint32_t kv_len, const uint32_t *__restrict__ start,
+                                  const uint32_t *__restrict__ end,
+                                  const uint32_t *__restrict__ ids, uint32_t n, SchedDev d,
+                                  unsigned long long step)
+{
+    const unsigned lane = threadIdx.x & 31;
+    const unsigned long long nw = ((unsigned long long)gridDim.x * blockDim.x) >> 5;
+    for (unsigned long long i = ((unsigned long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+         i < n; i += nw) {
+        const uint32_t s = start[i];
+        const uint32_t e = end[i] < kv_len ? end[i] : kv_len;
+        if (s >= e) continue;                          // warp-uniform
+        float acc = 0.f;
+        for (uint32_t h = 0; h < heads; h++) {
+            const float *row = avg + (size_t)h * kv_len;
+            for (uint32_t t = s + lane; t < e; t += 32) acc = __fadd_rn(acc, row[t]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, o));
+        if (lane == 0) record_mass(d, ids[i], acc, step);
+    }
+}
+
+int launch_range_mass(const float *avg, uint32_t heads, uint32_t kv_len, const uint32_t *start,
+                      const uint32_t *end, const uint32_t *ids, uint32_t n, const SchedDev &d,
+                      unsigned long long step, cudaStream_t s)
+{
+    if (!avg || !start || !end || !ids || heads == 0 || kv_len == 0) return ORCHKV_ERR_INVALID;
+    if (n == 0) return ORCHKV_OK;
+    unsigned grid = (unsigned)(((unsigned long long)n * 32 + 255) / 256);
+    if (grid > 148 * 16) grid = 148 * 16;
+    range_mass_kernel<<<grid, 256, 0, s>>>(avg, heads, kv_len, start, end, ids, n, d, step);
+    note_launches(1);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+// ---------------------------------------------------------------------------
 // K2: step_done (EMA) and classification sweep
 // ---------------------------------------------------------------------------
 

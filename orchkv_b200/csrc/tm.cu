@@ -949,6 +949,29 @@ int tm_report_attn_probs(tiered_manager_t *m, const float *probs, uint32_t n_row
                         t->stream);
 }
 
+int tm_report_attn_ranges(tiered_manager_t *m, const float *avg, uint32_t heads,
+                          uint32_t kv_len, const uint32_t *starts, const uint32_t *ends,
+                          const uint32_t *block_ids, uint32_t n)
+{
+    OKV_RANGE("tm_report_attn_ranges");
+    TmImpl *t = tm_impl(m);
+    if (!t || !avg || heads == 0 || kv_len == 0 || (n && (!starts || !ends || !block_ids)))
+        return ORCHKV_ERR_INVALID;
+    std::lock_guard<std::mutex> g(t->mu);
+    int rc = tm_flush_locked(t);
+    if (rc) return rc;
+    if (n == 0) return ORCHKV_OK;
+    const void *in[4] = {avg, starts, ends, block_ids};
+    const size_t bytes[4] = {(size_t)heads * kv_len * sizeof(float), (size_t)n * 4,
+                             (size_t)n * 4, (size_t)n * 4};
+    rc = stage_inputs(t, in, bytes, 4);
+    if (rc) return rc;
+    t->mirror_dirty = true;
+    return launch_range_mass((const float *)in[0], heads, kv_len, (const uint32_t *)in[1],
+                             (const uint32_t *)in[2], (const uint32_t *)in[3], n, t->d, t->step,
+                             t->stream);
+}
+
 int tm_report_attn_batch_dev(tiered_manager_t *m, const uint32_t *ids, const float *w,
                              uint32_t n)
 {
