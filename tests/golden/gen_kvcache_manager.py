@@ -90,9 +90,11 @@ class Recorder(types.ModuleType):
         self.calls.append(["tier", int(bid), int(tier)])
 
 
-def load_reference(rec):
+def load_reference(rec, path=REFERENCE, name="ref_kvcache_manager"):
+    """Load a reference manager module with `rec` as its orchkv_core and its
+    CUDA placements mapped to the CPU."""
     sys.modules["orchkv_core"] = rec
-    spec = importlib.util.spec_from_file_location("ref_kvcache_manager", REFERENCE)
+    spec = importlib.util.spec_from_file_location(name, path)
     mod = importlib.util.module_from_spec(spec)
     sys.modules[spec.name] = mod              # its dataclasses look their module up
     spec.loader.exec_module(mod)
@@ -105,6 +107,10 @@ def load_reference(rec):
         @staticmethod
         def zeros(*a, device=None, pin_memory=False, **k):
             return torch.zeros(*a, **k)
+
+        @staticmethod
+        def empty(*a, device=None, pin_memory=False, **k):
+            return torch.empty(*a, **k)
 
         @staticmethod
         def empty_like(t, device=None, pin_memory=False, **k):

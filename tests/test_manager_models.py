@@ -1,11 +1,17 @@
-"""The oracle's restatement of the reference KVCacheManager
-(oracle/kvcache_manager_model.py) pinned to the reference itself: replayed on
-the seeded inputs of tests/golden/kvcache_manager_decode.json (recorded from
-the reference's python/orchkv/kvcache_manager.py by
-tests/golden/gen_kvcache_manager.py), it makes every tracker call the
+"""The oracle's restatements of the reference's two Python managers pinned
+to the reference itself.  Replayed on the seeded inputs of a fixture recorded
+from the reference's own module, each model makes every tracker call the
 reference made, in the same order with the same arguments (scores and usage
-ratios bit for bit), and reaches the same schedule results, statistics, block
-tiers and access counts after every step and every rebuild."""
+ratios bit for bit), and reaches the same results after every step:
+
+* oracle/kvcache_manager_model.py vs python/orchkv/kvcache_manager.py
+  (tests/golden/kvcache_manager_decode.json, gen_kvcache_manager.py):
+  schedule results, statistics, block tiers and access counts, also after
+  every rebuild;
+* oracle/fast_manager_model.py vs python/orchkv/fast_kvcache_manager.py
+  (tests/golden/fast_manager_decode.json, gen_fast_manager.py, the reference
+  run against the reference scheduler compiled from its sources): schedule
+  results, statistics and evicted blocks, also after every restore."""
 import json
 import os
 
@@ -45,6 +51,9 @@ class RecordingTM:
         self.calls.append(["tier", int(bid), int(tier)])
         self.tm.set_block_tier(bid, tier)
 
+    def __getattr__(self, name):               # reads (score, heat, stats, s) pass through
+        return getattr(self.tm, name)
+
 
 def test_model_matches_reference_manager_run(oracle_mod):
     from oracle.kvcache_manager_model import ModelKVManager
@@ -83,3 +92,32 @@ def test_model_matches_reference_manager_run(oracle_mod):
             assert blocks() == want["after_build"]["blocks"], s
     assert model.tm.calls == fx["calls"]
     assert want["stats"]["migrations"]["ssd_to_dram"] > 0
+
+
+def test_fast_model_matches_reference_manager_run(oracle_mod):
+    from oracle.fast_manager_model import FastManagerModel
+    from tests.golden.gen_fast_manager import inputs
+    from tests.golden.gen_kvcache_manager import f32bits
+    with open(os.path.join(HERE, "golden", "fast_manager_decode.json")) as fh:
+        fx = json.load(fh)
+    c = fx["case"]
+    k0, v0, kt, vt, attn = inputs(c)
+    L, H, d, bs = c["n_layers"], c["n_kv_heads"], c["head_dim"], c["block_size"]
+    model = FastManagerModel(L, H, d, block_size=bs, dtype=np.float16,
+                             gpu_budget_bytes=c["budget_blocks_per_layer"] * L * 2 * H * bs * d * 2,
+                             max_seq_len=c["max_seq_len"], sink_tokens=c["sink_tokens"])
+    model.tm = RecordingTM(model.tm, f32bits)
+    model.ingest([k0[i] for i in range(L)], [v0[i] for i in range(L)])
+    for s, want in enumerate(fx["steps"]):
+        model.append([kt[s, i] for i in range(L)], [vt[s, i] for i in range(L)])
+        for layer in range(L):
+            model.report_attention(attn[s][layer][0, :, 0, :])
+        model.step_done()
+        assert model.schedule() == want["schedule"], s
+        assert model.get_stats() == want["stats"], s
+        assert model.evicted_blocks() == want["evicted"], s
+        if "after_restore" in want:
+            model.restore()
+            assert model.get_stats() == want["after_restore"]["stats"], s
+    assert model.tm.calls == fx["calls"]
+    assert sum(st["stats"]["migrations"]["evictions_this_step"] for st in fx["steps"]) > 20
