@@ -6,7 +6,8 @@ reports: after collecting several layers in each block-id mode (the default
 layer/head/block ids, a block_id_fn, a block table whose ids every head
 shares, and a mapping that puts two blocks on one tracker slot), the device
 tracker equals the oracle tracker fed the reference's per-block
-tm_report_attn sequence -- hits and last-hit steps exact, sums and EMA
+tm_report_attn sequence (oracle/hook_model.py, pinned to the reference
+hook's own run) -- hits and last-hit steps exact, sums and EMA
 within 1e-5 relative (the mean is summed in another order).  Also the hook
 manager's wrapping of a model's self-attention modules."""
 import ctypes as C
@@ -35,13 +36,12 @@ def tm(cuda):
 
 
 def torch_block_mean(torch, aw, n_blocks, block_size):
-    """The reference's reduction (attention_hook.py:118-140): zero-pad kv to
-    n_blocks * block_size, view as blocks, mean over batch, q and tokens."""
-    bs, h, q, kv = aw.shape
-    pad = n_blocks * block_size - kv
-    if pad:
-        aw = torch.nn.functional.pad(aw, (0, pad))
-    return aw.view(bs, h, q, n_blocks, block_size).mean(dim=(0, 2, 4))
+    """The reference's reduction (attention_hook.py:118-140), from the oracle's
+    hook model (pinned to the reference hook's own run)."""
+    from oracle.hook_model import block_means
+    out = block_means(aw, block_size)
+    assert out.shape[1] == n_blocks
+    return out
 
 
 def softmax_weights(torch, g, shape, dtype=None):
@@ -156,28 +156,22 @@ def test_reports_match_reference_sequence(hook_mod, cuda, oracle_mod):
         c = hook_mod.AttentionScoreCollector(tm, block_size=blk, sample_interval=1)
         g = torch.Generator(device="cuda").manual_seed(3)
         table = torch.tensor([[2000 + 7 * i for i in range(nb - 2)]], device="cuda")
+        from oracle.hook_model import hook_reports
         modes = [
-            ("default", {}, lambda layer, h, bi: layer * H * nb + h * nb + bi),
-            ("fn", {"block_id_fn": lambda layer, h, bi: 1000 + 31 * h + bi}, None),
-            ("table", {"block_table": table}, None),
+            ("default", {}),
+            ("fn", {"block_id_fn": lambda layer, h, bi: 1000 + 31 * h + bi}),
+            ("table", {"block_table": table}),
             # blocks 0, 3 and 6 all report to id 2500: one tracker slot, three columns
-            ("shared", {"block_id_fn": lambda layer, h, bi: 2500 + (bi % 3) + 4 * h}, None),
+            ("shared", {"block_id_fn": lambda layer, h, bi: 2500 + (bi % 3) + 4 * h}),
         ]
         for step in range(3):
-            for layer, (name, kw, default) in enumerate(modes):
+            for layer, (name, kw) in enumerate(modes):
                 aw = softmax_weights(torch, g, (bsz, H, 1, kv))
                 c.collect(layer, aw, **kw)
-                ref_scores = torch_block_mean(torch, aw, nb, blk).cpu()
-                for h in range(H):
-                    for bi in range(nb):
-                        if name == "default":
-                            bid = default(layer, h, bi)
-                        elif name == "table":
-                            bid = int(table[0, bi]) if bi < table.shape[1] else \
-                                layer * H * nb + h * nb + bi
-                        else:
-                            bid = kw["block_id_fn"](layer, h, bi)
-                        orc.update(bid, float(ref_scores[h, bi]))
+                # the reference hook's report sequence (oracle/hook_model.py)
+                for bid, score in hook_reports(layer, aw, blk, kw.get("block_table"),
+                                               kw.get("block_id_fn")):
+                    orc.update(bid, score)
             c.on_step_done()
             orc.step_done()
         core.tm_sync(tm)

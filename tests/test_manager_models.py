@@ -121,3 +121,31 @@ def test_fast_model_matches_reference_manager_run(oracle_mod):
             assert model.get_stats() == want["after_restore"]["stats"], s
     assert model.tm.calls == fx["calls"]
     assert sum(st["stats"]["migrations"]["evictions_this_step"] for st in fx["steps"]) > 20
+
+
+def test_hook_model_matches_reference_hook_run():
+    """oracle/hook_model.py (the report sequence the GPU hook tests compare
+    with) against the reference's own AttentionScoreCollector
+    (tests/golden/attention_hook_reports.json, gen_attention_hook.py): the
+    same tm_report_attn calls, scores bit for bit, in every block-id mode,
+    on the sampled steps only."""
+    from oracle.hook_model import hook_reports
+    from tests.golden.gen_attention_hook import MODES, id_fn, weights
+    from tests.golden.gen_kvcache_manager import f32bits
+    with open(os.path.join(HERE, "golden", "attention_hook_reports.json")) as fh:
+        fx = json.load(fh)
+    c = fx["case"]
+    ws = weights(c)
+    table = torch.tensor([c["table"]], dtype=torch.int64)
+    calls = []
+    for s in range(c["steps"]):
+        if s % c["sample_interval"] == 0:
+            for layer, mode in enumerate(MODES):
+                for bid, score in hook_reports(layer, torch.from_numpy(ws[s][layer]),
+                                               c["block_size"],
+                                               table if mode == "table" else None,
+                                               id_fn(mode)):
+                    calls.append(["rep", bid, f32bits(score)])
+        calls.append(["step"])
+    assert calls == fx["calls"]
+    assert fx["stats"]["blocks_reported"] == sum(1 for x in calls if x[0] == "rep")
