@@ -304,6 +304,15 @@ def pack_roofline(launch_ms, total_bytes, hbm_peak, peak_kind):
                               "full-chunk launch, scaled by bytes per launch"}
 
 
+def unpack_launches(L):
+    """Per-launch device times (ms) of the last promote's unpack kernels and
+    the bytes they moved in total."""
+    ms, nb, n = (C.c_float * 64)(), (C.c_ulonglong * 64)(), C.c_uint32()
+    L.orchkv_last_unpack_chunks(ms, nb, 64, C.byref(n))
+    k = min(64, n.value)
+    return [ms[i] for i in range(k)], sum(nb[i] for i in range(k))
+
+
 def pack_launches(L):
     """Per-launch device times (ms) of the last staged evict's pack kernels
     and the bytes they read and wrote in total."""
@@ -369,6 +378,7 @@ def run_ours(args, rank, world, local_rank):
     # the DRAM-resident remainder runs outside the brackets
     step_ms, phase_acc, score_ms = [], {}, []
     pack_ms_acc, pack_bytes_acc = [], 0
+    unpack_ms_acc, unpack_bytes_acc = [], 0
     migrated = 0
     launches0 = okv.lib().orchkv_kernel_launches()
     xch_ms, xch_calls = C.c_float(), C.c_uint32()
@@ -395,10 +405,13 @@ def run_ours(args, rank, world, local_rank):
             c = wl.h_counts.tolist()
             migrated += c[2] + c[4]
             launches_timed += okv.lib().orchkv_kernel_launches() - la
-            # this step's pack launches, timed by events around each launch
+            # this step's pack and unpack launches, timed by events around each
             pk = pack_launches(wl.L)
             pack_ms_acc.extend(pk[0])
             pack_bytes_acc += pk[1]
+            up = unpack_launches(wl.L)
+            unpack_ms_acc.extend(up[0])
+            unpack_bytes_acc += up[1]
             if comm:
                 okv.lib().orchkv_comm_exchange_time(comm, C.byref(xch_ms), C.byref(xch_calls))
                 xch[0] += xch_ms.value
@@ -486,6 +499,13 @@ def run_ours(args, rank, world, local_rank):
             "gpu_launches": int(launches_timed),
             "gpu_launches_per_step": round(launches_timed / args.steps, 1),
             "roofline": pack_roofline(pack_ms_acc, pack_bytes_acc, hbm_peak, peak_kind),
+            "unpack": ({"kernel": "promote unpack (H2D staging ring -> GPU slabs)",
+                        "launches": len(unpack_ms_acc),
+                        "ms_per_launch": round(sum(unpack_ms_acc) / len(unpack_ms_acc), 4),
+                        "bytes_per_launch": round(unpack_bytes_acc / len(unpack_ms_acc)),
+                        "achieved_gbs": round(unpack_bytes_acc / sum(unpack_ms_acc) / 1e6, 1),
+                        "frac": round(unpack_bytes_acc / sum(unpack_ms_acc) / 1e6 / hbm_peak, 4)}
+                       if unpack_ms_acc else None),
             "roofline_score": {
                 "kernel": "score (per-block attention mass, tm_report_attn_probs)",
                 "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,

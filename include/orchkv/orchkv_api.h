@@ -172,6 +172,13 @@ int  orchkv_last_migration_profile(float *pack_ms, unsigned long long *pack_byte
  * staging slots the evict used (0 when the zero-copy kernel ran alone). */
 int  orchkv_last_pack_chunks(float *ms, uint32_t max_chunks, uint32_t *chunks);
 
+/* Device time of each unpack launch of the last staged promote (or swap), in
+ * launch order, and the bytes each moved (the ring read plus the GPU slab
+ * write): ms[u], bytes[u] for u < min(*launches, max_launches) (synchronises).
+ * *launches = 0 when the promote ran zero-copy only. */
+int  orchkv_last_unpack_chunks(float *ms, unsigned long long *bytes, uint32_t max_launches,
+                               uint32_t *launches);
+
 /* How the last staged evict reached the DRAM tier: `runs` = runs of
  * consecutive DRAM slabs it filled, `ce_copies` = copy-engine copies issued
  * (one per run of at least 1 MiB, split at staging-slot boundaries),

@@ -143,6 +143,7 @@ _SIGS = {
     "orchkv_last_migration_profile": (i32, [P(f32), P(C.c_ulonglong), P(u32), P(f32)]),
     "orchkv_last_evict_layout": (i32, [P(u32), P(u32), P(u32)]),
     "orchkv_last_pack_chunks": (i32, [P(f32), u32, P(u32)]),
+    "orchkv_last_unpack_chunks": (i32, [P(f32), P(C.c_ulonglong), u32, P(u32)]),
     "orchkv_evict_batch_to_storage": (i32, [vp, vp, u32, vp]),
     "orchkv_promote_batch_from_storage": (i32, [vp, vp, u32, vp]),
     "orchkv_evict_cold_batch": (i32, [vp, vp, u32, vp]),

@@ -79,6 +79,9 @@ struct Sys {
     uint32_t ring_slabs = 0;          // slabs per ring slot
     std::vector<cudaEvent_t> ev_copied;
     cudaEvent_t ev_pk[2 * kMaxChunks] = {};
+    cudaEvent_t ev_up[2 * kMaxChunks] = {};       // around each unpack launch of a promote
+    uint32_t last_unpacks = 0;
+    unsigned long long last_unpack_bytes[kMaxChunks] = {};
     cudaEvent_t ev_mig[4] = {};
     cudaEvent_t ev_packed = nullptr;  // all of a swap's victims packed
     char *sort_mem = nullptr;         // SortScratch storage (evict, then promote)
@@ -301,6 +304,7 @@ void release_all()
     for (auto &e : g.ev_copied) if (e) cudaEventDestroy(e);
     g.ev_copied.clear();
     for (auto &e : g.ev_pk) if (e) { cudaEventDestroy(e); e = nullptr; }
+    for (auto &e : g.ev_up) if (e) { cudaEventDestroy(e); e = nullptr; }
     for (auto &e : g.ev_mig) if (e) { cudaEventDestroy(e); e = nullptr; }
     for (auto &e : g.ev_h2d) if (e) { cudaEventDestroy(e); e = nullptr; }
     for (auto &e : g.ev_unpacked) if (e) { cudaEventDestroy(e); e = nullptr; }
@@ -497,6 +501,7 @@ int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
     }
     for (auto &e : g.ev_copied) OKV_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     for (auto &e : g.ev_pk) OKV_CUDA_TRY(cudaEventCreate(&e));
+    for (auto &e : g.ev_up) OKV_CUDA_TRY(cudaEventCreate(&e));
     for (auto &e : g.ev_mig) OKV_CUDA_TRY(cudaEventCreate(&e));
     for (auto &e : g.ev_h2d) OKV_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     for (auto &e : g.ev_unpacked) OKV_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
@@ -1066,8 +1071,15 @@ int promote_drain(const MigPlan &mp, uint32_t done, uint32_t n_runs, cudaEvent_t
         }
         OKV_CUDA_TRY(cudaEventRecord(g.ev_h2d[c], g.copy_in));
         OKV_CUDA_TRY(cudaStreamWaitEvent(g.unpack, g.ev_h2d[c], 0));
+        const uint32_t u = g.last_unpacks;                     // < kMaxChunks: timed
+        if (u < (uint32_t)kMaxChunks) OKV_CUDA_TRY(cudaEventRecord(g.ev_up[2 * u], g.unpack));
         rc = launch_unpack(g.p, mp, g.ss2, buf, j0, n, min_len, g.unpack);
         if (rc) return rc;
+        if (u < (uint32_t)kMaxChunks) {
+            OKV_CUDA_TRY(cudaEventRecord(g.ev_up[2 * u + 1], g.unpack));
+            g.last_unpack_bytes[u] = 2ull * chunk_long * slab;  // ring read + GPU slab write
+            g.last_unpacks = u + 1;
+        }
         OKV_CUDA_TRY(cudaEventRecord(g.ev_unpacked[slot], g.unpack));
     }
     if (zc_slabs) {
@@ -1094,6 +1106,7 @@ void reset_profile()
     g.last_p_runs = g.last_p_ce_copies = g.last_p_zc_slabs = 0;
     g.last_swap_overlapped = 0;
     g.last_swap_conflicts = 0;
+    g.last_unpacks = 0;
 }
 
 bool scratch_fits(uint32_t max_n)
@@ -1267,6 +1280,21 @@ int orchkv_last_migration_profile(float *pack_ms, unsigned long long *pack_bytes
         *promote_ms = 0.f;
         if (g.last_promote_timed)
             OKV_CUDA_TRY(cudaEventElapsedTime(promote_ms, g.ev_mig[1], g.ev_mig[2]));
+    }
+    return ORCHKV_OK;
+}
+
+int orchkv_last_unpack_chunks(float *ms, unsigned long long *bytes, uint32_t max_launches,
+                              uint32_t *launches)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    const uint32_t n = g.last_unpacks;
+    if (launches) *launches = n;
+    for (uint32_t u = 0; u < n && u < max_launches; u++) {
+        if (ms) OKV_CUDA_TRY(cudaEventElapsedTime(&ms[u], g.ev_up[2 * u], g.ev_up[2 * u + 1]));
+        if (bytes) bytes[u] = g.last_unpack_bytes[u];
     }
     return ORCHKV_OK;
 }
