@@ -8,8 +8,13 @@ Two doors into the same native library (liborchkv_b200.so):
   ``core()`` loads it and registers it as the top-level module
   ``orchkv_core`` so unmodified callers doing ``import orchkv_core`` get it.
 
-There is no CPU fallback: if the library has not been built, importing the
-package fails.
+Callers of the reference's Python layer have B200 counterparts with the
+same interfaces: ``fast_manager.FastKVCacheManager``,
+``kvcache_manager.KVCacheManager``, ``vllm_connector.OrchKvOffloadingConnector``
+and ``attention_hook.AttentionScoreCollector`` / ``AttentionHookManager``.
+
+There is no CPU fallback: if the library has not been built, the first call
+into it (``lib()`` or ``core()``) raises.
 """
 from __future__ import annotations
 
