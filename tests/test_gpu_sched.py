@@ -269,3 +269,49 @@ def test_select_prefetch_vs_oracle(okv, oracle_mod, cuda):
         got = _select(okv, cuda, m, k, "prefetch", thg, thd)
         assert np.array_equal(got, want), (thg, thd, k)
     m.close()
+
+
+@pytest.mark.parametrize("where", ["device", "host"])
+def test_range_mass_vs_oracle(okv, oracle_mod, cuda, where):
+    """tm_report_attn_ranges: block i gets the sum over heads and tokens
+    [start_i, min(end_i, kv_len)) of avg; ranges clipped by kv_len, empty
+    ranges and ranges wholly past kv_len report nothing; unregistered ids are
+    ignored.  Against the oracle tracker fed the same per-block sums (summed
+    in another order: 1e-5)."""
+    rng = np.random.default_rng(31)
+    heads, kv_len, n = 6, 700, 60
+    avg = rng.random((heads, kv_len)).astype(np.float32) / kv_len
+    starts = rng.integers(0, 760, n).astype(np.uint32)
+    ends = (starts + rng.integers(0, 40, n)).astype(np.uint32)
+    starts[:3], ends[:3] = [5, 690, 720], [5, 740, 760]       # empty, clipped, past the end
+    ids = rng.permutation(4000)[:n].astype(np.uint32)
+    m = okv.Manager(tracker_cap=4096, max_blocks=1 << 20)
+    orc = oracle_mod.OracleSched(4096, 0.9, 0.5, 0.3, 0.2, 50.0)
+    for i in ids[::2]:                                         # every other id registered
+        m.register_id(int(i))
+        orc.register(int(i))
+    if where == "device":
+        bufs = [_dev(cuda, a) for a in (avg, starts, ends, ids)]
+    else:
+        bufs = [cuda.from_numpy(a.copy()) for a in (avg, starts, ends, ids)]
+    assert okv.lib().tm_report_attn_ranges(m.ref, bufs[0].data_ptr(), heads, kv_len,
+                                           bufs[1].data_ptr(), bufs[2].data_ptr(),
+                                           bufs[3].data_ptr(), n) == 0
+    reported = 0
+    for i in range(n):
+        s, e = int(starts[i]), min(int(ends[i]), kv_len)
+        if s < e:
+            orc.update(int(ids[i]), float(avg[:, s:e].astype(np.float64).sum()))
+            reported += int(i % 2 == 0)
+    m.step_done()
+    orc.step_done()
+    got, want = m.state(), orc.state()
+    sl = ids.astype(np.int64) & 4095
+    for key in ("hits", "last", "t_active"):
+        assert np.array_equal(got[key][sl], want[key][sl]), key
+    a, b = got["ema"][sl], want["ema"][sl]
+    assert np.all(np.abs(a - b) <= REL_TOL * np.maximum(np.abs(b), 1e-30))
+    assert int(np.count_nonzero(got["hits"][sl])) == reported > 10
+    assert okv.lib().tm_report_attn_ranges(m.ref, 0, heads, kv_len, bufs[1].data_ptr(),
+                                           bufs[2].data_ptr(), bufs[3].data_ptr(), n) == -2
+    m.close()
