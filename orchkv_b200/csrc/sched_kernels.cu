@@ -350,6 +350,103 @@ blockmean_kernel(const T *__restrict__ w, uint32_t batch, uint32_t heads, uint32
     }
 }
 
+constexpr int kMeanRows = 4;       // rows loaded ahead of their sums
+
+__device__ __forceinline__ uint4 ld_stream_u4(const void *p)
+{
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// Element i of a 16-byte vector of T, as fp32, without spilling the vector to
+// local memory.
+template <typename T> __device__ __forceinline__ float vec_elem(const uint4 &r, int i);
+__device__ __forceinline__ uint32_t vec_word(const uint4 &r, int w)
+{
+    return w == 0 ? r.x : w == 1 ? r.y : w == 2 ? r.z : r.w;
+}
+template <> __device__ __forceinline__ float vec_elem<float>(const uint4 &r, int i)
+{
+    return __uint_as_float(vec_word(r, i));
+}
+template <> __device__ __forceinline__ float vec_elem<__half>(const uint4 &r, int i)
+{
+    const uint32_t w = vec_word(r, i >> 1);
+    return __half2float(__ushort_as_half((unsigned short)((i & 1) ? w >> 16 : w & 0xFFFFu)));
+}
+template <> __device__ __forceinline__ float vec_elem<__nv_bfloat16>(const uint4 &r, int i)
+{
+    const uint32_t w = vec_word(r, i >> 1);
+    return __bfloat162float(
+        __ushort_as_bfloat16((unsigned short)((i & 1) ? w >> 16 : w & 0xFFFFu)));
+}
+
+// The same reduction with 16-byte loads: each thread takes V = 16 / sizeof(T)
+// consecutive tokens (8 for fp16 / bf16, 4 for fp32) of every row, so a tile
+// is kMeanThreads * V tokens.  Used when kv_len and block_size are multiples
+// of V and the weights are 16-byte aligned: every row then starts on a
+// 16-byte boundary and a token group lies wholly inside or past kv_len.  Each
+// token is summed over the rows in the scalar kernel's order, so the scores
+// are bit-identical to it.
+template <typename T>
+__global__ void __launch_bounds__(kMeanThreads)
+blockmean_vec_kernel(const T *__restrict__ w, uint32_t batch, uint32_t heads, uint32_t q_len,
+                     uint32_t kv_len, uint32_t bs, uint32_t nb, uint32_t bpc, float denom,
+                     float *scores)
+{
+    constexpr int V = 16 / (int)sizeof(T);
+    extern __shared__ float tok_sum[];
+    const uint32_t h = blockIdx.y;
+    const uint32_t b0 = blockIdx.x * bpc;
+    const uint32_t nblk = nb - b0 < bpc ? nb - b0 : bpc;
+    const uint32_t t0 = b0 * bs, ntok = nblk * bs;                // multiples of V
+    const size_t row_stride = (size_t)q_len * kv_len;
+    const size_t batch_stride = (size_t)heads * row_stride;
+    for (uint32_t j = threadIdx.x * V; j < ntok; j += kMeanThreads * V) {
+        const uint32_t t = t0 + j;
+        float acc[V];
+#pragma unroll
+        for (int i = 0; i < V; i++) acc[i] = 0.f;
+        if (t < kv_len) {
+            // rows (bi, q) in the scalar kernel's order, four loads in flight
+            // before their sums; p steps to the next row, q counts within bi
+            const T *p = w + (size_t)h * row_stride + t;
+            const size_t wrap = batch_stride - (size_t)(q_len - 1) * kv_len;
+            const uint32_t rows = batch * q_len;
+            uint32_t q = 0, r = 0;
+            for (; r + kMeanRows <= rows; r += kMeanRows) {
+                uint4 v[kMeanRows];
+#pragma unroll
+                for (int k = 0; k < kMeanRows; k++) {
+                    v[k] = ld_stream_u4(p);
+                    p += (++q == q_len) ? (q = 0, wrap) : (size_t)kv_len;
+                }
+#pragma unroll
+                for (int k = 0; k < kMeanRows; k++)
+#pragma unroll
+                    for (int i = 0; i < V; i++) acc[i] = __fadd_rn(acc[i], vec_elem<T>(v[k], i));
+            }
+            for (; r < rows; r++) {
+                const uint4 v = ld_stream_u4(p);
+                p += (++q == q_len) ? (q = 0, wrap) : (size_t)kv_len;
+#pragma unroll
+                for (int i = 0; i < V; i++) acc[i] = __fadd_rn(acc[i], vec_elem<T>(v, i));
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < V; i++) tok_sum[j + i] = acc[i];
+    }
+    __syncthreads();
+    for (uint32_t k = threadIdx.x; k < nblk; k += kMeanThreads) {
+        float s = 0.f;
+        for (uint32_t j = 0; j < bs; j++) s = __fadd_rn(s, tok_sum[k * bs + j]);
+        scores[(size_t)h * nb + b0 + k] = round_to<T>(__fdiv_rn(s, denom));
+    }
+}
+
 // One thread per block column b: the reports (h, b) for h = 0 .. heads-1 in
 // that order, so a column whose heads share an id (or a tracker slot) adds
 // them in the order the per-block calls would.
@@ -373,19 +470,31 @@ int launch_blockmean(const void *w, int dtype, uint32_t batch, uint32_t heads, u
     const unsigned long long count = (unsigned long long)batch * q_len * bs;
     const float denom = (float)count;         // elements averaged per block
     const uint32_t nb = (kv_len + bs - 1) / bs;
-    const uint32_t bpc = bs >= (uint32_t)kMeanThreads ? 1 : kMeanThreads / bs;
+    if (heads > 65535) return ORCHKV_ERR_INVALID;
+    const uint32_t V = dtype == 2 ? 4 : 8;                      // elements per 16-byte load
+    const bool vec = kv_len % V == 0 && bs % V == 0 && ((uintptr_t)w % 16) == 0;
+    const uint32_t tile = vec ? kMeanThreads * V : kMeanThreads; // tokens per CTA
+    const uint32_t bpc = bs >= tile ? 1 : tile / bs;
     const size_t smem = (size_t)bpc * bs * sizeof(float);
     const dim3 grid((nb + bpc - 1) / bpc, heads);
-    if (grid.y > 65535) return ORCHKV_ERR_INVALID;
-    if (dtype == 0)
-        blockmean_kernel<__half><<<grid, kMeanThreads, smem, s>>>(
-            (const __half *)w, batch, heads, q_len, kv_len, bs, nb, bpc, denom, scores);
-    else if (dtype == 1)
-        blockmean_kernel<__nv_bfloat16><<<grid, kMeanThreads, smem, s>>>(
-            (const __nv_bfloat16 *)w, batch, heads, q_len, kv_len, bs, nb, bpc, denom, scores);
+#define OKV_MEAN_LAUNCH(KERNEL)                                                            \
+    do {                                                                                   \
+        if (dtype == 0)                                                                    \
+            KERNEL<__half><<<grid, kMeanThreads, smem, s>>>(                               \
+                (const __half *)w, batch, heads, q_len, kv_len, bs, nb, bpc, denom, scores); \
+        else if (dtype == 1)                                                               \
+            KERNEL<__nv_bfloat16><<<grid, kMeanThreads, smem, s>>>(                        \
+                (const __nv_bfloat16 *)w, batch, heads, q_len, kv_len, bs, nb, bpc, denom, \
+                scores);                                                                   \
+        else                                                                               \
+            KERNEL<float><<<grid, kMeanThreads, smem, s>>>(                                \
+                (const float *)w, batch, heads, q_len, kv_len, bs, nb, bpc, denom, scores); \
+    } while (0)
+    if (vec)
+        OKV_MEAN_LAUNCH(blockmean_vec_kernel);
     else
-        blockmean_kernel<float><<<grid, kMeanThreads, smem, s>>>(
-            (const float *)w, batch, heads, q_len, kv_len, bs, nb, bpc, denom, scores);
+        OKV_MEAN_LAUNCH(blockmean_kernel);
+#undef OKV_MEAN_LAUNCH
     note_launches(1);
     if (ids && d) {
         blockmean_apply_kernel<<<(nb + 255) / 256, 256, 0, s>>>(scores, ids, heads, nb, *d, step);

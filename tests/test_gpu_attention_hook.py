@@ -261,3 +261,41 @@ def test_blockmean_rejects_bad_arguments(hook_mod, tm, cuda):
         args = list(ok)
         args[b["i"]] = b["v"]
         assert core.tm_report_attn_blockmean(*args) == -2, b
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
+@pytest.mark.parametrize("shape,block_size", [((2, 8, 3, 4096), 16), ((1, 4, 1, 8192), 256),
+                                              ((3, 2, 2, 1024), 4096), ((1, 1, 1, 64), 8)])
+def test_block_mean_vector_path_is_bit_identical(hook_mod, tm, cuda, shape, block_size, dtype):
+    """The 16-byte-load kernel (aligned weights, kv_len and block_size
+    multiples of the vector width) against the one-element kernel (the same
+    weights one element off a 16-byte boundary): scores equal bit for bit."""
+    torch = cuda
+    import orchkv_b200 as o
+    core = o.core()
+    dt = getattr(torch, dtype)
+    code = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}[dt]
+    vw = 4 if dt == torch.float32 else 8
+    if block_size % vw:
+        pytest.skip("block size below the vector width")
+    g = torch.Generator(device="cuda").manual_seed(5)
+    aw = softmax_weights(torch, g, shape, dt).contiguous()
+    n = aw.numel()
+    flat = torch.empty(n + 1, dtype=dt, device="cuda")
+    flat[1:].copy_(aw.reshape(-1))
+    off = flat[1:]
+    assert aw.data_ptr() % 16 == 0 and off.data_ptr() % 16 != 0
+    B, H, Q, T = shape
+    nb = (T + block_size - 1) // block_size
+    ids = torch.zeros(H, nb, dtype=torch.int32, device="cuda")
+    s_vec = torch.zeros(H, nb, device="cuda")
+    s_one = torch.zeros(H, nb, device="cuda")
+    assert core.tm_report_attn_blockmean(tm, aw.data_ptr(), code, B, H, Q, T, block_size,
+                                         ids.data_ptr(), s_vec.data_ptr()) == 0
+    assert core.tm_report_attn_blockmean(tm, off.data_ptr(), code, B, H, Q, T, block_size,
+                                         ids.data_ptr(), s_one.data_ptr()) == 0
+    core.tm_sync(tm)
+    assert torch.equal(s_vec.view(torch.int32), s_one.view(torch.int32))
+    want = torch_block_mean(torch, aw, nb, block_size).float()
+    rel = REL if dt == torch.float32 else (2.0 ** -7 if dt == torch.bfloat16 else 2.0 ** -10)
+    assert torch.all((s_vec - want).abs() <= rel * want.abs().clamp_min(1e-30))
