@@ -336,6 +336,44 @@ def pack_first_chunk(chunk_ms, total_bytes, chunks, hbm_peak):
             "later_chunks_ms_mean": round(sum(chunk_ms[1:]) / (len(chunk_ms) - 1), 4)}
 
 
+def hook_blockmean_probe(torch, L, tm, hbm_peak, passes=3, warm=2):
+    """The vLLM hook's block-mean reduction (tm_report_attn_blockmean, scores
+    only) on the workload's decode-step attention weights: bf16
+    [requests, q_heads, 1, context] per layer, one launch per layer over
+    distinct buffers (28 x 14.7 MB, larger than L2), timed with events on the
+    library's stream (torch's current stream)."""
+    B, Hq, T, tpb, Ly = WL["B"], WL["Hq"], WL["T"], WL["tpb"], WL["L"]
+    nb = (T + tpb - 1) // tpb
+    g = torch.Generator(device="cuda").manual_seed(77)
+    ws = [torch.softmax(torch.randn(B, Hq, 1, T, generator=g, device="cuda") * 2.0,
+                        dim=-1).to(torch.bfloat16) for _ in range(Ly)]
+    sc = torch.empty(Ly, Hq, nb, device="cuda")
+
+    def one_pass():
+        for i, w in enumerate(ws):
+            assert L.tm_report_attn_blockmean(tm, C.c_void_p(w.data_ptr()), 1, B, Hq, 1, T, tpb,
+                                              None, C.c_void_p(sc[i].data_ptr())) == 0
+
+    for _ in range(warm):
+        one_pass()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(passes):
+        one_pass()
+    e1.record()
+    e1.synchronize()
+    n = passes * Ly
+    ms = e0.elapsed_time(e1) / n
+    nbytes = B * Hq * T * 2 + Hq * nb * 4
+    del ws, sc
+    return {"kernel": "hook block mean (tm_report_attn_blockmean, scores only)",
+            "shape": f"bf16 [{B}, {Hq}, 1, {T}] per layer, block {tpb}, {Ly} layers",
+            "launches": n, "ms_per_launch": round(ms, 4), "bytes_per_launch": nbytes,
+            "achieved_gbs": round(nbytes / ms / 1e6, 1),
+            "frac": round(nbytes / ms / 1e6 / hbm_peak, 4)}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -451,6 +489,7 @@ def run_ours(args, rank, world, local_rank):
     wl.L.orchkv_last_promote_layout(*[C.byref(x) for x in play])
     c_last = wl.h_counts.tolist()
     wl.restore()
+    hook = hook_blockmean_probe(torch, wl.L, wl.tm.ref, hbm_peak)
 
     mean_ms = sum(step_ms) / len(step_ms)
     per_step_migrated = migrated / args.steps
@@ -516,6 +555,7 @@ def run_ours(args, rank, world, local_rank):
                 "traffic": round(SCORE_TRAFFIC_PER_REQUEST * WL["B"]),
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
                                   "8-request launch, scaled by requests"},
+            "hook": hook,
             "pack": {"kernel": "evict pack (HBM gather -> staging)",
                      "ms": round(pk_ms.value, 4), "bytes": pk_bytes.value,
                      "achieved_gbs": round(pk_bytes.value / max(pk_ms.value, 1e-9) / 1e6, 1),

@@ -312,45 +312,10 @@ template <> __device__ __forceinline__ float round_to<__nv_bfloat16>(float x)
     return __bfloat162float(__float2bfloat16_rn(x));
 }
 
-// One CTA per (head h, tile of `bpc` consecutive blocks).  Each thread sums
-// its tokens over the batch x q_len rows (coalesced along tokens; batch, then
-// query position, in order), the per-token sums go to shared memory, and one
-// thread per block adds its block's tokens in order and divides by
-// batch * q_len * block_size: tokens past kv_len count as zeros, as in the
-// hook's padded view.
-template <typename T>
-__global__ void __launch_bounds__(kMeanThreads)
-blockmean_kernel(const T *__restrict__ w, uint32_t batch, uint32_t heads, uint32_t q_len,
-                 uint32_t kv_len, uint32_t bs, uint32_t nb, uint32_t bpc, float denom,
-                 float *scores)
-{
-    extern __shared__ float tok_sum[];
-    const uint32_t h = blockIdx.y;
-    const uint32_t b0 = blockIdx.x * bpc;
-    const uint32_t nblk = nb - b0 < bpc ? nb - b0 : bpc;
-    const uint32_t t0 = b0 * bs, ntok = nblk * bs;
-    const size_t row_stride = (size_t)q_len * kv_len;            // next query position
-    const size_t batch_stride = (size_t)heads * row_stride;      // next batch entry
-    for (uint32_t j = threadIdx.x; j < ntok; j += kMeanThreads) {
-        const uint32_t t = t0 + j;
-        float acc = 0.f;
-        if (t < kv_len) {
-            const T *p = w + (size_t)h * row_stride + t;
-            for (uint32_t bi = 0; bi < batch; bi++, p += batch_stride)
-                for (uint32_t q = 0; q < q_len; q++)
-                    acc = __fadd_rn(acc, to_f32<T>(p[(size_t)q * kv_len]));
-        }
-        tok_sum[j] = acc;
-    }
-    __syncthreads();
-    for (uint32_t k = threadIdx.x; k < nblk; k += kMeanThreads) {
-        float s = 0.f;
-        for (uint32_t j = 0; j < bs; j++) s = __fadd_rn(s, tok_sum[k * bs + j]);
-        scores[(size_t)h * nb + b0 + k] = round_to<T>(__fdiv_rn(s, denom));
-    }
-}
-
-constexpr int kMeanRows = 4;       // rows loaded ahead of their sums
+constexpr int kMeanRows = 4;          // rows loaded ahead of their sums
+constexpr uint32_t kMeanMaxGroups = 8;  // row groups per CTA
+// threads that keep all of a B200's 148 SMs streaming (2048 resident each)
+constexpr unsigned long long kMeanFillThreads = 148ull * 2048ull;
 
 __device__ __forceinline__ uint4 ld_stream_u4(const void *p)
 {
@@ -361,88 +326,120 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void *p)
     return v;
 }
 
-// Element i of a 16-byte vector of T, as fp32, without spilling the vector to
-// local memory.
-template <typename T> __device__ __forceinline__ float vec_elem(const uint4 &r, int i);
 __device__ __forceinline__ uint32_t vec_word(const uint4 &r, int w)
 {
     return w == 0 ? r.x : w == 1 ? r.y : w == 2 ? r.z : r.w;
 }
-template <> __device__ __forceinline__ float vec_elem<float>(const uint4 &r, int i)
+
+// What one thread loads from one row: V consecutive tokens of type T, as one
+// element (V = 1) or one 16-byte vector (V = 16 / sizeof(T)); elem() returns
+// token i as fp32 without spilling the vector to local memory.
+template <typename T, int V> struct MeanLoad {
+    using Raw = uint4;
+    static __device__ __forceinline__ Raw load(const T *p) { return ld_stream_u4(p); }
+    static __device__ __forceinline__ float elem(const Raw &r, int i);
+};
+template <typename T> struct MeanLoad<T, 1> {
+    using Raw = T;
+    static __device__ __forceinline__ Raw load(const T *p) { return *p; }
+    static __device__ __forceinline__ float elem(const Raw &r, int) { return to_f32<T>(r); }
+};
+template <> __device__ __forceinline__ float MeanLoad<float, 4>::elem(const uint4 &r, int i)
 {
     return __uint_as_float(vec_word(r, i));
 }
-template <> __device__ __forceinline__ float vec_elem<__half>(const uint4 &r, int i)
+template <> __device__ __forceinline__ float MeanLoad<__half, 8>::elem(const uint4 &r, int i)
 {
     const uint32_t w = vec_word(r, i >> 1);
     return __half2float(__ushort_as_half((unsigned short)((i & 1) ? w >> 16 : w & 0xFFFFu)));
 }
-template <> __device__ __forceinline__ float vec_elem<__nv_bfloat16>(const uint4 &r, int i)
+template <> __device__ __forceinline__ float MeanLoad<__nv_bfloat16, 8>::elem(const uint4 &r,
+                                                                            int i)
 {
     const uint32_t w = vec_word(r, i >> 1);
     return __bfloat162float(
         __ushort_as_bfloat16((unsigned short)((i & 1) ? w >> 16 : w & 0xFFFFu)));
 }
 
-// The same reduction with 16-byte loads: each thread takes V = 16 / sizeof(T)
-// consecutive tokens (8 for fp16 / bf16, 4 for fp32) of every row, so a tile
-// is kMeanThreads * V tokens.  Used when kv_len and block_size are multiples
-// of V and the weights are 16-byte aligned: every row then starts on a
-// 16-byte boundary and a token group lies wholly inside or past kv_len.  Each
-// token is summed over the rows in the scalar kernel's order, so the scores
-// are bit-identical to it.
-template <typename T>
+// One CTA per (head h, tile of `bpc` consecutive blocks).  The batch x q_len
+// rows (batch, then query position) are cut into `rg` row groups of
+// ceil(rows / rg) consecutive rows; the CTA's threads form rg groups of
+// kMeanThreads / rg, and a thread of group g sums V consecutive tokens
+// (coalesced along tokens) over group g's rows in order, kMeanRows loads in
+// flight ahead of their sums.  The group sums of each token are then added in
+// group order in shared memory, and one thread per block adds its block's
+// tokens in order and divides by batch * q_len * block_size: tokens past
+// kv_len count as zeros, as in the hook's padded view.  The summation order
+// depends on rg and not on V, so the one-element (V = 1) and 16-byte
+// (V = 16 / sizeof(T)) instances give bit-identical scores; the 16-byte one
+// needs 16-byte-aligned weights and kv_len and block_size multiples of V, so
+// every row starts on a 16-byte boundary and a token group lies wholly
+// inside or past kv_len.
+template <typename T, int V>
 __global__ void __launch_bounds__(kMeanThreads)
-blockmean_vec_kernel(const T *__restrict__ w, uint32_t batch, uint32_t heads, uint32_t q_len,
-                     uint32_t kv_len, uint32_t bs, uint32_t nb, uint32_t bpc, float denom,
-                     float *scores)
+blockmean_kernel(const T *__restrict__ w, uint32_t batch, uint32_t heads, uint32_t q_len,
+                 uint32_t kv_len, uint32_t bs, uint32_t nb, uint32_t bpc, uint32_t rg,
+                 float denom, float *scores)
 {
-    constexpr int V = 16 / (int)sizeof(T);
-    extern __shared__ float tok_sum[];
+    using L = MeanLoad<T, V>;
+    extern __shared__ float part[];                 // [rg][bpc * bs] token sums per group
     const uint32_t h = blockIdx.y;
     const uint32_t b0 = blockIdx.x * bpc;
     const uint32_t nblk = nb - b0 < bpc ? nb - b0 : bpc;
-    const uint32_t t0 = b0 * bs, ntok = nblk * bs;                // multiples of V
-    const size_t row_stride = (size_t)q_len * kv_len;
-    const size_t batch_stride = (size_t)heads * row_stride;
-    for (uint32_t j = threadIdx.x * V; j < ntok; j += kMeanThreads * V) {
+    const uint32_t t0 = b0 * bs, ntok = nblk * bs, cap = bpc * bs;
+    const uint32_t tpg = kMeanThreads / rg;         // threads per row group
+    const uint32_t g = threadIdx.x / tpg, c = threadIdx.x % tpg;
+    const uint32_t rows = batch * q_len, rpg = (rows + rg - 1) / rg;
+    const uint32_t r0 = g * rpg < rows ? g * rpg : rows;
+    const uint32_t r1 = r0 + rpg < rows ? r0 + rpg : rows;
+    const size_t row_stride = (size_t)q_len * kv_len;            // next query position
+    const size_t batch_stride = (size_t)heads * row_stride;      // next batch entry
+    const size_t wrap = batch_stride - (size_t)(q_len - 1) * kv_len;
+    const T *row0 = w + (size_t)(r0 / q_len) * batch_stride + (size_t)h * row_stride +
+                    (size_t)(r0 % q_len) * kv_len;
+    for (uint32_t j = c * V; j < ntok; j += tpg * V) {
         const uint32_t t = t0 + j;
         float acc[V];
 #pragma unroll
         for (int i = 0; i < V; i++) acc[i] = 0.f;
         if (t < kv_len) {
-            // rows (bi, q) in the scalar kernel's order, four loads in flight
-            // before their sums; p steps to the next row, q counts within bi
-            const T *p = w + (size_t)h * row_stride + t;
-            const size_t wrap = batch_stride - (size_t)(q_len - 1) * kv_len;
-            const uint32_t rows = batch * q_len;
-            uint32_t q = 0, r = 0;
-            for (; r + kMeanRows <= rows; r += kMeanRows) {
-                uint4 v[kMeanRows];
+            // p steps through rows r0 .. r1-1; q is the row's query position
+            const T *p = row0 + t;
+            uint32_t q = r0 % q_len, r = r0;
+            for (; r + kMeanRows <= r1; r += kMeanRows) {
+                typename L::Raw v[kMeanRows];
 #pragma unroll
                 for (int k = 0; k < kMeanRows; k++) {
-                    v[k] = ld_stream_u4(p);
+                    v[k] = L::load(p);
                     p += (++q == q_len) ? (q = 0, wrap) : (size_t)kv_len;
                 }
 #pragma unroll
                 for (int k = 0; k < kMeanRows; k++)
 #pragma unroll
-                    for (int i = 0; i < V; i++) acc[i] = __fadd_rn(acc[i], vec_elem<T>(v[k], i));
+                    for (int i = 0; i < V; i++) acc[i] = __fadd_rn(acc[i], L::elem(v[k], i));
             }
-            for (; r < rows; r++) {
-                const uint4 v = ld_stream_u4(p);
+            for (; r < r1; r++) {
+                const typename L::Raw v = L::load(p);
                 p += (++q == q_len) ? (q = 0, wrap) : (size_t)kv_len;
 #pragma unroll
-                for (int i = 0; i < V; i++) acc[i] = __fadd_rn(acc[i], vec_elem<T>(v, i));
+                for (int i = 0; i < V; i++) acc[i] = __fadd_rn(acc[i], L::elem(v, i));
             }
         }
 #pragma unroll
-        for (int i = 0; i < V; i++) tok_sum[j + i] = acc[i];
+        for (int i = 0; i < V; i++) part[g * cap + j + i] = acc[i];
     }
     __syncthreads();
+    if (rg > 1) {
+        for (uint32_t j = threadIdx.x; j < ntok; j += kMeanThreads) {
+            float s = part[j];
+            for (uint32_t k = 1; k < rg; k++) s = __fadd_rn(s, part[k * cap + j]);
+            part[j] = s;
+        }
+        __syncthreads();
+    }
     for (uint32_t k = threadIdx.x; k < nblk; k += kMeanThreads) {
         float s = 0.f;
-        for (uint32_t j = 0; j < bs; j++) s = __fadd_rn(s, tok_sum[k * bs + j]);
+        for (uint32_t j = 0; j < bs; j++) s = __fadd_rn(s, part[k * bs + j]);
         scores[(size_t)h * nb + b0 + k] = round_to<T>(__fdiv_rn(s, denom));
     }
 }
@@ -470,30 +467,35 @@ int launch_blockmean(const void *w, int dtype, uint32_t batch, uint32_t heads, u
     const unsigned long long count = (unsigned long long)batch * q_len * bs;
     const float denom = (float)count;         // elements averaged per block
     const uint32_t nb = (kv_len + bs - 1) / bs;
-    if (heads > 65535) return ORCHKV_ERR_INVALID;
+    if (heads > 65535 || count / bs >= (1ull << 29)) return ORCHKV_ERR_INVALID;
+    // Row groups from the shape alone (so both kernels sum in one order).
+    // Splitting the rows only helps when a thread would otherwise stream
+    // more rows than it keeps in flight and the grid is short of the GPU's
+    // threads: double the groups while each keeps at least kMeanRows rows,
+    // the doubled grid (in 8-token columns) still fits the GPU's resident
+    // threads, and the group sums fit 32 KB of shared memory.
+    const uint32_t rows = batch * q_len;
+    const unsigned long long cols = (unsigned long long)heads * ((kv_len + 7) / 8);
+    uint32_t rg = 1;
+    while (rg < kMeanMaxGroups && rows >= rg * 2 * kMeanRows &&
+           cols * rg * 2 <= kMeanFillThreads && (unsigned long long)rg * 2 * bs <= 8192)
+        rg *= 2;
     const uint32_t V = dtype == 2 ? 4 : 8;                      // elements per 16-byte load
     const bool vec = kv_len % V == 0 && bs % V == 0 && ((uintptr_t)w % 16) == 0;
-    const uint32_t tile = vec ? kMeanThreads * V : kMeanThreads; // tokens per CTA
+    const uint32_t tile = (kMeanThreads / rg) * (vec ? V : 1);  // tokens per CTA
     const uint32_t bpc = bs >= tile ? 1 : tile / bs;
-    const size_t smem = (size_t)bpc * bs * sizeof(float);
+    const size_t smem = (size_t)rg * bpc * bs * sizeof(float);
     const dim3 grid((nb + bpc - 1) / bpc, heads);
-#define OKV_MEAN_LAUNCH(KERNEL)                                                            \
-    do {                                                                                   \
-        if (dtype == 0)                                                                    \
-            KERNEL<__half><<<grid, kMeanThreads, smem, s>>>(                               \
-                (const __half *)w, batch, heads, q_len, kv_len, bs, nb, bpc, denom, scores); \
-        else if (dtype == 1)                                                               \
-            KERNEL<__nv_bfloat16><<<grid, kMeanThreads, smem, s>>>(                        \
-                (const __nv_bfloat16 *)w, batch, heads, q_len, kv_len, bs, nb, bpc, denom, \
-                scores);                                                                   \
-        else                                                                               \
-            KERNEL<float><<<grid, kMeanThreads, smem, s>>>(                                \
-                (const float *)w, batch, heads, q_len, kv_len, bs, nb, bpc, denom, scores); \
-    } while (0)
-    if (vec)
-        OKV_MEAN_LAUNCH(blockmean_vec_kernel);
-    else
-        OKV_MEAN_LAUNCH(blockmean_kernel);
+#define OKV_MEAN_LAUNCH(T, VW)                                                             \
+    blockmean_kernel<T, VW><<<grid, kMeanThreads, smem, s>>>(                              \
+        (const T *)w, batch, heads, q_len, kv_len, bs, nb, bpc, rg, denom, scores)
+    if (dtype == 0) {
+        if (vec) OKV_MEAN_LAUNCH(__half, 8); else OKV_MEAN_LAUNCH(__half, 1);
+    } else if (dtype == 1) {
+        if (vec) OKV_MEAN_LAUNCH(__nv_bfloat16, 8); else OKV_MEAN_LAUNCH(__nv_bfloat16, 1);
+    } else {
+        if (vec) OKV_MEAN_LAUNCH(float, 4); else OKV_MEAN_LAUNCH(float, 1);
+    }
 #undef OKV_MEAN_LAUNCH
     note_launches(1);
     if (ids && d) {

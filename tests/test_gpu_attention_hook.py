@@ -265,11 +265,16 @@ def test_blockmean_rejects_bad_arguments(hook_mod, tm, cuda):
 
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
 @pytest.mark.parametrize("shape,block_size", [((2, 8, 3, 4096), 16), ((1, 4, 1, 8192), 256),
-                                              ((3, 2, 2, 1024), 4096), ((1, 1, 1, 64), 8)])
+                                              ((3, 2, 2, 1024), 4096), ((1, 1, 1, 64), 8),
+                                              ((32, 28, 1, 8192), 16), ((5, 4, 3, 2048), 16)])
 def test_block_mean_vector_path_is_bit_identical(hook_mod, tm, cuda, shape, block_size, dtype):
     """The 16-byte-load kernel (aligned weights, kv_len and block_size
     multiples of the vector width) against the one-element kernel (the same
-    weights one element off a 16-byte boundary): scores equal bit for bit."""
+    weights one element off a 16-byte boundary): scores equal bit for bit.
+    The shapes cover one row group and several (the rows are split into up
+    to 8 groups when heads x tokens alone would not fill the GPU), uneven
+    groups and a group that starts mid-batch (15 rows of 3 query
+    positions, groups of 8 and 7)."""
     torch = cuda
     import orchkv_b200 as o
     core = o.core()
