@@ -374,9 +374,12 @@ template <> __device__ __forceinline__ float MeanLoad<__nv_bfloat16, 8>::elem(co
 // (V = 16 / sizeof(T)) instances give bit-identical scores; the 16-byte one
 // needs 16-byte-aligned weights and kv_len and block_size multiples of V, so
 // every row starts on a 16-byte boundary and a token group lies wholly
-// inside or past kv_len.
-template <typename T, int V>
-__global__ void __launch_bounds__(kMeanThreads)
+// inside or past kv_len.  MINB is the resident CTAs per SM the registers
+// are fitted to: 8 for a row-split grid (a short grid gains more from one
+// wave than it loses to a few spilled registers), 1 otherwise; it changes no
+// arithmetic.
+template <typename T, int V, int MINB>
+__global__ void __launch_bounds__(kMeanThreads, MINB)
 blockmean_kernel(const T *__restrict__ w, uint32_t batch, uint32_t heads, uint32_t q_len,
                  uint32_t kv_len, uint32_t bs, uint32_t nb, uint32_t bpc, uint32_t rg,
                  float denom, float *scores)
@@ -486,16 +489,21 @@ int launch_blockmean(const void *w, int dtype, uint32_t batch, uint32_t heads, u
     const uint32_t bpc = bs >= tile ? 1 : tile / bs;
     const size_t smem = (size_t)rg * bpc * bs * sizeof(float);
     const dim3 grid((nb + bpc - 1) / bpc, heads);
-#define OKV_MEAN_LAUNCH(T, VW)                                                             \
-    blockmean_kernel<T, VW><<<grid, kMeanThreads, smem, s>>>(                              \
+#define OKV_MEAN_LAUNCH(T, VW, MB)                                                         \
+    blockmean_kernel<T, VW, MB><<<grid, kMeanThreads, smem, s>>>(                          \
         (const T *)w, batch, heads, q_len, kv_len, bs, nb, bpc, rg, denom, scores)
+#define OKV_MEAN_VEC(T, VW)                                                                \
+    do {                                                                                   \
+        if (rg > 1) OKV_MEAN_LAUNCH(T, VW, 8); else OKV_MEAN_LAUNCH(T, VW, 1);             \
+    } while (0)
     if (dtype == 0) {
-        if (vec) OKV_MEAN_LAUNCH(__half, 8); else OKV_MEAN_LAUNCH(__half, 1);
+        if (vec) OKV_MEAN_VEC(__half, 8); else OKV_MEAN_LAUNCH(__half, 1, 1);
     } else if (dtype == 1) {
-        if (vec) OKV_MEAN_LAUNCH(__nv_bfloat16, 8); else OKV_MEAN_LAUNCH(__nv_bfloat16, 1);
+        if (vec) OKV_MEAN_VEC(__nv_bfloat16, 8); else OKV_MEAN_LAUNCH(__nv_bfloat16, 1, 1);
     } else {
-        if (vec) OKV_MEAN_LAUNCH(float, 4); else OKV_MEAN_LAUNCH(float, 1);
+        if (vec) OKV_MEAN_VEC(float, 4); else OKV_MEAN_LAUNCH(float, 1, 1);
     }
+#undef OKV_MEAN_VEC
 #undef OKV_MEAN_LAUNCH
     note_launches(1);
     if (ids && d) {
