@@ -447,17 +447,50 @@ blockmean_kernel(const T *__restrict__ w, uint32_t batch, uint32_t heads, uint32
     }
 }
 
-// One thread per block column b: the reports (h, b) for h = 0 .. heads-1 in
-// that order, so a column whose heads share an id (or a tracker slot) adds
-// them in the order the per-block calls would.
+// One warp per block column b; lane l takes head h0 + l of each chunk of 32
+// heads, chunks in order.  Lanes whose ids map to one tracker slot (a column
+// may give every head the same id) form a group, and the group's lowest lane
+// applies the group's reports in head order -- sum, then maximum, then the
+// last-hit step, as consecutive tm_notify_attn calls would -- so the results
+// round exactly as the sequential calls.  One tracker round trip per slot
+// and chunk instead of one per head; __syncwarp orders a chunk's writes
+// before the next chunk's reads.  Different columns never share a slot.
 __global__ void blockmean_apply_kernel(const float *__restrict__ scores,
                                        const uint32_t *__restrict__ ids, uint32_t heads,
                                        uint32_t nb, SchedDev d, unsigned long long step)
 {
-    const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= nb) return;
-    for (uint32_t h = 0; h < heads; h++)
-        record_mass(d, ids[(size_t)h * nb + b], scores[(size_t)h * nb + b], step);
+    const unsigned long long b =
+        ((unsigned long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (b >= nb) return;                              // uniform across the warp
+    for (uint32_t h0 = 0; h0 < heads; h0 += 32) {
+        const uint32_t h = h0 + lane;
+        const uint32_t id = h < heads ? ids[(size_t)h * nb + b] : kNoBlock;
+        const float w = h < heads ? scores[(size_t)h * nb + b] : 0.f;
+        const bool rec = id != kNoBlock;
+        const uint32_t key = rec ? (id & d.mask) : 0xFFFFFFFFu;   // slots are <= mask
+        const unsigned grp = __match_any_sync(0xFFFFFFFFu, key);
+        const bool lead = rec && lane == __ffs(grp) - 1;
+        bool act = false;
+        float sum = 0.f, mx = 0.f;
+        if (lead) {
+            act = d.tact[key];                        // inactive slots ignore reports
+            if (act) { sum = d.sum[key]; mx = d.mx[key]; }
+        }
+        for (int k = 0; k < 32; k++) {                // the group's reports, head order
+            const float wk = __shfl_sync(0xFFFFFFFFu, w, k);
+            if (act && ((grp >> k) & 1u)) {
+                sum = __fadd_rn(sum, wk);
+                if (wk > mx) mx = wk;
+            }
+        }
+        if (act) {
+            d.sum[key] = sum;
+            d.mx[key] = mx;
+            d.last[key] = step;
+        }
+        __syncwarp();
+    }
 }
 
 int launch_blockmean(const void *w, int dtype, uint32_t batch, uint32_t heads, uint32_t q_len,
@@ -507,7 +540,9 @@ int launch_blockmean(const void *w, int dtype, uint32_t batch, uint32_t heads, u
 #undef OKV_MEAN_LAUNCH
     note_launches(1);
     if (ids && d) {
-        blockmean_apply_kernel<<<(nb + 255) / 256, 256, 0, s>>>(scores, ids, heads, nb, *d, step);
+        const unsigned long long threads = (unsigned long long)nb * 32;   // a warp per block
+        blockmean_apply_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+            scores, ids, heads, nb, *d, step);
         note_launches(1);
     }
     OKV_CUDA_TRY(cudaGetLastError());
