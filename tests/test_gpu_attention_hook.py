@@ -304,3 +304,50 @@ def test_block_mean_vector_path_is_bit_identical(hook_mod, tm, cuda, shape, bloc
     want = torch_block_mean(torch, aw, nb, block_size).float()
     rel = REL if dt == torch.float32 else (2.0 ** -7 if dt == torch.bfloat16 else 2.0 ** -10)
     assert torch.all((s_vec - want).abs() <= rel * want.abs().clamp_min(1e-30))
+
+
+@pytest.mark.parametrize("mode", ["default", "table", "fn"])
+def test_reports_more_heads_than_a_warp(hook_mod, cuda, oracle_mod, mode):
+    """72 heads: the tracker apply takes a column's heads 32 at a time, so a
+    slot shared by every head of a column (block-table mode) is updated in
+    three chunks that must follow one another in head order.  The tracker
+    equals the oracle fed the reference hook's per-block report sequence."""
+    torch = cuda
+    import orchkv_b200 as o
+    core = o.core()
+    cap = 8192
+    tm = core.tm_create(tracker_cap=cap, ema_lambda=0.9)
+    try:
+        orc = oracle_mod.OracleSched(cap, 0.9, 0.5, 0.3, 0.2, 50.0)
+        H, bsz, kv, blk = 72, 2, 200, 16
+        nb = (kv + blk - 1) // blk
+        for bid in range(6000):
+            assert core.tm_register_block_id(tm, bid, 0, 0) == 0
+            orc.register(bid)
+        c = hook_mod.AttentionScoreCollector(tm, block_size=blk, sample_interval=1)
+        g = torch.Generator(device="cuda").manual_seed(9)
+        kw = {"default": {},
+              "table": {"block_table": torch.tensor([[5000 + 3 * i for i in range(nb)]],
+                                                    device="cuda")},
+              # heads 0-35 and 36-71 pairwise share an id: groups span chunks
+              "fn": {"block_id_fn": lambda layer, h, bi: 4000 + 40 * bi + (h % 36)}}[mode]
+        from oracle.hook_model import hook_reports
+        for step in range(3):
+            for layer in range(2):
+                aw = softmax_weights(torch, g, (bsz, H, 1, kv))
+                c.collect(layer, aw, **kw)
+                for bid, score in hook_reports(layer, aw, blk, kw.get("block_table"),
+                                               kw.get("block_id_fn")):
+                    orc.update(bid, score)
+            c.on_step_done()
+            orc.step_done()
+        core.tm_sync(tm)
+        got, want = _state(tm), orc.state()
+        for key in ("hits", "last"):
+            assert np.array_equal(got[key], want[key]), key
+        for key in ("sum", "ema"):
+            a, b = got[key], want[key]
+            assert np.all(np.abs(a - b) <= REL * np.maximum(np.abs(b), 1e-30)), key
+        assert np.count_nonzero(want["hits"]) >= nb
+    finally:
+        core.tm_destroy(tm)
