@@ -571,9 +571,22 @@ __global__ void range_mass_kernel(const float *__restrict__ avg, uint32_t heads,
         const uint32_t e = end[i] < kv_len ? end[i] : kv_len;
         if (s >= e) continue;                          // warp-uniform
         float acc = 0.f;
-        for (uint32_t h = 0; h < heads; h++) {
-            const float *row = avg + (size_t)h * kv_len;
-            for (uint32_t t = s + lane; t < e; t += 32) acc = __fadd_rn(acc, row[t]);
+        if (e - s <= 32) {
+            // at most one token per lane: the heads' loads are independent,
+            // so the unrolled loop keeps several in flight while the sums
+            // stay in head order (the same order as the general loop)
+            const uint32_t t = s + lane;
+            if (t < e) {
+                const float *col = avg + t;
+#pragma unroll 8
+                for (uint32_t h = 0; h < heads; h++)
+                    acc = __fadd_rn(acc, col[(size_t)h * kv_len]);
+            }
+        } else {
+            for (uint32_t h = 0; h < heads; h++) {
+                const float *row = avg + (size_t)h * kv_len;
+                for (uint32_t t = s + lane; t < e; t += 32) acc = __fadd_rn(acc, row[t]);
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, o));
