@@ -123,7 +123,12 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 
 class Workload:
-    def __init__(self, torch, okv, rank, world, comm=None, seed=0):
+    """The decode-step workload on this rank.  staging: "whole" sizes the
+    evict staging buffer to a whole step's evict (what lets the swap overlap
+    both copy directions); "ring" keeps the library's default 3-slot ring, so
+    a step's 14 chunks reuse slots."""
+
+    def __init__(self, torch, okv, rank, world, comm=None, seed=0, staging="whole"):
         self.t, self.okv, self.L = torch, okv, okv.lib()
         w = WL
         self.B, self.Ly, self.Hq, self.Hkv, self.D, self.T, self.tpb = (
@@ -150,7 +155,7 @@ class Workload:
         ext = okv.OrchkvConfigExt()
         ext.max_blocks = 1 << 21
         # staging for a whole step's evict, so the swap can overlap both directions
-        ext.staging_mb = (self.k_evict * self.slab >> 20) + 256
+        ext.staging_mb = (self.k_evict * self.slab >> 20) + 256 if staging == "whole" else 0
         rc = L.orchkv_init_ext(C.byref(cfg), C.byref(ext))
         if rc != 0:
             raise RuntimeError(f"orchkv_init_ext failed: {rc}")
@@ -207,8 +212,10 @@ class Workload:
     def _ptr(self, t, off=0):
         return C.c_void_p(t.data_ptr() + off)
 
-    def step(self, e2e=False):
-        """One decode step; returns nothing (results land in self.counts)."""
+    def step(self, e2e=False, check=None):
+        """One decode step; returns nothing (results land in self.counts).
+        check (tests only, never timed): called with "scored" after the
+        scoring launch and with "selected" before the swap."""
         L, t, tm = self.L, self.t, self.tm.ref
         ev = self.ev
         ev[0].record()
@@ -227,12 +234,16 @@ class Workload:
         assert L.tm_report_attn_probs(tm, self._ptr(probs), self.rows, self.Hq, self.Hkv,
                                       self.T, self.tpb, None, self._ptr(self.ids)) == 0
         ev[3].record()
+        if check:
+            check("scored")
         assert L.tm_step_and_classify(tm) == 0
         assert L.tm_select_victims(tm, self.k_evict_sel, self._ptr(self.victims),
                                    self._ptr(self.counts)) == 0
         assert L.tm_select_prefetch(tm, self.k_promote_sel, 0.0, 0.0, self._ptr(self.pref),
                                     self._ptr(self.counts, 4)) == 0
         ev[4].record()
+        if check:
+            check("selected")
         assert L.orchkv_swap_batch(self._ptr(self.victims), self._ptr(self.counts), 1 << 21,
                                    self._ptr(self.pref), self._ptr(self.counts, 4), 1 << 21,
                                    self._ptr(self.counts, 8)) == 0

@@ -232,6 +232,17 @@ int  orchkv_copy_token_blocks(void *const *bufs, uint32_t n_bufs, uint32_t n_hea
 int  orchkv_block_id_table(kv_request_ctx_t *const *ctxs, uint32_t n,
                            uint32_t row_len, uint32_t *out);
 
+/* B200: a 64-bit checksum of each listed block's slab where it currently
+ * lives (HBM or the DRAM tier): out[i] = sum_j x_j * (mix64(j) | 1) mod 2^64
+ * over the slab's little-endian 64-bit words x_j, mix64 being splitmix64's
+ * output function.  Blocks in no GPU or DRAM slab get 0 (tier_out[i] = 7).
+ * ids, out and tier_out (may be NULL) are device memory, n entries.  Lets a
+ * caller compare a block's bytes before and after a migration without
+ * copying slabs out; no counterpart in the reference, whose tests compare
+ * seed-pattern words (test/test_gpu_dram.cu:40-55).  Asynchronous. */
+int  orchkv_block_checksums(const uint32_t *block_ids, uint32_t n,
+                            unsigned long long *out, uint8_t *tier_out);
+
 /* Introspection for tests and tools (synchronous). */
 int  orchkv_block_info(kv_request_ctx_t *ctx, uint32_t layer_id, uint32_t head_id,
                        uint32_t block_idx, uint64_t *block_id, int *tier,

@@ -149,6 +149,7 @@ _SIGS = {
     "orchkv_evict_cold_batch": (i32, [vp, vp, u32, vp]),
     "orchkv_last_promote_layout": (i32, [P(u32), P(u32), P(u32), P(i32)]),
     "orchkv_swap_batch": (i32, [vp, vp, u32, vp, vp, u32, vp]),
+    "orchkv_block_checksums": (i32, [vp, u32, vp, vp]),
     "orchkv_gpu_pool_base": (vp, []),
     "orchkv_dram_pool_base": (vp, []),
     # scheduler

@@ -31,7 +31,8 @@ NVFLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",
                   "-Xcompiler", "-Wall", "-I" + INCLUDE, "-I" + CSRC]
 
 CU_SOURCES = ["sched_kernels.cu", "select_kernels.cu", "pool_kernels.cu", "tm.cu",
-              "api.cu", "comm.cu", "static_select.cu", "manager_kernels.cu"]
+              "api.cu", "comm.cu", "static_select.cu", "manager_kernels.cu",
+              "integrity_kernels.cu"]
 
 
 def core_module_path() -> str:

@@ -1653,6 +1653,16 @@ int orchkv_read_block_locs(uint32_t *loc_out, uint8_t *state_out)
     return ORCHKV_OK;
 }
 
+int orchkv_block_checksums(const uint32_t *ids, uint32_t n, unsigned long long *out,
+                           uint8_t *tier_out)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    if (n && (!ids || !out)) return ORCHKV_ERR_INVALID;
+    if (g.p.slab % 16) return ORCHKV_ERR_INVALID;     // the kernel reads 16-byte words
+    return launch_block_checksums(g.p, ids, n, out, tier_out, g.stream);
+}
+
 uint32_t orchkv_max_blocks(void) { return g.inited ? g.p.max_blocks : 0; }
 
 /* Number of CUDA kernel launches this library has issued since it loaded. */

@@ -153,6 +153,9 @@ int launch_lhb_lookup(const PoolDev &p, const ReqDev &r, const uint32_t *lhb, ui
 // slabs; dir 2: GPU -> storage, pushing GPU slabs[j]).
 int launch_storage_commit(const PoolDev &p, const uint32_t *ids, const uint32_t *slabs,
                           uint32_t n, int dir, cudaStream_t s);
+// Per-block checksums of listed blocks' slabs (integrity_kernels.cu).
+int launch_block_checksums(const PoolDev &p, const uint32_t *ids, uint32_t n,
+                           unsigned long long *out, uint8_t *tier_out, cudaStream_t s);
 // scratch: >= 3 * ceil(L*H*mbph / 1024) words.
 int launch_request_free(const PoolDev &p, const ReqDev &r, uint32_t *scratch, cudaStream_t s);
 
