@@ -41,6 +41,8 @@ import sys
 import threading
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
@@ -279,6 +281,272 @@ class Workload:
             L.orchkv_request_destroy(c)
         self.tm.close()
         L.orchkv_shutdown()
+
+
+# ---------------------------------------------------------------------------
+# Llama-3-8B-shaped pool sharded by KV head (one fixed total pool at every N)
+# ---------------------------------------------------------------------------
+
+SH = dict(name="llama-3-8b-kv-head-sharded-capacity-40pct", B=8, L=32, Hq=32, Hkv=8, D=128,
+          T=32768, tpb=64, capacity=0.4, zipf=1.1)
+
+
+def orderable_u32(x):
+    """Ascending uint32 key of ascending float32 values (-0 as +0, NaN last),
+    the selection's key order."""
+    x = np.asarray(x, np.float32).copy()
+    x[x == 0.0] = 0.0
+    u = x.view(np.uint32)
+    k = np.where(u & np.uint32(0x80000000), ~u, u | np.uint32(0x80000000)).astype(np.uint32)
+    k[np.isnan(x)] = 0xFFFFFFFE
+    return k
+
+
+class ShardedWorkload:
+    """The Llama-3-8B-shaped pool (32 layers, 32 query / 8 KV heads, d_head
+    128, fp16, 64-token blocks, 32,768-token context) with its KV heads split
+    over the ranks: rank r holds KV heads [r*8/N, (r+1)*8/N) of every request
+    and the attention probabilities of their query heads, so the total pool
+    is the same at every N.  Probabilities: per (request, layer, KV head) a
+    Zipf(1.1) block mass over the blocks in a seeded order, spread over each
+    block's tokens with a seeded +-50% per-token jitter, normalised per query
+    head -- drawn per global KV head, so every N sees the same numbers.
+    A step: append one token per (request, layer), score, classify, select
+    the global coldest 60% of all ranks' blocks (GPU capacity 40%; the key
+    histograms are all-reduced over NCCL), evict them to the rank's pinned
+    DRAM tier, read the counts back.  The restore (untimed) promotes them."""
+
+    def __init__(self, torch, okv, rank, world, comm, requests, seed=0):
+        w = SH
+        self.t, self.L = torch, okv.lib()
+        self.world, self.rank = world, rank
+        self.B, self.Ly, self.D, self.T, self.tpb = requests, w["L"], w["D"], w["T"], w["tpb"]
+        self.G = w["Hq"] // w["Hkv"]
+        self.hkv = w["Hkv"] // world
+        self.hq = self.hkv * self.G
+        self.nb = self.T // self.tpb
+        self.rows = self.B * self.Ly
+        self.n_local = self.rows * self.hkv * self.nb
+        self.n_total = self.rows * w["Hkv"] * self.nb
+        self.slab = self.tpb * self.D * 2 * 2
+        self.k_global = self.n_total - int(w["capacity"] * self.n_total)
+        extra = self.rows * self.hkv * 4
+        cap = 1
+        while cap < self.n_local + extra + 1024:
+            cap <<= 1
+        self.cap = cap
+        # a rank's share of the global coldest 60% is 60% of its blocks up to
+        # the boundary ties (split in rank order): room for 75% + the appends
+        dram = int(0.75 * self.n_local) + extra + 4096
+        cfg = okv.make_config(gpu_pool_bytes=(self.n_local + extra + 1024) * self.slab,
+                              dram_pool_bytes=dram * self.slab, tokens_per_block=self.tpb,
+                              d_head=self.D, dtype=0, device=torch.cuda.current_device(),
+                              max_blocks_per_head=self.nb + 8)
+        ext = okv.OrchkvConfigExt()
+        ext.max_blocks = cap
+        L = self.L
+        rc = L.orchkv_init_ext(C.byref(cfg), C.byref(ext))
+        if rc != 0:
+            raise RuntimeError(f"orchkv_init_ext (sharded pool) failed: {rc}")
+        self.stream = torch.cuda.current_stream()
+        L.orchkv_set_stream(C.c_void_p(self.stream.cuda_stream))
+        self.tm = okv.Manager(tracker_cap=cap, max_blocks=2 * cap, ema_lambda=0.9, alpha=0.5,
+                              beta=0.3, gamma=0.2, recency_tau=50.0)
+        assert L.orchkv_attach_scheduler(self.tm.ref) == 0
+        if comm:
+            assert L.tm_set_comm(self.tm.ref, comm) == 0
+        g = torch.Generator(device="cuda").manual_seed(seed + 7 * rank + 1)
+        self.ctxs = [L.orchkv_request_create(i, self.Ly, self.hkv) for i in range(self.B)]
+        assert all(self.ctxs)
+        self.arr = (C.c_void_p * self.B)(*self.ctxs)
+        for c in self.ctxs:
+            for layer in range(self.Ly):
+                kv = torch.randn(2, self.hkv, self.T, self.D, generator=g, device="cuda",
+                                 dtype=torch.float16)
+                assert L.orchkv_prefill(c, layer, kv[0].data_ptr(), kv[1].data_ptr(), self.T) == 0
+        del kv
+        zipf = torch.arange(1, self.nb + 1, dtype=torch.float64, device="cuda") ** -w["zipf"]
+        zipf = (zipf / zipf.sum()).float()
+        self.probs = torch.empty(self.rows, self.hq, self.T, device="cuda")
+        for j in range(self.hkv):
+            gh = rank * self.hkv + j                          # global KV head
+            gg = torch.Generator(device="cuda").manual_seed(seed * 1000 + 100 + gh)
+            order = torch.argsort(torch.rand(self.rows, self.nb, generator=gg, device="cuda"), 1)
+            mass = zipf[order]                                # [rows, nb]
+            tok = mass.repeat_interleave(self.tpb, dim=1) / self.tpb
+            for q in range(self.G):
+                jit = 0.5 + torch.rand(self.rows, self.T, generator=gg, device="cuda")
+                p = tok * jit
+                self.probs[:, j * self.G + q] = p / p.sum(1, keepdim=True)
+        del zipf, order, mass, tok, jit, p
+        self.ids = torch.empty(self.rows * self.hkv * self.nb, dtype=torch.int32, device="cuda")
+        self.tok = torch.randn(2, self.B, self.Ly, self.hkv, self.D, generator=g, device="cuda",
+                               dtype=torch.float16)
+        self.victims = torch.empty(cap, dtype=torch.int32, device="cuda")
+        self.pref = torch.empty(cap, dtype=torch.int32, device="cuda")
+        self.counts = torch.zeros(16, dtype=torch.int32, device="cuda")
+        self.h_counts = torch.zeros(16, dtype=torch.int32).pin_memory()
+        self.ev = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+        torch.cuda.synchronize()
+
+    def _ptr(self, t, off=0):
+        return C.c_void_p(t.data_ptr() + off)
+
+    def step(self, check=None):
+        L, tm, ev = self.L, self.tm.ref, self.ev
+        ev[0].record()
+        assert L.orchkv_append_token_batch(self.arr, self.B, self._ptr(self.tok[0]),
+                                           self._ptr(self.tok[1])) == 0
+        ev[1].record()
+        assert L.orchkv_block_id_table(self.arr, self.B, self.T, self._ptr(self.ids)) == 0
+        ev[2].record()
+        assert L.tm_report_attn_probs(tm, self._ptr(self.probs), self.rows, self.hq, self.hkv,
+                                      self.T, self.tpb, None, self._ptr(self.ids)) == 0
+        ev[3].record()
+        assert L.tm_step_and_classify(tm) == 0
+        assert L.tm_select_victims(tm, self.k_global, self._ptr(self.victims),
+                                   self._ptr(self.counts)) == 0
+        ev[4].record()
+        if check:
+            check()
+        assert L.orchkv_evict_batch_to_dram(self._ptr(self.victims), self._ptr(self.counts),
+                                            self.cap, self._ptr(self.counts, 8)) == 0
+        ev[5].record()
+        self.h_counts.copy_(self.counts, non_blocking=True)
+        ev[6].record()
+
+    def restore(self):
+        """Every evicted block back to HBM (untimed; the prefetch selection is
+        global too, so every rank takes the same collective steps)."""
+        L, tm = self.L, self.tm.ref
+        assert L.tm_select_prefetch(tm, self.cap * self.world, 0.0, 0.0, self._ptr(self.pref),
+                                    self._ptr(self.counts, 32)) == 0
+        assert L.orchkv_promote_batch_to_gpu(self._ptr(self.pref), self._ptr(self.counts, 32),
+                                             self.cap, self._ptr(self.counts, 36)) == 0
+        self.t.cuda.synchronize()
+
+    def phases(self):
+        e = self.ev
+        names = ["append", "id_table", "score", "classify+select", "evict", "readback"]
+        return {n: e[i].elapsed_time(e[i + 1]) for i, n in enumerate(names)}
+
+    def selection_view(self):
+        """This rank's hotness, eligibility (tracker and classifier active, in
+        HBM, not migrating) and picks, for the global coldest-k check."""
+        st = self.tm.state()
+        loc = np.zeros(self.cap, np.uint32)
+        state = np.zeros(self.cap, np.uint8)
+        assert self.L.orchkv_read_block_locs(loc.ctypes.data, state.ctypes.data) == 0
+        elig = (st["t_active"] & st["c_active"] & ((loc >> 29) == 0) & (state != 5)).astype(bool)
+        n = int(self.counts[0].item())
+        picks = self.victims[:n].cpu().numpy().view(np.uint32).astype(np.int64)
+        return st["hot"], elig, picks
+
+    def close(self):
+        L = self.L
+        for c in self.ctxs:
+            L.orchkv_request_destroy(c)
+        self.tm.close()
+        L.orchkv_shutdown()
+
+
+def run_sharded(args, torch, okv, rank, world, comm, dist, link_d2h):
+    """The KV-head-sharded pool: K timed steps (W warm-up), each bracketed by
+    a barrier and a synchronize, step time = max over ranks; then one checked
+    step whose global picks are compared (rank 0) with a stable (hotness,
+    rank, slot) sort of all ranks' eligible blocks.  Returns the line's
+    `sharded` object on rank 0."""
+    if SH["Hkv"] % world:
+        return {"skipped": f"{SH['Hkv']} KV heads do not split over {world} ranks"}
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    sw = ShardedWorkload(torch, okv, rank, world, comm, args.sharded_requests)
+    L = sw.L
+    for _ in range(max(1, min(args.warmup, 2))):
+        sw.step()
+        sw.restore()
+    if comm:
+        L.orchkv_comm_exchange_time(comm, C.byref(C.c_float()), C.byref(C.c_uint32()))
+    step_ms, ph_acc, evicted, xch = [], {}, 0, [0.0, 0]
+    for _ in range(args.steps):
+        barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        sw.step()
+        t1.record()
+        barrier()
+        step_ms.append(t0.elapsed_time(t1))
+        for k, v in sw.phases().items():
+            ph_acc.setdefault(k, []).append(v)
+        evicted += sw.h_counts.tolist()[8]
+        if comm:
+            ms, calls = C.c_float(), C.c_uint32()
+            L.orchkv_comm_exchange_time(comm, C.byref(ms), C.byref(calls))
+            xch[0] += ms.value
+            xch[1] += calls.value
+        sw.restore()
+    # checked step (untimed): the ranks' union of picks vs the global order
+    view = {}
+    sw.step(check=lambda: view.update(v=sw.selection_view()))
+    sw.restore()
+    hot, elig, picks = view["v"]
+    if world > 1:
+        parts = [None] * world
+        dist.all_gather_object(parts, (hot, elig, picks))
+    else:
+        parts = [(hot, elig, picks)]
+    phases = {k: sum(v) / len(v) for k, v in ph_acc.items()}
+    mean_ms = sum(step_ms) / len(step_ms)
+    ev_ms = phases["evict"]
+    d2h = evicted / args.steps * sw.slab / (ev_ms * 1e-3) / 1e9
+    t = torch.tensor([mean_ms, evicted / args.steps, d2h, xch[0] / args.steps, link_d2h],
+                     dtype=torch.float64, device="cuda")
+    if world > 1:
+        allv = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(allv, t)
+        allv = [x.tolist() for x in allv]
+    else:
+        allv = [t.tolist()]
+    out = None
+    if rank == 0:
+        hot_all = np.concatenate([p[0] for p in parts])
+        elig_all = np.concatenate([p[1] for p in parts])
+        got = np.sort(np.concatenate([p[2] + r * sw.cap for r, p in enumerate(parts)]))
+        idx = np.nonzero(elig_all)[0]
+        order = np.lexsort((idx, orderable_u32(hot_all[idx])))[:sw.k_global]
+        want = np.sort(idx[order])
+        parity = bool(len(got) == len(want) == sw.k_global and np.array_equal(got, want))
+        ms_max = max(r[0] for r in allv)
+        moved = sum(r[1] for r in allv)
+        out = {
+            "workload": SH["name"], "requests": sw.B, "context": sw.T, "layers": sw.Ly,
+            "q_heads": SH["Hq"], "kv_heads": SH["Hkv"], "kv_heads_per_gpu": sw.hkv,
+            "d_head": sw.D, "tokens_per_block": sw.tpb, "dtype": "fp16",
+            "blocks_total": sw.n_total, "blocks_per_gpu": sw.n_local,
+            "pool_gib_total": round(sw.n_total * sw.slab / 2**30, 2),
+            "gpu_capacity": SH["capacity"], "evict_per_step_total": sw.k_global,
+            "sample": f"{sw.B} of the configuration's 64 requests (host RAM for the pinned "
+                      f"DRAM tier at every N); the same {sw.B} requests at every N",
+            "steps": args.steps, "ms_per_step": round(ms_max, 3),
+            "value": round(moved / (ms_max * 1e-3), 1), "unit": "evicted blocks/s (all ranks)",
+            "scaling": "strong (fixed total pool)",
+            "per_rank_evict_d2h_gbs": [round(r[2], 1) for r in allv],
+            "summed_evict_d2h_gbs": round(sum(r[2] for r in allv), 1),
+            "probe_d2h_gbs_per_rank": [round(r[4], 1) for r in allv],
+            "probe_d2h_gbs_summed": round(sum(r[4] for r in allv), 1),
+            "collective_ms_per_step": [round(r[3], 4) for r in allv] if world > 1 else None,
+            "phases_ms_rank0": {k: round(v, 4) for k, v in phases.items()},
+            "parity": {"global_coldest_k_equal": parity, "checked_blocks": int(len(idx)),
+                       "rule": "union of the ranks' picks == the k smallest (hotness, rank, "
+                               "slot) over every rank's eligible blocks"},
+        }
+    sw.close()
+    return out
 
 
 def score_bytes(wl):
@@ -536,6 +804,17 @@ def run_ours(args, rank, world, local_rank):
     phases = {k: round(sum(v) / len(v), 4) for k, v in phase_acc.items()}
     evict_bytes = c_last[2] * wl.slab
     promote_bytes = c_last[4] * wl.slab
+    # each rank's host-link bound of its swap (its synchronized probe), and
+    # the box's: every rank moves its own bytes at its share at once
+    bound_ms = 1e3 * max(evict_bytes / (link["d2h"] * 1e9), promote_bytes / (link["h2d"] * 1e9),
+                         (evict_bytes + promote_bytes) / (link["both"] * 1e9))
+    lt = torch.tensor([link["d2h"], link["h2d"], bound_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        lall = [torch.zeros_like(lt) for _ in range(world)]
+        dist.all_gather(lall, lt)
+        lall = [x.tolist() for x in lall]
+    else:
+        lall = [lt.tolist()]
     line = None
     if rank == 0:
         cpu = None
@@ -559,7 +838,10 @@ def run_ours(args, rank, world, local_rank):
                        "layers": WL["L"], "q_heads": WL["Hq"], "kv_heads": WL["Hkv"],
                        "d_head": WL["D"], "tokens_per_block": WL["tpb"],
                        "blocks_per_gpu": wl.n_blocks, "evict_frac": EVICT_FRAC,
-                       "promote_frac": PROMOTE_FRAC, "parallelism": f"kv-shard x{world}",
+                       "promote_frac": PROMOTE_FRAC, "parallelism": (f"replica x{world}: every rank holds the whole "
+                                       f"workload, selections global over ranks"
+                                       if world > 1 else "single GPU"),
+                       "value_scope": "all ranks' migrated blocks per second (whole job)",
                        "l2": "inputs larger than L2 (0.82 GB probs, 14 GiB KV pool)"},
             "gpu_launches": int(launches_timed),
             "gpu_launches_per_step": round(launches_timed / args.steps, 1),
@@ -611,6 +893,14 @@ def run_ours(args, rank, world, local_rank):
                                         promote_bytes / (link["h2d"] * 1e9),
                                         (evict_bytes + promote_bytes) / (link["both"] * 1e9))
                               / max(phases.get("swap", 1), 1e-9), 4)},
+            "box_host_link": {
+                "probe_d2h_gbs_per_rank": [round(x[0], 1) for x in lall],
+                "probe_d2h_gbs_summed": round(sum(x[0] for x in lall), 1),
+                "probe_h2d_gbs_summed": round(sum(x[1] for x in lall), 1),
+                "bound_ms_max_rank": round(max(x[2] for x in lall), 3),
+                "ceiling_blocks_s": round(migrated_total / (max(x[2] for x in lall) * 1e-3), 1),
+                "note": "every rank probes at once; the ceiling is the whole job's migrated "
+                        "blocks over the slowest rank's host-link bound"},
             "phases_ms": phases,
             "collective": ({"kind": "ncclAllReduce of 16 KB key histograms + ncclAllGather "
                                     "of tie counts inside each global selection",
@@ -627,6 +917,13 @@ def run_ours(args, rank, world, local_rank):
         if cpu:
             line["cpu_baseline"] = cpu
     wl.close()
+    del wl
+    torch.cuda.empty_cache()
+    if not args.no_sharded:
+        sharded = run_sharded(args, torch, okv, rank, world, comm, dist if world > 1 else None,
+                              link["d2h"])
+        if line is not None:
+            line["sharded"] = sharded
     if comm:
         okv.lib().orchkv_comm_destroy(comm)
     if world > 1:
@@ -905,6 +1202,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the KV-head-sharded Llama-3-8B-shaped pool")
+    ap.add_argument("--sharded-requests", type=int, default=SH["B"],
+                    help="requests of the sharded pool (the same at every N)")
     ap.add_argument("--requests", type=int, default=WL["B"],
                     help="requests per GPU (32 = the benchmark workload; smaller "
                          "values only for profiling captures)")

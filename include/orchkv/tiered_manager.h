@@ -321,8 +321,10 @@ int tm_select_prefetch(tiered_manager_t *m, uint32_t k, float th_gpu,
  * (device u32).  n is at most 1,048,576 (ORCHKV_ERR_INVALID beyond, with a
  * message).  Scratch is one static device array of ~4.1 MB in each GPU that
  * loads the library, kept until exit: the first call on a device looks its
- * address up (make that first call before any stream capture), every call
- * reuses it, so calls that overlap on the GPU race.  Asynchronous on
+ * address up (make that first call before any stream capture) and later
+ * calls reuse it, looking it up again only when the device's context was
+ * replaced (after cudaDeviceReset); every call shares the array, so calls
+ * that overlap on the GPU race.  Asynchronous on
  * `stream` (a cudaStream_t, NULL = default stream). */
 int orchkv_select_coldest_noalloc(const float *values, const uint8_t *eligible,
                                   uint32_t n, uint32_t k, uint32_t *out_ids,

@@ -8,6 +8,8 @@
 // value array, with every scratch word (keys, histograms, selection state,
 // compaction tiles) in the file-scope device array below.  The caller still
 // passes the inputs and the outputs.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "kernels.h"
@@ -26,16 +28,40 @@ static __device__ __align__(256) uint32_t g_noalloc_scratch[kScratchWords];
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 uint32_t *g_scratch_addr[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};
+typedef CUresult (*CtxGetCurrentFn)(CUcontext *);
+CtxGetCurrentFn g_ctx_current = nullptr;
+
+// The context the calling thread runs in on this device (a thread-local read
+// in the driver), so an address looked up in a context that has since been
+// destroyed -- cudaDeviceReset -- is not reused.
+CUcontext current_context()
+{
+    if (!g_ctx_current) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        g_ctx_current = (CtxGetCurrentFn)fn;
+    }
+    CUcontext c = nullptr;
+    return g_ctx_current(&c) == CUDA_SUCCESS ? c : nullptr;
+}
 
 // The array's name is only a host-side stand-in: its device address is looked
-// up once per device, with that device current.
+// up once per device (and again only if that device's context was replaced),
+// with that device current.
 int scratch_for_current_device(uint32_t **out)
 {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return ORCHKV_ERR_CUDA;
     if (dev < 0 || dev >= kMaxDevices) return ORCHKV_ERR_INVALID;
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_scratch_addr[dev]) {
+    // null until this thread's first runtime call that needs the device;
+    // the lookup below makes the context current
+    const CUcontext ctx = current_context();
+    if (!g_scratch_addr[dev] || !ctx || ctx != g_scratch_ctx[dev]) {
         void *p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || !p) {
@@ -44,6 +70,7 @@ int scratch_for_current_device(uint32_t **out)
             return ORCHKV_ERR_CUDA;
         }
         g_scratch_addr[dev] = static_cast<uint32_t *>(p);
+        g_scratch_ctx[dev] = current_context();
     }
     *out = g_scratch_addr[dev];
     return ORCHKV_OK;

@@ -95,3 +95,93 @@ def test_global_coldest_k_two_gpus(cuda, oracle_mod, k):
     got = np.sort(np.concatenate([np.array(res[r][0], np.int64) + r * N_PER_RANK
                                   for r in range(world)]))
     assert np.array_equal(got, want.astype(np.int64))
+
+
+def _sharded_worker(rank, world, port, q):
+    """One rank of bench.py's KV-head-sharded pool, cut to one request (the
+    Llama-3-8B shape: 32 layers, 8/world KV heads here, 32,768 tokens, fp16,
+    64-token blocks): one checked step, the victims' bytes before and after."""
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    import bench
+    import orchkv_b200 as okv
+    from tests.test_gpu_fullsize import _dram_total, dev_checksums, host_checksums
+    L = okv.lib()
+    try:
+        uid = (C.c_ubyte * 128)()
+        if rank == 0:
+            assert L.orchkv_comm_unique_id(uid) == 0
+        obj = [bytes(uid)]
+        dist.broadcast_object_list(obj, 0)
+        comm = L.orchkv_comm_create(rank, world, (C.c_ubyte * 128)(*obj[0]), 60.0)
+        assert comm
+        stream = torch.cuda.Stream()
+        torch.cuda.set_stream(stream)
+        sw = bench.ShardedWorkload(torch, okv, rank, world, comm, requests=1)
+        seen = {}
+
+        def check():
+            seen["view"] = sw.selection_view()
+            picks = torch.as_tensor(seen["view"][2].astype(np.int32), device="cuda")
+            seen["ids"] = picks
+            seen["before"], _ = dev_checksums(torch, L, picks)
+
+        sw.step(check=check)
+        torch.cuda.synchronize()
+        n_ev = sw.h_counts.tolist()[8]
+        loc = np.zeros(sw.cap, np.uint32)
+        assert L.orchkv_read_block_locs(loc.ctypes.data, None) == 0
+        picks = seen["view"][2]
+        on_dram = bool(((loc[picks] >> 29) == 1).all())
+        dram = host_checksums(L.orchkv_dram_pool_base(), sw.slab, _dram_total(L),
+                              loc[picks].astype(np.int64) & 0x1FFFFFFF)
+        sw.restore()
+        back, _ = dev_checksums(torch, L, seen["ids"])
+        ok = (on_dram and n_ev == len(picks) and np.array_equal(dram, seen["before"])
+              and np.array_equal(back, seen["before"]))
+        hot, elig, _ = seen["view"]
+        q.put((rank, hot, elig, picks, ok, sw.k_global, sw.cap))
+        sw.close()
+        L.orchkv_comm_destroy(comm)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_pool_step_two_gpus(cuda, oracle_mod):
+    """bench.py's sharded step on two GPUs: each rank holds 4 of the 8 KV
+    heads; the ranks' picks together are the oracle's global coldest 60% of
+    both ranks' blocks (ties in (rank, slot) order), and every picked block's
+    bytes reach the rank's DRAM tier and come back unchanged."""
+    if cuda.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sharded_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, hot, elig, picks, ok, k, cap = q.get(timeout=600)
+        res[r] = (hot, elig, picks, ok, k, cap)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert all(res[r][3] for r in range(world)), "victim bytes differ after the round trip"
+    k, cap = res[0][4], res[0][5]
+    hot = np.concatenate([res[r][0] for r in range(world)])
+    elig = np.concatenate([res[r][1] for r in range(world)]).astype(np.uint8)
+    want = oracle_mod.select_coldest(hot, elig, k).astype(np.int64)
+    got = np.sort(np.concatenate([res[r][2] + r * cap for r in range(world)]))
+    assert len(got) == k
+    assert np.array_equal(got, want)

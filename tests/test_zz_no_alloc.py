@@ -68,3 +68,31 @@ def test_noalloc_selection_rejects_oversize(cuda):
     rc = L.orchkv_select_coldest_noalloc(x.data_ptr(), x.data_ptr(), MAX_N + 1, 4,
                                          x.data_ptr(), x.data_ptr(), None)
     assert rc == -2                                   # ORCHKV_ERR_INVALID
+
+
+@pytest.mark.parametrize("n", [4097, 70001, MAX_N])
+def test_noalloc_selection_sizes(cuda, oracle_mod, n):
+    """A partial last 4,096-key tile (4,097 and 70,001 values) and the
+    documented maximum (1,048,576, every tile of the static scratch in use):
+    the picks equal the oracle's coldest-k over the same values -- ties
+    (values on a 1/8 grid) in ascending index order -- on calls in a row
+    with different k, the last taking every eligible value."""
+    import orchkv_b200 as okv
+    torch = cuda
+    L = okv.lib()
+    rng = np.random.default_rng(n)
+    vals = (rng.integers(0, 64, n) / 8).astype(np.float32)
+    elig = (rng.random(n) < 0.9).astype(np.uint8)
+    d_v = torch.from_numpy(vals).cuda()
+    d_e = torch.from_numpy(elig).cuda()
+    out = torch.full((n,), -1, dtype=torch.int32, device="cuda")
+    cnt = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    for k in (1, n // 3, n):
+        rc = L.orchkv_select_coldest_noalloc(d_v.data_ptr(), d_e.data_ptr(), n, k,
+                                             out.data_ptr(), cnt.data_ptr(), None)
+        assert rc == 0
+        torch.cuda.synchronize()
+        want = oracle_mod.select_coldest(vals, elig, k)
+        c = int(cnt.item())
+        assert c == len(want) == min(k, int(elig.sum()))
+        assert np.array_equal(out[:c].cpu().numpy().view(np.uint32), want)
