@@ -26,9 +26,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
+from tests.golden.refpath import reference_file  # noqa: E402
+
 from tests.golden.gen_kvcache_manager import f32bits  # noqa: E402
 
-REFERENCE = "/root/reference/python/orchkv/vllm_integration/attention_hook.py"
+REFERENCE = "python/orchkv/vllm_integration/attention_hook.py"      # inside the reference tree (tests/golden/refpath.py)
 CASE = dict(seed=9, steps=5, sample_interval=2, block_size=16, batch=2, heads=4, q_len=1,
             kv_len=100, table=[500, 507, 514, 521, 528])
 MODES = ["default", "fn", "table", "repeat"]
@@ -71,7 +73,7 @@ class Recorder(types.ModuleType):
 
 def load_reference(rec):
     sys.modules["orchkv_core"] = rec
-    spec = importlib.util.spec_from_file_location("ref_attention_hook", REFERENCE)
+    spec = importlib.util.spec_from_file_location("ref_attention_hook", reference_file(REFERENCE))
     mod = importlib.util.module_from_spec(spec)
     sys.modules[spec.name] = mod
     spec.loader.exec_module(mod)

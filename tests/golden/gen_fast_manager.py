@@ -4,8 +4,9 @@ decode loop on the CPU, with an orchkv_core stand-in backed by the
 reference's scheduler compiled from its sources (oracle/_ref), so the
 manager's score-ordered evictions see the reference's own scores.  Every
 mutating call the manager makes (register, report, step, usage, schedule) is
-recorded, and after each step its schedule result, statistics and the set of
-evicted blocks.
+recorded, with every tm_get_block_score the manager asks for (its position in
+the call stream, the block and the reference's answer), and after each step
+its schedule result, statistics and the set of evicted blocks.
 
 Only needed to regenerate; the fixture is committed.  Needs the reference
 source tree and `make -C oracle`.
@@ -24,10 +25,12 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 
+from tests.golden.refpath import reference_file  # noqa: E402
+
 from oracle import oracle as O  # noqa: E402
 from tests.golden.gen_kvcache_manager import f32bits, load_reference  # noqa: E402
 
-REFERENCE = "/root/reference/python/orchkv/fast_kvcache_manager.py"
+REFERENCE = "python/orchkv/fast_kvcache_manager.py"      # inside the reference tree (tests/golden/refpath.py)
 CASE = dict(n_layers=4, n_kv_heads=2, q_heads=4, head_dim=64, block_size=16, max_seq_len=1024,
             prefill=700, steps=40, budget_blocks_per_layer=40, sink_tokens=4, restore_every=6,
             seed=3)
@@ -58,6 +61,7 @@ class RefCore(types.ModuleType):
     def __init__(self):
         super().__init__("orchkv_core")
         self.calls = []
+        self.scores = []
         self.tm = None
 
     def tm_create(self, *a, **k):
@@ -88,7 +92,10 @@ class RefCore(types.ModuleType):
         self.tm.schedule_once()
 
     def tm_get_block_score(self, h, bid):
-        return self.tm.score(int(bid))
+        sc = self.tm.score(int(bid))
+        # where in the call stream the manager asked, and what it was told
+        self.scores.append([len(self.calls), int(bid), f32bits(sc)])
+        return sc
 
     def tm_get_stats(self, h):
         return {}
@@ -99,7 +106,7 @@ def main():
         raise SystemExit("build the reference first: make -C oracle")
     c = CASE
     core = RefCore()
-    mod = load_reference(core, REFERENCE, "ref_fast_kvcache_manager")
+    mod = load_reference(core, reference_file(REFERENCE), "ref_fast_kvcache_manager")
     k0, v0, kt, vt, attn = inputs(c)
     L, H, d, bs = c["n_layers"], c["n_kv_heads"], c["head_dim"], c["block_size"]
     block_bytes = 2 * H * bs * d * 2
@@ -122,7 +129,7 @@ def main():
             rec["after_restore"] = {"stats": mgr.get_stats()}
         steps.append(rec)
     mgr.destroy()
-    fx = {"case": c, "steps": steps, "calls": core.calls,
+    fx = {"case": c, "steps": steps, "calls": core.calls, "score_queries": core.scores,
           "source": "the reference's python/orchkv/fast_kvcache_manager.py run unmodified on "
                     "the CPU (CUDA placements mapped to the CPU) with orchkv_core backed by "
                     "the reference scheduler compiled from src/scheduler (oracle/_ref); "

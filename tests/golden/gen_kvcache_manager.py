@@ -22,8 +22,13 @@ import types
 import numpy as np
 import torch
 
+try:
+    from tests.golden.refpath import reference_file
+except ImportError:          # run as a script from tests/golden
+    from refpath import reference_file
+
 HERE = os.path.dirname(os.path.abspath(__file__))
-REFERENCE = "/root/reference/python/orchkv/kvcache_manager.py"
+REFERENCE = "python/orchkv/kvcache_manager.py"      # inside the reference tree (tests/golden/refpath.py)
 
 CASE = dict(n_layers=4, n_kv_heads=2, q_heads=4, head_dim=64, block_size=16, prefill=100,
             steps=30, budget_blocks=30, sink_tokens=4, build_every=5, seed=5)
@@ -90,10 +95,11 @@ class Recorder(types.ModuleType):
         self.calls.append(["tier", int(bid), int(tier)])
 
 
-def load_reference(rec, path=REFERENCE, name="ref_kvcache_manager"):
+def load_reference(rec, path=None, name="ref_kvcache_manager"):
     """Load a reference manager module with `rec` as its orchkv_core and its
     CUDA placements mapped to the CPU."""
     sys.modules["orchkv_core"] = rec
+    path = path or reference_file(REFERENCE)
     spec = importlib.util.spec_from_file_location(name, path)
     mod = importlib.util.module_from_spec(spec)
     sys.modules[spec.name] = mod              # its dataclasses look their module up

@@ -22,8 +22,13 @@ import random
 import sys
 from types import SimpleNamespace
 
+try:
+    from tests.golden.refpath import reference_file
+except ImportError:          # run as a script from tests/golden
+    from refpath import reference_file
+
 HERE = os.path.dirname(os.path.abspath(__file__))
-REFERENCE = "/root/reference/python/orchkv/vllm_integration/connector.py"
+REFERENCE = "python/orchkv/vllm_integration/connector.py"      # inside the reference tree (tests/golden/refpath.py)
 CONFIGS = [
     {"extra": {"dram_pool_gb": 1, "n_layers": 3}, "model": {"head_dim": 64}},
     {"extra": {"dram_pool_gb": 1, "n_layers": 5}, "model": {"head_dim": 128, "num_layers": 2}},
@@ -84,7 +89,7 @@ def run(connector_cls, role, case, ops):
 
 
 def main():
-    spec = importlib.util.spec_from_file_location("ref_orchkv_connector", REFERENCE)
+    spec = importlib.util.spec_from_file_location("ref_orchkv_connector", reference_file(REFERENCE))
     mod = importlib.util.module_from_spec(spec)
     sys.modules[spec.name] = mod
     spec.loader.exec_module(mod)
