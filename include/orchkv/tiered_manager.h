@@ -213,9 +213,14 @@ int       tm_read_state(tiered_manager_t *m, float *sum, float *ema,
  *   lens       uint32 [n_rows] valid tokens per row, or NULL (= row_len)
  *   block_ids  uint32 [n_rows][n_kv_heads][ceil(row_len/tpb)]: the block
  *              id receiving the mass of (row, kv head, token block);
- *              0xFFFFFFFF = none.  Within one call the ids must map to
- *              distinct tracker slots (slot = id & (capacity - 1)): unique
- *              ids below the tracker capacity do; aliasing ids would race.
+ *              0xFFFFFFFF = none.  Ids may repeat or share a tracker slot
+ *              (slot = id & (capacity - 1)), e.g. one block id per token
+ *              position shared by every layer's row: such reports apply in
+ *              (row, kv head, block) order, as that many tm_notify_attn calls
+ *              in that order would (attn_tracker_update_batch,
+ *              src/scheduler/attention_tracker.c:95-118).  A device pass over
+ *              the ids detects shared slots; only a call that has them takes
+ *              the slower ordered apply.
  *
  * mass(row,h,b) = sum over the n_q_heads/n_kv_heads query heads of KV group h
  * and the tokens of block b of probs.  A block's per-step sum, max and last
@@ -228,6 +233,19 @@ int tm_report_attn_probs(tiered_manager_t *m, const float *probs,
                          uint32_t row_len, uint32_t tokens_per_block,
                          const uint32_t *lens, const uint32_t *block_ids);
 
+/* B200: upload a host input of a later report call now, on the manager's
+ * own copy stream, so the copy overlaps whatever runs meanwhile (the current
+ * step's migrations, say).  The next tm_report_attn_probs /
+ * tm_report_attn_ranges call given exactly this host pointer and byte count
+ * for one of its arrays reads the uploaded copy (waiting for the upload on
+ * the device) instead of copying the array then.  The caller keeps the host
+ * bytes unchanged until that call; pinned memory makes the upload fully
+ * asynchronous.  Two uploads may wait for their reports at once, taken
+ * oldest first; a third returns ORCHKV_ERR_STATE.  host = NULL drops every
+ * waiting upload.  No counterpart in the reference (its reports arrive as
+ * per-block host floats). */
+int tm_stage_input_async(tiered_manager_t *m, const void *host, size_t bytes);
+
 /* The original KVCacheManager's per-block report in one call
  * (python/orchkv/kvcache_manager.py:317-347: one float(avg[:, s:e].sum()) and
  * one tm_report_attn per block).
@@ -239,16 +257,17 @@ int tm_report_attn_probs(tiered_manager_t *m, const float *probs,
  *
  * Block i records sum over h and t in [starts[i], min(ends[i], kv_len)) of
  * avg[h][t] as tm_notify_attn would; a block whose range is empty is not
- * reported.  The ids must map to different tracker slots.  Each array may
- * be in device or host memory (host arrays are copied once on the manager's
- * stream).  Asynchronous. */
+ * reported.  Ids that share a tracker slot apply in list order.  Each array
+ * may be in device or host memory (host arrays are copied once on the
+ * manager's stream).  Asynchronous. */
 int tm_report_attn_ranges(tiered_manager_t *m, const float *avg, uint32_t heads,
                           uint32_t kv_len, const uint32_t *starts, const uint32_t *ends,
                           const uint32_t *block_ids, uint32_t n);
 
 /* Report a batch of (id, weight) pairs already on the device, applied in
  * array order per block (attn_tracker_update_batch semantics,
- * src/scheduler/attention_tracker.c:95-118) provided ids are unique. */
+ * src/scheduler/attention_tracker.c:95-118), repeated ids and ids sharing a
+ * tracker slot included. */
 int tm_report_attn_batch_dev(tiered_manager_t *m, const uint32_t *block_ids,
                              const float *weights, uint32_t n);
 

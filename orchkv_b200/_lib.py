@@ -177,6 +177,7 @@ _SIGS = {
     "tm_read_state": (i32, [P(TieredManager), vp, vp, vp, vp, vp, vp, vp, vp]),
     "tm_report_attn_probs": (i32, [P(TieredManager), vp, u32, u32, u32, u32, u32, vp, vp]),
     "tm_report_attn_batch_dev": (i32, [P(TieredManager), vp, vp, u32]),
+    "tm_stage_input_async": (i32, [P(TieredManager), vp, C.c_size_t]),
     "tm_report_attn_ranges": (i32, [P(TieredManager), vp, u32, u32, vp, vp, vp, u32]),
     "tm_report_attn_blockmean": (i32, [P(TieredManager), vp, i32, u32, u32, u32, u32, u32, vp,
                                        vp]),

@@ -9,20 +9,42 @@
 namespace okv {
 
 // ---- scoring (sched_kernels.cu) ---------------------------------------------
+
+// Ordering of one report call whose ids may share tracker slots.  A mark pass
+// stamps every listed active slot with `epoch` (a value unique to the call)
+// and sets *flag = epoch when a slot is stamped twice.  Report kernels read
+// the flag: when it is not set they record straight into the tracker (no two
+// writers per slot); when it is, they leave the tracker alone and write each
+// entry's id and mass to ids_eff / mass, and the ordered pass applies them per
+// slot in entry order -- the sums consecutive single reports would give.
+struct ReportOrder {
+    uint32_t *mark;      // [cap] last epoch that stamped each slot
+    uint32_t *flag;      // one word: == epoch when this call has aliasing ids
+    uint32_t epoch;
+    uint32_t *ids_eff;   // [n] per entry: id, or kNoBlock when not reported
+    float *mass;         // [n] per entry mass
+};
+int launch_alias_mark(const uint32_t *ids, uint32_t n, const SchedDev &d, const ReportOrder &o,
+                      cudaStream_t s);
+// Applies (ids[i], w[i]) for i in [0, n) in entry order per slot, only when
+// the call's flag is set (otherwise returns at once on the device).
+int launch_report_ordered(const uint32_t *ids, const float *w, uint32_t n, const SchedDev &d,
+                          unsigned long long step, const ReportOrder &o, cudaStream_t s);
 int launch_score(const float *probs, uint32_t R, uint32_t Hq, uint32_t Hkv,
                  uint32_t T, uint32_t tpb, const uint32_t *lens,
                  const uint32_t *ids, const SchedDev &d, unsigned long long step,
-                 cudaStream_t s);
+                 const ReportOrder &o, cudaStream_t s);
 int launch_report_apply(const uint32_t *slots, const float *psum, const float *pmax,
                         uint32_t n, const SchedDev &d, unsigned long long step,
                         cudaStream_t s);
 int launch_report_batch(const uint32_t *ids, const float *w, uint32_t n,
-                        const SchedDev &d, unsigned long long step, cudaStream_t s);
+                        const SchedDev &d, unsigned long long step, const ReportOrder &o,
+                        cudaStream_t s);
 // Per-block mass over token ranges: sum over heads and tokens [start, min(end,
 // kv_len)) of avg [heads][kv_len], recorded for ids[i]; empty ranges skipped.
 int launch_range_mass(const float *avg, uint32_t heads, uint32_t kv_len, const uint32_t *start,
                       const uint32_t *end, const uint32_t *ids, uint32_t n, const SchedDev &d,
-                      unsigned long long step, cudaStream_t s);
+                      unsigned long long step, const ReportOrder &o, cudaStream_t s);
 // Block means of attention weights [batch][heads][q_len][kv_len] (dtype 0
 // fp16, 1 bf16, 2 fp32) into scores [heads][ceil(kv_len/bs)]; with ids and d,
 // each (h, b) is then recorded in the tracker, heads of one block in order.

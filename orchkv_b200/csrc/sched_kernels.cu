@@ -67,7 +67,8 @@ __global__ void __launch_bounds__(kScoreWarps * 32, 1)
 score_vec_kernel(const float *__restrict__ probs, uint32_t Hq, uint32_t Hkv,
                  uint32_t T, uint32_t tpb, const uint32_t *__restrict__ lens,
                  const uint32_t *__restrict__ ids, uint32_t nb, uint32_t n_chunks,
-                 unsigned long long n_tiles, SchedDev d, unsigned long long step)
+                 unsigned long long n_tiles, SchedDev d, unsigned long long step,
+                 ReportOrder o)
 {
     constexpr int LPB = 1 << LOG_LPB;              // lanes per block in one step
     constexpr int BPU = 32 / LPB;                  // blocks per step
@@ -86,6 +87,7 @@ score_vec_kernel(const float *__restrict__ probs, uint32_t Hq, uint32_t Hkv,
     if (len > T) len = T;
     const uint32_t T4 = T >> 2;
     const float4 *base = reinterpret_cast<const float4 *>(probs + (r * Hq + (unsigned long long)h * G) * T);
+    const bool ordered = *o.flag == o.epoch;       // this call's ids alias: no direct records
 
     // block ids of the blocks this lane records
     uint32_t bid[K];
@@ -159,7 +161,13 @@ score_vec_kernel(const float *__restrict__ probs, uint32_t Hq, uint32_t Hkv,
             const float t = __shfl_sync(0xFFFFFFFFu, part[u], src);
             if (uk == (uint32_t)u) w = t;
         }
-        if (bid[j] != kNoBlock && act[j]) {
+        if (ordered) {
+            const uint32_t b = c * NBLK + k;
+            if (k < (uint32_t)NBLK && b < nb) {
+                o.ids_eff[rh * nb + b] = bid[j];
+                o.mass[rh * nb + b] = w;
+            }
+        } else if (bid[j] != kNoBlock && act[j]) {
             const uint32_t sl = bid[j] & d.mask;
             d.sum[sl] = __fadd_rn(old_sum[j], w);
             if (w > old_max[j]) d.mx[sl] = w;
@@ -176,10 +184,11 @@ __global__ void score_scalar_kernel(const float *__restrict__ probs, uint32_t Hq
                                     const uint32_t *__restrict__ lens,
                                     const uint32_t *__restrict__ ids, uint32_t nb,
                                     unsigned long long n_items, SchedDev d,
-                                    unsigned long long step)
+                                    unsigned long long step, ReportOrder o)
 {
     const unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_items) return;
+    const bool ordered = *o.flag == o.epoch;
     const uint32_t b = (uint32_t)(i % nb);
     const unsigned long long rh = i / nb;
     const uint32_t h = (uint32_t)(rh % Hkv);
@@ -188,7 +197,10 @@ __global__ void score_scalar_kernel(const float *__restrict__ probs, uint32_t Hq
     uint32_t len = lens ? lens[r] : T;
     if (len > T) len = T;
     const uint32_t t0 = b * tpb;
-    if (t0 >= len) return;
+    if (t0 >= len) {
+        if (ordered) o.ids_eff[i] = kNoBlock;
+        return;
+    }
     uint32_t t1 = t0 + tpb;
     if (t1 > len) t1 = len;
     float acc = 0.0f;
@@ -196,13 +208,111 @@ __global__ void score_scalar_kernel(const float *__restrict__ probs, uint32_t Hq
         const float *row = probs + ((r * Hq) + (unsigned long long)h * G + g) * T;
         for (uint32_t t = t0; t < t1; t++) acc = __fadd_rn(acc, row[t]);
     }
-    record_mass(d, ids[rh * nb + b], acc, step);
+    if (ordered) {
+        o.ids_eff[i] = ids[i];
+        o.mass[i] = acc;
+    } else {
+        record_mass(d, ids[i], acc, step);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Reports whose ids share tracker slots within one call
+// ---------------------------------------------------------------------------
+
+// Stamps each listed active slot with the call's epoch; a slot stamped twice
+// means two entries would update it: the call then takes the ordered pass.
+__global__ void alias_mark_kernel(const uint32_t *__restrict__ ids, uint32_t n, SchedDev d,
+                                  ReportOrder o)
+{
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint32_t id = ids[i];
+    if (id == kNoBlock) return;
+    const uint32_t s = id & d.mask;
+    if (!d.tact[s]) return;                        // inactive slots ignore reports
+    if (atomicExch(&o.mark[s], o.epoch) == o.epoch) *o.flag = o.epoch;
+}
+
+int launch_alias_mark(const uint32_t *ids, uint32_t n, const SchedDev &d, const ReportOrder &o,
+                      cudaStream_t s)
+{
+    if (n == 0) return ORCHKV_OK;
+    alias_mark_kernel<<<(n + 255) / 256, 256, 0, s>>>(ids, n, d, o);
+    note_launches(1);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+constexpr int kOrderThreads = 1024;
+constexpr unsigned kOrderCtas = 296;          // two 1024-thread CTAs on each of 148 SMs
+
+// The ordered pass.  CTA c owns the slots with slot % gridDim.x == c and walks
+// the whole list in chunks of 1024 entries; a chunk's owned entries are
+// compacted in entry order into shared memory and applied by warp 0, 32 at a
+// time: lanes holding the same slot are grouped (__match_any_sync) and the
+// group's lowest lane adds their masses in lane order, so every slot sees its
+// entries' additions in list order, exactly as that many single reports.
+__global__ void __launch_bounds__(kOrderThreads)
+report_ordered_kernel(const uint32_t *__restrict__ ids, const float *__restrict__ w, uint32_t n,
+                      SchedDev d, unsigned long long step, ReportOrder o)
+{
+    if (*o.flag != o.epoch) return;
+    __shared__ uint32_t s_slot[kOrderThreads];
+    __shared__ float s_w[kOrderThreads];
+    __shared__ uint32_t tmp[33];
+    const uint32_t owner = blockIdx.x, owners = gridDim.x;
+    const int lane = threadIdx.x & 31;
+    for (uint32_t base = 0; base < n; base += kOrderThreads) {
+        const uint32_t i = base + threadIdx.x;
+        const uint32_t id = i < n ? ids[i] : kNoBlock;
+        const uint32_t slot = id & d.mask;
+        const bool own = id != kNoBlock && slot % owners == owner;
+        uint32_t total;
+        const uint32_t pos = block_excl_scan(own ? 1u : 0u, tmp, &total);
+        if (own) {
+            s_slot[pos] = slot;
+            s_w[pos] = w[i];
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            for (uint32_t q = 0; q < total; q += 32) {
+                const uint32_t j = q + lane;
+                const bool has = j < total;
+                const uint32_t sl = has ? s_slot[j] : 0xFFFFFFFFu;
+                const unsigned peers = __match_any_sync(0xFFFFFFFFu, sl);
+                if (has && lane == __ffs(peers) - 1 && d.tact[sl]) {
+                    float sum = d.sum[sl], mx = d.mx[sl];
+                    for (unsigned m = peers; m; m &= m - 1) {
+                        const float x = s_w[q + __ffs(m) - 1];
+                        sum = __fadd_rn(sum, x);
+                        if (x > mx) mx = x;
+                    }
+                    d.sum[sl] = sum;
+                    d.mx[sl] = mx;
+                    d.last[sl] = step;
+                }
+                __syncwarp();
+            }
+        }
+        __syncthreads();
+    }
+}
+
+int launch_report_ordered(const uint32_t *ids, const float *w, uint32_t n, const SchedDev &d,
+                          unsigned long long step, const ReportOrder &o, cudaStream_t s)
+{
+    if (n == 0) return ORCHKV_OK;
+    report_ordered_kernel<<<kOrderCtas, kOrderThreads, 0, s>>>(ids, w, n, d, step, o);
+    note_launches(1);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
 }
 
 int launch_score(const float *probs, uint32_t R, uint32_t Hq, uint32_t Hkv,
                  uint32_t T, uint32_t tpb, const uint32_t *lens,
                  const uint32_t *ids, const SchedDev &d, unsigned long long step,
-                 cudaStream_t s)
+                 const ReportOrder &o, cudaStream_t s)
 {
     if (!probs || !ids || R == 0 || Hq == 0 || Hkv == 0 || T == 0 || tpb == 0 ||
         Hq % Hkv != 0)
@@ -219,7 +329,8 @@ int launch_score(const float *probs, uint32_t R, uint32_t Hq, uint32_t Hkv,
 #define OKV_SCORE_CASE(L)                                                              \
     case L:                                                                            \
         score_vec_kernel<L><<<(unsigned)grid, kScoreWarps * 32, 0, s>>>(               \
-            probs, Hq, Hkv, T, tpb, lens, ids, nb, n_chunks, n_tiles, d, step); note_launches(1);        \
+            probs, Hq, Hkv, T, tpb, lens, ids, nb, n_chunks, n_tiles, d, step, o);             \
+        note_launches(1);                                                              \
         break;
         switch (log_lpb) {
             OKV_SCORE_CASE(0) OKV_SCORE_CASE(1) OKV_SCORE_CASE(2)
@@ -231,7 +342,7 @@ int launch_score(const float *probs, uint32_t R, uint32_t Hq, uint32_t Hkv,
         const unsigned long long n_items = (unsigned long long)R * Hkv * nb;
         const unsigned grid = (unsigned)((n_items + 255) / 256);
         score_scalar_kernel<<<grid, 256, 0, s>>>(probs, Hq, Hkv, T, tpb, lens, ids, nb,
-                                                 n_items, d, step); note_launches(1);
+                                                 n_items, d, step, o); note_launches(1);
     }
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
@@ -267,18 +378,19 @@ int launch_report_apply(const uint32_t *slots, const float *psum, const float *p
 
 __global__ void report_batch_kernel(const uint32_t *__restrict__ ids,
                                     const float *__restrict__ w, uint32_t n, SchedDev d,
-                                    unsigned long long step)
+                                    unsigned long long step, ReportOrder o)
 {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
+    if (i >= n || *o.flag == o.epoch) return;     // aliasing ids: the ordered pass applies them
     record_mass(d, ids[i], w[i], step);
 }
 
 int launch_report_batch(const uint32_t *ids, const float *w, uint32_t n,
-                        const SchedDev &d, unsigned long long step, cudaStream_t s)
+                        const SchedDev &d, unsigned long long step, const ReportOrder &o,
+                        cudaStream_t s)
 {
     if (n == 0) return ORCHKV_OK;
-    report_batch_kernel<<<(n + 255) / 256, 256, 0, s>>>(ids, w, n, d, step); note_launches(1);
+    report_batch_kernel<<<(n + 255) / 256, 256, 0, s>>>(ids, w, n, d, step, o); note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }
@@ -561,15 +673,19 @@ __global__ void range_mass_kernel(const float *__restrict__ avg, uint32_t heads,
                                   uint32_t kv_len, const uint32_t *__restrict__ start,
                                   const uint32_t *__restrict__ end,
                                   const uint32_t *__restrict__ ids, uint32_t n, SchedDev d,
-                                  unsigned long long step)
+                                  unsigned long long step, ReportOrder o)
 {
     const unsigned lane = threadIdx.x & 31;
     const unsigned long long nw = ((unsigned long long)gridDim.x * blockDim.x) >> 5;
+    const bool ordered = *o.flag == o.epoch;
     for (unsigned long long i = ((unsigned long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
          i < n; i += nw) {
         const uint32_t s = start[i];
         const uint32_t e = end[i] < kv_len ? end[i] : kv_len;
-        if (s >= e) continue;                          // warp-uniform
+        if (s >= e) {                                  // warp-uniform
+            if (ordered && lane == 0) o.ids_eff[i] = kNoBlock;
+            continue;
+        }
         float acc = 0.f;
         if (e - s <= 32) {
             // at most one token per lane: the heads' loads are independent,
@@ -590,19 +706,26 @@ __global__ void range_mass_kernel(const float *__restrict__ avg, uint32_t heads,
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, o));
-        if (lane == 0) record_mass(d, ids[i], acc, step);
+        if (lane == 0) {
+            if (ordered) {
+                o.ids_eff[i] = ids[i];
+                o.mass[i] = acc;
+            } else {
+                record_mass(d, ids[i], acc, step);
+            }
+        }
     }
 }
 
 int launch_range_mass(const float *avg, uint32_t heads, uint32_t kv_len, const uint32_t *start,
                       const uint32_t *end, const uint32_t *ids, uint32_t n, const SchedDev &d,
-                      unsigned long long step, cudaStream_t s)
+                      unsigned long long step, const ReportOrder &o, cudaStream_t s)
 {
     if (!avg || !start || !end || !ids || heads == 0 || kv_len == 0) return ORCHKV_ERR_INVALID;
     if (n == 0) return ORCHKV_OK;
     unsigned grid = (unsigned)(((unsigned long long)n * 32 + 255) / 256);
     if (grid > 148 * 16) grid = 148 * 16;
-    range_mass_kernel<<<grid, 256, 0, s>>>(avg, heads, kv_len, start, end, ids, n, d, step);
+    range_mass_kernel<<<grid, 256, 0, s>>>(avg, heads, kv_len, start, end, ids, n, d, step, o);
     note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;

@@ -67,8 +67,8 @@ static int alloc_device(TmImpl *t)
     uint32_t tiles = 0;
     const size_t sel_words = select_scratch_words(t->cap, &tiles);
     // every sub-array below is rounded up to 256 bytes: 32 slots of padding
-    const size_t bytes = n * (4 * 4 + 4 + 8 + 4 + 7) + 512 * 4 + sel_words * 4 +
-                         sizeof(ClassCounts) + 64 * 4 + 32 * 256;
+    const size_t bytes = n * (4 * 4 + 4 + 8 + 4 + 7 + 4) + 512 * 4 + sel_words * 4 +
+                         sizeof(ClassCounts) + 64 * 4 + 256 + 34 * 256;
     OKV_CUDA_TRY(cudaMalloc((void **)&t->dev_block, bytes));
     OKV_CUDA_TRY(cudaMemsetAsync(t->dev_block, 0, bytes, t->stream));
     char *p = t->dev_block;
@@ -97,6 +97,9 @@ static int alloc_device(TmImpl *t)
     t->sc.tile_offsets = (uint32_t *)take((size_t)2 * tiles * 4);
     t->counts = (ClassCounts *)take(sizeof(ClassCounts));
     t->small = (uint32_t *)take(64 * 4);
+    t->report_mark = (uint32_t *)take(n * 4);
+    t->report_flag = (uint32_t *)take(4);
+    t->report_epoch = 0;
     // TIER_NONE for never-registered slots keeps them out of every selection
     OKV_CUDA_TRY(cudaMemsetAsync(d.tier, TIER_NONE, n, t->stream));
     OKV_CUDA_TRY(cudaMemcpyAsync(table, t->table, 512 * 4, cudaMemcpyHostToDevice, t->stream));
@@ -118,6 +121,16 @@ static void free_device(TmImpl *t)
     cudaFree(t->up_dev);
     cudaFree(t->reg_dev);
     cudaFree(t->in_stage);
+    cudaFree(t->report_scratch);
+    if (t->early_copy) cudaStreamSynchronize(t->early_copy);
+    for (StagedInput &e : t->early) {
+        cudaFree(e.dev);
+        if (e.ready) cudaEventDestroy(e.ready);
+        if (e.consumed) cudaEventDestroy(e.consumed);
+        e = StagedInput();
+    }
+    if (t->early_copy) cudaStreamDestroy(t->early_copy);
+    t->early_copy = nullptr;
     cudaFreeHost(t->m_hot);
     cudaFreeHost(t->m_heat);
     cudaFreeHost(t->m_cact);
@@ -892,6 +905,32 @@ static bool on_device(const void *p)
     return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
 }
 
+// The oldest staged upload of exactly this host range, if any: the report
+// then reads the uploaded copy, after its upload, instead of copying again.
+static StagedInput *take_staged(TmImpl *t, const void *host, size_t bytes)
+{
+    StagedInput *best = nullptr;
+    for (StagedInput &e : t->early)
+        if (e.pending && e.host == host && e.bytes == bytes && (!best || e.seq < best->seq))
+            best = &e;
+    if (!best) return nullptr;
+    if (cudaStreamWaitEvent(t->stream, best->ready, 0) != cudaSuccess) return nullptr;
+    best->pending = false;
+    best->in_use = true;
+    return best;
+}
+
+// After a report's launches: staged inputs it read may be reused once they end.
+static int release_staged(TmImpl *t)
+{
+    for (StagedInput &e : t->early) {
+        if (!e.in_use) continue;
+        e.in_use = false;
+        OKV_CUDA_TRY(cudaEventRecord(e.consumed, t->stream));
+    }
+    return ORCHKV_OK;
+}
+
 static int stage_inputs(TmImpl *t, const void **ptrs, const size_t *bytes, int n)
 {
     size_t off[4] = {0}, need = 0;
@@ -899,6 +938,11 @@ static int stage_inputs(TmImpl *t, const void **ptrs, const size_t *bytes, int n
     for (int i = 0; i < n; i++) {
         host[i] = ptrs[i] && bytes[i] && !on_device(ptrs[i]);
         if (host[i]) {
+            if (StagedInput *e = take_staged(t, ptrs[i], bytes[i])) {
+                ptrs[i] = e->dev;
+                host[i] = false;
+                continue;
+            }
             off[i] = need;
             need += (bytes[i] + 255) & ~size_t(255);
         }
@@ -923,6 +967,36 @@ static int stage_inputs(TmImpl *t, const void **ptrs, const size_t *bytes, int n
     return ORCHKV_OK;
 }
 
+// A report call's ordering state (okv::ReportOrder): a new epoch, and when
+// the call computes its masses itself (scratch), room for n entry ids and
+// masses in case its ids turn out to share slots.
+static int begin_report(TmImpl *t, size_t n, bool scratch, okv::ReportOrder *o)
+{
+    if (++t->report_epoch == 0) {
+        // the stamps wrapped: clear them so no old stamp equals a new epoch
+        OKV_CUDA_TRY(cudaMemsetAsync(t->report_mark, 0, (size_t)t->cap * 4, t->stream));
+        OKV_CUDA_TRY(cudaMemsetAsync(t->report_flag, 0, 4, t->stream));
+        t->report_epoch = 1;
+    }
+    const size_t half = (n * 4 + 255) & ~size_t(255);
+    if (scratch && 2 * half > t->report_scratch_cap) {
+        size_t cap = t->report_scratch_cap ? t->report_scratch_cap : (1 << 20);
+        while (cap < 2 * half) cap *= 2;
+        OKV_CUDA_TRY(cudaStreamSynchronize(t->stream));   // an earlier call may still use it
+        cudaFree(t->report_scratch);
+        t->report_scratch = nullptr;
+        t->report_scratch_cap = 0;
+        OKV_CUDA_TRY(cudaMalloc((void **)&t->report_scratch, cap));
+        t->report_scratch_cap = cap;
+    }
+    o->mark = t->report_mark;
+    o->flag = t->report_flag;
+    o->epoch = t->report_epoch;
+    o->ids_eff = scratch ? (uint32_t *)t->report_scratch : nullptr;
+    o->mass = scratch ? (float *)(t->report_scratch + half) : nullptr;
+    return ORCHKV_OK;
+}
+
 int tm_report_attn_probs(tiered_manager_t *m, const float *probs, uint32_t n_rows,
                          uint32_t n_q_heads, uint32_t n_kv_heads, uint32_t row_len,
                          uint32_t tpb, const uint32_t *lens, const uint32_t *block_ids)
@@ -941,12 +1015,61 @@ int tm_report_attn_probs(tiered_manager_t *m, const float *probs, uint32_t n_row
     const size_t bytes[3] = {(size_t)n_rows * n_q_heads * row_len * sizeof(float),
                              lens ? (size_t)n_rows * sizeof(uint32_t) : 0,
                              (size_t)n_rows * n_kv_heads * nb * sizeof(uint32_t)};
+    const size_t n_ent = (size_t)n_rows * n_kv_heads * nb;
+    if (n_ent > 0xFFFFFFFFull) return ORCHKV_ERR_INVALID;
     rc = stage_inputs(t, in, bytes, 3);
     if (rc) return rc;
+    okv::ReportOrder o;
+    rc = begin_report(t, n_ent, true, &o);
+    if (rc) return rc;
     t->mirror_dirty = true;
-    return launch_score((const float *)in[0], n_rows, n_q_heads, n_kv_heads, row_len, tpb,
-                        (const uint32_t *)in[1], (const uint32_t *)in[2], t->d, t->step,
-                        t->stream);
+    const uint32_t *ids = (const uint32_t *)in[2];
+    rc = launch_alias_mark(ids, (uint32_t)n_ent, t->d, o, t->stream);
+    if (!rc) rc = launch_score((const float *)in[0], n_rows, n_q_heads, n_kv_heads, row_len, tpb,
+                               (const uint32_t *)in[1], ids, t->d, t->step, o, t->stream);
+    if (!rc) rc = launch_report_ordered(o.ids_eff, o.mass, (uint32_t)n_ent, t->d, t->step, o,
+                                        t->stream);
+    const int rr = release_staged(t);
+    return rc ? rc : rr;
+}
+
+int tm_stage_input_async(tiered_manager_t *m, const void *host, size_t bytes)
+{
+    OKV_RANGE("tm_stage_input_async");
+    TmImpl *t = tm_impl(m);
+    if (!t) return ORCHKV_ERR_INVALID;
+    std::lock_guard<std::mutex> g(t->mu);
+    if (!host) {                              // drop staged inputs nobody consumed
+        if (t->early_copy) OKV_CUDA_TRY(cudaStreamSynchronize(t->early_copy));
+        for (StagedInput &e : t->early) e.pending = false;
+        return ORCHKV_OK;
+    }
+    if (bytes == 0 || on_device(host)) return ORCHKV_ERR_INVALID;
+    StagedInput *e = nullptr;
+    for (StagedInput &x : t->early)
+        if (!x.pending && (!e || x.seq < e->seq)) e = &x;
+    if (!e) return ORCHKV_ERR_STATE;          // two uploads already wait for their reports
+    if (!t->early_copy)
+        OKV_CUDA_TRY(cudaStreamCreateWithFlags(&t->early_copy, cudaStreamNonBlocking));
+    if (!e->ready) OKV_CUDA_TRY(cudaEventCreateWithFlags(&e->ready, cudaEventDisableTiming));
+    if (!e->consumed) OKV_CUDA_TRY(cudaEventCreateWithFlags(&e->consumed, cudaEventDisableTiming));
+    if (bytes > e->cap) {
+        OKV_CUDA_TRY(cudaEventSynchronize(e->consumed));   // its last reader is done
+        cudaFree(e->dev);
+        e->dev = nullptr;
+        e->cap = 0;
+        OKV_CUDA_TRY(cudaMalloc((void **)&e->dev, bytes));
+        e->cap = bytes;
+    }
+    // the slot's previous report must have read it before it is overwritten
+    OKV_CUDA_TRY(cudaStreamWaitEvent(t->early_copy, e->consumed, 0));
+    OKV_CUDA_TRY(cudaMemcpyAsync(e->dev, host, bytes, cudaMemcpyHostToDevice, t->early_copy));
+    OKV_CUDA_TRY(cudaEventRecord(e->ready, t->early_copy));
+    e->host = host;
+    e->bytes = bytes;
+    e->pending = true;
+    e->seq = ++t->early_seq;
+    return ORCHKV_OK;
 }
 
 int tm_report_attn_ranges(tiered_manager_t *m, const float *avg, uint32_t heads,
@@ -966,10 +1089,17 @@ int tm_report_attn_ranges(tiered_manager_t *m, const float *avg, uint32_t heads,
                              (size_t)n * 4, (size_t)n * 4};
     rc = stage_inputs(t, in, bytes, 4);
     if (rc) return rc;
+    okv::ReportOrder o;
+    rc = begin_report(t, n, true, &o);
+    if (rc) return rc;
     t->mirror_dirty = true;
-    return launch_range_mass((const float *)in[0], heads, kv_len, (const uint32_t *)in[1],
-                             (const uint32_t *)in[2], (const uint32_t *)in[3], n, t->d, t->step,
-                             t->stream);
+    const uint32_t *ids = (const uint32_t *)in[3];
+    rc = launch_alias_mark(ids, n, t->d, o, t->stream);
+    if (!rc) rc = launch_range_mass((const float *)in[0], heads, kv_len, (const uint32_t *)in[1],
+                                    (const uint32_t *)in[2], ids, n, t->d, t->step, o, t->stream);
+    if (!rc) rc = launch_report_ordered(o.ids_eff, o.mass, n, t->d, t->step, o, t->stream);
+    const int rr = release_staged(t);
+    return rc ? rc : rr;
 }
 
 int tm_report_attn_batch_dev(tiered_manager_t *m, const uint32_t *ids, const float *w,
@@ -980,8 +1110,15 @@ int tm_report_attn_batch_dev(tiered_manager_t *m, const uint32_t *ids, const flo
     std::lock_guard<std::mutex> g(t->mu);
     int rc = tm_flush_locked(t);
     if (rc) return rc;
+    if (n == 0) return ORCHKV_OK;
+    okv::ReportOrder o;
+    rc = begin_report(t, n, false, &o);
+    if (rc) return rc;
     t->mirror_dirty = true;
-    return launch_report_batch(ids, w, n, t->d, t->step, t->stream);
+    rc = launch_alias_mark(ids, n, t->d, o, t->stream);
+    if (!rc) rc = launch_report_batch(ids, w, n, t->d, t->step, o, t->stream);
+    if (!rc) rc = launch_report_ordered(ids, w, n, t->d, t->step, o, t->stream);
+    return rc;
 }
 
 int tm_report_attn_blockmean(tiered_manager_t *m, const void *weights, int dtype,

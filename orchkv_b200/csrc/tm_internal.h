@@ -25,6 +25,20 @@ struct RegEntry {
     uint8_t tier;
 };
 
+// A host input uploaded ahead of the report call that consumes it
+// (tm_stage_input_async).
+struct StagedInput {
+    const void *host = nullptr;
+    size_t bytes = 0;
+    char *dev = nullptr;
+    size_t cap = 0;
+    cudaEvent_t ready = nullptr;      // the upload finished (on the staging stream)
+    cudaEvent_t consumed = nullptr;   // the consuming report's kernels finished
+    bool pending = false;             // uploaded (or uploading), not yet consumed
+    bool in_use = false;              // taken by the report call being launched
+    unsigned long long seq = 0;
+};
+
 struct TmImpl {
     std::mutex mu;
     int device = 0;
@@ -102,6 +116,16 @@ struct TmImpl {
     size_t reg_cap = 0;
     char *in_stage = nullptr;     // device copies of host inputs to tm_report_attn_probs
     size_t in_stage_cap = 0;
+    // ordering of tensor-level reports whose ids share slots (okv::ReportOrder)
+    uint32_t *report_mark = nullptr;   // [cap], inside dev_block
+    uint32_t *report_flag = nullptr;   // one word, inside dev_block
+    uint32_t report_epoch = 0;
+    char *report_scratch = nullptr;    // per-entry ids and masses of an ordered call
+    size_t report_scratch_cap = 0;
+    // inputs staged ahead of their report (two slots, consumed oldest first)
+    StagedInput early[2];
+    cudaStream_t early_copy = nullptr;
+    unsigned long long early_seq = 0;
 
     // multi-GPU selection hooks (set by the comm layer)
     okv::hist_reduce_fn comm_reduce = nullptr;
