@@ -5,8 +5,9 @@ classes, methods, metadata and statistics; the worker's data plane is
 batched: a layer's save is one copy launch gathering every listed block of
 the layer's cache tensor into a pinned store, a layer's load one launch
 scattering them back (the reference: one ``copy_`` per block and layer,
-connector.py:136-195).  The scheduler side is the reference's bookkeeping
-(connector.py:220-282), unchanged in behaviour.
+connector.py:136-195).  The scheduler side keeps one table of the blocks
+each finished request left in the store and gives the reference's answers
+(connector.py:220-282), pinned by a recorded run of the reference connector.
 
 Cache tensors are indexed by block along dim 0 (``kv_layer[block_id]``), as
 the reference assumes; a layer whose blocks are not contiguous chunks falls
@@ -248,50 +249,71 @@ class OrchKvConnectorWorker:
 
 
 class OrchKvConnectorScheduler:
-    """Scheduler side: which blocks to offload / load (connector.py:220-282)."""
+    """Scheduler role: one table, request id -> the blocks that request left
+    in the store when it finished, serves both questions the scheduler asks.
+    A returning request can reuse as many tokens as the table holds blocks
+    for it beyond what is already computed; a preempted request has its
+    blocks queued for saving on every layer.  The queues go to the workers in
+    the step's metadata and start empty again (the reference's observable
+    behaviour, connector.py:227-289)."""
 
     def __init__(self, orchkv_cfg: dict[str, Any]):
-        self._orchkv_cfg = orchkv_cfg
-        self._cached_requests: dict[str, set[int]] = {}
-        self._pending_offload: dict[str, list[int]] = {}
-        self._pending_load: dict[str, list[int]] = {}
+        n_layers = int(orchkv_cfg.get("n_layers", 32))
+        self._layer_names = tuple(f"layer_{i}" for i in range(n_layers))
+        self._stored: dict[str, set[int]] = {}
+        self._save_queue: dict[str, list[int]] = {}
+        self._load_queue: dict[str, list[int]] = {}
 
     def get_num_new_matched_tokens(self, request, num_computed_tokens: int):
-        cached = self._cached_requests.get(request.request_id)
-        if cached is None:
-            return 0, False
-        new_tokens = max(0, len(cached) - num_computed_tokens)
-        return new_tokens, (new_tokens > 0)
+        stored = self._stored.get(request.request_id, ())
+        reusable = len(stored) - num_computed_tokens
+        return (reusable, True) if reusable > 0 else (0, False)
 
     def update_state_after_alloc(self, request, blocks, num_external_tokens: int):
-        pass
-
-    def build_connector_meta(self, scheduler_output) -> OrchKvConnectorMetadata:
-        meta = OrchKvConnectorMetadata()
-        meta.blocks_to_save = dict(self._pending_offload)
-        meta.blocks_to_load = dict(self._pending_load)
-        self._pending_offload.clear()
-        self._pending_load.clear()
-        return meta
+        """Nothing to record: loads are driven by the table alone."""
 
     def request_finished(self, request, block_ids: list[int]):
-        self._cached_requests[request.request_id] = set(block_ids)
+        self._stored[request.request_id] = set(block_ids)
         return False, None
 
     def handle_preemptions(self, preempted_req_ids: set[str]):
-        for req_id in preempted_req_ids:
-            cached = self._cached_requests.get(req_id)
-            if cached:
-                for layer_name in self._get_layer_names():
-                    self._pending_offload.setdefault(layer_name, []).extend(cached)
+        for rid in preempted_req_ids:
+            blocks = self._stored.get(rid)
+            if not blocks:
+                continue
+            for name in self._layer_names:
+                self._save_queue.setdefault(name, []).extend(blocks)
 
-    def _get_layer_names(self) -> list[str]:
-        return [f"layer_{i}" for i in range(self._orchkv_cfg.get("n_layers", 32))]
+    def build_connector_meta(self, scheduler_output) -> OrchKvConnectorMetadata:
+        meta = OrchKvConnectorMetadata(blocks_to_save=self._save_queue,
+                                       blocks_to_load=self._load_queue)
+        self._save_queue, self._load_queue = {}, {}
+        return meta
+
+
+def _connector_settings(vllm_config) -> dict[str, Any]:
+    """The data-plane settings of the connector: the connector's extra config
+    (dram_pool_gb, tokens_per_block, num_cuda_streams, io_workers, and d_head
+    / n_layers where the model config has none), with the model config's
+    head_dim and num_layers taking precedence (connector.py:311-331)."""
+    ktc = getattr(vllm_config, "kv_transfer_config", None)
+    extra = (getattr(ktc, "kv_connector_extra_config", None) or {}) if ktc is not None else {}
+    model = getattr(vllm_config, "model_config", None)
+    return {
+        "dram_pool_bytes": int(extra.get("dram_pool_gb", 8)) << 30,
+        "d_head": getattr(model, "head_dim", extra.get("d_head", 128)),
+        "tokens_per_block": extra.get("tokens_per_block", 16),
+        "num_cuda_streams": extra.get("num_cuda_streams", 4),
+        "io_workers": extra.get("io_workers", 4),
+        "n_layers": getattr(model, "num_layers", extra.get("n_layers", 32)),
+    }
 
 
 class OrchKvOffloadingConnector(KVConnectorBase_V1):
-    """vLLM V1 connector routing KV offloading through the B200 data plane
-    (connector.py:285-421)."""
+    """vLLM V1 connector offloading KV blocks through the B200 data plane.
+    One object per role: the scheduler role answers prefix-match queries and
+    builds the per-step metadata, the worker role moves blocks; each call is
+    routed to the role object that serves it (connector.py:285-421)."""
 
     @property
     def prefer_cross_layer_blocks(self) -> bool:
@@ -299,73 +321,64 @@ class OrchKvOffloadingConnector(KVConnectorBase_V1):
 
     def __init__(self, vllm_config, role, kv_cache_config=None):
         super().__init__(vllm_config, role, kv_cache_config)
-        extra_cfg = {}
-        ktc = getattr(vllm_config, "kv_transfer_config", None)
-        if ktc is not None and hasattr(ktc, "kv_connector_extra_config"):
-            extra_cfg = ktc.kv_connector_extra_config or {}
-        mc = getattr(vllm_config, "model_config", None)
-        orchkv_cfg = {
-            "dram_pool_bytes": int(extra_cfg.get("dram_pool_gb", 8)) * (1 << 30),
-            "d_head": getattr(mc, "head_dim", extra_cfg.get("d_head", 128)),
-            "tokens_per_block": extra_cfg.get("tokens_per_block", 16),
-            "num_cuda_streams": extra_cfg.get("num_cuda_streams", 4),
-            "io_workers": extra_cfg.get("io_workers", 4),
-            "n_layers": getattr(mc, "num_layers", extra_cfg.get("n_layers", 32)),
-        }
-        self._worker = None
-        self._scheduler = None
-        if role == KVConnectorRole.SCHEDULER:
-            self._scheduler = OrchKvConnectorScheduler(orchkv_cfg)
-        elif role == KVConnectorRole.WORKER:
-            self._worker = OrchKvConnectorWorker(orchkv_cfg)
+        settings = _connector_settings(vllm_config)
+        self._scheduler = (OrchKvConnectorScheduler(settings)
+                           if role == KVConnectorRole.SCHEDULER else None)
+        self._worker = (OrchKvConnectorWorker(settings)
+                        if role == KVConnectorRole.WORKER else None)
 
-    # worker side
+    def _as_worker(self) -> "OrchKvConnectorWorker":
+        if self._worker is None:
+            raise RuntimeError("worker call on a connector built for the scheduler role")
+        return self._worker
+
+    def _as_scheduler(self) -> OrchKvConnectorScheduler:
+        if self._scheduler is None:
+            raise RuntimeError("scheduler call on a connector built for the worker role")
+        return self._scheduler
+
+    def _step_meta(self):
+        meta = self._connector_metadata
+        return meta if isinstance(meta, OrchKvConnectorMetadata) else None
+
+    # ---- worker role ----
     def register_kv_caches(self, kv_caches: dict[str, torch.Tensor]):
-        assert self._worker is not None
-        self._worker.register_kv_caches(kv_caches)
+        self._as_worker().register_kv_caches(kv_caches)
 
     def start_load_kv(self, forward_context, **kwargs: Any) -> None:
-        assert self._worker is not None
-        meta = self._connector_metadata
-        if isinstance(meta, OrchKvConnectorMetadata):
-            self._worker.start_load_kv(meta)
+        worker, meta = self._as_worker(), self._step_meta()
+        if meta is not None:
+            worker.start_load_kv(meta)
 
     def wait_for_layer_load(self, layer_name: str) -> None:
-        assert self._worker is not None
-        self._worker.wait_for_layer_load(layer_name)
+        self._as_worker().wait_for_layer_load(layer_name)
 
     def save_kv_layer(self, layer_name: str, kv_layer: torch.Tensor, attn_metadata,
                       **kwargs: Any) -> None:
-        assert self._worker is not None
-        meta = self._connector_metadata
-        if isinstance(meta, OrchKvConnectorMetadata):
-            self._worker.save_kv_layer(layer_name, kv_layer, meta)
+        worker, meta = self._as_worker(), self._step_meta()
+        if meta is not None:
+            worker.save_kv_layer(layer_name, kv_layer, meta)
 
     def wait_for_save(self):
-        assert self._worker is not None
-        self._worker.wait_for_save()
-
-    def handle_preemptions(self, preempted_req_ids: set[str]):
-        if self._scheduler is not None:
-            self._scheduler.handle_preemptions(preempted_req_ids)
+        self._as_worker().wait_for_save()
 
     def shutdown(self):
         if self._worker is not None:
             self._worker.shutdown()
 
-    # scheduler side
+    # ---- scheduler role ----
+    def handle_preemptions(self, preempted_req_ids: set[str]):
+        if self._scheduler is not None:
+            self._scheduler.handle_preemptions(preempted_req_ids)
+
     def get_num_new_matched_tokens(self, request, num_computed_tokens: int):
-        assert self._scheduler is not None
-        return self._scheduler.get_num_new_matched_tokens(request, num_computed_tokens)
+        return self._as_scheduler().get_num_new_matched_tokens(request, num_computed_tokens)
 
     def update_state_after_alloc(self, request, blocks, num_external_tokens: int):
-        assert self._scheduler is not None
-        self._scheduler.update_state_after_alloc(request, blocks, num_external_tokens)
+        self._as_scheduler().update_state_after_alloc(request, blocks, num_external_tokens)
 
     def build_connector_meta(self, scheduler_output):
-        assert self._scheduler is not None
-        return self._scheduler.build_connector_meta(scheduler_output)
+        return self._as_scheduler().build_connector_meta(scheduler_output)
 
     def request_finished(self, request, block_ids: list[int]):
-        assert self._scheduler is not None
-        return self._scheduler.request_finished(request, block_ids)
+        return self._as_scheduler().request_finished(request, block_ids)
