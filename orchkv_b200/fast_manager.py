@@ -44,6 +44,47 @@ TIER_DRAM = 1
 TIER_SSD = 2
 
 
+class _DeviceKV:
+    """Every layer's persistent K and V in one device tensor
+    [2 (K, V), layers, 1, kv heads, capacity tokens, head_dim].  Per-layer
+    views keep the [1, heads, tokens, head_dim] shape of a legacy cache
+    entry, and the K/V pointers of all layers are what one
+    orchkv_copy_token_blocks launch gathers from or scatters into."""
+
+    def __init__(self, layers: int, heads: int, head_dim: int, dtype: torch.dtype,
+                 capacity: int):
+        self.layers, self.heads, self.head_dim, self.dtype = layers, heads, head_dim, dtype
+        self.t = torch.zeros(2, layers, 1, heads, capacity, head_dim, dtype=dtype, device="cuda")
+
+    @property
+    def capacity(self) -> int:
+        return self.t.shape[4]
+
+    def layer(self, li: int) -> tuple[torch.Tensor, torch.Tensor]:
+        return self.t[0, li], self.t[1, li]
+
+    def store(self, li: int, pos: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        """Write k, v [heads, n, head_dim] at token positions [pos, pos + n)."""
+        n = k.shape[1]
+        self.t[0, li, 0, :, pos:pos + n] = k
+        self.t[1, li, 0, :, pos:pos + n] = v
+
+    def grow(self, capacity: int) -> None:
+        """Reallocate for `capacity` tokens, keeping the tokens that fit."""
+        new = torch.zeros(2, self.layers, 1, self.heads, capacity, self.head_dim,
+                          dtype=self.dtype, device="cuda")
+        keep = min(capacity, self.capacity)
+        new[..., :keep, :] = self.t[..., :keep, :]
+        self.t = new
+
+    def pointers(self) -> list[int]:
+        """K then V of layer 0, K then V of layer 1, ..."""
+        return [self.t[kv, li].data_ptr() for li in range(self.layers) for kv in (0, 1)]
+
+    def head_stride_bytes(self) -> int:
+        return self.t.stride(3) * self.t.element_size()
+
+
 class FastKVCacheManager:
     """KV-cache manager with persistent per-layer buffers; scoring,
     selection and block movement run as single GPU launches."""
@@ -52,34 +93,26 @@ class FastKVCacheManager:
                  dtype: torch.dtype = torch.float16, gpu_budget_bytes: int = 0,
                  max_seq_len: int = 4096, ssd_dir: Optional[str] = None,
                  sink_tokens: int = 4):
-        self.n_layers = n_layers
-        self.n_kv_heads = n_kv_heads
-        self.head_dim = head_dim
-        self.block_size = block_size
-        self.dtype = dtype
-        self.gpu_budget_bytes = gpu_budget_bytes
-        self.max_seq_len = max_seq_len
-        self.ssd_dir = ssd_dir
-        self.sink_tokens = sink_tokens
-
-        self._block_bytes = 2 * n_kv_heads * block_size * head_dim * dtype.itemsize
+        # the reference's public attributes (fast_kvcache_manager.py:44-60)
+        self.n_layers, self.n_kv_heads, self.head_dim = n_layers, n_kv_heads, head_dim
+        self.block_size, self.dtype = block_size, dtype
+        self.gpu_budget_bytes, self.max_seq_len = gpu_budget_bytes, max_seq_len
+        self.ssd_dir, self.sink_tokens = ssd_dir, sink_tokens
         self._row_bytes = head_dim * dtype.itemsize
         if self._row_bytes % 16:
             raise ValueError("head_dim * itemsize must be a multiple of 16 bytes")
+        self._block_bytes = 2 * n_kv_heads * block_size * self._row_bytes
+        self._kv = _DeviceKV(n_layers, n_kv_heads, head_dim, dtype, max_seq_len)
         self._total_tokens = 0
         self._step = 0
-        self._key_bufs = [torch.zeros(1, n_kv_heads, max_seq_len, head_dim, dtype=dtype,
-                                      device="cuda") for _ in range(n_layers)]
-        self._val_bufs = [torch.zeros(1, n_kv_heads, max_seq_len, head_dim, dtype=dtype,
-                                      device="cuda") for _ in range(n_layers)]
         # evicted block -> (start, end) token range at eviction; batches of
         # (first store slot, device block list, count, tokens at eviction)
         self._evicted: dict[int, tuple[int, int]] = {}
         self._batches: list[tuple[int, torch.Tensor, int, int]] = []
         self._store: Optional[torch.Tensor] = None
         self._store_used = 0
-        self._stats = {"gpu_to_dram": 0, "dram_to_gpu": 0, "dram_to_ssd": 0, "ssd_to_dram": 0,
-                       "total_blocks": 0, "evictions_this_step": 0}
+        self._stats = dict.fromkeys(("gpu_to_dram", "dram_to_gpu", "dram_to_ssd", "ssd_to_dram",
+                                     "total_blocks", "evictions_this_step"), 0)
 
         self._C = core()
         self._tm_handle: Optional[int] = self._C.tm_create()
@@ -110,15 +143,24 @@ class FastKVCacheManager:
         return self._total_tokens
 
     @property
+    def _key_bufs(self) -> list[torch.Tensor]:
+        return [self._kv.layer(li)[0] for li in range(self.n_layers)]
+
+    @property
+    def _val_bufs(self) -> list[torch.Tensor]:
+        return [self._kv.layer(li)[1] for li in range(self.n_layers)]
+
+    @property
     def _evicted_ranges(self) -> list[list[tuple[int, int]]]:
         """Per layer, the evicted token ranges (the reference's bookkeeping)."""
         r = sorted(self._evicted.values())
         return [list(r) for _ in range(self.n_layers)]
 
+    def _n_blocks(self) -> int:
+        return (self._total_tokens + self.block_size - 1) // self.block_size
+
     def gpu_kv_bytes(self) -> int:
-        n_blocks = (self._total_tokens + self.block_size - 1) // self.block_size
-        evicted = len(self._evicted) * self.n_layers
-        return (n_blocks * self.n_layers - evicted) * self._block_bytes
+        return (self._n_blocks() - len(self._evicted)) * self.n_layers * self._block_bytes
 
     def _stream(self) -> int:
         return torch.cuda.current_stream().cuda_stream
@@ -149,59 +191,56 @@ class FastKVCacheManager:
             return DynamicCache(ddp_cache_data=legacy_cache)    # transformers >= 5
         return legacy_cache
 
-    def ingest_step(self, past_key_values) -> None:
-        legacy = self._to_legacy(past_key_values)
-        for li, (k, v) in enumerate(legacy):
-            seq_len = k.shape[2]
-            if seq_len > self.max_seq_len:
-                self._grow_buffers(seq_len)
-            self._key_bufs[li][0, :, :seq_len, :] = k[0, :, :seq_len, :]
-            self._val_bufs[li][0, :, :seq_len, :] = v[0, :, :seq_len, :]
-        self._total_tokens = legacy[0][0].shape[2]
-        n_blocks = (self._total_tokens + self.block_size - 1) // self.block_size
-        for bid in range(n_blocks):
-            flags = 1 if (bid * self.block_size) < self.sink_tokens else 0
-            self._C.tm_register_block_id(self._tm_handle, bid, flags, 0)
-        self._stats["total_blocks"] = n_blocks * self.n_layers
+    def _register(self, first_block: int, last_block: int) -> None:
+        """Register token blocks [first, last) with the scheduler.  Blocks
+        holding sink tokens carry flag 1, passed in the binding's tier
+        position as the reference does (fast_kvcache_manager.py:155,173:
+        tm_register_block_id(tm, bid, flags, 0))."""
+        for bid in range(first_block, last_block):
+            sink = 1 if bid * self.block_size < self.sink_tokens else 0
+            self._C.tm_register_block_id(self._tm_handle, bid, sink, 0)
 
-    def append_token(self, past_key_values) -> None:
-        legacy = self._to_legacy(past_key_values)
-        pos = self._total_tokens
-        if pos >= self.max_seq_len:
-            self._grow_buffers(pos + 256)
-        for li, (k, v) in enumerate(legacy):
-            self._key_bufs[li][0, :, pos, :] = k[0, :, -1, :]
-            self._val_bufs[li][0, :, pos, :] = v[0, :, -1, :]
-        self._total_tokens = pos + 1
-        if pos % self.block_size == 0:
-            flags = 1 if pos < self.sink_tokens else 0
-            self._C.tm_register_block_id(self._tm_handle, pos // self.block_size, flags, 0)
+    def _ensure_capacity(self, tokens: int) -> None:
+        """Buffers for at least `tokens` tokens, grown in steps of 256."""
+        if tokens <= self._kv.capacity:
+            return
+        self._grow_buffers(tokens)
 
     def _grow_buffers(self, new_max: int):
-        new_max = ((new_max + 255) // 256) * 256
-        for li in range(self.n_layers):
-            old_k, old_v = self._key_bufs[li], self._val_bufs[li]
-            new_k = torch.zeros(1, self.n_kv_heads, new_max, self.head_dim, dtype=self.dtype,
-                                device="cuda")
-            new_v = torch.zeros_like(new_k)
-            n = min(old_k.shape[2], new_max)
-            new_k[0, :, :n, :] = old_k[0, :, :n, :]
-            new_v[0, :, :n, :] = old_v[0, :, :n, :]
-            self._key_bufs[li] = new_k
-            self._val_bufs[li] = new_v
+        new_max = -(-new_max // 256) * 256
+        self._kv.grow(new_max)
         self.max_seq_len = new_max
         need = new_max // self.block_size + 1
         if self._ids.numel() < need:
             self._ids = torch.arange(need, dtype=torch.int32, device="cuda")
 
-    # -- block movement ----------------------------------------------------
+    def ingest_step(self, past_key_values) -> None:
+        """Take a prefill's cache: every layer's tokens into the buffers and
+        every token block registered."""
+        layers = self._to_legacy(past_key_values)
+        for li, (k, v) in enumerate(layers):
+            n = k.shape[2]
+            self._ensure_capacity(n)
+            self._kv.store(li, 0, k[0, :, :n], v[0, :, :n])
+        self._total_tokens = layers[0][0].shape[2]
+        n_blocks = self._n_blocks()
+        self._register(0, n_blocks)
+        self._stats["total_blocks"] = n_blocks * self.n_layers
 
-    def _bufs(self) -> list[int]:
-        out = []
-        for li in range(self.n_layers):
-            out.append(self._key_bufs[li].data_ptr())
-            out.append(self._val_bufs[li].data_ptr())
-        return out
+    def append_token(self, past_key_values) -> None:
+        """Take one decode step's token (the last position of each layer's
+        cache); a token that opens a block registers the block."""
+        layers = self._to_legacy(past_key_values)
+        pos = self._total_tokens
+        if pos >= self._kv.capacity:
+            self._grow_buffers(pos + 256)
+        for li, (k, v) in enumerate(layers):
+            self._kv.store(li, pos, k[0, :, -1:], v[0, :, -1:])
+        self._total_tokens = pos + 1
+        if pos % self.block_size == 0:
+            self._register(pos // self.block_size, pos // self.block_size + 1)
+
+    # -- block movement ----------------------------------------------------
 
     def _slot_elems(self) -> int:
         return 2 * self.n_layers * self.n_kv_heads * self.block_size * self.head_dim
@@ -221,9 +260,9 @@ class FastKVCacheManager:
         return first
 
     def _copy_blocks(self, blocks: torch.Tensor, n: int, n_tokens: int, slot: int, direction: int):
-        head_stride = self._key_bufs[0].stride(1) * self.dtype.itemsize
         store_ptr = self._store.data_ptr() + slot * self._slot_elems() * self.dtype.itemsize
-        rc = self._C.copy_token_blocks(self._bufs(), self.n_kv_heads, head_stride,
+        rc = self._C.copy_token_blocks(self._kv.pointers(), self.n_kv_heads,
+                                       self._kv.head_stride_bytes(),
                                        self._row_bytes, self.block_size, n_tokens,
                                        blocks.data_ptr(), n, store_ptr, direction, self._stream())
         if rc != 0:
@@ -234,10 +273,8 @@ class FastKVCacheManager:
     def build_past_kv(self, device: str = "cuda"):
         n = self._total_tokens
         self._restore_evicted_blocks()
-        result = []
-        for li in range(self.n_layers):
-            result.append((self._key_bufs[li][:, :, :n, :], self._val_bufs[li][:, :, :n, :]))
-        return self._from_legacy(tuple(result))
+        return self._from_legacy(tuple((k[:, :, :n], v[:, :, :n])
+                                       for k, v in map(self._kv.layer, range(self.n_layers))))
 
     def _restore_evicted_blocks(self):
         for slot, blocks, n, n_tokens in self._batches:
@@ -281,7 +318,7 @@ class FastKVCacheManager:
         with torch.no_grad():
             gqa_ratio = q.shape[1] // self.n_kv_heads
             q_for_kv = q[:, ::gqa_ratio, :, :] if gqa_ratio > 1 else q
-            k_all = self._key_bufs[layer_idx][:, :, :n, :]
+            k_all = self._kv.layer(layer_idx)[0][:, :, :n, :]
             qk = torch.matmul(q_for_kv, k_all.transpose(-1, -2))
             qk_abs = qk.abs().squeeze(0).squeeze(1).float()
             self._report_map(qk_abs, n)
@@ -297,7 +334,7 @@ class FastKVCacheManager:
     def schedule(self) -> dict:
         if self._tm_handle is None:
             return {}
-        n_blocks = (self._total_tokens + self.block_size - 1) // self.block_size
+        n_blocks = self._n_blocks()
         evicted_count = len(self._evicted) * self.n_layers
         total_block_layers = n_blocks * self.n_layers
         gpu_ratio = 1.0 - evicted_count / total_block_layers if total_block_layers > 0 else 0.0
@@ -310,7 +347,7 @@ class FastKVCacheManager:
         return {"step": self._step, "gpu_ratio": gpu_ratio}
 
     def _evict_cold_blocks(self, max_evict: int = 8) -> int:
-        n_blocks = (self._total_tokens + self.block_size - 1) // self.block_size
+        n_blocks = self._n_blocks()
         first = min((self.sink_tokens + self.block_size - 1) // self.block_size, n_blocks)
         n_cand = n_blocks - first - sum(1 for b in self._evicted if b >= first)
         if n_cand <= 0 or max_evict <= 0:
@@ -350,21 +387,18 @@ class FastKVCacheManager:
     # -- stats -------------------------------------------------------------
 
     def get_stats(self) -> dict:
-        n_blocks = (self._total_tokens + self.block_size - 1) // self.block_size
-        evicted = len(self._evicted) * self.n_layers
-        gpu_blocks = n_blocks * self.n_layers - evicted
-        return {
-            "step": self._step,
-            "total_tokens": self._total_tokens,
-            "blocks_gpu": gpu_blocks,
-            "blocks_dram": evicted,
-            "blocks_ssd": 0,
-            "blocks_total": n_blocks * self.n_layers,
-            "gpu_kv_mb": gpu_blocks * self._block_bytes / (1 << 20),
-            "migrations": dict(self._stats),
-        }
+        """The reference's statistics dict (fast_kvcache_manager.py:347-360):
+        block counts over all layers, the GPU-resident KV in MiB, and the
+        migration counters."""
+        total = self._n_blocks() * self.n_layers
+        off_gpu = len(self._evicted) * self.n_layers
+        on_gpu = total - off_gpu
+        return {"step": self._step, "total_tokens": self._total_tokens,
+                "blocks_gpu": on_gpu, "blocks_dram": off_gpu, "blocks_ssd": 0,
+                "blocks_total": total, "gpu_kv_mb": on_gpu * self._block_bytes / (1 << 20),
+                "migrations": dict(self._stats)}
 
     def __repr__(self) -> str:
-        s = self.get_stats()
-        return (f"FastKVCacheManager(tokens={s['total_tokens']}, "
-                f"gpu={s['blocks_gpu']}, dram={s['blocks_dram']})")
+        on_gpu = (self._n_blocks() - len(self._evicted)) * self.n_layers
+        return (f"FastKVCacheManager(tokens={self._total_tokens}, gpu={on_gpu}, "
+                f"dram={len(self._evicted) * self.n_layers})")
