@@ -415,6 +415,8 @@ class ShardedWorkload:
         ev[4].record()
         if check:
             check()
+        # counts words: 0 picks, 2-3 evict {evicted, skipped}, 8 restore set,
+        # 9-10 restore {promoted, skipped}; _ptr offsets are in bytes
         assert L.orchkv_evict_batch_to_dram(self._ptr(self.victims), self._ptr(self.counts),
                                             self.cap, self._ptr(self.counts, 8)) == 0
         ev[5].record()
@@ -489,7 +491,7 @@ def run_sharded(args, torch, okv, rank, world, comm, dist, link_d2h):
         step_ms.append(t0.elapsed_time(t1))
         for k, v in sw.phases().items():
             ph_acc.setdefault(k, []).append(v)
-        evicted += sw.h_counts.tolist()[8]
+        evicted += sw.h_counts.tolist()[2]            # the evict's {evicted, skipped}: words 2-3
         if comm:
             ms, calls = C.c_float(), C.c_uint32()
             L.orchkv_comm_exchange_time(comm, C.byref(ms), C.byref(calls))

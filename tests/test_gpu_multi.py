@@ -136,7 +136,7 @@ def _sharded_worker(rank, world, port, q):
 
         sw.step(check=check)
         torch.cuda.synchronize()
-        n_ev = sw.h_counts.tolist()[8]
+        n_ev = sw.h_counts.tolist()[2]                 # the evict's result, words 2-3
         loc = np.zeros(sw.cap, np.uint32)
         assert L.orchkv_read_block_locs(loc.ctypes.data, None) == 0
         picks = seen["view"][2]
