@@ -243,6 +243,23 @@ int  orchkv_block_id_table(kv_request_ctx_t *const *ctxs, uint32_t n,
 int  orchkv_block_checksums(const uint32_t *block_ids, uint32_t n,
                             unsigned long long *out, uint8_t *tier_out);
 
+/* B200: the checked build (liborchkv_b200.so compiled with -DOKV_CHECKED,
+ * built into orchkv_b200/_checked/).  Every slab, free-stack and block index
+ * a data-plane kernel reads from memory is compared with its bound first; one
+ * out of range is recorded and its access skipped, nothing traps, and
+ * orchkv_sync / tm_sync return ORCHKV_ERR_CUDA from then on.  The regular
+ * build compiles the comparisons away.  No counterpart in the reference.
+ *   orchkv_checked_build: 1 in the checked build, else 0.
+ *   orchkv_check_status: words[4] = {indices out of range, source line of
+ *     the first, its value, its bound} since load or the last reset, shutdowns
+ *     included (all 0 in the regular build); reset != 0 clears them.
+ *   orchkv_check_inject: checked build only (else ORCHKV_ERR_INVALID):
+ *     record one violation at `line` without touching any other memory, to
+ *     test what a caller does with the error. */
+int  orchkv_checked_build(void);
+int  orchkv_check_status(uint32_t *words, int reset);
+int  orchkv_check_inject(uint32_t line);
+
 /* Introspection for tests and tools (synchronous). */
 int  orchkv_block_info(kv_request_ctx_t *ctx, uint32_t layer_id, uint32_t head_id,
                        uint32_t block_idx, uint64_t *block_id, int *tier,

@@ -48,7 +48,7 @@ def core():
     global _CORE
     if _CORE is None:
         from .build import core_module_path
-        path = core_module_path()
+        path = core_module_path(_lib.LIB_DIR)
         if not os.path.exists(path):
             raise ImportError(f"{path} not built: run `python -m orchkv_b200.build`")
         loader = importlib.machinery.ExtensionFileLoader("orchkv_core", path)

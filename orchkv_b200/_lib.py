@@ -9,7 +9,9 @@ import ctypes as C
 import os
 
 PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(PKG, "liborchkv_b200.so")
+# ORCHKV_CHECKED=1 selects the checked build (bounds-checked data-plane kernels)
+LIB_DIR = os.path.join(PKG, "_checked") if os.environ.get("ORCHKV_CHECKED") == "1" else PKG
+LIB_PATH = os.path.join(LIB_DIR, "liborchkv_b200.so")
 
 vp = C.c_void_p
 u8, u32, u64, i32, f32, f64 = C.c_uint8, C.c_uint32, C.c_uint64, C.c_int, C.c_float, C.c_double
@@ -150,6 +152,9 @@ _SIGS = {
     "orchkv_last_promote_layout": (i32, [P(u32), P(u32), P(u32), P(i32)]),
     "orchkv_swap_batch": (i32, [vp, vp, u32, vp, vp, u32, vp]),
     "orchkv_block_checksums": (i32, [vp, u32, vp, vp]),
+    "orchkv_checked_build": (i32, []),
+    "orchkv_check_status": (i32, [vp, i32]),
+    "orchkv_check_inject": (i32, [u32]),
     "orchkv_gpu_pool_base": (vp, []),
     "orchkv_dram_pool_base": (vp, []),
     # scheduler

@@ -149,6 +149,35 @@ ReqDev req_dev(const kv_request_ctx *c)
     return r;
 }
 
+// Checked build: out-of-range indices met so far, folded in from the device
+// words (which shutdown frees); {count, line, index, bound} of the first.
+uint32_t g_check_tally[4] = {0, 0, 0, 0};
+
+int fold_check_words()
+{
+    if (!kCheckedBuild || !g.p.chk) return ORCHKV_OK;
+    uint32_t w[4];
+    OKV_CUDA_TRY(cudaMemcpy(w, g.p.chk, sizeof(w), cudaMemcpyDeviceToHost));
+    if (w[0] == 0) return ORCHKV_OK;
+    if (g_check_tally[0] == 0) {
+        fprintf(stderr, "[orchkv] checked build: %u index(es) out of range; first at "
+                        "pool_kernels.cu:%u (index %u, bound %u)\n", w[0], w[1], w[2], w[3]);
+        memcpy(g_check_tally + 1, w + 1, 3 * sizeof(uint32_t));
+    }
+    g_check_tally[0] += w[0];
+    OKV_CUDA_TRY(cudaMemset(g.p.chk, 0, sizeof(w)));
+    return ORCHKV_OK;
+}
+
+// ORCHKV_ERR_CUDA once a checked build met an index out of range (until
+// orchkv_check_status resets the tally).
+int check_words()
+{
+    const int rc = fold_check_words();
+    if (rc) return rc;
+    return g_check_tally[0] ? ORCHKV_ERR_CUDA : ORCHKV_OK;
+}
+
 int sync_result(int *rc_out)
 {
     OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
@@ -278,6 +307,7 @@ void release_all()
     if (g.copy_in) cudaStreamSynchronize(g.copy_in);
     if (g.unpack) cudaStreamSynchronize(g.unpack);
     if (g.stream) cudaStreamSynchronize(g.stream);
+    fold_check_words();
     cudaFree(g.p.gpu_base);
     if (g.p.dram_base) cudaFreeHost(g.p.dram_base);
     cudaFree(g.dev_meta);
@@ -423,7 +453,7 @@ int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
     }
 
     const size_t meta = ((size_t)p.g_total + p.d_total + 2 * (size_t)p.max_blocks) * 4 +
-                        (size_t)p.max_blocks * 6 + sizeof(PoolCounters) + 8 * 256;
+                        (size_t)p.max_blocks * 6 + sizeof(PoolCounters) + 16 + 9 * 256;
     if (cudaMalloc((void **)&g.dev_meta, meta) != cudaSuccess) { release_all(); return ORCHKV_ERR_CUDA; }
     char *q = g.dev_meta;
     auto take = [&](size_t sz) { char *r = q; q += (sz + 255) & ~size_t(255); return r; };
@@ -435,6 +465,8 @@ int orchkv_init_ext(const orchkv_config_t *cfg, const orchkv_config_ext_t *ext)
     p.state = (uint8_t *)take(p.max_blocks);
     p.flags = (uint8_t *)take(p.max_blocks);
     p.ctr = (PoolCounters *)take(sizeof(PoolCounters));
+    p.chk = (uint32_t *)take(16);
+    OKV_CUDA_TRY(cudaMemset(p.chk, 0, 16));
 
     // stacks hold N-1 ... 0 so the first pops return 0, 1, 2, ...
     // (src/tiered_store/gpu_tier.cu:41-42)
@@ -829,7 +861,38 @@ int orchkv_sync(void)
     std::lock_guard<std::recursive_mutex> lk(g.mu);
     if (!g.inited) return ORCHKV_ERR_INIT;
     OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+    return check_words();
+}
+
+int orchkv_checked_build(void) { return kCheckedBuild ? 1 : 0; }
+
+int orchkv_check_status(uint32_t *words, int reset)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!words) return ORCHKV_ERR_INVALID;
+    if (g.inited) {
+        OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
+        const int rc = fold_check_words();
+        if (rc) return rc;
+    }
+    memcpy(words, g_check_tally, sizeof(g_check_tally));
+    if (reset) memset(g_check_tally, 0, sizeof(g_check_tally));
     return ORCHKV_OK;
+}
+
+int orchkv_check_inject(uint32_t line)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_ERR_INIT;
+    return launch_check_inject(g.p, line, g.stream);
+}
+
+// Called by tm_sync: the data plane's check words (checked builds).
+int okv_data_plane_check(void)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return ORCHKV_OK;
+    return check_words();
 }
 
 // Called by tm_destroy: a manager that goes away while attached is detached
@@ -1230,7 +1293,7 @@ int orchkv_swap_batch(const uint32_t *evict_ids, const uint32_t *evict_count, ui
     // block read from a DRAM slab this evict is still filling.
     bool overlap = runs_e && runs_p && (de + g.ring_slabs - 1) / g.ring_slabs <= g.ev_copied.size();
     if (overlap) {
-        rc = launch_conflicts(mq, g.ss, g.h_meta + 8, g.stream);
+        rc = launch_conflicts(g.p, mq, g.ss, g.h_meta + 8, g.stream);
         if (rc) return rc;
         OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
         g.last_swap_conflicts = g.h_meta[8];

@@ -27,7 +27,42 @@ struct PoolDev {
     PoolCounters *ctr;
     SchedDev sd;                     // attached scheduler (valid if attached)
     int attached;
+    uint32_t *chk;                   // checked build: {count, line, index, bound} of the
+                                     // first out-of-range index (device, 4 words)
 };
+
+// ---- checked build ------------------------------------------------------------
+// Compiled with -DOKV_CHECKED, every slab, stack and block index a data-plane
+// kernel takes from memory is compared with its bound before it is used.  An
+// index out of range is counted in the check words (the first one's source
+// line, value and bound recorded) and its access is skipped -- nothing traps;
+// orchkv_sync / tm_sync then return ORCHKV_ERR_CUDA.  The regular build
+// compiles every comparison to `true`.
+#ifdef OKV_CHECKED
+constexpr bool kCheckedBuild = true;
+#else
+constexpr bool kCheckedBuild = false;
+#endif
+
+__device__ __forceinline__ bool in_bounds(uint32_t *chk, unsigned long long i,
+                                          unsigned long long n, uint32_t line)
+{
+    if (!kCheckedBuild || i < n) return true;
+    if (chk && atomicAdd(chk, 1u) == 0) {
+        chk[1] = line;
+        chk[2] = (uint32_t)i;
+        chk[3] = (uint32_t)n;
+    }
+    return false;
+}
+#define OKV_IN(chk, i, n) okv::in_bounds((chk), (i), (n), __LINE__)
+
+// The pool sizes a kernel that only sees raw pointers checks against.
+struct Bounds {
+    uint32_t *chk;
+    uint32_t g_total, d_total, max_blocks;
+};
+inline Bounds bounds_of(const PoolDev &p) { return Bounds{p.chk, p.g_total, p.d_total, p.max_blocks}; }
 
 // A request's region in the block-table array:
 //   [0]              seq_len
@@ -140,7 +175,8 @@ int launch_promote_short(const PoolDev &p, const MigPlan &mp, const SortScratch 
                          uint32_t min_len, cudaStream_t s);
 // *conflicts = promote sources among the slabs an evict's sorted assignment
 // popped (evict_ss.flags).
-int launch_conflicts(const MigPlan &promote, const SortScratch &evict_ss, uint32_t *conflicts,
+int launch_conflicts(const PoolDev &p, const MigPlan &promote, const SortScratch &evict_ss,
+                     uint32_t *conflicts,
                      cudaStream_t s);
 int launch_id_table(const PoolDev &p, uint32_t *const *regions, uint32_t n, uint32_t L,
                     uint32_t H, uint32_t mbph, uint32_t row_len, uint32_t *out,
@@ -153,6 +189,9 @@ int launch_lhb_lookup(const PoolDev &p, const ReqDev &r, const uint32_t *lhb, ui
 // slabs; dir 2: GPU -> storage, pushing GPU slabs[j]).
 int launch_storage_commit(const PoolDev &p, const uint32_t *ids, const uint32_t *slabs,
                           uint32_t n, int dir, cudaStream_t s);
+// Checked build: record a violation at `line` without any other access (a
+// test of the check words' plumbing).
+int launch_check_inject(const PoolDev &p, uint32_t line, cudaStream_t s);
 // Per-block checksums of listed blocks' slabs (integrity_kernels.cu).
 int launch_block_checksums(const PoolDev &p, const uint32_t *ids, uint32_t n,
                            unsigned long long *out, uint8_t *tier_out, cudaStream_t s);

@@ -110,10 +110,18 @@ compat_op_kernel(PoolDev p, ReqDev r, int op, uint32_t l, uint32_t h, uint32_t b
                 else if (p.flags[id] & KV_FLAG_PIN) rc = ORCHKV_ERR_LOCKED;
                 else if (c->d_top == 0) rc = ORCHKV_ERR_TIER_FULL;
                 else { src = loc_slab(w); dst = p.d_stack[--c->d_top]; dir = 0; }
+                if (dir == 0 && (!OKV_IN(p.chk, src, p.g_total) || !OKV_IN(p.chk, dst, p.d_total))) {
+                    rc = ORCHKV_ERR_CUDA;
+                    dir = -1;
+                }
             } else if (op == OP_PROMOTE || op == OP_GET) {
                 if (tier == TIER_HOST_DRAM) {
                     if (c->g_top == 0) rc = ORCHKV_ERR_TIER_FULL;
                     else { src = loc_slab(w); dst = p.g_stack[--c->g_top]; dir = 1; }
+                    if (dir == 1 && (!OKV_IN(p.chk, src, p.d_total) || !OKV_IN(p.chk, dst, p.g_total))) {
+                        rc = ORCHKV_ERR_CUDA;
+                        dir = -1;
+                    }
                 } else if (op == OP_PROMOTE || tier != TIER_GPU_HBM) {
                     rc = ORCHKV_ERR_STATE;
                 }
@@ -123,12 +131,14 @@ compat_op_kernel(PoolDev p, ReqDev r, int op, uint32_t l, uint32_t h, uint32_t b
             } else if (op == OP_DRAM_POP) {
                 if (c->d_top == 0) rc = ORCHKV_ERR_TIER_FULL;
                 else res->aux = p.d_stack[--c->d_top];
+                if (rc == ORCHKV_OK && !OKV_IN(p.chk, res->aux, p.d_total)) rc = ORCHKV_ERR_CUDA;
             } else if (op == OP_SET_LOC) {
                 const uint8_t st = (uint8_t)(arg2 & 0xFF);
                 const uint32_t push = arg2 >> 8;
                 p.loc[id] = arg;
                 p.state[id] = st;
-                if (push) p.d_stack[c->d_top++] = push - 1;
+                if (push && OKV_IN(p.chk, c->d_top, p.d_total) && OKV_IN(p.chk, push - 1, p.d_total))
+                    p.d_stack[c->d_top++] = push - 1;
                 sched_move(p, id, (uint8_t)loc_tier(arg), st);
             }
         }
@@ -144,14 +154,14 @@ compat_op_kernel(PoolDev p, ReqDev r, int op, uint32_t l, uint32_t h, uint32_t b
         if (dir == 0) {
             p.loc[id] = make_loc(TIER_HOST_DRAM, dst);
             p.state[id] = KV_STATE_WARM;
-            p.g_stack[c->g_top++] = src;
+            if (OKV_IN(p.chk, c->g_top, p.g_total)) p.g_stack[c->g_top++] = src;
             c->transfers_d2h++;
             c->bytes_d2h += p.slab;
             sched_move(p, id, TIER_HOST_DRAM, KV_STATE_WARM);
         } else if (dir == 1) {
             p.loc[id] = make_loc(TIER_GPU_HBM, dst);
             p.state[id] = KV_STATE_HOT;
-            p.d_stack[c->d_top++] = src;
+            if (OKV_IN(p.chk, c->d_top, p.d_total)) p.d_stack[c->d_top++] = src;
             c->transfers_h2d++;
             c->bytes_h2d += p.slab;
             sched_move(p, id, TIER_GPU_HBM, KV_STATE_HOT);
@@ -163,7 +173,7 @@ compat_op_kernel(PoolDev p, ReqDev r, int op, uint32_t l, uint32_t h, uint32_t b
             res->loc = w;
             res->state = p.state[id];
             res->flags = p.flags[id];
-            if (loc_tier(w) == TIER_GPU_HBM) {
+            if (loc_tier(w) == TIER_GPU_HBM && OKV_IN(p.chk, loc_slab(w), p.g_total)) {
                 res->k_ptr = (unsigned long long)(p.gpu_base + (unsigned long long)loc_slab(w) * p.slab);
                 res->v_ptr = res->k_ptr + p.half;
             } else {
@@ -209,6 +219,7 @@ append_one_kernel(PoolDev p, ReqDev r, uint32_t l, const char *k, const char *v,
                 for (uint32_t hh = 0; hh < r.H; hh++) {
                     const uint32_t id = p.id_stack[--c->id_top];
                     tab[(size_t)hh * r.mbph + b] = id;
+                    if (!OKV_IN(p.chk, id, p.max_blocks)) { rc = ORCHKV_ERR_CUDA; continue; }
                     p.loc[id] = make_loc(TIER_NONE, 0);
                     p.state[id] = KV_STATE_FREE;
                     p.flags[id] = 0;
@@ -216,16 +227,22 @@ append_one_kernel(PoolDev p, ReqDev r, uint32_t l, const char *k, const char *v,
                 for (uint32_t hh = 0; hh < r.H; hh++) {
                     const uint32_t id = tab[(size_t)hh * r.mbph + b];
                     const uint32_t g = p.g_stack[--c->g_top];
+                    if (!OKV_IN(p.chk, id, p.max_blocks) || !OKV_IN(p.chk, g, p.g_total)) {
+                        rc = ORCHKV_ERR_CUDA;
+                        continue;
+                    }
                     p.loc[id] = make_loc(TIER_GPU_HBM, g);
                     p.state[id] = KV_STATE_HOT;
                     c->live_blocks++;
                     sched_register(p, id, 0);
                 }
             }
-            for (uint32_t hh = 0; hh < r.H; hh++) {
+            for (uint32_t hh = 0; rc == ORCHKV_OK && hh < r.H; hh++) {
                 const uint32_t id = tab[(size_t)hh * r.mbph + b];
+                if (!OKV_IN(p.chk, id, p.max_blocks)) { rc = ORCHKV_ERR_CUDA; break; }
                 const uint32_t w = p.loc[id];
                 if (loc_tier(w) != TIER_GPU_HBM) { rc = ORCHKV_ERR_STATE; break; }
+                if (!OKV_IN(p.chk, loc_slab(w), p.g_total)) { rc = ORCHKV_ERR_CUDA; break; }
                 slab_of[hh] = loc_slab(w);
                 n_ok = hh + 1;
             }
@@ -308,6 +325,7 @@ prefill_copy_kernel(PoolDev p, ReqDev r, uint32_t l, const char *k, const char *
         const uint32_t hh = it / nn, j = it % nn;
         const uint32_t id = p.id_stack[id_top - 1 - (j * r.H + hh)];
         const uint32_t g = p.g_stack[g_top - 1 - it];
+        if (!OKV_IN(p.chk, id, p.max_blocks) || !OKV_IN(p.chk, g, p.g_total)) continue;
         if (lane == 0) {
             tab[(size_t)hh * r.mbph + have + j] = id;
             p.flags[id] = 0;
@@ -352,9 +370,11 @@ append_plan_kernel(PoolDev p, uint32_t *const *regions, uint32_t n, uint32_t L, 
             if (!need) {
                 const uint32_t *tab = reg + 1 + L + (size_t)l * H * mbph;
                 const uint32_t b = (tok - 1) / p.tpb;
-                for (uint32_t hh = 0; hh < H; hh++)
-                    if (loc_tier(p.loc[tab[(size_t)hh * mbph + b]]) != TIER_GPU_HBM)
+                for (uint32_t hh = 0; hh < H; hh++) {
+                    const uint32_t id = tab[(size_t)hh * mbph + b];
+                    if (!OKV_IN(p.chk, id, p.max_blocks) || loc_tier(p.loc[id]) != TIER_GPU_HBM)
                         atomicOr(&bad_state, 1u);
+                }
             }
             scratch[2 * pr] = tok;
         }
@@ -409,6 +429,7 @@ append_write_kernel(PoolDev p, uint32_t *const *regions, uint32_t n, uint32_t L,
         const uint32_t j = ord * H + hh;
         const uint32_t id = p.id_stack[scratch[2 * P + 2] - 1 - j];
         g = p.g_stack[scratch[2 * P + 1] - 1 - j];
+        if (!OKV_IN(p.chk, id, p.max_blocks)) return;
         if (lane == 0) {
             tab[(size_t)hh * mbph + b] = id;
             p.loc[id] = make_loc(TIER_GPU_HBM, g);
@@ -417,8 +438,11 @@ append_write_kernel(PoolDev p, uint32_t *const *regions, uint32_t n, uint32_t L,
             sched_register(p, id, 0);
         }
     } else {
-        g = loc_slab(p.loc[tab[(size_t)hh * mbph + b]]);
+        const uint32_t id = tab[(size_t)hh * mbph + b];
+        if (!OKV_IN(p.chk, id, p.max_blocks)) return;
+        g = loc_slab(p.loc[id]);
     }
+    if (!OKV_IN(p.chk, g, p.g_total)) return;
     char *dst = p.gpu_base + (unsigned long long)g * p.slab + (unsigned long long)slot * p.row;
     const size_t src = ((size_t)pr * H + hh) * p.row;
     if (k) coop_copy(dst, k + src, p.row, lane, 32);
@@ -544,6 +568,15 @@ mig_plan_kernel(PoolDev p, int dir, const uint32_t *ids, const uint32_t *count,
             const uint32_t id = idv[j];
             const uint32_t s = loc_slab(p.loc[id]);
             const uint32_t d = dstk[dst_top - 1 - o];
+            const uint32_t src_n = dir == 0 ? p.g_total : p.d_total;
+            const uint32_t dst_n = dir == 0 ? p.d_total : p.g_total;
+            if (!OKV_IN(p.chk, s, src_n) || !OKV_IN(p.chk, d, dst_n) ||
+                !OKV_IN(p.chk, src_top + o, src_n)) {
+                plan_src[o] = plan_dst[o] = kNoBlock;   // the copy kernels skip the entry
+                plan_id[o] = id;
+                o++;
+                continue;
+            }
             srck[src_top + o] = s;
             p.loc[id] = make_loc(dst_tier, d);
             p.state[id] = new_state;
@@ -559,7 +592,8 @@ mig_plan_kernel(PoolDev p, int dir, const uint32_t *ids, const uint32_t *count,
 // One warp per slab; 16-byte lanes, eight vectors in flight per lane.
 __global__ void __launch_bounds__(256)
 mig_copy_kernel(const char *src_base, char *dst_base, unsigned long long slab,
-                const uint32_t *plan_src, const uint32_t *plan_dst, const uint32_t *meta)
+                const uint32_t *plan_src, const uint32_t *plan_dst, const uint32_t *meta,
+                Bounds bd, uint32_t src_n, uint32_t dst_n)
 {
     const uint32_t done = meta[0];
     const unsigned lane = threadIdx.x & 31;
@@ -567,6 +601,7 @@ mig_copy_kernel(const char *src_base, char *dst_base, unsigned long long slab,
     const unsigned long long warp0 = ((unsigned long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const unsigned long long nwarps = ((unsigned long long)gridDim.x * blockDim.x) >> 5;
     for (unsigned long long w = warp0; w < done; w += nwarps) {
+        if (!OKV_IN(bd.chk, plan_src[w], src_n) || !OKV_IN(bd.chk, plan_dst[w], dst_n)) continue;
         const uint4 *s = reinterpret_cast<const uint4 *>(src_base + plan_src[w] * slab);
         uint4 *d = reinterpret_cast<uint4 *>(dst_base + plan_dst[w] * slab);
         unsigned long long i = lane;
@@ -587,11 +622,12 @@ mig_copy_kernel(const char *src_base, char *dst_base, unsigned long long slab,
 // then gets the o-th smallest popped slab, and the copy engine drains the
 // staging buffer run by run (maximal runs of consecutive slabs).
 
-__global__ void mig_mark_kernel(const uint32_t *plan_dst, const uint32_t *meta, uint8_t *flags)
+__global__ void mig_mark_kernel(const uint32_t *plan_dst, const uint32_t *meta, uint8_t *flags,
+                                Bounds bd)
 {
     const uint32_t done = meta[0];
     for (uint32_t o = blockIdx.x * blockDim.x + threadIdx.x; o < done; o += gridDim.x * blockDim.x)
-        flags[plan_dst[o]] = 1;
+        if (OKV_IN(bd.chk, plan_dst[o], bd.d_total)) flags[plan_dst[o]] = 1;
 }
 
 // Per-tile count of set bytes in flags[0 .. n) (n capped at *n_dev if given).
@@ -657,7 +693,8 @@ __global__ void mig_assign_kernel(PoolDev p, const uint32_t *meta, const uint32_
     for (uint32_t o = blockIdx.x * blockDim.x + threadIdx.x; o < done; o += gridDim.x * blockDim.x) {
         const uint32_t d = sorted[o];
         plan_dst[o] = d;
-        p.loc[plan_id[o]] = make_loc(TIER_HOST_DRAM, d);
+        if (OKV_IN(p.chk, plan_id[o], p.max_blocks) && OKV_IN(p.chk, d, p.d_total))
+            p.loc[plan_id[o]] = make_loc(TIER_HOST_DRAM, d);
         run_flag[o] = (o == 0 || sorted[o - 1] + 1 != d) ? 1 : 0;
     }
 }
@@ -728,7 +765,7 @@ __device__ __forceinline__ void copy_slab_warp(const char *src, char *dst,
 __global__ void __launch_bounds__(256)
 mig_pack_kernel(const char *src_base, char *staging, unsigned long long slab,
                 const uint32_t *plan_src, uint32_t pos0, uint32_t n, const uint32_t *run_o,
-                const uint32_t *meta, uint32_t min_len)
+                const uint32_t *meta, uint32_t min_len, Bounds bd)
 {
     const unsigned lane = threadIdx.x & 31;
     const unsigned long long nvec = slab >> 4;
@@ -738,6 +775,7 @@ mig_pack_kernel(const char *src_base, char *staging, unsigned long long slab,
     for (unsigned long long w = warp0; w < n; w += nwarps) {
         const uint32_t o = pos0 + (uint32_t)w;
         if (min_len && run_len_at(run_o, n_runs, done, o) < min_len) continue;
+        if (!OKV_IN(bd.chk, plan_src[o], bd.g_total)) continue;
         copy_slab_warp(src_base + plan_src[o] * slab, staging + w * slab, nvec, lane);
     }
 }
@@ -752,7 +790,7 @@ __global__ void __launch_bounds__(256)
 mig_drain_short_kernel(const char *src_base, char *dram_base, unsigned long long slab,
                        const uint32_t *plan_src, const uint32_t *plan_dst, uint32_t pos0,
                        uint32_t n, const uint32_t *run_o, const uint32_t *meta, uint32_t min_len,
-                       const char *staged)
+                       const char *staged, Bounds bd)
 {
     const unsigned lane = threadIdx.x & 31;
     const unsigned long long nvec = slab >> 4;
@@ -762,6 +800,9 @@ mig_drain_short_kernel(const char *src_base, char *dram_base, unsigned long long
     for (unsigned long long w = warp0; w < n; w += nwarps) {
         const uint32_t o = pos0 + (uint32_t)w;
         if (run_len_at(run_o, n_runs, done, o) >= min_len) continue;
+        if ((!staged && !OKV_IN(bd.chk, plan_src[o], bd.g_total)) ||
+            !OKV_IN(bd.chk, plan_dst[o], bd.d_total))
+            continue;
         const char *src = staged ? staged + w * slab : src_base + plan_src[o] * slab;
         copy_slab_warp(src, dram_base + plan_dst[o] * slab, nvec, lane);
     }
@@ -775,10 +816,11 @@ mig_drain_short_kernel(const char *src_base, char *dram_base, unsigned long long
 // scattered by mig_unpack_kernel; short runs are read zero-copy.
 
 __global__ void mig_src_mark_kernel(const uint32_t *plan_src, const uint32_t *meta,
-                                    uint8_t *flags, uint32_t *pos_of)
+                                    uint8_t *flags, uint32_t *pos_of, Bounds bd)
 {
     const uint32_t done = meta[0];
     for (uint32_t o = blockIdx.x * blockDim.x + threadIdx.x; o < done; o += gridDim.x * blockDim.x) {
+        if (!OKV_IN(bd.chk, plan_src[o], bd.d_total)) continue;
         flags[plan_src[o]] = 1;
         pos_of[plan_src[o]] = o;
     }
@@ -797,7 +839,7 @@ __global__ void __launch_bounds__(256)
 mig_unpack_kernel(const char *staging, char *gpu_base, unsigned long long slab,
                   const uint32_t *sorted, const uint32_t *pos_of, const uint32_t *plan_dst,
                   uint32_t j0, uint32_t n, const uint32_t *run_o, const uint32_t *meta,
-                  uint32_t min_len)
+                  uint32_t min_len, Bounds bd)
 {
     const unsigned lane = threadIdx.x & 31;
     const unsigned long long nvec = slab >> 4;
@@ -807,7 +849,10 @@ mig_unpack_kernel(const char *staging, char *gpu_base, unsigned long long slab,
     for (unsigned long long w = warp0; w < n; w += nwarps) {
         const uint32_t j = j0 + (uint32_t)w;
         if (min_len && run_len_at(run_o, n_runs, done, j) < min_len) continue;
+        if (!OKV_IN(bd.chk, sorted[j], bd.d_total) || !OKV_IN(bd.chk, pos_of[sorted[j]], done))
+            continue;
         const uint32_t d = plan_dst[pos_of[sorted[j]]];
+        if (!OKV_IN(bd.chk, d, bd.g_total)) continue;
         copy_slab_warp(staging + w * slab, gpu_base + d * slab, nvec, lane);
     }
 }
@@ -817,7 +862,8 @@ mig_unpack_kernel(const char *staging, char *gpu_base, unsigned long long slab,
 __global__ void __launch_bounds__(256)
 mig_promote_short_kernel(const char *dram_base, char *gpu_base, unsigned long long slab,
                          const uint32_t *sorted, const uint32_t *pos_of, const uint32_t *plan_dst,
-                         const uint32_t *run_o, const uint32_t *meta, uint32_t min_len)
+                         const uint32_t *run_o, const uint32_t *meta, uint32_t min_len,
+                         Bounds bd)
 {
     const unsigned lane = threadIdx.x & 31;
     const unsigned long long nvec = slab >> 4;
@@ -828,6 +874,9 @@ mig_promote_short_kernel(const char *dram_base, char *gpu_base, unsigned long lo
         const uint32_t j = (uint32_t)w;
         if (run_len_at(run_o, n_runs, done, j) >= min_len) continue;
         const uint32_t s = sorted[j];
+        if (!OKV_IN(bd.chk, s, bd.d_total) || !OKV_IN(bd.chk, pos_of[s], done) ||
+            !OKV_IN(bd.chk, plan_dst[pos_of[s]], bd.g_total))
+            continue;
         copy_slab_warp(dram_base + s * slab, gpu_base + plan_dst[pos_of[s]] * slab, nvec, lane);
     }
 }
@@ -836,12 +885,12 @@ mig_promote_short_kernel(const char *dram_base, char *gpu_base, unsigned long lo
 // just popped (evict_flags, its byte map): the promote must then wait for
 // the evict's bytes to land.  Counted into *conflicts.
 __global__ void mig_conflict_kernel(const uint32_t *plan_src, const uint32_t *meta,
-                                    const uint8_t *evict_flags, uint32_t *conflicts)
+                                    const uint8_t *evict_flags, uint32_t *conflicts, Bounds bd)
 {
     const uint32_t done = meta[0];
     uint32_t c = 0;
     for (uint32_t o = blockIdx.x * blockDim.x + threadIdx.x; o < done; o += gridDim.x * blockDim.x)
-        c += evict_flags[plan_src[o]];
+        if (OKV_IN(bd.chk, plan_src[o], bd.d_total)) c += evict_flags[plan_src[o]];
     c = __reduce_add_sync(0xFFFFFFFFu, c);
     if ((threadIdx.x & 31) == 0 && c) atomicAdd(conflicts, c);
 }
@@ -969,9 +1018,15 @@ req_free_write_kernel(PoolDev p, ReqDev r, const uint32_t *tile_pos)
     for (int j = 0; j < 4; j++) {
         if (!ok[j]) continue;
         const uint32_t id = ids[j], w = ws[j];
-        if (loc_tier(w) == TIER_GPU_HBM) p.g_stack[og++] = loc_slab(w);
-        else if (loc_tier(w) == TIER_HOST_DRAM) p.d_stack[od++] = loc_slab(w);
-        p.id_stack[oi++] = id;
+        if (loc_tier(w) == TIER_GPU_HBM) {
+            if (OKV_IN(p.chk, og, p.g_total)) p.g_stack[og] = loc_slab(w);
+            og++;
+        } else if (loc_tier(w) == TIER_HOST_DRAM) {
+            if (OKV_IN(p.chk, od, p.d_total)) p.d_stack[od] = loc_slab(w);
+            od++;
+        }
+        if (OKV_IN(p.chk, oi, p.max_blocks)) p.id_stack[oi] = id;
+        oi++;
         p.loc[id] = make_loc(TIER_NONE, 0);
         p.state[id] = KV_STATE_EVICTED;
         p.flags[id] = 0;
@@ -1073,14 +1128,19 @@ storage_commit_kernel(PoolDev p, const uint32_t *ids, const uint32_t *slabs, uin
     const uint32_t top = dir == 2 ? c->g_top : c->d_top;
     for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
         const uint32_t id = ids[j];
+        if (!OKV_IN(p.chk, id, p.max_blocks)) continue;
         if (dir == 1) {
+            if (!OKV_IN(p.chk, p.d_stack[top - 1 - j], p.d_total)) continue;
             p.loc[id] = make_loc(TIER_HOST_DRAM, p.d_stack[top - 1 - j]);
             p.state[id] = KV_STATE_WARM;
             sched_move(p, id, (uint8_t)TIER_HOST_DRAM, KV_STATE_WARM);
             continue;
         }
-        if (dir == 0) p.d_stack[top + j] = slabs[j];
-        else p.g_stack[top + j] = slabs[j];
+        if (dir == 0) {
+            if (OKV_IN(p.chk, top + j, p.d_total)) p.d_stack[top + j] = slabs[j];
+        } else if (OKV_IN(p.chk, top + j, p.g_total)) {
+            p.g_stack[top + j] = slabs[j];
+        }
         p.loc[id] = make_loc(TIER_NVM, 0);
         p.state[id] = KV_STATE_COLD;
         sched_move(p, id, (uint8_t)TIER_NVM, KV_STATE_COLD);
@@ -1144,8 +1204,10 @@ int launch_migrate_zero_copy(const PoolDev &p, int dir, const MigPlan &mp, cudaS
     if (mp.max_n == 0) return ORCHKV_OK;
     const char *src_base = dir == 0 ? p.gpu_base : p.dram_base;
     char *dst_base = dir == 0 ? p.dram_base : p.gpu_base;
-    mig_copy_kernel<<<copy_grid(mp.max_n, 8), 256, 0, s>>>(src_base, dst_base, p.slab,
-                                                           mp.plan_src, mp.plan_dst, mp.meta); note_launches(1);
+    mig_copy_kernel<<<copy_grid(mp.max_n, 8), 256, 0, s>>>(
+        src_base, dst_base, p.slab, mp.plan_src, mp.plan_dst, mp.meta, bounds_of(p),
+        dir == 0 ? p.g_total : p.d_total, dir == 0 ? p.d_total : p.g_total);
+    note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }
@@ -1156,7 +1218,7 @@ int launch_sorted_assign(const PoolDev &p, const MigPlan &mp, const SortScratch 
     OKV_CUDA_TRY(cudaMemsetAsync(ss.flags, 0, p.d_total, s));
     const unsigned g = copy_grid(mp.max_n, 256);
     const uint32_t tiles = (p.d_total + kTileN - 1) / kTileN;
-    mig_mark_kernel<<<g, 256, 0, s>>>(mp.plan_dst, mp.meta, ss.flags);
+    mig_mark_kernel<<<g, 256, 0, s>>>(mp.plan_dst, mp.meta, ss.flags, bounds_of(p));
     mig_flag_count_kernel<<<tiles, 256, 0, s>>>(ss.flags, p.d_total, nullptr, ss.tile_cnt);
     mig_tile_scan_kernel<<<1, 1024, 0, s>>>(ss.tile_cnt, tiles, nullptr);
     mig_flag_write_kernel<<<tiles, 256, 0, s>>>(ss.flags, p.d_total, ss.tile_cnt, ss.sorted);
@@ -1184,7 +1246,8 @@ int launch_pack(const PoolDev &p, const MigPlan &mp, char *staging, uint32_t pos
 {
     if (n == 0) return ORCHKV_OK;
     mig_pack_kernel<<<copy_grid(n, 8), 256, 0, s>>>(p.gpu_base, staging, p.slab, mp.plan_src,
-                                                     pos0, n, ss.run_o, mp.meta, min_len);
+                                                     pos0, n, ss.run_o, mp.meta, min_len,
+                                                     bounds_of(p));
     note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
@@ -1197,7 +1260,8 @@ int launch_drain_short(const PoolDev &p, const MigPlan &mp, uint32_t pos0, uint3
     if (n == 0 || min_len == 0) return ORCHKV_OK;
     mig_drain_short_kernel<<<copy_grid(n, 8), 256, 0, s>>>(p.gpu_base, p.dram_base, p.slab,
                                                             mp.plan_src, mp.plan_dst, pos0, n,
-                                                            ss.run_o, mp.meta, min_len, staged);
+                                                            ss.run_o, mp.meta, min_len, staged,
+                                                            bounds_of(p));
     note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
@@ -1210,7 +1274,8 @@ int launch_sorted_sources(const PoolDev &p, const MigPlan &mp, const SortScratch
     OKV_CUDA_TRY(cudaMemsetAsync(ss.flags, 0, p.d_total, s));
     const unsigned g = copy_grid(mp.max_n, 256);
     const uint32_t tiles = (p.d_total + kTileN - 1) / kTileN;
-    mig_src_mark_kernel<<<g, 256, 0, s>>>(mp.plan_src, mp.meta, ss.flags, ss.pos_of);
+    mig_src_mark_kernel<<<g, 256, 0, s>>>(mp.plan_src, mp.meta, ss.flags, ss.pos_of,
+                                          bounds_of(p));
     mig_flag_count_kernel<<<tiles, 256, 0, s>>>(ss.flags, p.d_total, nullptr, ss.tile_cnt);
     mig_tile_scan_kernel<<<1, 1024, 0, s>>>(ss.tile_cnt, tiles, nullptr);
     mig_flag_write_kernel<<<tiles, 256, 0, s>>>(ss.flags, p.d_total, ss.tile_cnt, ss.sorted);
@@ -1237,7 +1302,7 @@ int launch_unpack(const PoolDev &p, const MigPlan &mp, const SortScratch &ss,
     if (n == 0) return ORCHKV_OK;
     mig_unpack_kernel<<<copy_grid(n, 8), 256, 0, s>>>(staging, p.gpu_base, p.slab, ss.sorted,
                                                        ss.pos_of, mp.plan_dst, j0, n, ss.run_o,
-                                                       mp.meta, min_len);
+                                                       mp.meta, min_len, bounds_of(p));
     note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
@@ -1249,18 +1314,32 @@ int launch_promote_short(const PoolDev &p, const MigPlan &mp, const SortScratch 
     if (min_len == 0) return ORCHKV_OK;
     mig_promote_short_kernel<<<copy_grid(mp.max_n, 8), 256, 0, s>>>(
         p.dram_base, p.gpu_base, p.slab, ss.sorted, ss.pos_of, mp.plan_dst, ss.run_o, mp.meta,
-        min_len);
+        min_len, bounds_of(p));
     note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;
 }
 
-int launch_conflicts(const MigPlan &promote, const SortScratch &evict_ss, uint32_t *conflicts,
-                     cudaStream_t s)
+int launch_conflicts(const PoolDev &p, const MigPlan &promote, const SortScratch &evict_ss,
+                     uint32_t *conflicts, cudaStream_t s)
 {
     OKV_CUDA_TRY(cudaMemsetAsync(conflicts, 0, 4, s));
     mig_conflict_kernel<<<copy_grid(promote.max_n, 256), 256, 0, s>>>(
-        promote.plan_src, promote.meta, evict_ss.flags, conflicts);
+        promote.plan_src, promote.meta, evict_ss.flags, conflicts, bounds_of(p));
+    note_launches(1);
+    OKV_CUDA_TRY(cudaGetLastError());
+    return ORCHKV_OK;
+}
+
+__global__ void check_inject_kernel(uint32_t *chk, uint32_t line)
+{
+    in_bounds(chk, 1, 0, line);
+}
+
+int launch_check_inject(const PoolDev &p, uint32_t line, cudaStream_t s)
+{
+    if (!kCheckedBuild || !p.chk) return ORCHKV_ERR_INVALID;
+    check_inject_kernel<<<1, 1, 0, s>>>(p.chk, line);
     note_launches(1);
     OKV_CUDA_TRY(cudaGetLastError());
     return ORCHKV_OK;

@@ -838,7 +838,7 @@ int tm_sync(tiered_manager_t *m)
     int rc = tm_flush_locked(t);
     if (rc) return rc;
     OKV_CUDA_TRY(cudaStreamSynchronize(t->stream));
-    return ORCHKV_OK;
+    return okv_data_plane_check();
 }
 
 uint32_t tm_capacity(const tiered_manager_t *m)

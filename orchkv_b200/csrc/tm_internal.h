@@ -137,5 +137,8 @@ struct TmImpl {
 TmImpl *tm_impl(const tiered_manager_t *m);
 // data plane hook (api.cu): detach m if it is the attached manager
 extern "C" __attribute__((visibility("hidden"))) void okv_manager_destroyed(tiered_manager_t *m);
+// data plane hook (api.cu): ORCHKV_ERR_CUDA when a checked build met an
+// out-of-range index
+extern "C" __attribute__((visibility("hidden"))) int okv_data_plane_check(void);
 int tm_flush_locked(TmImpl *t);
 int tm_refresh_mirror_locked(TmImpl *t);

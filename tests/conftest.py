@@ -27,3 +27,25 @@ def cuda():
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
     torch.cuda.init()
     return torch
+
+
+def pytest_sessionfinish(session, exitstatus):
+    """Under the checked build (ORCHKV_CHECKED=1) the session fails if any
+    data-plane kernel met an index out of range; the tally is printed."""
+    if os.environ.get("ORCHKV_CHECKED") != "1" or "orchkv_b200" not in sys.modules:
+        return
+    import ctypes as C
+    import orchkv_b200
+    words = (C.c_uint32 * 4)()
+    if orchkv_b200.lib().orchkv_check_status(words, 0) != 0:
+        return
+    msg = (f"checked build: {words[0]} indices out of range"
+           + (f" (first at pool_kernels.cu:{words[1]}, index {words[2]}, bound {words[3]})"
+              if words[0] else ""))
+    tr = session.config.pluginmanager.get_plugin("terminalreporter")
+    if tr is not None:
+        tr.write_line(msg)
+    else:
+        print(msg)
+    if words[0]:
+        session.exitstatus = 1
