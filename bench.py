@@ -557,6 +557,216 @@ def run_sharded(args, torch, okv, rank, world, comm, dist, link_d2h):
     return out
 
 
+# ---------------------------------------------------------------------------
+# Mistral-7B-shaped time-multiplexed pool, KV heads sharded over the ranks
+# ---------------------------------------------------------------------------
+
+MX = dict(name="mistral-7b-time-multiplexed-4-sub-batches", B=32, L=32, Hq=32, Hkv=8, D=128,
+          T=4096, tpb=16, sub_batches=4, resident=2)
+
+
+class MultiplexedWorkload:
+    """The Mistral-7B-shaped shared pool (32 layers, 32 query / 8 KV heads,
+    d_head 128, bf16, 16-token blocks, 4096-token context) rotated through
+    the GPU in four sub-batches of requests, two resident at a time, KV heads
+    split over the ranks like the sharded pool.  A step scores the resident
+    sub-batches' query rows (logits N(0, 1.5), softmax), classifies, and one
+    orchkv_swap_batch evicts the older resident sub-batch while promoting the
+    next one from the DRAM tier: half of the GPU's blocks leave and half
+    arrive, every step, with no restore between steps."""
+
+    def __init__(self, torch, okv, rank, world, requests, seed=0):
+        w = MX
+        self.t, self.L = torch, okv.lib()
+        self.B, self.Ly, self.D, self.T, self.tpb = requests, w["L"], w["D"], w["T"], w["tpb"]
+        self.S = w["sub_batches"]
+        if self.B % self.S:
+            raise ValueError("requests must split into the sub-batches")
+        self.G = w["Hq"] // w["Hkv"]
+        self.hkv = w["Hkv"] // world
+        self.hq = self.hkv * self.G
+        self.nb = self.T // self.tpb
+        self.per_sb = self.B // self.S                          # requests per sub-batch
+        self.rows_sb = self.per_sb * self.Ly
+        self.blocks_sb = self.rows_sb * self.hkv * self.nb      # this rank's blocks per sub-batch
+        self.n_total = self.B * self.Ly * w["Hkv"] * self.nb
+        self.slab = self.tpb * self.D * 2 * 2
+        cap = 1
+        while cap < self.S * self.blocks_sb + 1024:
+            cap <<= 1
+        self.cap = cap
+        resident = w["resident"] * self.blocks_sb
+        cfg = okv.make_config(gpu_pool_bytes=(self.S * self.blocks_sb + 1024) * self.slab,
+                              dram_pool_bytes=(resident + self.blocks_sb + 1024) * self.slab,
+                              tokens_per_block=self.tpb, d_head=self.D, dtype=1,
+                              device=torch.cuda.current_device(),
+                              max_blocks_per_head=self.nb + 8)
+        ext = okv.OrchkvConfigExt()
+        ext.max_blocks = cap
+        # staging for a whole sub-batch, so each swap overlaps both directions
+        ext.staging_mb = (self.blocks_sb * self.slab >> 20) + 256
+        L = self.L
+        rc = L.orchkv_init_ext(C.byref(cfg), C.byref(ext))
+        if rc != 0:
+            raise RuntimeError(f"orchkv_init_ext (multiplexed pool) failed: {rc}")
+        self.stream = torch.cuda.current_stream()
+        L.orchkv_set_stream(C.c_void_p(self.stream.cuda_stream))
+        self.tm = okv.Manager(tracker_cap=cap, max_blocks=2 * cap, ema_lambda=0.9, alpha=0.5,
+                              beta=0.3, gamma=0.2, recency_tau=50.0)
+        assert L.orchkv_attach_scheduler(self.tm.ref) == 0
+        g = torch.Generator(device="cuda").manual_seed(seed + 11 * rank + 3)
+        self.ctxs = [L.orchkv_request_create(i, self.Ly, self.hkv) for i in range(self.B)]
+        assert all(self.ctxs)
+        for c in self.ctxs:
+            for layer in range(self.Ly):
+                kv = torch.randn(2, self.hkv, self.T, self.D, generator=g, device="cuda",
+                                 dtype=torch.bfloat16)
+                assert L.orchkv_prefill(c, layer, kv[0].data_ptr(), kv[1].data_ptr(), self.T) == 0
+        del kv
+        # per sub-batch: its requests, their block ids ([rows, kv heads, blocks]) and
+        # their probabilities, drawn per global KV head so every N sees the same numbers
+        self.arrs, self.ids, self.probs = [], [], []
+        for sb in range(self.S):
+            arr = (C.c_void_p * self.per_sb)(*self.ctxs[sb * self.per_sb:(sb + 1) * self.per_sb])
+            ids = torch.empty(self.blocks_sb, dtype=torch.int32, device="cuda")
+            assert L.orchkv_block_id_table(arr, self.per_sb, self.T, C.c_void_p(ids.data_ptr())) == 0
+            p = torch.empty(self.rows_sb, self.hq, self.T, device="cuda")
+            for j in range(self.hkv):
+                gg = torch.Generator(device="cuda").manual_seed(seed * 1000 + 500 + 8 * sb +
+                                                                rank * self.hkv + j)
+                x = torch.randn(self.rows_sb, self.G, self.T, generator=gg, device="cuda") * 1.5
+                p[:, j * self.G:(j + 1) * self.G] = torch.softmax(x, -1)
+            self.arrs.append(arr)
+            self.ids.append(ids)
+            self.probs.append(p)
+        del x
+        self.counts = torch.zeros(16, dtype=torch.int32, device="cuda")
+        self.h_counts = torch.zeros(16, dtype=torch.int32).pin_memory()
+        self.ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        # start: sub-batches 0 and 1 resident, the others in the DRAM tier
+        for sb in range(w["resident"], self.S):
+            assert L.orchkv_evict_batch_to_dram(C.c_void_p(self.ids[sb].data_ptr()), None,
+                                                self.blocks_sb,
+                                                C.c_void_p(self.counts.data_ptr())) == 0
+        torch.cuda.synchronize()
+        self.t_step = 0
+
+    def checksums(self):
+        """Every block's slab checksum, sub-batch by sub-batch (device)."""
+        out = []
+        for ids in self.ids:
+            o = self.t.empty(self.blocks_sb, dtype=self.t.int64, device="cuda")
+            assert self.L.orchkv_block_checksums(C.c_void_p(ids.data_ptr()), self.blocks_sb,
+                                                 C.c_void_p(o.data_ptr()), None) == 0
+            out.append(o)
+        assert self.L.orchkv_sync() == 0
+        return self.t.cat(out).cpu()
+
+    def step(self):
+        L, tm, ev = self.L, self.tm.ref, self.ev
+        out_sb = self.t_step % self.S
+        in_sb = (self.t_step + MX["resident"]) % self.S
+        ev[0].record()
+        for sb in (out_sb, (out_sb + 1) % self.S):            # the resident sub-batches
+            assert L.tm_report_attn_probs(tm, C.c_void_p(self.probs[sb].data_ptr()),
+                                          self.rows_sb, self.hq, self.hkv, self.T, self.tpb,
+                                          None, C.c_void_p(self.ids[sb].data_ptr())) == 0
+        ev[1].record()
+        assert L.tm_step_and_classify(tm) == 0
+        ev[2].record()
+        assert L.orchkv_swap_batch(C.c_void_p(self.ids[out_sb].data_ptr()), None, self.blocks_sb,
+                                   C.c_void_p(self.ids[in_sb].data_ptr()), None, self.blocks_sb,
+                                   C.c_void_p(self.counts.data_ptr())) == 0
+        ev[3].record()
+        self.h_counts.copy_(self.counts, non_blocking=True)
+        ev[4].record()
+        self.t_step += 1
+
+    def phases(self):
+        e = self.ev
+        names = ["score", "classify", "swap", "readback"]
+        return {n: e[i].elapsed_time(e[i + 1]) for i, n in enumerate(names)}
+
+    def close(self):
+        L = self.L
+        for c in self.ctxs:
+            L.orchkv_request_destroy(c)
+        self.tm.close()
+        L.orchkv_shutdown()
+
+
+def run_multiplexed(args, torch, okv, rank, world, dist, link):
+    """The time-multiplexed pool: W warm-up steps, K timed steps (barrier +
+    synchronize around each, max over ranks), then the rotation completed to
+    a multiple of four steps and every block's checksum compared with its
+    checksum before the first step (each block has made whole round trips)."""
+    if MX["Hkv"] % world:
+        return {"skipped": f"{MX['Hkv']} KV heads do not split over {world} ranks"}
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    mw = MultiplexedWorkload(torch, okv, rank, world, args.multiplexed_requests)
+    before = mw.checksums()
+    for _ in range(args.warmup):
+        mw.step()
+    step_ms, ph, moved = [], {}, 0
+    for _ in range(args.steps):
+        barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        mw.step()
+        t1.record()
+        barrier()
+        step_ms.append(t0.elapsed_time(t1))
+        for k, v in mw.phases().items():
+            ph.setdefault(k, []).append(v)
+        c = mw.h_counts.tolist()
+        moved += c[0] + c[2]
+    ov = [C.c_uint32() for _ in range(3)] + [C.c_int()]
+    mw.L.orchkv_last_promote_layout(*[C.byref(x) for x in ov])
+    while mw.t_step % MX["sub_batches"]:
+        mw.step()
+    intact = bool(torch.equal(mw.checksums(), before))
+    phases = {k: sum(v) / len(v) for k, v in ph.items()}
+    swap_bytes = 2 * mw.blocks_sb * mw.slab
+    t = torch.tensor([sum(step_ms) / len(step_ms), moved / args.steps, float(intact),
+                      phases["swap"], link["both"]], dtype=torch.float64, device="cuda")
+    if world > 1:
+        allv = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(allv, t)
+        allv = [x.tolist() for x in allv]
+    else:
+        allv = [t.tolist()]
+    out = None
+    if rank == 0:
+        ms_max = max(r[0] for r in allv)
+        out = {
+            "workload": MX["name"], "requests": mw.B, "context": mw.T, "layers": mw.Ly,
+            "q_heads": MX["Hq"], "kv_heads": MX["Hkv"], "kv_heads_per_gpu": mw.hkv,
+            "d_head": mw.D, "tokens_per_block": mw.tpb, "dtype": "bf16",
+            "sub_batches": MX["sub_batches"], "resident": MX["resident"],
+            "blocks_total": mw.n_total, "blocks_per_gpu": mw.S * mw.blocks_sb,
+            "pool_gib_total": round(mw.n_total * mw.slab / 2**30, 2),
+            "sample": f"{mw.B} of the configuration's 256 requests (host RAM for the DRAM tier "
+                      f"at one GPU); the same {mw.B} requests at every N",
+            "steps": args.steps, "ms_per_step": round(ms_max, 3),
+            "value": round(sum(r[1] for r in allv) / (ms_max * 1e-3), 1),
+            "unit": "migrated blocks/s (evicted + promoted, all ranks)",
+            "scaling": "strong (fixed total pool)",
+            "swap_gbs_per_rank": [round(swap_bytes / (r[3] * 1e-3) / 1e9, 1) for r in allv],
+            "probe_both_directions_gbs_per_rank": [round(r[4], 1) for r in allv],
+            "swap_overlapped": bool(ov[3].value),
+            "phases_ms_rank0": {k: round(v, 4) for k, v in phases.items()},
+            "round_trip_checksums_equal": all(bool(r[2]) for r in allv),
+        }
+    mw.close()
+    return out
+
+
 def score_bytes(wl):
     """Algorithmic bytes of one scoring launch: probabilities read once, block
     id table read, per-block tracker read (active, sum, max) and written (sum,
@@ -936,6 +1146,11 @@ def run_ours(args, rank, world, local_rank):
                               link["d2h"])
         if line is not None:
             line["sharded"] = sharded
+        torch.cuda.empty_cache()
+    if not args.no_multiplexed:
+        mx = run_multiplexed(args, torch, okv, rank, world, dist if world > 1 else None, link)
+        if line is not None:
+            line["multiplexed"] = mx
     if comm:
         okv.lib().orchkv_comm_destroy(comm)
     if world > 1:
@@ -1218,6 +1433,10 @@ def main():
                     help="skip the KV-head-sharded Llama-3-8B-shaped pool")
     ap.add_argument("--sharded-requests", type=int, default=SH["B"],
                     help="requests of the sharded pool (the same at every N)")
+    ap.add_argument("--no-multiplexed", action="store_true",
+                    help="skip the Mistral-7B-shaped time-multiplexed pool")
+    ap.add_argument("--multiplexed-requests", type=int, default=MX["B"],
+                    help="requests of the time-multiplexed pool (the same at every N)")
     ap.add_argument("--requests", type=int, default=WL["B"],
                     help="requests per GPU (32 = the benchmark workload; smaller "
                          "values only for profiling captures)")

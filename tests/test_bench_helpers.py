@@ -48,3 +48,25 @@ def test_command_line():
     assert out.returncode == 0
     for flag in ("--gpus", "--steps", "--warmup", "--impl"):
         assert flag in out.stdout
+
+
+def test_sharded_pick_rule_matches_oracle(oracle_mod):
+    """The sharded bench's check of the ranks' global picks (numpy: keys of
+    the hotness, stable sort by (key, global index)) is the oracle's coldest-k
+    over the same concatenated arrays, ties included (values on a 1/16 grid,
+    -0.0 beside +0.0)."""
+    import numpy as np
+
+    import bench
+    rng = np.random.default_rng(7)
+    n = 50000
+    hot = (rng.integers(-8, 40, n) / 16).astype(np.float32)
+    hot[rng.random(n) < 0.01] = -0.0
+    elig = rng.random(n) < 0.8
+    assert np.array_equal(bench.orderable_u32(hot), oracle_mod.orderable(hot))
+    for k in (1, 777, int(elig.sum()) // 2, int(elig.sum())):
+        idx = np.nonzero(elig)[0]
+        order = np.lexsort((idx, bench.orderable_u32(hot[idx])))[:k]
+        got = np.sort(idx[order])
+        want = oracle_mod.select_coldest(hot, elig.astype(np.uint8), k).astype(np.int64)
+        assert np.array_equal(got, want)
