@@ -767,6 +767,170 @@ def run_multiplexed(args, torch, okv, rank, world, dist, link):
     return out
 
 
+# ---------------------------------------------------------------------------
+# The CPU-runnable scheduler step (one request) as a latency figure
+# ---------------------------------------------------------------------------
+
+C1 = dict(name="cpu-runnable-step-1req-8L-4kvh-4096", L=8, Hq=28, Hkv=4, D=128, T=4096, tpb=64,
+          hist=16, evict_frac=0.5)
+
+
+def _c1_inputs():
+    """Seed 0: probabilities softmax(N(0,2) + 0.002 * position) per (layer,
+    28 q-heads, token); K/V N(0,1) fp16; a 16-step history in which every
+    slab has min(Poisson(3), 16) hits with uniform weights."""
+    w = C1
+    nb = w["T"] // w["tpb"]
+    n = w["L"] * w["Hkv"] * nb
+    rng = np.random.default_rng(0)
+    logits = (rng.normal(0, 2, (w["L"], w["Hq"], w["T"])).astype(np.float32)
+              + (0.002 * np.arange(w["T"])).astype(np.float32))
+    logits -= logits.max(-1, keepdims=True)
+    p = np.exp(logits)
+    probs = (p / p.sum(-1, keepdims=True)).astype(np.float32)
+    kv = rng.standard_normal((w["L"], 2, w["Hkv"], w["T"], w["D"])).astype(np.float16)
+    hits = np.minimum(rng.poisson(3, n), w["hist"])
+    history = [([], []) for _ in range(w["hist"])]
+    for i in range(n):
+        for s, x in zip(rng.choice(w["hist"], hits[i], replace=False),
+                        rng.random(hits[i]).astype(np.float32)):
+            history[int(s)][0].append(i)
+            history[int(s)][1].append(float(x))
+    return probs, kv, history
+
+
+def run_cpu_step(args, torch, okv):
+    """One request, 8 layers x 4 KV heads, 64-token blocks, 4096 tokens (2,048
+    slabs of 32 KB), after a 16-step hit history.  A step: report the
+    probabilities (one launch), step + classify, select the coldest 50%, evict
+    them to pinned DRAM and promote them back, read the counts -- device time
+    per step (events) and wall time per step with the host waiting for the
+    counts.  Beside it (unless --no-cpu-baseline) the reference's own path for
+    the same step on one host core: the C restatement of the managers'
+    reduction, the reference scheduler (attn_tracker_update_batch,
+    tm_step_done, tm_schedule_once, coldest-first order) and its data plane
+    evicting and promoting block by block."""
+    w = C1
+    nb = w["T"] // w["tpb"]
+    n = w["L"] * w["Hkv"] * nb
+    slab = w["tpb"] * w["D"] * 2 * 2
+    k = int(w["evict_frac"] * n)
+    probs, kv, history = _c1_inputs()
+    L = okv.lib()
+    cfg = okv.make_config(gpu_pool_bytes=(n + 64) * slab, dram_pool_bytes=n * slab,
+                          tokens_per_block=w["tpb"], d_head=w["D"], dtype=0,
+                          device=torch.cuda.current_device(), max_blocks_per_head=nb + 8)
+    ext = okv.OrchkvConfigExt()
+    ext.max_blocks = 4096
+    assert L.orchkv_init_ext(C.byref(cfg), C.byref(ext)) == 0
+    stream = torch.cuda.current_stream()
+    L.orchkv_set_stream(C.c_void_p(stream.cuda_stream))
+    tm = okv.Manager(tracker_cap=4096, max_blocks=8192, ema_lambda=0.9, alpha=0.5, beta=0.3,
+                     gamma=0.2, recency_tau=50.0, cooldown_sec=0.0)
+    assert L.orchkv_attach_scheduler(tm.ref) == 0
+    ctx = L.orchkv_request_create(0, w["L"], w["Hkv"])
+    for layer in range(w["L"]):
+        assert L.orchkv_prefill(ctx, layer, kv[layer, 0].ctypes.data, kv[layer, 1].ctypes.data,
+                                w["T"]) == 0
+    arr = (C.c_void_p * 1)(ctx)
+    ids = torch.empty(n, dtype=torch.int32, device="cuda")
+    assert L.orchkv_block_id_table(arr, 1, w["T"], C.c_void_p(ids.data_ptr())) == 0
+    for sl, wt in history:
+        if sl:
+            hid = ids[torch.as_tensor(sl, device="cuda")].contiguous()
+            hw = torch.as_tensor(wt, dtype=torch.float32, device="cuda")
+            assert L.tm_report_attn_batch_dev(tm.ref, C.c_void_p(hid.data_ptr()),
+                                              C.c_void_p(hw.data_ptr()), len(sl)) == 0
+        assert L.tm_step_and_classify(tm.ref) == 0
+    dprobs = torch.from_numpy(probs).cuda()
+    victims = torch.empty(n, dtype=torch.int32, device="cuda")
+    counts = torch.zeros(8, dtype=torch.int32, device="cuda")
+    h_counts = torch.zeros(8, dtype=torch.int32).pin_memory()
+    vp = lambda t, off=0: C.c_void_p(t.data_ptr() + off)   # noqa: E731
+
+    def step():
+        assert L.tm_report_attn_probs(tm.ref, vp(dprobs), w["L"], w["Hq"], w["Hkv"], w["T"],
+                                      w["tpb"], None, vp(ids)) == 0
+        assert L.tm_step_and_classify(tm.ref) == 0
+        assert L.tm_select_victims(tm.ref, k, vp(victims), vp(counts)) == 0
+        assert L.orchkv_evict_batch_to_dram(vp(victims), vp(counts), n, vp(counts, 8)) == 0
+        assert L.orchkv_promote_batch_to_gpu(vp(victims), vp(counts), n, vp(counts, 16)) == 0
+        h_counts.copy_(counts, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    dev_us, wall_us = [], []
+    for _ in range(max(args.steps, 10)):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record()
+        step()
+        e1.record()
+        e1.synchronize()
+        wall_us.append((time.perf_counter() - t0) * 1e6)
+        dev_us.append(e0.elapsed_time(e1) * 1e3)
+    c = h_counts.tolist()
+    assert c[0] == k and c[2] == k and c[4] == k, c
+    L.orchkv_request_destroy(ctx)
+    tm.close()
+    L.orchkv_shutdown()
+    out = {"workload": w["name"], "blocks": n, "evicted_and_promoted": k,
+           "us_per_step_device": round(statistics.median(dev_us), 1),
+           "us_per_step_wall": round(statistics.median(wall_us), 1),
+           "steps": len(dev_us),
+           "note": "median over steps; wall time includes the host waiting for the counts"}
+    if not args.no_cpu_baseline:
+        out["cpu_baseline"] = _c1_reference(probs, kv, history, k)
+    return out
+
+
+def _c1_reference(probs, kv, history, k):
+    """The reference's own path for the step above, on one host core
+    (oracle/_ref: its scheduler and data plane compiled from its sources)."""
+    from oracle import oracle as O
+    if not O.ref_available():
+        return None
+    w = C1
+    nb = w["T"] // w["tpb"]
+    n = w["L"] * w["Hkv"] * nb
+    slab = w["tpb"] * w["D"] * 2 * 2
+    R = O.ref()
+    rtm = O.RefTM(tracker_cap=4096, max_blocks=8192, ema_lambda=0.9, alpha=0.5, beta=0.3,
+                  gamma=0.2, recency_tau=50.0, cooldown_sec=0.0)
+    rtm.register_range(n)
+    ids = np.arange(n, dtype=np.uint64)
+    for sl, wt in history:
+        if sl:
+            rtm.report_batch(ids[sl], np.asarray(wt, np.float32))
+        rtm.step_done()
+    assert R.ref_api_init(0, (n + 64) * slab, n * slab, w["tpb"], w["D"], 0, 4, nb + 8,
+                          b"/dev/shm/orchkv_ref_c1") == 0
+    ctx = R.ref_api_request_create(0, w["L"], w["Hkv"])
+    for layer in range(w["L"]):
+        assert R.ref_api_prefill(ctx, layer, kv[layer, 0].ctypes.data, kv[layer, 1].ctypes.data,
+                                 w["T"]) == 0
+    vict = np.zeros(k, np.uint64)
+    times = []
+    for s in range(6):
+        t0 = time.perf_counter()
+        mass = O.score_blocks(probs, w["Hq"], w["Hkv"], w["tpb"]).reshape(-1)
+        c = R.ref_arm_sched_step(rtm.h, ids, mass.copy(), n, 1.0, k, vict, np.zeros(3))
+        v = vict[:c].astype(np.int64)
+        lhb = np.stack([v // (w["Hkv"] * nb), (v // nb) % w["Hkv"], v % nb], 1).astype(np.uint32)
+        tmp = np.zeros(2)
+        assert R.ref_api_migrate_list(ctx, lhb.reshape(-1), c, 0, tmp) == 0
+        assert R.ref_api_migrate_list(ctx, lhb.reshape(-1), 0, c, tmp) == 0
+        if s:
+            times.append((time.perf_counter() - t0) * 1e6)
+    R.ref_api_request_destroy(ctx)
+    R.ref_api_shutdown()
+    rtm.close()
+    return {"kind": "reference", "cores": 1, "us_per_step": round(statistics.median(times), 1),
+            "sample": "the whole configuration (one request), median of 5 steps after one"}
+
+
 def score_bytes(wl):
     """Algorithmic bytes of one scoring launch: probabilities read once, block
     id table read, per-block tracker read (active, sum, max) and written (sum,
@@ -1151,6 +1315,8 @@ def run_ours(args, rank, world, local_rank):
         mx = run_multiplexed(args, torch, okv, rank, world, dist if world > 1 else None, link)
         if line is not None:
             line["multiplexed"] = mx
+    if world == 1 and not args.no_cpu_step:
+        line["cpu_step"] = run_cpu_step(args, torch, okv)
     if comm:
         okv.lib().orchkv_comm_destroy(comm)
     if world > 1:
@@ -1433,6 +1599,8 @@ def main():
                     help="skip the KV-head-sharded Llama-3-8B-shaped pool")
     ap.add_argument("--sharded-requests", type=int, default=SH["B"],
                     help="requests of the sharded pool (the same at every N)")
+    ap.add_argument("--no-cpu-step", action="store_true",
+                    help="skip the one-request CPU-runnable step (one GPU only)")
     ap.add_argument("--no-multiplexed", action="store_true",
                     help="skip the Mistral-7B-shaped time-multiplexed pool")
     ap.add_argument("--multiplexed-requests", type=int, default=MX["B"],
