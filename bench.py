@@ -165,6 +165,7 @@ class Workload:
         self.tm = okv.Manager(tracker_cap=1 << 21, max_blocks=1 << 22, ema_lambda=0.9,
                               alpha=0.5, beta=0.3, gamma=0.2, recency_tau=50.0)
         assert L.orchkv_attach_scheduler(self.tm.ref) == 0
+        assert L.tm_profile_reports(self.tm.ref, 1) == 0      # the score kernel's own time
         if comm:
             assert L.tm_set_comm(self.tm.ref, comm) == 0
         g = torch_.Generator(device="cuda").manual_seed(seed + 1000 * rank)
@@ -768,6 +769,256 @@ def run_multiplexed(args, torch, okv, rank, world, dist, link):
 
 
 # ---------------------------------------------------------------------------
+# Llama-3-70B-shaped three tiers: HBM 20%, pinned DRAM 50%, files 30%
+# ---------------------------------------------------------------------------
+
+TT = dict(name="llama-3-70b-three-tier", B=1, L=80, Hq=64, Hkv=8, D=128, T=131072, tpb=64,
+          gpu=0.2, dram=0.5)
+
+
+class ThreeTierWorkload:
+    """The Llama-3-70B-shaped pool over three tiers (80 layers, 64 query / 8
+    KV heads, d_head 128, fp16, 64-token blocks, 131,072-token context), KV
+    heads split over the ranks.  A step scores (logits N(0, 2), softmax),
+    classifies, sends the global coldest 30% two hops to the file tier
+    (orchkv_evict_cold_batch: the reference's file layout, 1 MiB runs, the
+    runs spread over the IO workers) and the next coldest 50% to pinned DRAM,
+    leaving 20% in HBM.  The restore (untimed) promotes the DRAM blocks,
+    reads the file blocks back into DRAM and promotes them too."""
+
+    def __init__(self, torch, okv, rank, world, comm, requests, seed=0):
+        w = TT
+        self.t, self.L = torch, okv.lib()
+        self.rank, self.world = rank, world
+        self.B, self.Ly, self.D, self.T, self.tpb = requests, w["L"], w["D"], w["T"], w["tpb"]
+        self.G = w["Hq"] // w["Hkv"]
+        self.hkv = w["Hkv"] // world
+        self.hq = self.hkv * self.G
+        self.nb = self.T // self.tpb
+        self.rows = self.B * self.Ly
+        self.n_local = self.rows * self.hkv * self.nb
+        self.n_total = self.rows * w["Hkv"] * self.nb
+        self.slab = self.tpb * self.D * 2 * 2
+        self.k_file = int((1.0 - w["gpu"] - w["dram"]) * self.n_total)
+        self.k_dram = int(w["dram"] * self.n_total)
+        cap = 1
+        while cap < self.n_local + 1024:
+            cap <<= 1
+        self.cap = cap
+        self.base = f"/dev/shm/orchkv_three_tier_r{rank}"
+        cfg = okv.make_config(gpu_pool_bytes=(self.n_local + 1024) * self.slab,
+                              dram_pool_bytes=(int(0.6 * self.n_local) + 4096) * self.slab,
+                              tokens_per_block=self.tpb, d_head=self.D, dtype=0,
+                              device=torch.cuda.current_device(),
+                              max_blocks_per_head=self.nb + 8)
+        cfg.orchfs_base_dir = self.base.encode()
+        cfg.orchfs_io_workers = 8
+        ext = okv.OrchkvConfigExt()
+        ext.max_blocks = cap
+        L = self.L
+        rc = L.orchkv_init_ext(C.byref(cfg), C.byref(ext))
+        if rc != 0:
+            raise RuntimeError(f"orchkv_init_ext (three-tier pool) failed: {rc}")
+        self.stream = torch.cuda.current_stream()
+        L.orchkv_set_stream(C.c_void_p(self.stream.cuda_stream))
+        self.tm = okv.Manager(tracker_cap=cap, max_blocks=2 * cap, ema_lambda=0.9, alpha=0.5,
+                              beta=0.3, gamma=0.2, recency_tau=50.0)
+        assert L.orchkv_attach_scheduler(self.tm.ref) == 0
+        if comm:
+            assert L.tm_set_comm(self.tm.ref, comm) == 0
+        g = torch.Generator(device="cuda").manual_seed(seed + 13 * rank + 5)
+        self.ctxs = [L.orchkv_request_create(rank * 1000 + i, self.Ly, self.hkv)
+                     for i in range(self.B)]
+        assert all(self.ctxs)
+        for c in self.ctxs:
+            for layer in range(self.Ly):
+                kv = torch.randn(2, self.hkv, self.T, self.D, generator=g, device="cuda",
+                                 dtype=torch.float16)
+                assert L.orchkv_prefill(c, layer, kv[0].data_ptr(), kv[1].data_ptr(), self.T) == 0
+        del kv
+        self.arr = (C.c_void_p * self.B)(*self.ctxs)
+        self.ids = torch.empty(self.n_local, dtype=torch.int32, device="cuda")
+        assert L.orchkv_block_id_table(self.arr, self.B, self.T, C.c_void_p(self.ids.data_ptr())) == 0
+        # block id -> (request, layer, head, block) for the file tier's lists
+        ids_h = self.ids.cpu().numpy().view(np.uint32).astype(np.int64)
+        self.where = np.full(cap, -1, np.int64)
+        self.where[ids_h] = np.arange(self.n_local)
+        self.probs = torch.empty(self.rows, self.hq, self.T, device="cuda")
+        for j in range(self.hkv):
+            gg = torch.Generator(device="cuda").manual_seed(seed * 1000 + 900 + rank * self.hkv + j)
+            for r0 in range(0, self.rows, 16):
+                x = torch.randn(min(16, self.rows - r0), self.G, self.T, generator=gg,
+                                device="cuda") * 2.0
+                self.probs[r0:r0 + 16, j * self.G:(j + 1) * self.G] = torch.softmax(x, -1)
+        del x
+        self.victims = torch.empty(cap, dtype=torch.int32, device="cuda")
+        self.pref = torch.empty(cap, dtype=torch.int32, device="cuda")
+        self.counts = torch.zeros(16, dtype=torch.int32, device="cuda")
+        self.h_counts = torch.zeros(16, dtype=torch.int32).pin_memory()
+        self.files = []                   # per request: the lhb list sent to the file tier
+        self.ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        torch.cuda.synchronize()
+
+    def _ptr(self, t, off=0):
+        return C.c_void_p(t.data_ptr() + off)
+
+    def _lhb_by_request(self, ids):
+        pos = self.where[ids]
+        req, rem = np.divmod(pos, self.Ly * self.hkv * self.nb)
+        lay, rem = np.divmod(rem, self.hkv * self.nb)
+        head, blk = np.divmod(rem, self.nb)
+        out = []
+        for b in range(self.B):
+            m = req == b
+            out.append(np.ascontiguousarray(np.stack([lay[m], head[m], blk[m]], 1)
+                                            .astype(np.uint32).reshape(-1)))
+        return out
+
+    def step(self):
+        L, tm, ev = self.L, self.tm.ref, self.ev
+        ev[0].record()
+        assert L.tm_report_attn_probs(tm, self._ptr(self.probs), self.rows, self.hq, self.hkv,
+                                      self.T, self.tpb, None, self._ptr(self.ids)) == 0
+        assert L.tm_step_and_classify(tm) == 0
+        assert L.tm_select_victims(tm, self.k_file, self._ptr(self.victims),
+                                   self._ptr(self.counts)) == 0
+        ev[1].record()
+        # the coldest 30%: GPU -> (pinned staging) -> the request's file
+        n = int(self.counts[0].item())
+        vic = self.victims[:n].cpu().numpy().view(np.uint32).astype(np.int64)
+        self.files = self._lhb_by_request(vic)
+        res = (C.c_uint32 * 2)()
+        self.file_moved = 0
+        for c, lhb in zip(self.ctxs, self.files):
+            if len(lhb):
+                assert L.orchkv_evict_cold_batch(c, lhb.ctypes.data, len(lhb) // 3, res) == 0
+                self.file_moved += res[0]
+        ev[2].record()
+        # the next coldest 50%: GPU -> pinned DRAM
+        assert L.tm_select_victims(tm, self.k_dram, self._ptr(self.victims),
+                                   self._ptr(self.counts)) == 0
+        assert L.orchkv_evict_batch_to_dram(self._ptr(self.victims), self._ptr(self.counts),
+                                            self.cap, self._ptr(self.counts, 8)) == 0
+        ev[3].record()
+        self.h_counts.copy_(self.counts, non_blocking=True)
+        ev[4].record()
+
+    def restore(self):
+        L, tm = self.L, self.tm.ref
+
+        def promote_dram():
+            assert L.tm_select_prefetch(tm, self.cap * self.world, 0.0, 0.0, self._ptr(self.pref),
+                                        self._ptr(self.counts, 32)) == 0
+            assert L.orchkv_promote_batch_to_gpu(self._ptr(self.pref), self._ptr(self.counts, 32),
+                                                 self.cap, self._ptr(self.counts, 36)) == 0
+        promote_dram()
+        res = (C.c_uint32 * 2)()
+        for c, lhb in zip(self.ctxs, self.files):
+            if len(lhb):
+                assert L.orchkv_promote_batch_from_storage(c, lhb.ctypes.data, len(lhb) // 3,
+                                                           res) == 0
+        promote_dram()
+        self.t.cuda.synchronize()
+
+    def checksums(self):
+        o = self.t.empty(self.n_local, dtype=self.t.int64, device="cuda")
+        tier = self.t.empty(self.n_local, dtype=self.t.uint8, device="cuda")
+        assert self.L.orchkv_block_checksums(self._ptr(self.ids), self.n_local, self._ptr(o),
+                                             self._ptr(tier)) == 0
+        assert self.L.orchkv_sync() == 0
+        return o.cpu(), tier.cpu()
+
+    def phases(self):
+        e = self.ev
+        names = ["score+select", "two-hop to files", "evict to dram", "readback"]
+        return {n: e[i].elapsed_time(e[i + 1]) for i, n in enumerate(names)}
+
+    def close(self):
+        L = self.L
+        for c in self.ctxs:
+            L.orchkv_request_destroy(c)
+        self.tm.close()
+        L.orchkv_shutdown()
+        try:
+            os.rmdir(self.base)
+        except OSError:
+            pass
+
+
+def run_three_tier(args, torch, okv, rank, world, comm, dist):
+    """The three-tier pool: W warm-up and K timed steps (wall time with a
+    barrier and synchronize around each, as the step's file IO runs on host
+    threads; max over ranks), each followed by the untimed restore; every
+    block's checksum after the last restore equals its checksum before the
+    first step."""
+    if TT["Hkv"] % world:
+        return {"skipped": f"{TT['Hkv']} KV heads do not split over {world} ranks"}
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    tw = ThreeTierWorkload(torch, okv, rank, world, comm, args.three_tier_requests)
+    before, tier0 = tw.checksums()
+    for _ in range(max(1, min(args.warmup, 2))):
+        tw.step()
+        tw.restore()
+    ms, ph, moved_file, moved_dram = [], {}, 0, 0
+    for _ in range(args.steps):
+        barrier()
+        t0 = time.perf_counter()
+        tw.step()
+        torch.cuda.synchronize()
+        barrier()
+        ms.append((time.perf_counter() - t0) * 1e3)
+        for k, v in tw.phases().items():
+            ph.setdefault(k, []).append(v)
+        moved_file += tw.file_moved
+        moved_dram += tw.h_counts.tolist()[2]
+        tw.restore()
+    after, tier1 = tw.checksums()
+    intact = bool(torch.equal(before, after) and bool((tier0 == 0).all()) and
+                  bool((tier1 == 0).all()))
+    phases = {k: sum(v) / len(v) for k, v in ph.items()}
+    t = torch.tensor([sum(ms) / len(ms), moved_file / args.steps, moved_dram / args.steps,
+                      float(intact), phases["two-hop to files"]], dtype=torch.float64,
+                     device="cuda")
+    if world > 1:
+        allv = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(allv, t)
+        allv = [x.tolist() for x in allv]
+    else:
+        allv = [t.tolist()]
+    out = None
+    if rank == 0:
+        ms_max = max(r[0] for r in allv)
+        f_tot, d_tot = sum(r[1] for r in allv), sum(r[2] for r in allv)
+        out = {
+            "workload": TT["name"], "requests": tw.B, "context": tw.T, "layers": tw.Ly,
+            "q_heads": TT["Hq"], "kv_heads": TT["Hkv"], "kv_heads_per_gpu": tw.hkv,
+            "d_head": tw.D, "tokens_per_block": tw.tpb, "dtype": "fp16",
+            "blocks_total": tw.n_total, "pool_gib_total": round(tw.n_total * tw.slab / 2**30, 2),
+            "tiers": {"gpu": TT["gpu"], "dram": TT["dram"], "files": round(1 - TT["gpu"] - TT["dram"], 2)},
+            "sample": f"{tw.B} of the configuration's 16 requests (host RAM for the pinned DRAM "
+                      f"tier and the RAM-backed files at one GPU); the same at every N",
+            "file_tier": f"{tw.base} (tmpfs), 8 IO workers",
+            "steps": args.steps, "ms_per_step": round(ms_max, 2),
+            "value": round((f_tot + d_tot) / (ms_max * 1e-3), 1),
+            "unit": "migrated blocks/s (to files + to DRAM, all ranks), wall-timed",
+            "scaling": "strong (fixed total pool)",
+            "blocks_to_files_per_step": int(f_tot), "blocks_to_dram_per_step": int(d_tot),
+            "file_write_gbs_per_rank": [round(r[1] * tw.slab / (r[4] * 1e-3) / 1e9, 2)
+                                        for r in allv],
+            "phases_ms_rank0": {k: round(v, 3) for k, v in phases.items()},
+            "round_trip_checksums_equal": all(bool(r[3]) for r in allv),
+        }
+    tw.close()
+    return out
+
+
+# ---------------------------------------------------------------------------
 # The CPU-runnable scheduler step (one request) as a latency figure
 # ---------------------------------------------------------------------------
 
@@ -1090,7 +1341,7 @@ def run_ours(args, rank, world, local_rank):
         wl.restore()
     # timed: K steps, each bracketed by barrier + synchronize; the restore of
     # the DRAM-resident remainder runs outside the brackets
-    step_ms, phase_acc, score_ms = [], {}, []
+    step_ms, phase_acc, score_ms, report_pass_ms = [], {}, [], []
     pack_ms_acc, pack_bytes_acc = [], 0
     unpack_ms_acc, unpack_bytes_acc = [], 0
     migrated = 0
@@ -1115,7 +1366,10 @@ def run_ours(args, rank, world, local_rank):
             ph = wl.phases()
             for k, v in ph.items():
                 phase_acc.setdefault(k, []).append(v)
-            score_ms.append(ph["score"])
+            mk, sc, od = C.c_float(), C.c_float(), C.c_float()
+            assert wl.L.tm_last_report_times(wl.tm.ref, C.byref(mk), C.byref(sc), C.byref(od)) == 0
+            score_ms.append(sc.value)
+            report_pass_ms.append((mk.value, od.value))
             c = wl.h_counts.tolist()
             migrated += c[2] + c[4]
             launches_timed += okv.lib().orchkv_kernel_launches() - la
@@ -1246,6 +1500,14 @@ def run_ours(args, rank, world, local_rank):
                 "traffic": round(SCORE_TRAFFIC_PER_REQUEST * WL["B"]),
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
                                   "8-request launch, scaled by requests"},
+            "report_passes": {
+                "duplicate_slot_pass_ms": round(sum(x[0] for x in report_pass_ms)
+                                                / len(report_pass_ms), 4),
+                "ordered_pass_ms": round(sum(x[1] for x in report_pass_ms)
+                                         / len(report_pass_ms), 4),
+                "note": "tm_report_attn_probs = duplicate-slot pass + score kernel + ordered "
+                        "pass (returns at once when no slot repeats); the score phase covers "
+                        "all three"},
             "hook": hook,
             "pack": {"kernel": "evict pack (HBM gather -> staging)",
                      "ms": round(pk_ms.value, 4), "bytes": pk_bytes.value,
@@ -1315,6 +1577,11 @@ def run_ours(args, rank, world, local_rank):
         mx = run_multiplexed(args, torch, okv, rank, world, dist if world > 1 else None, link)
         if line is not None:
             line["multiplexed"] = mx
+    if not args.no_three_tier:
+        tt = run_three_tier(args, torch, okv, rank, world, comm, dist if world > 1 else None)
+        if line is not None:
+            line["three_tier"] = tt
+        torch.cuda.empty_cache()
     if world == 1 and not args.no_cpu_step:
         line["cpu_step"] = run_cpu_step(args, torch, okv)
     if comm:
@@ -1599,6 +1866,10 @@ def main():
                     help="skip the KV-head-sharded Llama-3-8B-shaped pool")
     ap.add_argument("--sharded-requests", type=int, default=SH["B"],
                     help="requests of the sharded pool (the same at every N)")
+    ap.add_argument("--no-three-tier", action="store_true",
+                    help="skip the Llama-3-70B-shaped three-tier pool")
+    ap.add_argument("--three-tier-requests", type=int, default=TT["B"],
+                    help="requests of the three-tier pool (the same at every N)")
     ap.add_argument("--no-cpu-step", action="store_true",
                     help="skip the one-request CPU-runnable step (one GPU only)")
     ap.add_argument("--no-multiplexed", action="store_true",

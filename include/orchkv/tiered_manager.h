@@ -233,6 +233,14 @@ int tm_report_attn_probs(tiered_manager_t *m, const float *probs,
                          uint32_t row_len, uint32_t tokens_per_block,
                          const uint32_t *lens, const uint32_t *block_ids);
 
+/* B200: device timing of tm_report_attn_probs, opt-in (on != 0 starts it):
+ * tm_last_report_times gives the last call's duplicate-slot pass, score
+ * kernel and ordered pass in ms (waiting for them); ORCHKV_ERR_STATE while
+ * profiling is off.  No counterpart in the reference. */
+int tm_profile_reports(tiered_manager_t *m, int on);
+int tm_last_report_times(tiered_manager_t *m, float *mark_ms, float *score_ms,
+                         float *ordered_ms);
+
 /* B200: upload a host input of a later report call now, on the manager's
  * own copy stream, so the copy overlaps whatever runs meanwhile (the current
  * step's migrations, say).  The next tm_report_attn_probs /

@@ -183,6 +183,8 @@ _SIGS = {
     "tm_report_attn_probs": (i32, [P(TieredManager), vp, u32, u32, u32, u32, u32, vp, vp]),
     "tm_report_attn_batch_dev": (i32, [P(TieredManager), vp, vp, u32]),
     "tm_stage_input_async": (i32, [P(TieredManager), vp, C.c_size_t]),
+    "tm_profile_reports": (i32, [P(TieredManager), i32]),
+    "tm_last_report_times": (i32, [P(TieredManager), P(f32), P(f32), P(f32)]),
     "tm_report_attn_ranges": (i32, [P(TieredManager), vp, u32, u32, vp, vp, vp, u32]),
     "tm_report_attn_blockmean": (i32, [P(TieredManager), vp, i32, u32, u32, u32, u32, u32, vp,
                                        vp]),

@@ -18,6 +18,8 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
+#include <thread>
 #include <unordered_set>
 
 #include <map>
@@ -1423,51 +1425,101 @@ int lookup_lhb(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t n, std::vect
     return ORCHKV_OK;
 }
 
+// One pwritev / preadv run: k buffers at consecutive file offsets from off0,
+// resumed after short transfers (the iovecs are consumed).
+bool io_run(bool write, int fd, iovec *v, int cnt, off_t off0)
+{
+    size_t done = 0, left = 0;
+    for (int j = 0; j < cnt; j++) left += v[j].iov_len;
+    while (left > 0) {
+        const ssize_t r = write ? pwritev(fd, v, cnt, off0 + (off_t)done)
+                                : preadv(fd, v, cnt, off0 + (off_t)done);
+        if (r < 0) {
+            if (errno == EINTR) continue;
+            return false;
+        }
+        if (r == 0) return false;      // short read: a slab that was never written
+        done += (size_t)r;
+        left -= (size_t)r;
+        size_t adv = (size_t)r;
+        while (cnt > 0 && adv >= v->iov_len) { adv -= v->iov_len; v++; cnt--; }
+        if (cnt > 0 && adv) {
+            v->iov_base = (char *)v->iov_base + adv;
+            v->iov_len -= adv;
+        }
+    }
+    return true;
+}
+
+struct IoRun {
+    off_t off;           // file offset of the first buffer
+    size_t first, n;     // iovecs [first, first + n)
+};
+
+// Runs of a batch spread over the configured IO workers (the reference's
+// orchfs_io_workers, its IO worker pool size, src/tiered_store/io_worker.c:
+// 52-133): each worker takes the next run until all are done or one fails.
+// Runs write disjoint file ranges and disjoint buffers, so their order does
+// not matter.  Small batches stay on the calling thread.
+bool io_runs(bool write, int fd, std::vector<iovec> &iov, const std::vector<IoRun> &runs)
+{
+    std::atomic<size_t> next{0};
+    std::atomic<bool> ok{true};
+    auto work = [&]() {
+        for (size_t r = next++; r < runs.size() && ok.load(); r = next++)
+            if (!io_run(write, fd, iov.data() + runs[r].first, (int)runs[r].n, runs[r].off))
+                ok = false;
+    };
+    size_t workers = g.cfg.orchfs_io_workers > 0 ? (size_t)g.cfg.orchfs_io_workers : 1;
+    if (workers > 64) workers = 64;
+    if (workers > runs.size()) workers = runs.size();
+    std::vector<std::thread> pool;
+    for (size_t t = 1; t < workers; t++) pool.emplace_back(work);
+    work();
+    for (auto &t : pool) t.join();
+    return ok.load();
+}
+
+// Runs of consecutive file offsets (up to kStorageRunBytes each) over
+// entries sorted by offset; bufs[j] is entry j's buffer.
+void plan_runs(const std::vector<off_t> &offs, const std::vector<char *> &bufs, size_t slab,
+               std::vector<iovec> &iov, std::vector<IoRun> &runs)
+{
+    size_t per_call = kStorageRunBytes / slab;
+    if (per_call < 1) per_call = 1;
+    if (per_call > (size_t)IOV_MAX) per_call = IOV_MAX;
+    iov.resize(offs.size());
+    runs.clear();
+    for (size_t i = 0; i < offs.size();) {
+        size_t k = 0;
+        while (i + k < offs.size() && k < per_call && offs[i + k] == offs[i] + (off_t)(k * slab)) {
+            iov[i + k].iov_base = bufs[i + k];
+            iov[i + k].iov_len = slab;
+            k++;
+        }
+        runs.push_back(IoRun{offs[i], i, k});
+        i += k;
+    }
+}
+
 // Write (evict) or read (promote) entries between their DRAM slabs and the
 // request's file: sorted by file offset, consecutive offsets go out in one
-// pwritev / preadv of up to kStorageRunBytes, straight from / into the slabs.
+// pwritev / preadv of up to kStorageRunBytes, straight from / into the
+// slabs, the runs spread over the IO workers.
 bool storage_io(bool write, int fd, std::vector<LhbEntry> e)
 {
     std::sort(e.begin(), e.end(), [](const LhbEntry &a, const LhbEntry &b) { return a.off < b.off; });
     const size_t slab = g.p.slab;
-    size_t per_call = kStorageRunBytes / slab;
-    if (per_call < 1) per_call = 1;
-    if (per_call > (size_t)IOV_MAX) per_call = IOV_MAX;
-    std::vector<iovec> iov(per_call);
-    size_t i = 0;
-    while (i < e.size()) {
-        size_t k = 0;
-        const off_t off0 = e[i].off;
-        while (i + k < e.size() && k < per_call &&
-               e[i + k].off == off0 + (off_t)(k * slab)) {
-            iov[k].iov_base = g.p.dram_base + (size_t)e[i + k].slab * slab;
-            iov[k].iov_len = slab;
-            k++;
-        }
-        // move all k slabs, resuming after short transfers
-        size_t done = 0, left = k * slab;
-        iovec *v = iov.data();
-        int cnt = (int)k;
-        while (left > 0) {
-            const ssize_t r = write ? pwritev(fd, v, cnt, off0 + (off_t)done)
-                                    : preadv(fd, v, cnt, off0 + (off_t)done);
-            if (r < 0) {
-                if (errno == EINTR) continue;
-                return false;
-            }
-            if (r == 0) return false;      // short read: a slab that was never written
-            done += (size_t)r;
-            left -= (size_t)r;
-            size_t adv = (size_t)r;
-            while (cnt > 0 && adv >= v->iov_len) { adv -= v->iov_len; v++; cnt--; }
-            if (cnt > 0 && adv) {
-                v->iov_base = (char *)v->iov_base + adv;
-                v->iov_len -= adv;
-            }
-        }
-        i += k;
+    std::vector<off_t> offs(e.size());
+    std::vector<char *> bufs(e.size());
+    for (size_t j = 0; j < e.size(); j++) {
+        offs[j] = e[j].off;
+        bufs[j] = g.p.dram_base + (size_t)e[j].slab * slab;
     }
-    return true;
+    std::vector<iovec> iov;
+    std::vector<IoRun> runs;
+    plan_runs(offs, bufs, slab, iov, runs);
+    return io_runs(write, fd, iov, runs);
 }
 
 // Upload the committed entries (list order) and apply them on the device.
@@ -1629,17 +1681,18 @@ int orchkv_evict_cold_batch(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t
         rc = launch_pack(g.p, gp, h_cold_dev, 0, k, g.ss, 0, g.stream);
         if (rc) return rc;
         OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
-        // write the chunk: consecutive file offsets in one pwritev each
-        size_t i = 0;
-        while (i < k) {
-            size_t m = 1;
-            while (i + m < k && io[c0 + i + m].off == io[c0 + i].off + (off_t)(m * slab) &&
-                   m * slab < kStorageRunBytes)
-                m++;
-            if (!full_io(true, ctx->fd, g.h_cold + i * slab, m * slab, io[c0 + i].off))
-                return ORCHKV_ERR_IO;
-            i += m;
+        // write the chunk: consecutive file offsets in one pwritev each, the
+        // runs spread over the IO workers
+        std::vector<off_t> offs(k);
+        std::vector<char *> bufs(k);
+        for (uint32_t j = 0; j < k; j++) {
+            offs[j] = io[c0 + j].off;
+            bufs[j] = g.h_cold + (size_t)j * slab;
         }
+        std::vector<iovec> iov;
+        std::vector<IoRun> runs;
+        plan_runs(offs, bufs, slab, iov, runs);
+        if (!io_runs(true, ctx->fd, iov, runs)) return ORCHKV_ERR_IO;
     }
     rc = storage_commit(e, 2);
     if (rc) return rc;

@@ -131,6 +131,7 @@ static void free_device(TmImpl *t)
     }
     if (t->early_copy) cudaStreamDestroy(t->early_copy);
     t->early_copy = nullptr;
+    for (auto &e : t->rep_ev) if (e) { cudaEventDestroy(e); e = nullptr; }
     cudaFreeHost(t->m_hot);
     cudaFreeHost(t->m_heat);
     cudaFreeHost(t->m_cact);
@@ -1024,13 +1025,43 @@ int tm_report_attn_probs(tiered_manager_t *m, const float *probs, uint32_t n_row
     if (rc) return rc;
     t->mirror_dirty = true;
     const uint32_t *ids = (const uint32_t *)in[2];
+    auto mark = [&](int i) { if (t->rep_prof) cudaEventRecord(t->rep_ev[i], t->stream); };
+    mark(0);
     rc = launch_alias_mark(ids, (uint32_t)n_ent, t->d, o, t->stream);
+    mark(1);
     if (!rc) rc = launch_score((const float *)in[0], n_rows, n_q_heads, n_kv_heads, row_len, tpb,
                                (const uint32_t *)in[1], ids, t->d, t->step, o, t->stream);
+    mark(2);
     if (!rc) rc = launch_report_ordered(o.ids_eff, o.mass, (uint32_t)n_ent, t->d, t->step, o,
                                         t->stream);
+    mark(3);
     const int rr = release_staged(t);
     return rc ? rc : rr;
+}
+
+int tm_profile_reports(tiered_manager_t *m, int on)
+{
+    TmImpl *t = tm_impl(m);
+    if (!t) return ORCHKV_ERR_INVALID;
+    std::lock_guard<std::mutex> g(t->mu);
+    for (auto &e : t->rep_ev)
+        if (!e) OKV_CUDA_TRY(cudaEventCreate(&e));
+    t->rep_prof = on != 0;
+    return ORCHKV_OK;
+}
+
+int tm_last_report_times(tiered_manager_t *m, float *mark_ms, float *score_ms, float *ordered_ms)
+{
+    TmImpl *t = tm_impl(m);
+    if (!t) return ORCHKV_ERR_INVALID;
+    std::lock_guard<std::mutex> g(t->mu);
+    if (!t->rep_prof) return ORCHKV_ERR_STATE;
+    OKV_CUDA_TRY(cudaEventSynchronize(t->rep_ev[3]));
+    float x = 0.f;
+    if (mark_ms) { OKV_CUDA_TRY(cudaEventElapsedTime(&x, t->rep_ev[0], t->rep_ev[1])); *mark_ms = x; }
+    if (score_ms) { OKV_CUDA_TRY(cudaEventElapsedTime(&x, t->rep_ev[1], t->rep_ev[2])); *score_ms = x; }
+    if (ordered_ms) { OKV_CUDA_TRY(cudaEventElapsedTime(&x, t->rep_ev[2], t->rep_ev[3])); *ordered_ms = x; }
+    return ORCHKV_OK;
 }
 
 int tm_stage_input_async(tiered_manager_t *m, const void *host, size_t bytes)

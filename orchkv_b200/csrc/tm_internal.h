@@ -122,6 +122,11 @@ struct TmImpl {
     uint32_t report_epoch = 0;
     char *report_scratch = nullptr;    // per-entry ids and masses of an ordered call
     size_t report_scratch_cap = 0;
+    // opt-in device timing of tm_report_attn_probs' launches (tm_profile_reports):
+    // before the duplicate-slot pass, before the score kernel, after it, after
+    // the ordered pass
+    bool rep_prof = false;
+    cudaEvent_t rep_ev[4] = {};
     // inputs staged ahead of their report (two slots, consumed oldest first)
     StagedInput early[2];
     cudaStream_t early_copy = nullptr;
