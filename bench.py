@@ -482,7 +482,8 @@ def run_sharded(args, torch, okv, rank, world, comm, dist, link_d2h):
     if comm:
         L.orchkv_comm_exchange_time(comm, C.byref(C.c_float()), C.byref(C.c_uint32()))
     step_ms, ph_acc, evicted, xch = [], {}, 0, [0.0, 0]
-    for _ in range(args.steps):
+    n_steps = min(args.steps, 5)          # a secondary workload: a few steps keep the run short
+    for _ in range(n_steps):
         barrier()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()
@@ -512,8 +513,8 @@ def run_sharded(args, torch, okv, rank, world, comm, dist, link_d2h):
     phases = {k: sum(v) / len(v) for k, v in ph_acc.items()}
     mean_ms = sum(step_ms) / len(step_ms)
     ev_ms = phases["evict"]
-    d2h = evicted / args.steps * sw.slab / (ev_ms * 1e-3) / 1e9
-    t = torch.tensor([mean_ms, evicted / args.steps, d2h, xch[0] / args.steps, link_d2h],
+    d2h = evicted / n_steps * sw.slab / (ev_ms * 1e-3) / 1e9
+    t = torch.tensor([mean_ms, evicted / n_steps, d2h, xch[0] / n_steps, link_d2h],
                      dtype=torch.float64, device="cuda")
     if world > 1:
         allv = [torch.zeros_like(t) for _ in range(world)]
@@ -541,7 +542,7 @@ def run_sharded(args, torch, okv, rank, world, comm, dist, link_d2h):
             "gpu_capacity": SH["capacity"], "evict_per_step_total": sw.k_global,
             "sample": f"{sw.B} of the configuration's 64 requests (host RAM for the pinned "
                       f"DRAM tier at every N); the same {sw.B} requests at every N",
-            "steps": args.steps, "ms_per_step": round(ms_max, 3),
+            "steps": n_steps, "ms_per_step": round(ms_max, 3),
             "value": round(moved / (ms_max * 1e-3), 1), "unit": "evicted blocks/s (all ranks)",
             "scaling": "strong (fixed total pool)",
             "per_rank_evict_d2h_gbs": [round(r[2], 1) for r in allv],
@@ -712,10 +713,11 @@ def run_multiplexed(args, torch, okv, rank, world, dist, link):
 
     mw = MultiplexedWorkload(torch, okv, rank, world, args.multiplexed_requests)
     before = mw.checksums()
-    for _ in range(args.warmup):
+    for _ in range(min(args.warmup, 4)):
         mw.step()
     step_ms, ph, moved = [], {}, 0
-    for _ in range(args.steps):
+    n_steps = min(args.steps, 8)          # a secondary workload: two rotations at most
+    for _ in range(n_steps):
         barrier()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()
@@ -734,7 +736,7 @@ def run_multiplexed(args, torch, okv, rank, world, dist, link):
     intact = bool(torch.equal(mw.checksums(), before))
     phases = {k: sum(v) / len(v) for k, v in ph.items()}
     swap_bytes = 2 * mw.blocks_sb * mw.slab
-    t = torch.tensor([sum(step_ms) / len(step_ms), moved / args.steps, float(intact),
+    t = torch.tensor([sum(step_ms) / len(step_ms), moved / n_steps, float(intact),
                       phases["swap"], link["both"]], dtype=torch.float64, device="cuda")
     if world > 1:
         allv = [torch.zeros_like(t) for _ in range(world)]
@@ -754,7 +756,7 @@ def run_multiplexed(args, torch, okv, rank, world, dist, link):
             "pool_gib_total": round(mw.n_total * mw.slab / 2**30, 2),
             "sample": f"{mw.B} of the configuration's 256 requests (host RAM for the DRAM tier "
                       f"at one GPU); the same {mw.B} requests at every N",
-            "steps": args.steps, "ms_per_step": round(ms_max, 3),
+            "steps": n_steps, "ms_per_step": round(ms_max, 3),
             "value": round(sum(r[1] for r in allv) / (ms_max * 1e-3), 1),
             "unit": "migrated blocks/s (evicted + promoted, all ranks)",
             "scaling": "strong (fixed total pool)",
@@ -966,7 +968,8 @@ def run_three_tier(args, torch, okv, rank, world, comm, dist):
         tw.step()
         tw.restore()
     ms, ph, moved_file, moved_dram = [], {}, 0, 0
-    for _ in range(args.steps):
+    n_steps = min(args.steps, 3)          # a secondary workload: seconds per step
+    for _ in range(n_steps):
         barrier()
         t0 = time.perf_counter()
         tw.step()
@@ -982,7 +985,7 @@ def run_three_tier(args, torch, okv, rank, world, comm, dist):
     intact = bool(torch.equal(before, after) and bool((tier0 == 0).all()) and
                   bool((tier1 == 0).all()))
     phases = {k: sum(v) / len(v) for k, v in ph.items()}
-    t = torch.tensor([sum(ms) / len(ms), moved_file / args.steps, moved_dram / args.steps,
+    t = torch.tensor([sum(ms) / len(ms), moved_file / n_steps, moved_dram / n_steps,
                       float(intact), phases["two-hop to files"]], dtype=torch.float64,
                      device="cuda")
     if world > 1:
@@ -1004,7 +1007,7 @@ def run_three_tier(args, torch, okv, rank, world, comm, dist):
             "sample": f"{tw.B} of the configuration's 16 requests (host RAM for the pinned DRAM "
                       f"tier and the RAM-backed files at one GPU); the same at every N",
             "file_tier": f"{tw.base} (tmpfs), 8 IO workers",
-            "steps": args.steps, "ms_per_step": round(ms_max, 2),
+            "steps": n_steps, "ms_per_step": round(ms_max, 2),
             "value": round((f_tot + d_tot) / (ms_max * 1e-3), 1),
             "unit": "migrated blocks/s (to files + to DRAM, all ranks), wall-timed",
             "scaling": "strong (fixed total pool)",
