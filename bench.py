@@ -814,7 +814,8 @@ class ThreeTierWorkload:
                               device=torch.cuda.current_device(),
                               max_blocks_per_head=self.nb + 8)
         cfg.orchfs_base_dir = self.base.encode()
-        cfg.orchfs_io_workers = 8
+        self.io_workers = max(4, min(16, host_threads()))
+        cfg.orchfs_io_workers = self.io_workers
         ext = okv.OrchkvConfigExt()
         ext.max_blocks = cap
         L = self.L
@@ -1006,7 +1007,7 @@ def run_three_tier(args, torch, okv, rank, world, comm, dist):
             "tiers": {"gpu": TT["gpu"], "dram": TT["dram"], "files": round(1 - TT["gpu"] - TT["dram"], 2)},
             "sample": f"{tw.B} of the configuration's 16 requests (host RAM for the pinned DRAM "
                       f"tier and the RAM-backed files at one GPU); the same at every N",
-            "file_tier": f"{tw.base} (tmpfs), 8 IO workers",
+            "file_tier": f"{tw.base} (tmpfs), {tw.io_workers} IO workers",
             "steps": n_steps, "ms_per_step": round(ms_max, 2),
             "value": round((f_tot + d_tot) / (ms_max * 1e-3), 1),
             "unit": "migrated blocks/s (to files + to DRAM, all ranks), wall-timed",

@@ -90,7 +90,8 @@ struct Sys {
     SortScratch ss, ss2;
     uint32_t *h_runs = nullptr;       // pinned: run_o then run_d (evict)
     uint32_t *h_runs2 = nullptr;      // pinned: run_o then run_d (promote)
-    char *h_cold = nullptr;           // pinned, mapped: staging of batched cold evicts
+    char *h_cold = nullptr;           // pinned, mapped: staging of batched cold evicts (2 halves)
+    cudaEvent_t ev_cold[2] = {};      // each half gathered
     uint32_t *h_meta = nullptr;       // pinned
     // staged promote: copy-engine H2D on copy_in into its own ring, unpack
     // kernels on their own stream
@@ -329,6 +330,7 @@ void release_all()
     cudaFreeHost(g.h_runs2);
     if (g.h_cold) cudaFreeHost(g.h_cold);
     g.h_cold = nullptr;
+    for (auto &e : g.ev_cold) if (e) { cudaEventDestroy(e); e = nullptr; }
     g.sort_mem = nullptr;
     g.h_runs = g.h_runs2 = nullptr;
     g.scratch2 = nullptr;
@@ -1660,39 +1662,65 @@ int orchkv_evict_cold_batch(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t
                                  g.stream));
     OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
     if (g.h_ctr->d_top == 0) return ORCHKV_OK;      // no DRAM slab to pass through: TIER_FULL
-    // stage in file-offset order, in chunks of the pinned staging buffer
+    // stage in file-offset order, in chunks of the pinned staging buffer:
+    // two halves, so chunk c + 1 is gathered on the GPU while the IO workers
+    // write chunk c from the other half
     std::vector<LhbEntry> io = e;
     std::sort(io.begin(), io.end(), [](const LhbEntry &a, const LhbEntry &b) { return a.off < b.off; });
     const size_t slab = g.p.slab;
     const uint32_t chunk = g.ring_slabs;
-    if (!g.h_cold) OKV_CUDA_TRY(cudaHostAlloc((void **)&g.h_cold, (size_t)chunk * slab,
+    if (!g.h_cold) OKV_CUDA_TRY(cudaHostAlloc((void **)&g.h_cold, 2 * (size_t)chunk * slab,
                                               cudaHostAllocMapped | cudaHostAllocPortable));
+    if (!g.ev_cold[0])
+        for (auto &ev : g.ev_cold)
+            OKV_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
     char *h_cold_dev = nullptr;
     OKV_CUDA_TRY(cudaHostGetDevicePointer((void **)&h_cold_dev, g.h_cold, 0));
-    std::vector<uint32_t> src(chunk);
-    for (size_t c0 = 0; c0 < io.size(); c0 += chunk) {
+    if ((size_t)2 * chunk + 16 > g.scratch_words) return ORCHKV_ERR_INVALID;
+    std::vector<uint32_t> src[2] = {std::vector<uint32_t>(chunk), std::vector<uint32_t>(chunk)};
+    const size_t n_chunks = (io.size() + chunk - 1) / chunk;
+    auto gather = [&](size_t c) -> int {        // chunk c -> staging half c % 2
+        const size_t c0 = c * chunk, h = c % 2;
         const uint32_t k = (uint32_t)std::min<size_t>(chunk, io.size() - c0);
-        for (uint32_t j = 0; j < k; j++) src[j] = io[c0 + j].slab;
-        OKV_CUDA_TRY(cudaMemcpyAsync(g.scratch, src.data(), (size_t)4 * k,
+        for (uint32_t j = 0; j < k; j++) src[h][j] = io[c0 + j].slab;
+        OKV_CUDA_TRY(cudaMemcpyAsync(g.scratch + h * chunk, src[h].data(), (size_t)4 * k,
                                      cudaMemcpyHostToDevice, g.stream));
         MigPlan gp{};
-        gp.plan_src = g.scratch;
+        gp.plan_src = g.scratch + h * chunk;
         gp.max_n = k;
-        rc = launch_pack(g.p, gp, h_cold_dev, 0, k, g.ss, 0, g.stream);
+        const int r = launch_pack(g.p, gp, h_cold_dev + h * (size_t)chunk * slab, 0, k, g.ss, 0,
+                                  g.stream);
+        if (r) return r;
+        OKV_CUDA_TRY(cudaEventRecord(g.ev_cold[h], g.stream));
+        return ORCHKV_OK;
+    };
+    if (n_chunks) {
+        rc = gather(0);
         if (rc) return rc;
-        OKV_CUDA_TRY(cudaStreamSynchronize(g.stream));
-        // write the chunk: consecutive file offsets in one pwritev each, the
+    }
+    for (size_t c = 0; c < n_chunks; c++) {
+        const size_t c0 = c * chunk, h = c % 2;
+        const uint32_t k = (uint32_t)std::min<size_t>(chunk, io.size() - c0);
+        OKV_CUDA_TRY(cudaEventSynchronize(g.ev_cold[h]));
+        if (c + 1 < n_chunks) {                  // its half was written in the last round
+            rc = gather(c + 1);
+            if (rc) return rc;
+        }
+        // write chunk c: consecutive file offsets in one pwritev each, the
         // runs spread over the IO workers
         std::vector<off_t> offs(k);
         std::vector<char *> bufs(k);
         for (uint32_t j = 0; j < k; j++) {
             offs[j] = io[c0 + j].off;
-            bufs[j] = g.h_cold + (size_t)j * slab;
+            bufs[j] = g.h_cold + (h * (size_t)chunk + j) * slab;
         }
         std::vector<iovec> iov;
         std::vector<IoRun> runs;
         plan_runs(offs, bufs, slab, iov, runs);
-        if (!io_runs(true, ctx->fd, iov, runs)) return ORCHKV_ERR_IO;
+        if (!io_runs(true, ctx->fd, iov, runs)) {
+            cudaStreamSynchronize(g.stream);      // the next gather may still write its half
+            return ORCHKV_ERR_IO;
+        }
     }
     rc = storage_commit(e, 2);
     if (rc) return rc;
