@@ -227,3 +227,74 @@ def test_storage_batches_equal_per_block_calls(cuda):
     assert b[0] == [[4, 4], [9, 3], [5, 3]]
     for x, y in zip(b[1:], p[1:]):
         assert x == y
+
+
+def test_two_hop_batch_spanning_staging_chunks(cuda):
+    """One orchkv_evict_cold_batch of 78,643 blocks of 8 KB (614 MB, three
+    256 MB staging chunks: the next chunk is gathered while the IO workers
+    write the current one), listed in a shuffled order, then
+    orchkv_promote_batch_from_storage and a promote back to HBM: every
+    block's checksum equals its checksum before, and the counts and tiers
+    are those of the per-block calls."""
+    import orchkv_b200 as o
+    torch = cuda
+    L = o.lib()
+    Ly, H, T, tpb, d = 48, 8, 4096, 16, 128
+    nb = T // tpb
+    n = Ly * H * nb
+    slab = tpb * d * 2 * 2
+    cfg = o.make_config(gpu_pool_bytes=(n + 64) * slab, dram_pool_bytes=(n + 64) * slab,
+                        tokens_per_block=tpb, d_head=d, dtype=1, max_blocks_per_head=nb + 8)
+    cfg.orchfs_base_dir = (BASE + "_chunks").encode()
+    cfg.orchfs_io_workers = 8
+    ext = o.OrchkvConfigExt()
+    ext.max_blocks = 1 << 17
+    assert L.orchkv_init_ext(C.byref(cfg), C.byref(ext)) == 0
+    try:
+        ctx = L.orchkv_request_create(777, Ly, H)
+        g = torch.Generator(device="cuda").manual_seed(31)
+        for layer in range(Ly):
+            kv = torch.randn(2, H, T, d, generator=g, device="cuda", dtype=torch.bfloat16)
+            assert L.orchkv_prefill(ctx, layer, kv[0].data_ptr(), kv[1].data_ptr(), T) == 0
+        arr = (C.c_void_p * 1)(ctx)
+        ids = torch.empty(n, dtype=torch.int32, device="cuda")
+        assert L.orchkv_block_id_table(arr, 1, T, C.c_void_p(ids.data_ptr())) == 0
+        sums = torch.empty(n, dtype=torch.int64, device="cuda")
+        tier = torch.empty(n, dtype=torch.uint8, device="cuda")
+
+        def checksums():
+            assert L.orchkv_block_checksums(C.c_void_p(ids.data_ptr()), n,
+                                            C.c_void_p(sums.data_ptr()),
+                                            C.c_void_p(tier.data_ptr())) == 0
+            assert L.orchkv_sync() == 0
+            return sums.cpu().numpy().copy(), tier.cpu().numpy().copy()
+
+        before, t0 = checksums()
+        assert (t0 == 0).all()
+        rng = np.random.default_rng(5)
+        pick = rng.permutation(n)[: n * 4 // 5]                 # 78,643 blocks, shuffled
+        lay, rem = np.divmod(pick, H * nb)
+        head, blk = np.divmod(rem, nb)
+        lhb = np.ascontiguousarray(np.stack([lay, head, blk], 1).astype(np.uint32).reshape(-1))
+        res = (C.c_uint32 * 2)()
+        assert L.orchkv_evict_cold_batch(ctx, lhb.ctypes.data, len(pick), res) == 0
+        assert list(res) == [len(pick), 0]
+        _, t1 = checksums()
+        assert (t1[pick] == 7).all()                            # in no GPU or DRAM slab
+        assert int((t1 == 0).sum()) == n - len(pick)
+        assert L.orchkv_promote_batch_from_storage(ctx, lhb.ctypes.data, len(pick), res) == 0
+        assert list(res) == [len(pick), 0]
+        mid, t2 = checksums()
+        assert (t2[pick] == 1).all()
+        assert np.array_equal(mid[pick], before[pick])
+        dp = ids[torch.as_tensor(pick, device="cuda")].contiguous()
+        cnt = torch.zeros(2, dtype=torch.int32, device="cuda")
+        assert L.orchkv_promote_batch_to_gpu(C.c_void_p(dp.data_ptr()), None, len(pick),
+                                             C.c_void_p(cnt.data_ptr())) == 0
+        after, t3 = checksums()
+        assert cnt.tolist() == [len(pick), 0]
+        assert (t3 == 0).all()
+        assert np.array_equal(after, before)
+        assert L.orchkv_request_destroy(ctx) == 0
+    finally:
+        L.orchkv_shutdown()
