@@ -783,8 +783,8 @@ class ThreeTierWorkload:
     KV heads, d_head 128, fp16, 64-token blocks, 131,072-token context), KV
     heads split over the ranks.  A step scores (logits N(0, 2), softmax),
     classifies, sends the global coldest 30% two hops to the file tier
-    (orchkv_evict_cold_batch: the reference's file layout, 1 MiB runs, the
-    runs spread over the IO workers) and the next coldest 50% to pinned DRAM,
+    (orchkv_evict_cold_batch: the reference's file layout, 1 MiB runs) and
+    the next coldest 50% to pinned DRAM,
     leaving 20% in HBM.  The restore (untimed) promotes the DRAM blocks,
     reads the file blocks back into DRAM and promotes them too."""
 
@@ -1007,7 +1007,7 @@ def run_three_tier(args, torch, okv, rank, world, comm, dist):
             "tiers": {"gpu": TT["gpu"], "dram": TT["dram"], "files": round(1 - TT["gpu"] - TT["dram"], 2)},
             "sample": f"{tw.B} of the configuration's 16 requests (host RAM for the pinned DRAM "
                       f"tier and the RAM-backed files at one GPU); the same at every N",
-            "file_tier": f"{tw.base} (tmpfs), {tw.io_workers} IO workers",
+            "file_tier": f"{tw.base} (tmpfs); reads over {tw.io_workers} IO workers",
             "steps": n_steps, "ms_per_step": round(ms_max, 2),
             "value": round((f_tot + d_tot) / (ms_max * 1e-3), 1),
             "unit": "migrated blocks/s (to files + to DRAM, all ranks), wall-timed",

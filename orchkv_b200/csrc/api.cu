@@ -1458,11 +1458,15 @@ struct IoRun {
     size_t first, n;     // iovecs [first, first + n)
 };
 
-// Runs of a batch spread over the configured IO workers (the reference's
-// orchfs_io_workers, its IO worker pool size, src/tiered_store/io_worker.c:
-// 52-133): each worker takes the next run until all are done or one fails.
-// Runs write disjoint file ranges and disjoint buffers, so their order does
-// not matter.  Small batches stay on the calling thread.
+// Runs of a batch, in offset order.  Reads are spread over the configured IO
+// workers (the reference's orchfs_io_workers, its IO worker pool size,
+// src/tiered_store/io_worker.c:52-133): each worker takes the next run until
+// all are done or one fails; runs read disjoint file ranges into disjoint
+// buffers, so their order does not matter.  Writes stay on the calling
+// thread: writers into one file queue on the file's lock in the kernel, and
+// on a B200 box's tmpfs a 0.8 GB scattered two-hop evict wrote at 2.0 GB/s
+// with one thread against 1.8 with four and 1.3 with sixteen, while reading
+// it back ran at 4.7, 14.7 and 35.4 GB/s.
 bool io_runs(bool write, int fd, std::vector<iovec> &iov, const std::vector<IoRun> &runs)
 {
     std::atomic<size_t> next{0};
@@ -1473,6 +1477,7 @@ bool io_runs(bool write, int fd, std::vector<iovec> &iov, const std::vector<IoRu
                 ok = false;
     };
     size_t workers = g.cfg.orchfs_io_workers > 0 ? (size_t)g.cfg.orchfs_io_workers : 1;
+    if (write) workers = 1;
     if (workers > 64) workers = 64;
     if (workers > runs.size()) workers = runs.size();
     std::vector<std::thread> pool;
