@@ -15,9 +15,10 @@ memory, synchronises and calls tm_report_attn once per block from Python.
 Here one call, tm_report_attn_blockmean, reduces and records every report on
 the device in the reference's order (heads of a block in head order), so a
 sampled layer costs two kernel launches and no host round trip.  Reports
-whose ids would make two blocks share a tracker slot are the exception: they
-go through tm_report_attn one by one, in the hook's order, after the same
-device reduction.
+whose ids would make two blocks share a tracker slot take the same device
+reduction and then one device batch of reports in the hook's order, whose
+shared slots are applied in list order; only an id whose low 32 bits equal
+the device's no-block marker still goes through tm_report_attn one by one.
 
 The manager handle is an ``orchkv_core.tm_create`` handle, as in the
 reference; the manager's GPU work runs on torch's current stream.
@@ -168,7 +169,23 @@ class AttentionScoreCollector:
             ids32 = np.where(valid, ids & 0xFFFFFFFF, _NO_BLOCK).astype(np.uint32)
             ids_d = torch.from_numpy(ids32.view(np.int32)).to(w.device)
             self._reduce(w, dt, ids_d)
+        elif not np.any((ids[valid] & 0xFFFFFFFF) == _NO_BLOCK):
+            # blocks sharing tracker slots: the scores' reports in the hook's
+            # order (head by head, block by block) as one device batch, which
+            # applies a shared slot's reports in list order, as that many
+            # tm_report_attn calls would
+            scores = self._reduce(w, dt, None)
+            flat = np.flatnonzero(valid.reshape(-1))
+            ids_d = torch.from_numpy((ids.reshape(-1)[flat] & 0xFFFFFFFF).astype(np.uint32)
+                                     .view(np.int32)).to(w.device)
+            w_d = scores.reshape(-1)[torch.from_numpy(flat).to(w.device)].contiguous()
+            rc = self._C.tm_report_attn_batch_dev(self._tm, ids_d.data_ptr(), w_d.data_ptr(),
+                                                  len(flat))
+            if rc != 0:
+                raise RuntimeError(f"tm_report_attn_batch_dev failed: {rc}")
         else:
+            # an id whose low 32 bits are the device's no-block marker: one
+            # report at a time through the per-block call
             scores = self._reduce(w, dt, None).cpu()
             for h in range(heads):
                 for bi in range(nb):

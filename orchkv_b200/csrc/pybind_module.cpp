@@ -376,6 +376,12 @@ PYBIND11_MODULE(orchkv_core, m)
           },
           py::arg("tm"), py::arg("avg_ptr"), py::arg("heads"), py::arg("kv_len"),
           py::arg("starts_ptr"), py::arg("ends_ptr"), py::arg("block_ids_ptr"), py::arg("n"));
+    m.def("tm_report_attn_batch_dev",
+          [](uintptr_t tm, uintptr_t ids, uintptr_t weights, uint32_t n) {
+              return tm_report_attn_batch_dev(P<tiered_manager_t>(tm), P<const uint32_t>(ids),
+                                              P<const float>(weights), n);
+          },
+          py::arg("tm"), py::arg("block_ids_ptr"), py::arg("weights_ptr"), py::arg("n"));
     m.def("tm_report_attn_blockmean",
           [](uintptr_t tm, uintptr_t weights, int dtype, uint32_t batch, uint32_t heads,
              uint32_t q_len, uint32_t kv_len, uint32_t block_size, uintptr_t ids,
