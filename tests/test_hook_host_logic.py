@@ -1,10 +1,12 @@
 """Host logic of orchkv_b200.attention_hook that needs no GPU: the report ids
 the collector chooses (against oracle/hook_model.py, the reference hook's
 choice, python/orchkv/vllm_integration/attention_hook.py:171-182) and the
-check that sends a layer to the device reports or to the per-block host
-fallback.  The device records a block column's heads in order and the
-columns in parallel, so it is exact only when no tracker slot is shared by
-two columns and no id's low 32 bits equal the no-block marker."""
+check that sends a layer to the fused device reports or to the ordered
+device batch.  The fused reports record a block column's heads in order and
+the columns in parallel, so they are exact only when no tracker slot is
+shared by two columns and no id's low 32 bits equal the no-block marker;
+other layers' reports go as one device batch in the hook's order (or, for
+the marker, one host call each)."""
 import numpy as np
 import pytest
 import torch
@@ -53,7 +55,7 @@ def test_device_path_check():
     # every head of a column shares one id (block-table mode): heads in order
     shared_in_column = np.tile(np.arange(nb, dtype=np.int64) * 5, (heads, 1))
     assert c._device_order_ok(shared_in_column)
-    # two columns' ids on one tracker slot: the host fallback
+    # two columns' ids on one tracker slot: the ordered device batch
     cross = distinct.copy()
     cross[2, 4] = cross[1, 1] + CAP
     assert not c._device_order_ok(cross)
