@@ -556,6 +556,9 @@ def run_sharded(args, torch, okv, rank, world, comm, dist, link_d2h):
                                "slot) over every rank's eligible blocks"},
         }
     sw.close()
+    if out is not None and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = _ref_pool_sample((SH["L"], SH["Hq"], SH["Hkv"], SH["D"], SH["T"],
+                                                SH["tpb"]), 0, 1.0 - SH["capacity"])
     return out
 
 
@@ -767,6 +770,9 @@ def run_multiplexed(args, torch, okv, rank, world, dist, link):
             "round_trip_checksums_equal": all(bool(r[2]) for r in allv),
         }
     mw.close()
+    if out is not None and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = _ref_pool_sample((MX["L"], MX["Hq"], MX["Hkv"], MX["D"], MX["T"],
+                                                MX["tpb"]), 1, 0.5)
     return out
 
 
@@ -1019,7 +1025,81 @@ def run_three_tier(args, torch, okv, rank, world, comm, dist):
             "round_trip_checksums_equal": all(bool(r[3]) for r in allv),
         }
     tw.close()
+    if out is not None and world == 1 and not args.no_cpu_baseline:
+        # 8 of the 80 layers: the per-block reference path takes seconds per step
+        out["cpu_baseline"] = _ref_pool_sample((8, TT["Hq"], TT["Hkv"], TT["D"], TT["T"],
+                                                TT["tpb"]), 0, TT["dram"],
+                                               file_frac=1.0 - TT["gpu"] - TT["dram"])
     return out
+
+
+def _ref_pool_sample(geo, dtype, evict_frac, file_frac=0.0, steps=2):
+    """The reference's own path on a one-request sample of a pool's shape
+    (its scheduler and per-block data plane compiled from its sources into
+    oracle/_ref), on one host core: a step reduces the request's attention
+    probabilities (logits N(0, 2), softmax) to per-block mass with the C
+    restatement of the managers' reduction, runs the reference scheduler
+    (attn_tracker_update_batch, tm_step_done, tm_schedule_once, coldest-first
+    order), then sends the coldest `file_frac` of the blocks two hops to its
+    file tier (orchkv_evict_cold per block) and the next `evict_frac` to DRAM
+    (orchkv_evict_to_dram per block); the restore (untimed) promotes them
+    back.  geo = (layers, q heads, kv heads, d_head, tokens, tokens per block).
+    Returns migrated blocks/s and the step time."""
+    from oracle import oracle as O
+    if not O.ref_available():
+        return None
+    Ly, Hq, Hkv, D, T, tpb = geo
+    nb = T // tpb
+    n = Ly * Hkv * nb
+    slab = tpb * D * 2 * 2
+    rng = np.random.default_rng(0)
+    probs = np.empty((Ly, Hq, T), np.float32)
+    for layer in range(Ly):
+        x = rng.normal(0, 2, (Hq, T)).astype(np.float32)
+        x = np.exp(x - x.max(-1, keepdims=True))
+        probs[layer] = x / x.sum(-1, keepdims=True)
+    kv = rng.standard_normal((Hkv, T, D)).astype(np.float16)
+    R = O.ref()
+    base = b"/dev/shm/orchkv_ref_pool"
+    assert R.ref_api_init(0, (n + 64) * slab, (n + 64) * slab, tpb, D, dtype, 4, nb + 8,
+                          base) == 0
+    ctx = R.ref_api_request_create(0, Ly, Hkv)
+    for layer in range(Ly):
+        assert R.ref_api_prefill(ctx, layer, kv.ctypes.data, kv.ctypes.data, T) == 0
+    rtm = O.RefTM(tracker_cap=n, max_blocks=n, ema_lambda=0.9, alpha=0.5, beta=0.3, gamma=0.2,
+                  recency_tau=50.0, cooldown_sec=0.0)
+    rtm.register_range(n)
+    ids = np.arange(n, dtype=np.uint64)
+    k_file, k_all = int(file_frac * n), int((file_frac + evict_frac) * n)
+    vict = np.zeros(max(k_all, 1), np.uint64)
+    times = []
+    for s in range(steps + 1):
+        t0 = time.perf_counter()
+        mass = O.score_blocks(probs, Hq, Hkv, tpb).reshape(-1)
+        c = R.ref_arm_sched_step(rtm.h, ids, mass.copy(), n, 1.0, k_all, vict, np.zeros(3))
+        v = vict[:c].astype(np.int64)           # coldest first
+        lhb = np.stack([v // (Hkv * nb), (v // nb) % Hkv, v % nb], 1).astype(np.uint32)
+        nf = min(k_file, c)
+        for i in range(nf):
+            assert R.ref_api_evict_cold(ctx, *lhb[i].tolist()) == 0
+        rest = np.ascontiguousarray(lhb[nf:].reshape(-1))
+        assert R.ref_api_migrate_list(ctx, rest, c - nf, 0, np.zeros(2)) == 0
+        dt = time.perf_counter() - t0
+        if s:
+            times.append(dt)
+        for i in range(nf):                      # back to the start (untimed)
+            assert R.ref_api_promote_storage(ctx, *lhb[i].tolist()) == 0
+        allb = np.ascontiguousarray(lhb.reshape(-1))
+        assert R.ref_api_migrate_list(ctx, allb, 0, c, np.zeros(2)) == 0
+    R.ref_api_request_destroy(ctx)
+    R.ref_api_shutdown()
+    rtm.close()
+    step_s = statistics.median(times)
+    return {"kind": "reference", "cores": 1, "value": round(c / step_s, 1),
+            "unit": "migrated blocks/s", "ms_per_step": round(step_s * 1e3, 1),
+            "sample": f"1 request x {Ly} layers x {Hkv} KV heads x {nb} blocks ({n} blocks): "
+                      f"scheduler step, coldest {round(100 * (file_frac + evict_frac))}% moved "
+                      f"block by block; median of {steps} steps after one"}
 
 
 # ---------------------------------------------------------------------------
