@@ -1707,7 +1707,7 @@ int orchkv_evict_cold_batch(kv_request_ctx_t *ctx, const uint32_t *lhb, uint32_t
         const size_t c0 = c * chunk, h = c % 2;
         const uint32_t k = (uint32_t)std::min<size_t>(chunk, io.size() - c0);
         OKV_CUDA_TRY(cudaEventSynchronize(g.ev_cold[h]));
-        if (c + 1 < n_chunks) {                  // its half was written in the last round
+        if (c + 1 < n_chunks) {                  // its half was written in the previous iteration
             rc = gather(c + 1);
             if (rc) return rc;
         }
