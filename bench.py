@@ -551,6 +551,13 @@ def run_sharded(args, torch, okv, rank, world, comm, dist, link_d2h):
             "probe_d2h_gbs_summed": round(sum(r[4] for r in allv), 1),
             "collective_ms_per_step": [round(r[3], 4) for r in allv] if world > 1 else None,
             "phases_ms_rank0": {k: round(v, 4) for k, v in phases.items()},
+            "limiter": {
+                "phase": "evict (gather-pack + device-to-host drain)",
+                "share_of_step_rank0": round(ev_ms / mean_ms, 3),
+                "frac_of_d2h_probe_per_rank": [round(r[2] / r[4], 3) if r[4] else None
+                                               for r in allv],
+                "bound": f"the box's host link, device-to-host: {sum(r[4] for r in allv):.1f} "
+                         f"GB/s summed over {world} rank(s), probed with all ranks copying"},
             "parity": {"global_coldest_k_equal": parity, "checked_blocks": int(len(idx)),
                        "rule": "union of the ranks' picks == the k smallest (hotness, rank, "
                                "slot) over every rank's eligible blocks"},
@@ -767,6 +774,15 @@ def run_multiplexed(args, torch, okv, rank, world, dist, link):
             "probe_both_directions_gbs_per_rank": [round(r[4], 1) for r in allv],
             "swap_overlapped": bool(ov[3].value),
             "phases_ms_rank0": {k: round(v, 4) for k, v in phases.items()},
+            "limiter": {
+                "phase": "swap (evict and promote, both copy directions at once)",
+                "share_of_step_rank0": round(phases["swap"] / (sum(step_ms) / len(step_ms)), 3),
+                "frac_of_two_way_probe_per_rank": [
+                    round(swap_bytes / (r[3] * 1e-3) / 1e9 / r[4], 3) if r[4] else None
+                    for r in allv],
+                "bound": f"the box's host link, both directions: "
+                         f"{sum(r[4] for r in allv):.1f} GB/s summed over {world} rank(s), "
+                         f"probed with all ranks copying"},
             "round_trip_checksums_equal": all(bool(r[2]) for r in allv),
         }
     mw.close()
@@ -1022,6 +1038,11 @@ def run_three_tier(args, torch, okv, rank, world, comm, dist):
             "file_write_gbs_per_rank": [round(r[1] * tw.slab / (r[4] * 1e-3) / 1e9, 2)
                                         for r in allv],
             "phases_ms_rank0": {k: round(v, 3) for k, v in phases.items()},
+            "limiter": {
+                "phase": "two-hop to files (pack, device-to-host, pwritev)",
+                "share_of_step_rank0": round(phases["two-hop to files"] / (sum(ms) / len(ms)), 3),
+                "bound": "the file writes: one writer thread per rank copying into the page "
+                         "cache (tmpfs)"},
             "round_trip_checksums_equal": all(bool(r[3]) for r in allv),
         }
     tw.close()
