@@ -1495,7 +1495,7 @@ def run_ours(args, rank, world, local_rank):
     # library sizes its staging for host inputs on first use)
     wl.step(e2e=True)
     wl.restore()
-    e2e_ms = []
+    e2e_ms, e2e_ph = [], {}
     for _ in range(max(1, min(args.steps, 5))):
         barrier()
         t0 = torch.cuda.Event(enable_timing=True)
@@ -1505,6 +1505,8 @@ def run_ours(args, rank, world, local_rank):
         t1.record()
         barrier()
         e2e_ms.append(t0.elapsed_time(t1))
+        for k, v in wl.phases().items():
+            e2e_ph.setdefault(k, []).append(v)
         c_e2e = wl.h_counts.tolist()
         wl.restore()
     assert wl.L.tm_stage_input_async(wl.tm.ref, None, 0) == 0      # the last step's upload
@@ -1662,6 +1664,7 @@ def run_ours(args, rank, world, local_rank):
                     "input_pipelining": "each step uploads the next step's host probabilities "
                                         "(tm_stage_input_async) while its swap runs; the "
                                         "next step's report reads that copy",
+                    "phases_ms_rank0": {k: round(sum(v) / len(v), 4) for k, v in e2e_ph.items()},
                     "h2d_bytes_per_step": int(wl.probs.numel() * 4 + wl.tok.numel() * 2
                                               + c_e2e[4] * wl.slab),
                     "d2h_bytes_per_step": int(c_e2e[2] * wl.slab + 32)},
