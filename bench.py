@@ -1576,7 +1576,7 @@ def run_ours(args, rank, world, local_rank):
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "bf16",
+            "dtype": "f32+bf16",          # scores, EMA and hotness in f32; KV slabs moved as bf16
             "data": "synthetic (seeded: logits N(0,2) + 1% heavy hitters, KV N(0,1))",
             "config": {"workload": WL["name"], "requests": WL["B"], "context": WL["T"],
                        "layers": WL["L"], "q_heads": WL["Hq"], "kv_heads": WL["Hkv"],
@@ -1949,7 +1949,7 @@ def run_reference(args, rank, world):
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "blocks/s",
             "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(m["step_s"] * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32+fp16",
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32+bf16",
             "data": "synthetic (seeded)", "config": {"workload": WL["name"],
                                                      "sample_requests": threads},
             "cpu_baseline": {"value": v, "unit": "blocks/s", "cores": threads,
