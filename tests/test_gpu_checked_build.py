@@ -3,9 +3,11 @@ data-plane kernel reads from memory is compared with its bound, an index out
 of range is recorded and its access skipped (nothing traps), and
 orchkv_sync / tm_sync report it.
 
-The small-shape GPU suites run once more in a child process on that build
-(ORCHKV_CHECKED=1 selects orchkv_b200/_checked/); the session ends by reading
-the check words and fails if any index was out of range.  The check words'
+The data-plane GPU suites run once more in a child process on that build
+(ORCHKV_CHECKED=1 selects orchkv_b200/_checked/): the small shapes, and the
+bench's own step at full size (1,835,008 slabs, 14-chunk evicts through the
+whole-evict staging and through the wrapping three-slot rings); the session
+ends by reading the check words and fails if any index was out of range.  The check words'
 plumbing is tested by a recorded violation that touches no other memory
 (orchkv_check_inject): orchkv_sync and tm_sync then return ORCHKV_ERR_CUDA
 until the tally is reset."""
@@ -19,12 +21,13 @@ pytestmark = pytest.mark.gpu
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 CHECKED_LIB = os.path.join(ROOT, "orchkv_b200", "_checked", "liborchkv_b200.so")
-SMALL_SHAPE = ["tests/test_gpu_pool.py", "tests/test_gpu_staged_evict.py",
+CHECKED_SUITES = ["tests/test_gpu_pool.py", "tests/test_gpu_staged_evict.py",
                "tests/test_gpu_staged_promote_swap.py", "tests/test_gpu_storage.py",
                "tests/test_gpu_sched.py", "tests/test_gpu_c4_callbacks.py",
                "tests/test_gpu_cpu_step_e2e.py", "tests/test_gpu_workloads.py",
                "tests/test_gpu_core_module.py", "tests/test_gpu_fast_manager.py",
-               "tests/test_gpu_kvcache_manager.py", "tests/test_gpu_report_aliasing.py"]
+               "tests/test_gpu_kvcache_manager.py", "tests/test_gpu_report_aliasing.py",
+               "tests/test_gpu_staged_input.py", "tests/test_gpu_fullsize.py"]
 
 PLUMBING = r'''
 import ctypes as C
@@ -65,10 +68,10 @@ def test_check_words_plumbing(cuda):
     assert r.returncode == 0 and "plumbing ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
 
 
-def test_small_shape_suites_on_checked_build(cuda):
+def test_data_plane_suites_on_checked_build(cuda):
     if not os.path.exists(CHECKED_LIB):
         pytest.fail("the checked build is missing: python -m orchkv_b200.build --checked")
-    r = _child(["-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider"] + SMALL_SHAPE,
+    r = _child(["-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider"] + CHECKED_SUITES,
                1500)
     tail = r.stdout[-3000:] + r.stderr[-2000:]
     assert r.returncode == 0, tail
