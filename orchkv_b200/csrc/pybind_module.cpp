@@ -304,6 +304,12 @@ PYBIND11_MODULE(orchkv_core, m)
                                                P<const void>(v));
           },
           py::arg("ctxs"), py::arg("k_ptr"), py::arg("v_ptr"));
+    m.def("block_checksums",
+          [](uintptr_t ids, uint32_t n, uintptr_t out, uintptr_t tiers) {
+              return orchkv_block_checksums(P<const uint32_t>(ids), n,
+                                            P<unsigned long long>(out), P<uint8_t>(tiers));
+          },
+          py::arg("block_ids_ptr"), py::arg("n"), py::arg("out_ptr"), py::arg("tiers_ptr") = 0);
     m.def("block_id_table",
           [](const std::vector<uintptr_t> &ctxs, uint32_t row_len, uintptr_t out) {
               auto l = ctx_list(ctxs);
@@ -382,6 +388,11 @@ PYBIND11_MODULE(orchkv_core, m)
                                               P<const float>(weights), n);
           },
           py::arg("tm"), py::arg("block_ids_ptr"), py::arg("weights_ptr"), py::arg("n"));
+    m.def("tm_stage_input_async",
+          [](uintptr_t tm, uintptr_t host, size_t bytes) {
+              return tm_stage_input_async(P<tiered_manager_t>(tm), P<const void>(host), bytes);
+          },
+          py::arg("tm"), py::arg("host_ptr"), py::arg("nbytes"));
     m.def("tm_report_attn_blockmean",
           [](uintptr_t tm, uintptr_t weights, int dtype, uint32_t batch, uint32_t heads,
              uint32_t q_len, uint32_t kv_len, uint32_t block_size, uintptr_t ids,

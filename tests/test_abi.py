@@ -113,3 +113,19 @@ def test_orchkv_core_names_and_defaults():
         assert re.search(kw + r":[^=,]*= " + re.escape(val) + r"\b", doc), kw
     assert re.search(r"tier:[^=,]*= 0\b", m.tm_register_block_id.__doc__)
     assert re.search(r"flags:[^=,]*= 0\b", m.tm_register_block_id.__doc__)
+
+
+def test_orchkv_core_tensor_level_extensions():
+    """The module's additions for device-resident inputs (no counterpart in
+    the reference binding): every batched data-plane and report call of the
+    C ABI is reachable from Python without ctypes."""
+    import orchkv_b200
+    m = orchkv_b200.core()
+    for n in ["append_token", "append_token_batch", "block_id_table", "block_checksums",
+              "evict_batch_to_dram", "promote_batch_to_gpu", "swap_batch", "evict_cold_batch",
+              "copy_token_blocks", "attach_scheduler", "set_stream", "sync", "tm_sync",
+              "tm_report_attn_probs", "tm_report_attn_ranges", "tm_report_attn_batch_dev",
+              "tm_report_attn_blockmean", "tm_stage_input_async", "tm_step_and_classify",
+              "tm_select_victims", "tm_select_victims_masked", "tm_select_prefetch"]:
+        assert hasattr(m, n), n
+    assert re.search(r"tiers_ptr:[^=,]*= 0\b", m.block_checksums.__doc__)

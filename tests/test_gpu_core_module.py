@@ -102,3 +102,68 @@ def test_core_module_errors_and_data_plane(core, cuda):
         assert core.request_destroy(ctx) == core.OK
     finally:
         assert core.shutdown() == core.OK
+
+
+def test_core_module_staged_report_and_checksums(core, cuda):
+    """The module's tm_stage_input_async and block_checksums: a report from a
+    host buffer staged ahead of the call scores exactly as the report from
+    device memory, and a block's checksum, computed where the block lives,
+    is unchanged by an evict to the DRAM tier and the promote back, with tier
+    codes 0 (HBM) and 1 (DRAM)."""
+    torch = cuda
+    g = torch.Generator(device="cuda").manual_seed(5)
+    R, Hq, Hkv, T, tpb = 2, 4, 2, 128, 64
+    n = R * Hkv * (T // tpb)
+    probs = torch.softmax(torch.randn(R, Hq, T, generator=g, device="cuda") * 2, -1)
+    host = probs.cpu().pin_memory()
+    rid = torch.arange(n, dtype=torch.int32, device="cuda")
+    scores = []
+    for staged in (False, True):
+        tm = core.tm_create(tracker_cap=64, cooldown_sec=0.0)
+        try:
+            for i in range(n):
+                core.tm_register_block_id(tm, i)
+            src = probs.data_ptr()
+            if staged:
+                assert core.tm_stage_input_async(tm, host.data_ptr(), host.numel() * 4) == core.OK
+                src = host.data_ptr()
+            assert core.tm_report_attn_probs(tm, src, R, Hq, Hkv, T, tpb, rid.data_ptr()) == core.OK
+            core.tm_step_done(tm)
+            scores.append(np.array([core.tm_get_block_score(tm, i) for i in range(n)], np.float32))
+        finally:
+            core.tm_destroy(tm)
+    assert (scores[0] > 0).all()
+    assert np.array_equal(scores[0].view(np.uint32), scores[1].view(np.uint32))
+
+    cfg = core.Config()
+    cfg.gpu_pool_bytes = 64 * 32768
+    cfg.dram_pool_bytes = 64 * 32768
+    assert core.init(cfg) == core.OK
+    try:
+        ctx = core.request_create(7, 2, 2)                  # 2 layers x 2 KV heads
+        for layer in range(2):
+            kv = torch.randn(2, 2, 100, 128, generator=g, device="cuda").half()
+            assert core.prefill(ctx, layer, kv[0].data_ptr(), kv[1].data_ptr(), 100) == core.OK
+        ids = torch.empty(8, dtype=torch.int32, device="cuda")   # [layer][head][block]
+        assert core.block_id_table([ctx], 100, ids.data_ptr()) == core.OK
+        out = torch.empty(8, dtype=torch.int64, device="cuda")
+        tiers = torch.empty(8, dtype=torch.uint8, device="cuda")
+
+        def sums():
+            assert core.block_checksums(ids.data_ptr(), 8, out.data_ptr(),
+                                        tiers.data_ptr()) == core.OK
+            torch.cuda.synchronize()
+            return out.cpu().numpy().copy(), tiers.cpu().numpy().copy()
+
+        before, t0 = sums()
+        assert (t0 == 0).all() and (before != 0).all()
+        assert core.evict_to_dram(ctx, 0, 1, 1) == core.OK    # layer 0, head 1, block 1: entry 3
+        mid, t1 = sums()
+        assert t1[3] == 1 and (np.delete(t1, 3) == 0).all()
+        assert np.array_equal(mid, before)
+        assert core.promote_to_gpu(ctx, 0, 1, 1) == core.OK
+        after, t2 = sums()
+        assert (t2 == 0).all() and np.array_equal(after, before)
+        assert core.request_destroy(ctx) == core.OK
+    finally:
+        assert core.shutdown() == core.OK
