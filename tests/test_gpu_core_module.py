@@ -129,6 +129,7 @@ def test_core_module_staged_report_and_checksums(core, cuda):
                 src = host.data_ptr()
             assert core.tm_report_attn_probs(tm, src, R, Hq, Hkv, T, tpb, rid.data_ptr()) == core.OK
             core.tm_step_done(tm)
+            core.tm_schedule_once(tm)                   # classifies: the scores are its hotness
             scores.append(np.array([core.tm_get_block_score(tm, i) for i in range(n)], np.float32))
         finally:
             core.tm_destroy(tm)
