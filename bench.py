@@ -483,7 +483,9 @@ def run_sharded(args, torch, okv, rank, world, comm, dist, link_d2h):
         L.orchkv_comm_exchange_time(comm, C.byref(C.c_float()), C.byref(C.c_uint32()))
     step_ms, ph_acc, evicted, xch = [], {}, 0, [0.0, 0]
     n_steps = min(args.steps, 5)          # a secondary workload: a few steps keep the run short
-    for _ in range(n_steps):
+    pk_ms, pk_bytes, pk_chunks, pr_ms = C.c_float(), C.c_ulonglong(), C.c_uint32(), C.c_float()
+    chunk_ms, n_chunk_ms = (C.c_float * 1024)(), C.c_uint32()
+    for i in range(n_steps):
         barrier()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record()
@@ -499,7 +501,13 @@ def run_sharded(args, torch, okv, rank, world, comm, dist, link_d2h):
             L.orchkv_comm_exchange_time(comm, C.byref(ms), C.byref(calls))
             xch[0] += ms.value
             xch[1] += calls.value
+        if i == n_steps - 1:                          # the last timed evict's pack kernels
+            L.orchkv_last_migration_profile(C.byref(pk_ms), C.byref(pk_bytes),
+                                            C.byref(pk_chunks), C.byref(pr_ms))
+            L.orchkv_last_pack_chunks(chunk_ms, 1024, C.byref(n_chunk_ms))
         sw.restore()
+    chunk_ms = [chunk_ms[i] for i in range(min(1024, n_chunk_ms.value))]
+    hbm_peak = peaks()[0]
     # checked step (untimed): the ranks' union of picks vs the global order
     view = {}
     sw.step(check=lambda: view.update(v=sw.selection_view()))
@@ -551,6 +559,14 @@ def run_sharded(args, torch, okv, rank, world, comm, dist, link_d2h):
             "probe_d2h_gbs_summed": round(sum(r[4] for r in allv), 1),
             "collective_ms_per_step": [round(r[3], 4) for r in allv] if world > 1 else None,
             "phases_ms_rank0": {k: round(v, 4) for k, v in phases.items()},
+            "pack_rank0": {"kernel": "evict pack (HBM gather -> staging ring), 32 KB slabs",
+                           "ms": round(pk_ms.value, 4), "bytes": pk_bytes.value,
+                           "achieved_gbs": round(pk_bytes.value / max(pk_ms.value, 1e-9) / 1e6, 1),
+                           "frac": round(pk_bytes.value / max(pk_ms.value, 1e-9) / 1e6
+                                         / hbm_peak, 4),
+                           "first_chunk": pack_first_chunk(chunk_ms, pk_bytes.value,
+                                                           pk_chunks.value, hbm_peak),
+                           "chunks": pk_chunks.value},
             "limiter": {
                 "phase": "evict (gather-pack + device-to-host drain)",
                 "share_of_step_rank0": round(ev_ms / mean_ms, 3),
