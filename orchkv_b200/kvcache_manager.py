@@ -20,6 +20,13 @@ What changes is where the per-block work of a decode step runs:
   ``torch.cat`` per tensor instead of one copy per block (:270-315); the
   result is the same.
 
+The bookkeeping is organised around tier moves: every change of a block's
+tier goes through ``_relocate``, which moves the bytes, counts the move
+under the statistic the reference keeps for it and tells the tracker the
+new tier where the reference does (not for a file read back into DRAM,
+:513-527); eviction, spill and promotion candidates come from one stable
+ranking by access count (``_ranked``).
+
 Block ids come from a counter, registered with the reference binding's
 positional quirk (``tm_register_block_id(tm, bid, flags, GPU_HBM)``: a sink
 block lands on tier 1, :157-161).  Blocks whose ids would share a tracker
@@ -30,7 +37,9 @@ from __future__ import annotations
 
 import logging
 import os
+from collections import Counter
 from dataclasses import dataclass
+from operator import attrgetter
 from pathlib import Path
 from typing import Optional
 
@@ -52,6 +61,13 @@ TIER_DRAM = 1
 TIER_SSD = 2
 
 _TIER_NAMES = {TIER_GPU: "GPU", TIER_DRAM: "DRAM", TIER_SSD: "SSD"}
+
+# the statistic each tier move counts under, in the order get_stats lists them
+_MOVES = {(TIER_GPU, TIER_DRAM): "gpu_to_dram", (TIER_DRAM, TIER_GPU): "dram_to_gpu",
+          (TIER_DRAM, TIER_SSD): "dram_to_ssd", (TIER_SSD, TIER_DRAM): "ssd_to_dram"}
+
+# GPU-budget thresholds of one schedule cycle (kvcache_manager.py:381, 387, 422)
+_EVICT_ABOVE, _EVICT_DOWN_TO, _PROMOTE_BELOW = 0.85, 0.70, 0.60
 
 
 @dataclass
@@ -76,21 +92,16 @@ class KVCacheManager:
     def __init__(self, n_layers: int, n_kv_heads: int, head_dim: int, block_size: int = 16,
                  dtype: torch.dtype = torch.float16, gpu_budget_bytes: int = 0,
                  ssd_dir: Optional[str] = None, sink_tokens: int = 4):
-        self.n_layers = n_layers
-        self.n_kv_heads = n_kv_heads
-        self.head_dim = head_dim
-        self.block_size = block_size
-        self.dtype = dtype
-        self.gpu_budget_bytes = gpu_budget_bytes
-        self.ssd_dir = ssd_dir
-        self.sink_tokens = sink_tokens
-        self._block_bytes = 2 * n_kv_heads * block_size * head_dim * dtype.itemsize
-        self._next_block_id = 0
-        self._total_tokens = 0
+        self.n_layers, self.n_kv_heads, self.head_dim = n_layers, n_kv_heads, head_dim
+        self.block_size, self.dtype = block_size, dtype
+        self.gpu_budget_bytes, self.ssd_dir, self.sink_tokens = gpu_budget_bytes, ssd_dir, sink_tokens
+        self._shape = (2, n_kv_heads, block_size, head_dim)      # one block: [K|V][head][token][d]
+        self._block_bytes = int(np.prod(self._shape)) * dtype.itemsize
         self._blocks: list[list[KVBlock]] = [[] for _ in range(n_layers)]
+        self._ids = 0                                            # next block id
+        self._total_tokens = 0
         self._step = 0
-        self._stats = {"gpu_to_dram": 0, "dram_to_gpu": 0, "dram_to_ssd": 0,
-                       "ssd_to_dram": 0, "total_blocks": 0}
+        self._moves: Counter = Counter()
         if ssd_dir:
             Path(ssd_dir).mkdir(parents=True, exist_ok=True)
         self._C = core()
@@ -112,118 +123,110 @@ class KVCacheManager:
     def block_bytes(self) -> int:
         return self._block_bytes
 
-    def _all_blocks(self):
-        for layer_blocks in self._blocks:
-            yield from layer_blocks
+    def _every_block(self):
+        """All blocks, layer by layer, each layer's in token order."""
+        for layer in self._blocks:
+            yield from layer
+
+    def _tier_counts(self) -> Counter:
+        return Counter(b.tier for b in self._every_block())
 
     def gpu_kv_bytes(self) -> int:
-        return sum(1 for b in self._all_blocks() if b.tier == TIER_GPU) * self._block_bytes
+        return self._tier_counts()[TIER_GPU] * self._block_bytes
 
-    # -- blocks -------------------------------------------------------------------
-    def _alloc_block(self, layer: int, token_start: int) -> KVBlock:
-        bid = self._next_block_id
-        self._next_block_id += 1
-        sink = token_start < self.sink_tokens
-        blk = KVBlock(block_id=bid, layer=layer, token_start=token_start,
-                      capacity=self.block_size, is_sink=sink)
-        self._blocks[layer].append(blk)
-        self._stats["total_blocks"] += 1
-        if self._tm_handle is not None:
-            # positional, as the reference calls it: tier := flags, flags := GPU_HBM
-            self._C.tm_register_block_id(self._tm_handle, bid, 1 if sink else 0,
-                                         int(self._C.GPU_HBM))
-        return blk
-
-    def _make_block_tensor(self, device: str = "cuda") -> torch.Tensor:
-        shape = (2, self.n_kv_heads, self.block_size, self.head_dim)
-        if device == "cpu":
-            return torch.zeros(*shape, dtype=self.dtype, device="cpu", pin_memory=True)
-        return torch.zeros(*shape, dtype=self.dtype, device="cuda")
-
-    # -- past_key_values formats ------------------------------------------------------
+    # -- past_key_values formats ---------------------------------------------------
     @staticmethod
     def _to_legacy(past_key_values):
-        if HAS_DYNAMIC_CACHE and isinstance(past_key_values, DynamicCache):
-            if hasattr(past_key_values, "to_legacy_cache"):
-                return past_key_values.to_legacy_cache()
-            return tuple((lay.keys, lay.values) for lay in past_key_values.layers)
-        return past_key_values
+        """(key, value) per layer, from a DynamicCache or a legacy tuple."""
+        if not (HAS_DYNAMIC_CACHE and isinstance(past_key_values, DynamicCache)):
+            return past_key_values
+        convert = getattr(past_key_values, "to_legacy_cache", None)
+        if convert is not None:
+            return convert()
+        return tuple((lay.keys, lay.values) for lay in past_key_values.layers)
 
     @staticmethod
     def _from_legacy(legacy_cache):
-        if HAS_DYNAMIC_CACHE:
-            if hasattr(DynamicCache, "from_legacy_cache"):
-                return DynamicCache.from_legacy_cache(legacy_cache)
-            return DynamicCache(ddp_cache_data=legacy_cache)
-        return legacy_cache
+        """The DynamicCache HF models take back (the tuple where there is none)."""
+        if not HAS_DYNAMIC_CACHE:
+            return legacy_cache
+        build = getattr(DynamicCache, "from_legacy_cache", None)
+        return build(legacy_cache) if build is not None else DynamicCache(ddp_cache_data=legacy_cache)
 
-    # -- ingest -------------------------------------------------------------------------
+    # -- blocks -------------------------------------------------------------------
+    def _new_block(self, layer: int, token_start: int) -> KVBlock:
+        """A zeroed GPU block at the end of `layer`, registered with the tracker
+        as the reference registers it (tier := sink flag, flags := GPU_HBM)."""
+        blk = KVBlock(block_id=self._ids, layer=layer, token_start=token_start,
+                      capacity=self.block_size, is_sink=token_start < self.sink_tokens,
+                      gpu_data=torch.zeros(self._shape, dtype=self.dtype, device="cuda"))
+        self._ids += 1
+        self._blocks[layer].append(blk)
+        if self._tm_handle is not None:
+            self._C.tm_register_block_id(self._tm_handle, blk.block_id, int(blk.is_sink),
+                                         int(self._C.GPU_HBM))
+        return blk
+
+    def _held(self, layer: int) -> int:
+        return sum(b.token_count for b in self._blocks[layer])
+
+    def _absorb_range(self, layer: int, key: torch.Tensor, value: torch.Tensor, upto: int):
+        """New blocks for positions [held, upto) of `layer`, block_size at a time
+        (a partly filled last block is left as it is, as the reference does)."""
+        for start in range(self._held(layer), upto, self.block_size):
+            n = min(self.block_size, upto - start)
+            blk = self._new_block(layer, start)
+            blk.gpu_data[0, :, :n] = key[0, :, start:start + n]
+            blk.gpu_data[1, :, :n] = value[0, :, start:start + n]
+            blk.token_count = n
+
     def ingest_step(self, past_key_values) -> None:
         """Take in the KV cache of a forward pass (positions not yet managed)."""
-        legacy = self._to_legacy(past_key_values)
-        for layer, (k, v) in enumerate(legacy):
-            self._ingest_layer(layer, k, v, k.shape[2])
-        self._total_tokens = legacy[0][0].shape[2]
-
-    def _ingest_layer(self, layer: int, key: torch.Tensor, value: torch.Tensor, seq_len: int):
-        have = sum(b.token_count for b in self._blocks[layer])
-        for pos in range(have, seq_len, self.block_size):
-            end = min(pos + self.block_size, seq_len)
-            blk = self._alloc_block(layer, pos)
-            blk.token_count = end - pos
-            data = self._make_block_tensor("cuda")
-            data[0, :, :end - pos] = key[0, :, pos:end]
-            data[1, :, :end - pos] = value[0, :, pos:end]
-            blk.gpu_data = data
-            blk.tier = TIER_GPU
+        layers = self._to_legacy(past_key_values)
+        for layer, (key, value) in enumerate(layers):
+            self._absorb_range(layer, key, value, key.shape[2])
+        self._total_tokens = layers[0][0].shape[2]
 
     def append_token(self, past_key_values) -> None:
-        """Take in only the newest position of every layer."""
-        legacy = self._to_legacy(past_key_values)
-        for layer, (k, v) in enumerate(legacy):
-            seq_len = k.shape[2]
-            blocks = self._blocks[layer]
-            if not blocks:
-                self._ingest_layer(layer, k, v, seq_len)
+        """Take in only the newest position of every layer (one token, however
+        many positions the cache is ahead)."""
+        layers = self._to_legacy(past_key_values)
+        for layer, (key, value) in enumerate(layers):
+            if not self._blocks[layer]:
+                self._absorb_range(layer, key, value, key.shape[2])
                 continue
-            have = sum(b.token_count for b in blocks)
-            if seq_len <= have:
+            held = self._held(layer)
+            if key.shape[2] <= held:
                 continue
-            last = blocks[-1]
-            if last.token_count < last.capacity:
-                if last.tier != TIER_GPU:
-                    self._promote_block(last)
-                last.gpu_data[0, :, last.token_count] = k[0, :, -1]
-                last.gpu_data[1, :, last.token_count] = v[0, :, -1]
-                last.token_count += 1
-            else:
-                blk = self._alloc_block(layer, have)
-                blk.token_count = 1
-                data = self._make_block_tensor("cuda")
-                data[0, :, 0] = k[0, :, -1]
-                data[1, :, 0] = v[0, :, -1]
-                blk.gpu_data = data
-        self._total_tokens = legacy[0][0].shape[2]
+            tail = self._blocks[layer][-1]
+            if tail.token_count == tail.capacity:
+                tail = self._new_block(layer, held)
+            elif tail.tier != TIER_GPU:
+                self._promote_block(tail)
+            slot = tail.token_count
+            tail.gpu_data[0, :, slot] = key[0, :, -1]
+            tail.gpu_data[1, :, slot] = value[0, :, -1]
+            tail.token_count = slot + 1
+        self._total_tokens = layers[0][0].shape[2]
 
     # -- build -------------------------------------------------------------------------
     def build_past_kv(self, device: str = "cuda"):
         """past_key_values of every managed position, promoting blocks that are
         not on the GPU first."""
-        out = []
+        per_layer = []
         for layer in range(self.n_layers):
-            blocks = [b for b in self._blocks[layer] if b.token_count > 0]
-            if not blocks:
-                empty = torch.zeros(1, self.n_kv_heads, 0, self.head_dim, dtype=self.dtype,
-                                    device=device)
-                out.append((empty, empty.clone()))
-                continue
-            for b in blocks:
+            live = [b for b in self._blocks[layer] if b.token_count > 0]
+            for b in live:
                 if b.tier != TIER_GPU:
                     self._promote_block(b)
-            key = torch.cat([b.gpu_data[0, :, :b.token_count] for b in blocks], dim=1)
-            val = torch.cat([b.gpu_data[1, :, :b.token_count] for b in blocks], dim=1)
-            out.append((key.unsqueeze(0).to(device), val.unsqueeze(0).to(device)))
-        return self._from_legacy(tuple(out))
+            if live:
+                kv = [torch.cat([b.gpu_data[half, :, :b.token_count] for b in live], dim=1)
+                      .unsqueeze(0).to(device) for half in (0, 1)]
+            else:
+                kv = [torch.zeros(1, self.n_kv_heads, 0, self.head_dim, dtype=self.dtype,
+                                  device=device) for _ in (0, 1)]
+            per_layer.append(tuple(kv))
+        return self._from_legacy(tuple(per_layer))
 
     # -- attention reports ------------------------------------------------------------------
     def _bind_stream(self):
@@ -277,121 +280,127 @@ class KVCacheManager:
             self._C.tm_step_done(self._tm_handle)
 
     def schedule(self) -> dict:
-        """One cycle: usage to the manager, its schedule pass, then the
-        manager-side evictions, spills and promotions."""
+        """One cycle: the GPU usage to the manager and its schedule pass, then
+        the manager-side moves decided from the usage measured before them."""
         if self._tm_handle is None:
             return {}
-        gpu_bytes = self.gpu_kv_bytes()
         budget = self.gpu_budget_bytes
-        ratio = min(gpu_bytes / budget, 1.0) if budget > 0 else 0.0
+        used = self.gpu_kv_bytes()
+        ratio = min(used / budget, 1.0) if budget > 0 else 0.0
         self._bind_stream()
         self._C.tm_set_usage(self._tm_handle, ratio, 0.0)
         self._C.tm_schedule_once(self._tm_handle)
-        raw = self._C.tm_get_stats(self._tm_handle)
-        evicted = promoted = 0
-        if budget > 0 and gpu_bytes > budget * 0.85:
-            evicted = self._evict_cold_blocks()
+        tm_stats = self._C.tm_get_stats(self._tm_handle)
+        evicted = self._evict_cold_blocks() if budget > 0 and used > budget * _EVICT_ABOVE else 0
         if self.ssd_dir:
             self._spill_dram_to_ssd()
-        if budget > 0 and gpu_bytes < budget * 0.60:
-            promoted = self._promote_warm_blocks()
-        return {"step": self._step, "gpu_kv_bytes": gpu_bytes, "gpu_ratio": ratio,
-                "evicted": evicted, "promoted": promoted, "tm_stats": raw}
+        promoted = (self._promote_warm_blocks()
+                    if budget > 0 and used < budget * _PROMOTE_BELOW else 0)
+        return {"step": self._step, "gpu_kv_bytes": used, "gpu_ratio": ratio,
+                "evicted": evicted, "promoted": promoted, "tm_stats": tm_stats}
+
+    def _ranked(self, tier: int, holder: str, *, most_accessed_first: bool = False,
+                skip_sinks: bool = False) -> list[KVBlock]:
+        """Blocks on `tier` whose `holder` tensor exists, by access count (ties
+        keep layer-then-token order)."""
+        found = [b for b in self._every_block() if b.tier == tier
+                 and getattr(b, holder) is not None and not (skip_sinks and b.is_sink)]
+        return sorted(found, key=attrgetter("access_count"), reverse=most_accessed_first)
 
     def _evict_cold_blocks(self, max_evict: int = 8) -> int:
-        """Least-accessed non-sink GPU blocks to DRAM until 70% of the budget."""
-        cands = [b for b in self._all_blocks()
-                 if b.tier == TIER_GPU and not b.is_sink and b.gpu_data is not None]
-        cands.sort(key=lambda b: b.access_count)                 # stable: block order on ties
-        evicted = 0
-        for b in cands[:max_evict]:
-            if self.gpu_budget_bytes > 0 and self.gpu_kv_bytes() <= self.gpu_budget_bytes * 0.7:
+        """Least-accessed non-sink GPU blocks to DRAM, while the GPU holds more
+        than 70% of the budget."""
+        moved = 0
+        for blk in self._ranked(TIER_GPU, "gpu_data", skip_sinks=True)[:max_evict]:
+            if self.gpu_budget_bytes > 0 and \
+                    self.gpu_kv_bytes() <= self.gpu_budget_bytes * _EVICT_DOWN_TO:
                 break
-            self._demote_block(b)
-            evicted += 1
-        return evicted
+            self._demote_block(blk)
+            moved += 1
+        return moved
 
     def _promote_warm_blocks(self, max_promote: int = 4) -> int:
         """Most-accessed DRAM blocks back to the GPU."""
-        cands = [b for b in self._all_blocks() if b.tier == TIER_DRAM and b.dram_data is not None]
-        cands.sort(key=lambda b: b.access_count, reverse=True)
-        for b in cands[:max_promote]:
-            self._promote_block(b)
-        return min(len(cands), max_promote)
+        chosen = self._ranked(TIER_DRAM, "dram_data", most_accessed_first=True)[:max_promote]
+        for blk in chosen:
+            self._promote_block(blk)
+        return len(chosen)
 
     def _spill_dram_to_ssd(self, max_spill: int = 4):
-        """Least-accessed non-sink DRAM blocks to files, once at least 4 are in DRAM."""
-        dram = [b for b in self._all_blocks()
-                if b.tier == TIER_DRAM and b.dram_data is not None and not b.is_sink]
-        if len(dram) < 4:
-            return
-        dram.sort(key=lambda b: b.access_count)
-        for b in dram[:max_spill]:
-            self._save_to_ssd(b)
+        """Least-accessed non-sink DRAM blocks to files, once at least four
+        such blocks are in DRAM."""
+        ranked = self._ranked(TIER_DRAM, "dram_data", skip_sinks=True)
+        if len(ranked) >= 4:
+            for blk in ranked[:max_spill]:
+                self._save_to_ssd(blk)
 
-    # -- data movement ---------------------------------------------------------------------
+    # -- tier moves ---------------------------------------------------------------------------
+    def _file_of(self, blk: KVBlock) -> str:
+        return os.path.join(self.ssd_dir, f"blk_{blk.block_id}.bin")
+
+    def _relocate(self, blk: KVBlock, dest: int):
+        """Move one block's bytes one tier (GPU <-> pinned DRAM <-> file), count
+        the move and record the new tier with the tracker where the reference
+        does.  A promoted block keeps its pinned copy for its next demotion."""
+        src = blk.tier
+        if (src, dest) == (TIER_GPU, TIER_DRAM):
+            if blk.dram_data is None:
+                blk.dram_data = torch.empty(self._shape, dtype=self.dtype, pin_memory=True)
+            blk.dram_data.copy_(blk.gpu_data)
+            blk.gpu_data = None
+        elif (src, dest) == (TIER_DRAM, TIER_GPU):
+            blk.gpu_data = blk.dram_data.to("cuda")
+        elif (src, dest) == (TIER_DRAM, TIER_SSD):
+            blk.ssd_path = self._file_of(blk)
+            with open(blk.ssd_path, "wb") as fh:          # the tensor's raw bytes
+                fh.write(blk.dram_data.contiguous().view(torch.uint8).numpy().tobytes())
+            blk.dram_data = None
+        elif (src, dest) == (TIER_SSD, TIER_DRAM):
+            with open(blk.ssd_path, "rb") as fh:
+                raw = torch.frombuffer(bytearray(fh.read()), dtype=torch.uint8)
+            blk.dram_data = raw.view(self.dtype).reshape(self._shape).clone().pin_memory()
+        else:
+            raise ValueError(f"no move from tier {src} to tier {dest}")
+        blk.tier = dest
+        self._moves[_MOVES[(src, dest)]] += 1
+        if self._tm_handle is not None and (dest != TIER_DRAM or src == TIER_GPU):
+            tier = {TIER_GPU: self._C.GPU_HBM, TIER_DRAM: self._C.HOST_DRAM,
+                    TIER_SSD: self._C.SSD}[dest]
+            self._C.tm_set_block_tier(self._tm_handle, blk.block_id, int(tier))
+
     def _demote_block(self, blk: KVBlock):
-        if blk.tier != TIER_GPU or blk.gpu_data is None:
-            return
-        if blk.dram_data is None:
-            blk.dram_data = torch.empty_like(blk.gpu_data, device="cpu", pin_memory=True)
-        blk.dram_data.copy_(blk.gpu_data)
-        blk.gpu_data = None
-        blk.tier = TIER_DRAM
-        self._stats["gpu_to_dram"] += 1
-        if self._tm_handle is not None:
-            self._C.tm_set_block_tier(self._tm_handle, blk.block_id, int(self._C.HOST_DRAM))
+        if blk.tier == TIER_GPU and blk.gpu_data is not None:
+            self._relocate(blk, TIER_DRAM)
 
     def _promote_block(self, blk: KVBlock):
-        if blk.tier == TIER_SSD:
-            self._load_from_ssd(blk)
+        """To the GPU, through DRAM for a block in a file (a missing file
+        leaves the block where it is)."""
+        if blk.tier == TIER_SSD and blk.ssd_path is not None and os.path.exists(blk.ssd_path):
+            self._relocate(blk, TIER_DRAM)
         if blk.tier == TIER_DRAM and blk.dram_data is not None:
-            blk.gpu_data = blk.dram_data.to("cuda")
-            blk.tier = TIER_GPU
-            self._stats["dram_to_gpu"] += 1
-            if self._tm_handle is not None:
-                self._C.tm_set_block_tier(self._tm_handle, blk.block_id, int(self._C.GPU_HBM))
+            self._relocate(blk, TIER_GPU)
 
     def _save_to_ssd(self, blk: KVBlock):
-        if self.ssd_dir is None or blk.dram_data is None:
-            return
-        path = os.path.join(self.ssd_dir, f"blk_{blk.block_id}.bin")
-        with open(path, "wb") as fh:                  # the tensor's raw bytes (any dtype)
-            fh.write(blk.dram_data.contiguous().view(torch.uint8).numpy().tobytes())
-        blk.ssd_path = path
-        blk.dram_data = None
-        blk.tier = TIER_SSD
-        self._stats["dram_to_ssd"] += 1
-        if self._tm_handle is not None:
-            self._C.tm_set_block_tier(self._tm_handle, blk.block_id, int(self._C.SSD))
-
-    def _load_from_ssd(self, blk: KVBlock):
-        if blk.ssd_path is None or not os.path.exists(blk.ssd_path):
-            return
-        with open(blk.ssd_path, "rb") as fh:
-            raw = bytearray(fh.read())
-        shape = (2, self.n_kv_heads, self.block_size, self.head_dim)
-        data = torch.frombuffer(raw, dtype=torch.uint8).view(self.dtype).reshape(shape)
-        blk.dram_data = data.clone().pin_memory()
-        blk.tier = TIER_DRAM
-        self._stats["ssd_to_dram"] += 1
+        if self.ssd_dir is not None and blk.dram_data is not None:
+            self._relocate(blk, TIER_SSD)
 
     # -- statistics -----------------------------------------------------------------------
     def get_stats(self) -> dict:
-        n = {TIER_GPU: 0, TIER_DRAM: 0, TIER_SSD: 0}
-        for b in self._all_blocks():
-            if b.tier in n:
-                n[b.tier] += 1
+        n = self._tier_counts()
+        gpu, dram, ssd = n[TIER_GPU], n[TIER_DRAM], n[TIER_SSD]
+        migrations = {name: self._moves[name] for name in _MOVES.values()}
+        migrations["total_blocks"] = self._ids
         tm_stats = self._C.tm_get_stats(self._tm_handle) if self._tm_handle is not None else {}
         return {"step": self._step, "total_tokens": self._total_tokens,
-                "blocks_gpu": n[TIER_GPU], "blocks_dram": n[TIER_DRAM], "blocks_ssd": n[TIER_SSD],
-                "blocks_total": sum(n.values()),
-                "gpu_kv_mb": n[TIER_GPU] * self._block_bytes / (1 << 20),
-                "dram_kv_mb": n[TIER_DRAM] * self._block_bytes / (1 << 20),
-                "migrations": dict(self._stats), "tm": tm_stats}
+                "blocks_gpu": gpu, "blocks_dram": dram, "blocks_ssd": ssd,
+                "blocks_total": gpu + dram + ssd,
+                "gpu_kv_mb": gpu * self._block_bytes / (1 << 20),
+                "dram_kv_mb": dram * self._block_bytes / (1 << 20),
+                "migrations": migrations, "tm": tm_stats}
 
     def __repr__(self) -> str:
         s = self.get_stats()
+        tiers = " ".join(f"{_TIER_NAMES[t]}:{s['blocks_' + _TIER_NAMES[t].lower()]}"
+                         for t in (TIER_GPU, TIER_DRAM, TIER_SSD))
         return (f"KVCacheManager(tokens={s['total_tokens']}, blocks={s['blocks_total']} "
-                f"[GPU:{s['blocks_gpu']} DRAM:{s['blocks_dram']} SSD:{s['blocks_ssd']}], "
-                f"gpu_kv={s['gpu_kv_mb']:.1f}MB)")
+                f"[{tiers}], gpu_kv={s['gpu_kv_mb']:.1f}MB)")

@@ -69,183 +69,205 @@ class OrchKvConnectorMetadata(KVConnectorMetadata):
     req_block_map: dict[str, dict[int, int]] = field(default_factory=dict)
 
 
-class _LayerStore:
-    """Pinned slots holding saved blocks of one layer: block id -> slot."""
+class _SlotStore:
+    """Pinned copies of one layer's saved blocks, one fixed-size slot per
+    block id.  Freed slots are handed out again before the store grows; a
+    growth doubles the slot count (16 at least) and is planned, with its
+    byte cost, before any slot is assigned."""
 
-    def __init__(self, block_elems: int, dtype: torch.dtype):
-        self.block_elems, self.dtype = block_elems, dtype
-        self.buf = None
-        self.slot: dict[int, int] = {}
-        self.free: list[int] = []
+    def __init__(self, slot_elems: int, dtype: torch.dtype):
+        self.slot_elems, self.dtype = slot_elems, dtype
+        self.buf: torch.Tensor | None = None    # [capacity, slot_elems], pinned
+        self.where: dict[int, int] = {}         # block id -> slot
+        self.spare: list[int] = []              # freed slots
+        self.top = 0                            # slots ever handed out
 
-    def slots_for(self, block_ids: list[int], streams) -> list[int]:
-        out = []
-        for bid in block_ids:
-            s = self.slot.get(bid)
-            if s is None:
-                s = self.free.pop() if self.free else len(self.slot)
-                self.slot[bid] = s
-            out.append(s)
-        need = max(out) + 1 if out else 0
-        if self.buf is None or self.buf.shape[0] < need:
-            cap = max(need, 2 * (0 if self.buf is None else self.buf.shape[0]), 16)
-            new = torch.empty(cap, self.block_elems, dtype=self.dtype).pin_memory()
+    @property
+    def capacity(self) -> int:
+        return 0 if self.buf is None else self.buf.shape[0]
+
+    @property
+    def slot_bytes(self) -> int:
+        return self.slot_elems * self.dtype.itemsize
+
+    def growth_for(self, block_ids: list[int]) -> int:
+        """Slot count the store needs to take `block_ids` (its capacity if none)."""
+        fresh = len({b for b in block_ids if b not in self.where})
+        top = self.top + max(0, fresh - len(self.spare))
+        return self.capacity if top <= self.capacity else max(top, 2 * self.capacity, 16)
+
+    def assign(self, block_ids: list[int], capacity: int, busy_streams) -> list[int]:
+        """Slots of `block_ids`, new ones assigned, the store grown to
+        `capacity` first (copies in flight on the old buffer end before it
+        is copied over)."""
+        if capacity > self.capacity:
+            grown = torch.empty(capacity, self.slot_elems, dtype=self.dtype).pin_memory()
             if self.buf is not None:
-                for st in streams:                   # copies in flight on the old buffer
-                    st.synchronize()
-                new[: self.buf.shape[0]].copy_(self.buf)
-            self.buf = new
-        return out
+                for stream in busy_streams:
+                    stream.synchronize()
+                grown[: self.buf.shape[0]].copy_(self.buf)
+            self.buf = grown
+        slots = []
+        for b in block_ids:
+            if b not in self.where:
+                if self.spare:
+                    self.where[b] = self.spare.pop()
+                else:
+                    self.where[b] = self.top
+                    self.top += 1
+            slots.append(self.where[b])
+        return slots
 
-    def release(self, bid: int):
-        s = self.slot.pop(bid, None)
-        if s is not None:
-            self.free.append(s)
+    def drop(self, block_id: int):
+        slot = self.where.pop(block_id, None)
+        if slot is not None:
+            self.spare.append(slot)
+
+
+class _CopyLane:
+    """One copy direction: its CUDA stream and the blocks it was asked to move."""
+
+    def __init__(self):
+        self.stream = torch.cuda.Stream()
+        self.requested = 0
 
 
 class OrchKvConnectorWorker:
-    """Worker side: batched GPU <-> pinned DRAM block copies."""
+    """Worker role.  Each layer's saved blocks sit in a pinned slot store; a
+    layer's save or load is one orchkv_copy_token_blocks launch between
+    vLLM's cache tensor and that store (per-block copies for a cache whose
+    blocks are not contiguous chunks), saves on one lane and loads on the
+    other, loads ordered after the saves issued before them, and a layer's
+    load awaited through the event recorded after it.  The reference worker
+    also opens the orchkv data plane with a DRAM pool of `dram_pool_bytes`
+    it never copies through; these copies need no pool, so the setting caps
+    the pinned bytes the stores may hold instead (a save that would pass it
+    raises RuntimeError and changes nothing)."""
 
     def __init__(self, orchkv_cfg: dict[str, Any]):
-        self._kv_caches: dict[str, torch.Tensor] = {}
-        self._save_stream = torch.cuda.Stream()
-        self._load_stream = torch.cuda.Stream()
-        self._pending_saves: list[tuple[str, int]] = []
-        self._pending_loads: list[tuple[str, int]] = []
-        self._load_events: dict[str, torch.cuda.Event] = {}
-        self._stores: dict[str, _LayerStore] = {}
-        self._lock = threading.Lock()
-        self._save_count = 0
-        self._load_count = 0
-        self._initialized = False
-        self._orchkv_cfg = orchkv_cfg
+        self._pinned_limit = int(orchkv_cfg.get("dram_pool_bytes", 8 << 30))
+        self._caches: dict[str, torch.Tensor] = {}
+        self._stores: dict[str, _SlotStore] = {}
+        self._saves, self._loads = _CopyLane(), _CopyLane()
+        self._load_done: dict[str, torch.cuda.Event] = {}
+        self._mu = threading.Lock()
         self._C = core()
 
-    def _ensure_init(self):
-        if self._initialized:
-            return
-        cfg = self._C.Config()
-        cfg.gpu_pool_bytes = 0  # GPU memory is managed by vLLM
-        cfg.dram_pool_bytes = self._orchkv_cfg.get("dram_pool_bytes", 8 * (1 << 30))
-        cfg.d_head = self._orchkv_cfg.get("d_head", 128)
-        cfg.tokens_per_block = self._orchkv_cfg.get("tokens_per_block", 16)
-        cfg.num_cuda_streams = self._orchkv_cfg.get("num_cuda_streams", 4)
-        cfg.orchfs_io_workers = self._orchkv_cfg.get("io_workers", 4)
-        self._C.init(cfg)
-        self._initialized = True
-
     def register_kv_caches(self, kv_caches: dict[str, torch.Tensor]):
-        self._kv_caches = kv_caches
-        self._ensure_init()
+        self._caches = kv_caches
         logger.info("OrchKvConnector: registered %d KV cache layers", len(kv_caches))
 
-    def _store(self, layer_name: str, kv_layer: torch.Tensor) -> _LayerStore:
-        st = self._stores.get(layer_name)
-        if st is None:
-            st = _LayerStore(kv_layer[0].numel(), kv_layer.dtype)
-            self._stores[layer_name] = st
-        return st
+    def _pinned_bytes(self) -> int:
+        return sum(st.capacity * st.slot_bytes for st in self._stores.values())
+
+    def _reserve(self, layer_name: str, kv_layer: torch.Tensor,
+                 block_ids: list[int]) -> tuple[_SlotStore, list[int]]:
+        with self._mu:
+            st = self._stores.get(layer_name)
+            if st is None:
+                st = self._stores[layer_name] = _SlotStore(kv_layer[0].numel(), kv_layer.dtype)
+            capacity = st.growth_for(block_ids)
+            extra = (capacity - st.capacity) * st.slot_bytes
+            if extra and self._pinned_bytes() + extra > self._pinned_limit:
+                raise RuntimeError(
+                    f"OrchKv: saving {len(block_ids)} blocks of {layer_name} would hold "
+                    f"{self._pinned_bytes() + extra} pinned bytes, over dram_pool_bytes "
+                    f"({self._pinned_limit})")
+            return st, st.assign(block_ids, capacity, (self._saves.stream, self._loads.stream))
 
     @staticmethod
-    def _batched(kv_layer: torch.Tensor) -> bool:
+    def _contiguous_blocks(kv_layer: torch.Tensor) -> bool:
         chunk = kv_layer[0].numel() * kv_layer.element_size()
         return (kv_layer[0].is_contiguous() and kv_layer.stride(0) == kv_layer[0].numel()
                 and chunk % 16 == 0 and kv_layer.data_ptr() % 16 == 0)
 
-    def _copy(self, kv_layer, store, block_ids, slots, direction, stream):
-        chunk = kv_layer[0].numel() * kv_layer.element_size()
+    def _move(self, kv_layer: torch.Tensor, st: _SlotStore, block_ids: list[int],
+              slots: list[int], to_store: bool, stream: torch.cuda.Stream):
+        """Blocks between the cache tensor and their slots, on `stream` (the
+        caller's current stream)."""
+        if not self._contiguous_blocks(kv_layer):
+            for b, s in zip(block_ids, slots):
+                if to_store:
+                    st.buf[s].view(kv_layer[b].shape).copy_(kv_layer[b], non_blocking=True)
+                else:
+                    kv_layer[b].copy_(st.buf[s].view(kv_layer[b].shape), non_blocking=True)
+            return
         dev = kv_layer.device
         ids = torch.tensor(block_ids, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
         sl = torch.tensor(slots, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        chunk = kv_layer[0].numel() * kv_layer.element_size()
         rc = self._C.copy_token_blocks([kv_layer.data_ptr()], 1, 0, chunk, 1, kv_layer.shape[0],
-                                       ids.data_ptr(), len(block_ids), store.buf.data_ptr(),
-                                       direction, stream.cuda_stream, sl.data_ptr())
+                                       ids.data_ptr(), len(block_ids), st.buf.data_ptr(),
+                                       0 if to_store else 1, stream.cuda_stream, sl.data_ptr())
         if rc != 0:
             raise RuntimeError(f"orchkv_copy_token_blocks failed: {rc}")
-        # keep the index tensors alive until the copy has run
-        ids.record_stream(stream)
+        ids.record_stream(stream)              # the index tensors live until the copy ran
         sl.record_stream(stream)
 
     def save_kv_layer(self, layer_name: str, kv_layer: torch.Tensor,
                       metadata: OrchKvConnectorMetadata, block_ids: list[int] | None = None):
-        """Async save: GPU -> pinned DRAM, one launch for the layer."""
-        if block_ids is None:
-            block_ids = metadata.blocks_to_save.get(layer_name, [])
-        if not block_ids:
+        """The listed blocks (the metadata's for this layer by default) into
+        the layer's store, asynchronously, after the work already queued on
+        the current stream."""
+        ids = metadata.blocks_to_save.get(layer_name, []) if block_ids is None else block_ids
+        if not ids:
             return
-        self._save_stream.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(self._save_stream):
-            with self._lock:
-                st = self._store(layer_name, kv_layer)
-                slots = st.slots_for(block_ids, (self._save_stream, self._load_stream))
-            if self._batched(kv_layer):
-                self._copy(kv_layer, st, block_ids, slots, 0, self._save_stream)
-            else:
-                for bid, s in zip(block_ids, slots):
-                    st.buf[s].view(kv_layer[bid].shape).copy_(kv_layer[bid], non_blocking=True)
-            self._pending_saves.extend((layer_name, b) for b in block_ids)
-        self._save_count += len(block_ids)
+        st, slots = self._reserve(layer_name, kv_layer, ids)
+        lane = self._saves
+        lane.stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(lane.stream):
+            self._move(kv_layer, st, ids, slots, True, lane.stream)
+        lane.requested += len(ids)
 
     def wait_for_save(self):
-        """Block until all pending saves are complete."""
-        self._save_stream.synchronize()
-        self._pending_saves.clear()
+        self._saves.stream.synchronize()
 
     def start_load_kv(self, metadata: OrchKvConnectorMetadata):
-        """Kick off async loads: pinned DRAM -> GPU, one launch per layer."""
-        self._load_stream.wait_stream(torch.cuda.current_stream())
-        for layer_name, block_ids in metadata.blocks_to_load.items():
-            kv_layer = self._kv_caches.get(layer_name)
+        """Every layer's stored blocks back into the cache tensors,
+        asynchronously; blocks with no stored copy are left alone (warned)."""
+        lane = self._loads
+        lane.stream.wait_stream(torch.cuda.current_stream())
+        lane.stream.wait_stream(self._saves.stream)
+        for layer_name, ids in metadata.blocks_to_load.items():
+            kv_layer = self._caches.get(layer_name)
             if kv_layer is None:
                 continue
-            with self._lock:
+            with self._mu:
                 st = self._stores.get(layer_name)
-                have = [(b, st.slot[b]) for b in block_ids if b in st.slot] if st else []
-            missing = [b for b in block_ids if not st or b not in st.slot]
-            for b in missing:
-                logger.warning("OrchKv: no DRAM buffer for %s block %d", layer_name, b)
-            with torch.cuda.stream(self._load_stream):
-                if have:
-                    self._load_stream.wait_stream(self._save_stream)
-                    bids = [b for b, _ in have]
-                    slots = [s for _, s in have]
-                    if self._batched(kv_layer):
-                        self._copy(kv_layer, st, bids, slots, 1, self._load_stream)
-                    else:
-                        for b, s in have:
-                            kv_layer[b].copy_(st.buf[s].view(kv_layer[b].shape),
-                                              non_blocking=True)
-                    self._pending_loads.extend((layer_name, b) for b in bids)
-                event = self._load_stream.record_event()
-                self._load_events[layer_name] = event
-        self._load_count += sum(len(b) for b in metadata.blocks_to_load.values())
+                held = {b: st.where[b] for b in ids if b in st.where} if st else {}
+            for b in ids:
+                if b not in held:
+                    logger.warning("OrchKv: no DRAM buffer for %s block %d", layer_name, b)
+            with torch.cuda.stream(lane.stream):
+                if held:
+                    self._move(kv_layer, st, list(held), list(held.values()), False,
+                               lane.stream)
+                self._load_done[layer_name] = lane.stream.record_event()
+        lane.requested += sum(len(ids) for ids in metadata.blocks_to_load.values())
 
     def wait_for_layer_load(self, layer_name: str):
-        """Block until a specific layer's load is complete."""
-        event = self._load_events.pop(layer_name, None)
-        if event is not None:
-            event.synchronize()
+        done = self._load_done.pop(layer_name, None)
+        if done is not None:
+            done.synchronize()
 
     def free_blocks(self, layer_name: str, block_ids: list[int]):
-        """Release the DRAM slots of freed blocks."""
-        with self._lock:
+        """The stored copies of freed blocks are dropped (their slots reused)."""
+        with self._mu:
             st = self._stores.get(layer_name)
-            if st:
-                for b in block_ids:
-                    st.release(b)
+            for b in block_ids if st else ():
+                st.drop(b)
 
     def get_stats(self) -> dict[str, Any]:
-        return {"save_count": self._save_count, "load_count": self._load_count,
-                "dram_buffers": sum(len(s.slot) for s in self._stores.values())}
+        with self._mu:
+            held = sum(len(st.where) for st in self._stores.values())
+        return {"save_count": self._saves.requested, "load_count": self._loads.requested,
+                "dram_buffers": held}
 
     def shutdown(self):
-        self._save_stream.synchronize()
-        self._load_stream.synchronize()
-        with self._lock:
+        for lane in (self._saves, self._loads):
+            lane.stream.synchronize()
+        with self._mu:
             self._stores.clear()
-        if self._initialized:
-            self._C.shutdown()
-            self._initialized = False
 
 
 class OrchKvConnectorScheduler:

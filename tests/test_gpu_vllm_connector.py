@@ -117,3 +117,35 @@ def test_connector_roles_and_scheduler_metadata(cuda):
         assert wk.prefer_cross_layer_blocks
     finally:
         wk.shutdown()
+
+
+def test_worker_pinned_bytes_cap(cuda):
+    """dram_pool_bytes caps the pinned bytes the worker's stores hold: a save
+    that would grow a store past it raises and changes nothing; a freed slot
+    is reused without growing."""
+    torch = cuda
+    from orchkv_b200.vllm_connector import OrchKvConnectorMetadata, OrchKvConnectorWorker
+    kv = _caches(torch, n_layers=1, nb=64)
+    del kv["layer_1"]                                   # keep the contiguous layer
+    t = kv["layer_0"]
+    slot = t[0].numel() * t.element_size()              # 16 KB per block
+    w = OrchKvConnectorWorker({"dram_pool_bytes": 16 * slot})
+    w.register_kv_caches(kv)
+    try:
+        orig = t.clone()
+        w.save_kv_layer("layer_0", t, None, block_ids=list(range(16)))   # one 16-slot store
+        w.wait_for_save()
+        assert w.get_stats() == {"save_count": 16, "load_count": 0, "dram_buffers": 16}
+        with pytest.raises(RuntimeError):
+            w.save_kv_layer("layer_0", t, None, block_ids=[40])   # a 17th slot: 32 slots
+        assert w.get_stats() == {"save_count": 16, "load_count": 0, "dram_buffers": 16}
+        w.free_blocks("layer_0", [3])
+        w.save_kv_layer("layer_0", t, None, block_ids=[40])       # takes the freed slot
+        w.wait_for_save()
+        t[[0, 40]] = 0
+        w.start_load_kv(OrchKvConnectorMetadata(blocks_to_load={"layer_0": [0, 40]}))
+        w.wait_for_layer_load("layer_0")
+        assert torch.equal(t, orig)
+        assert w.get_stats() == {"save_count": 17, "load_count": 2, "dram_buffers": 16}
+    finally:
+        w.shutdown()
