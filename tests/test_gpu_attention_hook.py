@@ -351,3 +351,58 @@ def test_reports_more_heads_than_a_warp(hook_mod, cuda, oracle_mod, mode):
         assert np.count_nonzero(want["hits"]) >= nb
     finally:
         core.tm_destroy(tm)
+
+
+@pytest.mark.parametrize("shape,dtype", [((4, 8, 1, 8192), "float32"),
+                                         ((4, 8, 1, 8192), "bfloat16"),
+                                         ((32, 4, 1, 4096), "bfloat16")])
+@pytest.mark.parametrize("mode", ["default", "column"])
+def test_reports_over_many_tiles(cuda, oracle_mod, shape, dtype, mode):
+    """Decode-length weights (several CTA tiles of blocks in the block-mean
+    launch, the row-split instance for 32 rows): the oracle tracker is fed
+    the launch's own scores in the reference hook's order (head by head,
+    block by block), so with distinct ids per (head, block) and with every
+    head of a column on one id the tracker must be bit-identical."""
+    torch = cuda
+    import orchkv_b200 as o
+    core = o.core()
+    bsz, H, q, kv = shape
+    blk = 16
+    nb = kv // blk
+    code = {"float16": 0, "bfloat16": 1, "float32": 2}[dtype]
+    cap = 1 << 15
+    tm = core.tm_create(tracker_cap=cap, ema_lambda=0.9)
+    try:
+        orc = oracle_mod.OracleSched(cap, 0.9, 0.5, 0.3, 0.2, 50.0)
+        h_idx = torch.arange(H, device="cuda")[:, None]
+        b_idx = torch.arange(nb, device="cuda")[None, :]
+        if mode == "default":
+            tables = [(layer * H * nb + h_idx * nb + b_idx).int() for layer in range(2)]
+        else:
+            tables = [(20000 + 600 * layer + b_idx).expand(H, nb).int().contiguous()
+                      for layer in range(2)]
+        for bid in sorted({int(x) for t in tables for x in t.flatten().tolist()}):
+            assert core.tm_register_block_id(tm, bid, 0, 0) == 0
+            orc.register(bid)
+        scores = torch.empty(H, nb, dtype=torch.float32, device="cuda")
+        g = torch.Generator(device="cuda").manual_seed(21)
+        for step in range(3):
+            for layer in range(2):
+                aw = softmax_weights(torch, g, shape, getattr(torch, dtype)).contiguous()
+                assert core.tm_report_attn_blockmean(tm, aw.data_ptr(), code, bsz, H, q, kv, blk,
+                                                     tables[layer].data_ptr(),
+                                                     scores.data_ptr()) == 0
+                core.tm_sync(tm)
+                ids_h, sc_h = tables[layer].cpu().numpy(), scores.cpu().numpy()
+                for h in range(H):
+                    for bi in range(nb):
+                        orc.update(int(ids_h[h, bi]), float(sc_h[h, bi]))
+            core.tm_step_done(tm)
+            orc.step_done()
+        core.tm_sync(tm)
+        got, want = _state(tm), orc.state()
+        for key in ("hits", "last", "sum", "ema"):
+            assert np.array_equal(got[key], want[key]), key
+        assert np.count_nonzero(want["hits"]) >= 2 * nb
+    finally:
+        core.tm_destroy(tm)
