@@ -54,10 +54,10 @@ EVICT_FRAC, PROMOTE_FRAC = 0.25, 0.05
 # 8-request launch; the launch streams each request's rows once, so it scales
 SCORE_TRAFFIC_PER_REQUEST = 216.95e6 / 8
 # DRAM bytes (read + write) of one pack launch over a full staging chunk of
-# 32,768 slabs (536.9 MB of algorithmic bytes): 268.58 MB read + 218.92 MB
+# 32,768 slabs (536.9 MB of algorithmic bytes): 268.58 MB read + 216.66 MB
 # written by ncu on an 8-request step (the rest of its writes are still in L2
 # when the launch ends)
-PACK_TRAFFIC_PER_FULL_LAUNCH = 268.58e6 + 218.92e6
+PACK_TRAFFIC_PER_FULL_LAUNCH = 268.58e6 + 216.66e6
 PACK_FULL_LAUNCH_BYTES = 2 * 32768 * 8192
 NOMINAL_HBM_GBS = 7700.0          # B200 HBM3e, HGX figure
 
