@@ -227,7 +227,10 @@ int       tm_read_state(tiered_manager_t *m, float *sum, float *ema,
  * hit then update exactly as attn_tracker_update
  * (src/scheduler/attention_tracker.c:27-33,75-92).  Each array may be in
  * device memory (read in place) or in host memory, pinned or pageable
- * (copied once to the device on the manager's stream).  Asynchronous. */
+ * (copied once to the device on the manager's stream).  Asynchronous: a
+ * pageable host array may be reused when the call returns (the copy has
+ * taken it by then); a pinned one is read by the copy engine later and must
+ * stay unchanged until the manager's stream has run the call (tm_sync). */
 int tm_report_attn_probs(tiered_manager_t *m, const float *probs,
                          uint32_t n_rows, uint32_t n_q_heads, uint32_t n_kv_heads,
                          uint32_t row_len, uint32_t tokens_per_block,
@@ -267,7 +270,8 @@ int tm_stage_input_async(tiered_manager_t *m, const void *host, size_t bytes);
  * avg[h][t] as tm_notify_attn would; a block whose range is empty is not
  * reported.  Ids that share a tracker slot apply in list order.  Each array
  * may be in device or host memory (host arrays are copied once on the
- * manager's stream).  Asynchronous. */
+ * manager's stream).  Asynchronous; host arrays may be reused as for
+ * tm_report_attn_probs (pageable ones on return, pinned ones after tm_sync). */
 int tm_report_attn_ranges(tiered_manager_t *m, const float *avg, uint32_t heads,
                           uint32_t kv_len, const uint32_t *starts, const uint32_t *ends,
                           const uint32_t *block_ids, uint32_t n);
