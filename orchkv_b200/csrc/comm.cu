@@ -235,14 +235,15 @@ int orchkv_comm_allreduce_u32(void *h, const uint32_t *send, uint32_t *recv, uin
 
 /* Route the manager's selections through the communicator: k and fractions
  * then refer to the union of all ranks' blocks, ties split by rank order.
- * NULL detaches. */
+ * A one-rank communicator takes the same path (its exchanges are local
+ * copies and the picks those of a detached manager).  NULL detaches. */
 int tm_set_comm(tiered_manager_t *m, void *h)
 {
     TmImpl *t = tm_impl(m);
     if (!t) return ORCHKV_ERR_INVALID;
     std::lock_guard<std::mutex> g(t->mu);
     Comm *c = (Comm *)h;
-    if (!c || c->world <= 1) {
+    if (!c) {
         t->comm_reduce = nullptr;
         t->comm_gather = nullptr;
         t->comm_ctx = nullptr;

@@ -316,7 +316,7 @@ int launch_select(const SchedDev &d, const SelectScratch &sc, const SelectArgs &
                   cudaStream_t s)
 {
     const uint32_t n = d.cap;
-    const bool multi = a.reduce != nullptr && a.world > 1;
+    const bool multi = a.reduce != nullptr;      // a communicator is attached
     uint32_t *hg = multi ? sc.hist_global : sc.hist_local;
     const unsigned g = hist_grid(n);
 

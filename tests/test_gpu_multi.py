@@ -1,4 +1,5 @@
-"""Multi-GPU selection through NCCL (needs >= 2 GPUs; skipped otherwise).
+"""Multi-GPU selection through NCCL (two-rank cases need >= 2 GPUs and are
+skipped otherwise; the one-rank case runs on any GPU box).
 
 Each rank owns one shard of blocks (KV-head sharding) with its own manager;
 with a communicator set, tm_select_victims(k) selects the global coldest k:
@@ -63,7 +64,9 @@ def _worker(rank, world, port, k, q):
         c = int(cnt.item())
         picks = out[:c].cpu().numpy().tolist()
         st = m.state()
-        q.put((rank, picks, st["hot"][:N_PER_RANK].tolist()))
+        ms, calls = C.c_float(), C.c_uint32()
+        assert L.orchkv_comm_exchange_time(comm, C.byref(ms), C.byref(calls)) == 0
+        q.put((rank, picks, st["hot"][:N_PER_RANK].tolist(), calls.value))
         L.tm_set_comm(m.ref, None)
         m.close()
         L.orchkv_comm_destroy(comm)
@@ -85,7 +88,7 @@ def test_global_coldest_k_two_gpus(cuda, oracle_mod, k):
         p.start()
     res = {}
     for _ in range(world):
-        r, picks, hot = q.get(timeout=300)
+        r, picks, hot, _ = q.get(timeout=300)
         res[r] = (picks, hot)
     for p in procs:
         p.join(timeout=120)
@@ -95,6 +98,25 @@ def test_global_coldest_k_two_gpus(cuda, oracle_mod, k):
     got = np.sort(np.concatenate([np.array(res[r][0], np.int64) + r * N_PER_RANK
                                   for r in range(world)]))
     assert np.array_equal(got, want.astype(np.int64))
+
+
+@pytest.mark.parametrize("k", [7000, 1])
+def test_global_coldest_k_one_rank_communicator(cuda, oracle_mod, k):
+    """The same selection through a one-rank NCCL communicator, on any box
+    with a GPU: the histogram all-reduces and the tie all-gather of comm.cu
+    run, and the picks equal the oracle's coldest k of the rank's scores."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_worker, args=(0, 1, _free_port(), k, q))
+    p.start()
+    r, picks, hot, exchanges = q.get(timeout=300)
+    p.join(timeout=120)
+    assert p.exitcode == 0 and r == 0
+    assert exchanges >= 4              # three histogram all-reduces and the tie all-gather
+    hot = np.array(hot, np.float32)
+    want = oracle_mod.select_coldest(hot, np.ones(len(hot), np.uint8), k)
+    assert np.array_equal(np.sort(np.array(picks, np.int64)), want.astype(np.int64))
 
 
 def _sharded_worker(rank, world, port, q):
