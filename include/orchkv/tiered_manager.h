@@ -375,7 +375,8 @@ int tm_get_threshold_state(const tiered_manager_t *m, float *threshold_hot,
  * are split in (rank, block id) order via ncclAllGather, so each rank selects
  * exactly its share of the global order.  Communicator: orchkv_comm_create
  * (one rank takes the same path: its exchanges are local copies and its
- * picks those of a manager without one).  NULL detaches. */
+ * picks those of a manager without one); at most 48 ranks (else
+ * ORCHKV_ERR_INVALID).  NULL detaches. */
 int   orchkv_comm_unique_id(unsigned char *out128);
 void *orchkv_comm_create(int rank, int world, const unsigned char *id128, double timeout_s);
 int   orchkv_comm_destroy(void *comm);

@@ -243,6 +243,7 @@ int tm_set_comm(tiered_manager_t *m, void *h)
     if (!t) return ORCHKV_ERR_INVALID;
     std::lock_guard<std::mutex> g(t->mu);
     Comm *c = (Comm *)h;
+    if (c && c->world > kMaxSelectRanks) return ORCHKV_ERR_INVALID;   // tie gather room
     if (!c) {
         t->comm_reduce = nullptr;
         t->comm_gather = nullptr;

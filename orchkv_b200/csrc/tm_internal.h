@@ -39,6 +39,10 @@ struct StagedInput {
     unsigned long long seq = 0;
 };
 
+// Ranks a selection can split ties over: the tie all-gather lands in the 48
+// words of `small` after its first 16.
+constexpr int kMaxSelectRanks = 48;
+
 struct TmImpl {
     std::mutex mu;
     int device = 0;
@@ -136,7 +140,7 @@ struct TmImpl {
     okv::hist_reduce_fn comm_reduce = nullptr;
     okv::tie_gather_fn comm_gather = nullptr;
     void *comm_ctx = nullptr;
-    int comm_rank = 0, comm_world = 1;
+    int comm_rank = 0, comm_world = 1;      // comm_world <= kMaxSelectRanks
 };
 
 TmImpl *tm_impl(const tiered_manager_t *m);
