@@ -57,6 +57,24 @@ typedef struct dram_tier {
     pthread_mutex_t lock;
 } dram_tier_t;
 
+/* The file tier's snapshot (fields as in src/tiered_store/orchfs_tier.h:40-51;
+ * counters since orchkv_init: one write per slab written to a request's file,
+ * one read per slab read back, as src/api/orchkv_api.cu:453,496 record them,
+ * batched calls counting each slab). */
+typedef struct orchfs_tier {
+    bool            initialized;
+    char            base_dir[256];
+    size_t          slab_size;
+    uint64_t        total_writes;
+    uint64_t        total_reads;
+    uint64_t        bytes_written;
+    uint64_t        bytes_read;
+    pthread_mutex_t lock;
+} orchfs_tier_t;
+
+static inline uint64_t orchfs_tier_writes(const orchfs_tier_t *t) { return t->total_writes; }
+static inline uint64_t orchfs_tier_reads(const orchfs_tier_t *t) { return t->total_reads; }
+
 /* ---- reference entry points --------------------------------------------- */
 int  orchkv_init(const orchkv_config_t *config);
 int  orchkv_shutdown(void);
@@ -90,6 +108,7 @@ void orchkv_storage_flush(void);
 int  orchkv_get_stats(orchkv_stats_t *stats);
 gpu_tier_t  *orchkv_gpu_tier(void);
 dram_tier_t *orchkv_dram_tier(void);
+orchfs_tier_t *orchkv_orchfs_tier(void);   /* snapshot refreshed at each call */
 
 /* ---- B200 ------------------------------------------------------------------ */
 

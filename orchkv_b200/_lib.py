@@ -129,6 +129,7 @@ _SIGS = {
     "orchkv_get_stats": (i32, [P(OrchkvStats)]),
     "orchkv_gpu_tier": (vp, []),
     "orchkv_dram_tier": (vp, []),
+    "orchkv_orchfs_tier": (vp, []),
     "orchkv_set_stream": (i32, [vp]),
     "orchkv_sync": (i32, []),
     "orchkv_attach_scheduler": (i32, [P(TieredManager)]),

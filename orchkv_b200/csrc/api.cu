@@ -111,6 +111,7 @@ struct Sys {
     uint32_t last_swap_conflicts = 0;
     gpu_tier_t gsnap;
     dram_tier_t dsnap;
+    orchfs_tier_t fsnap;
     std::vector<uint32_t> gsnap_stack, dsnap_stack;
     // storage tier
     char base_dir[256] = {0};
@@ -845,6 +846,21 @@ dram_tier_t *orchkv_dram_tier(void)
     t.free_stack = g.dsnap_stack.data();
     t.free_top = top;
     t.is_pinned = true;
+    return &t;
+}
+
+orchfs_tier_t *orchkv_orchfs_tier(void)
+{
+    std::lock_guard<std::recursive_mutex> lk(g.mu);
+    if (!g.inited) return nullptr;
+    orchfs_tier_t &t = g.fsnap;
+    t.initialized = true;
+    snprintf(t.base_dir, sizeof(t.base_dir), "%s", g.base_dir);
+    t.slab_size = g.p.slab;
+    t.total_writes = g.storage_writes;
+    t.total_reads = g.storage_reads;
+    t.bytes_written = g.storage_bytes_written;
+    t.bytes_read = g.storage_bytes_read;
     return &t;
 }
 

@@ -57,6 +57,32 @@ def test_struct_layouts_match_reference_abi():
     assert C.sizeof(_lib.TmStats) == 232
 
 
+def test_orchfs_tier_snapshot_layout():
+    """orchfs_tier_t as the reference lays it out on x86-64 (computed from
+    src/tiered_store/orchfs_tier.h:40-51): 344 bytes, total_writes at 272,
+    total_reads at 280, the mutex at 304, so the reference's inline
+    orchfs_tier_writes / orchfs_tier_reads read the counters."""
+    src = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "orchkv/orchkv_api.h"
+int main(void) {
+  printf("%zu %zu %zu %zu\n", sizeof(orchfs_tier_t), offsetof(orchfs_tier_t, total_writes),
+         offsetof(orchfs_tier_t, total_reads), offsetof(orchfs_tier_t, lock));
+  return 0;
+}
+"""
+    import tempfile
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        open(c, "w").write(src)
+        exe = os.path.join(d, "t")
+        subprocess.run(["gcc", "-std=gnu11", "-I" + os.path.join(ROOT, "include"), c, "-o", exe],
+                       check=True)
+        out = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()
+    assert [int(x) for x in out] == [344, 272, 280, 304]
+
+
 def test_struct_layouts_against_headers():
     """Compile the public headers and compare sizeof() with the ctypes mirror."""
     src = r"""

@@ -33,6 +33,15 @@ def sp(cuda):
     assert L.orchkv_shutdown() == 0
 
 
+def _file_tier_counts(L):
+    """(total_writes, total_reads) of the orchkv_orchfs_tier() snapshot, read
+    at the reference's field offsets (src/tiered_store/orchfs_tier.h:40-51)."""
+    p = L.orchkv_orchfs_tier()
+    assert p
+    w = (C.c_uint64 * 2).from_address(p + 272)
+    return int(w[0]), int(w[1])
+
+
 def test_two_hop_round_trip_and_file_layout(sp, cuda):
     o, L = sp
     from oracle import oracle as O
@@ -51,6 +60,7 @@ def test_two_hop_round_trip_and_file_layout(sp, cuda):
     s = o.OrchkvStats()
     L.orchkv_get_stats(C.byref(s))
     assert s.dram_slabs_used == 0 and s.gpu_slabs_used == 2 * 4 - 3
+    assert _file_tier_counts(L) == (3, 0)            # one write per slab, as the reference
     # the file holds each slab at the reference offset
     with open(path, "rb") as fh:
         data = fh.read()
@@ -69,6 +79,7 @@ def test_two_hop_round_trip_and_file_layout(sp, cuda):
     assert tier == 1 and st == 3
     assert np.array_equal(read_host(L.orchkv_dram_pool_base() + slab * SLAB, SLAB),
                           expected_slab(k, v, h, b))
+    assert _file_tier_counts(L) == (3, 1)
     for (l, h, b) in cold:
         kp, vp = C.c_void_p(), C.c_void_p()
         assert L.orchkv_get_kv_block(ctx, l, h, b, C.byref(kp), C.byref(vp)) == 0
@@ -76,6 +87,7 @@ def test_two_hop_round_trip_and_file_layout(sp, cuda):
         assert np.array_equal(read_dev(kp.value, SLAB), expected_slab(k, v, h, b))
     L.orchkv_get_stats(C.byref(s))
     assert s.gpu_slabs_used == 8 and s.dram_slabs_used == 0
+    assert _file_tier_counts(L) == (3, 3)            # get_kv_block read the other two
     assert L.orchkv_request_destroy(ctx) == 0
     assert not os.path.exists(path)                             # removed with the request
 
@@ -203,8 +215,9 @@ def _storage_scenario(o, L, batched):
     files = {(l, h, b): data[((l * H + h) * MBPH + b) * SLAB:((l * H + h) * MBPH + b + 1) * SLAB]
              for l in range(2) for h in range(H) for b in range(12)
              if blocks[(l * H + h) * 12 + b][2] == 2}
+    counts = _file_tier_counts(L)
     assert L.orchkv_request_destroy(ctx) == 0
-    return out, g[:tg.value].tolist(), d[:td.value].tolist(), blocks, dram_used, files
+    return out, g[:tg.value].tolist(), d[:td.value].tolist(), blocks, dram_used, files, counts
 
 
 def test_storage_batches_equal_per_block_calls(cuda):
@@ -225,6 +238,7 @@ def test_storage_batches_equal_per_block_calls(cuda):
     b, p = results
     assert b[0] == p[0]
     assert b[0] == [[4, 4], [9, 3], [5, 3]]
+    assert b[-1] == (4 + 9, 5)               # file-tier counters: one per slab moved
     for x, y in zip(b[1:], p[1:]):
         assert x == y
 
