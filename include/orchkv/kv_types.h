@@ -94,6 +94,26 @@ static inline size_t dtype_size(DataType dt)
     }
 }
 
+/* Printable names of the enums (src/core/kv_types.h:142-178). */
+static inline const char *dtype_name(DataType dt)
+{
+    static const char *const n[] = {"fp16", "bf16", "fp32", "int8", "int4"};
+    return (unsigned)dt < sizeof(n) / sizeof(n[0]) ? n[dt] : "unknown";
+}
+
+static inline const char *tier_name(StorageTier t)
+{
+    static const char *const n[] = {"GPU_HBM", "HOST_DRAM", "NVM", "SSD", "NONE"};
+    return (unsigned)t < sizeof(n) / sizeof(n[0]) ? n[t] : "UNKNOWN";
+}
+
+static inline const char *block_state_name(KVBlockState s)
+{
+    static const char *const n[] = {"FREE", "ALLOCATED", "HOT", "WARM", "COLD", "MIGRATING",
+                                    "EVICTED"};
+    return (unsigned)s < sizeof(n) / sizeof(n[0]) ? n[s] : "UNKNOWN";
+}
+
 /* Bytes of one slab: K and V halves of tokens_per_block rows of d_head. */
 static inline size_t kv_block_data_bytes(uint32_t token_count, uint32_t d_head,
                                          DataType dtype)

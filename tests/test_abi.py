@@ -83,6 +83,34 @@ int main(void) {
     assert [int(x) for x in out] == [344, 272, 280, 304]
 
 
+def test_enum_names_as_the_reference_prints_them():
+    """dtype_name, tier_name and block_state_name return the reference's
+    strings (src/core/kv_types.h:142-178), "unknown"/"UNKNOWN" out of range."""
+    src = r"""
+#include <stdio.h>
+#include "orchkv/kv_types.h"
+int main(void) {
+  for (int i = 0; i <= 5; i++) printf("%s ", dtype_name((DataType)i));
+  for (int i = 0; i <= 5; i++) printf("%s ", tier_name((StorageTier)i));
+  for (int i = 0; i <= 7; i++) printf("%s ", block_state_name((KVBlockState)i));
+  printf("%s\n", tier_name((StorageTier)-1));
+  return 0;
+}
+"""
+    import tempfile
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        open(c, "w").write(src)
+        exe = os.path.join(d, "t")
+        subprocess.run(["gcc", "-std=gnu11", "-I" + os.path.join(ROOT, "include"), c, "-o", exe],
+                       check=True)
+        out = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()
+    assert out == ["fp16", "bf16", "fp32", "int8", "int4", "unknown",
+                   "GPU_HBM", "HOST_DRAM", "NVM", "SSD", "NONE", "UNKNOWN",
+                   "FREE", "ALLOCATED", "HOT", "WARM", "COLD", "MIGRATING", "EVICTED", "UNKNOWN",
+                   "UNKNOWN"]
+
+
 def test_struct_layouts_against_headers():
     """Compile the public headers and compare sizeof() with the ctypes mirror."""
     src = r"""
