@@ -40,6 +40,17 @@ def test_library_loads_and_exports_every_declared_function():
     assert set(names) <= set(_lib.exported_names())
 
 
+def test_accessors_before_init_return_null():
+    """The subsystem accessors answer NULL while the data plane is not
+    initialised (no CUDA call is made)."""
+    from orchkv_b200 import _lib
+    L = _lib.load()
+    assert not L.orchkv_is_initialized()
+    assert L.orchkv_gpu_tier() is None
+    assert L.orchkv_dram_tier() is None
+    assert L.orchkv_orchfs_tier() is None
+
+
 def test_no_gpu_code_path_without_library():
     # the package refuses to run without the native library (no CPU fallback)
     import orchkv_b200._lib as lb
